@@ -1,0 +1,493 @@
+"""Benchmark of the relm_mp fan-out / fan-in path on B200.
+
+One step = one pass of the hot path over one batch of the workload: the index
+plans of the batch are built (the plan cache is cleared first) and the six ops
+run through ``torch.ops.relm_mp`` (the reference's op API): fanout_scatter,
+fanout_scatter_backward, fanin_reduce sum and logsumexp, fanin_reduce_sum_backward
+and fanin_reduce_logsumexp_backward.
+
+Default workload (N=1): cfg2, the reference's large op benchmark - N=2^20
+nodes, E=2^24 messages, D=64, fp32, truncated Zipf(1.3) destinations in
+generation order ("unsorted"), uniform sources, values ~N(0,1); synthetic data
+from a fixed seed. Inputs are far larger than L2 (4.3 GB message matrix).
+
+metric: GB/s of compulsory HBM traffic (each referenced input row read once,
+every int64 index read once, each output row written once; plan/sort traffic
+not counted), summed over the six ops and all ranks, divided by the max over
+ranks of the step time (which does include the plan builds).
+
+--gpus N (torchrun, one rank per GPU): every rank processes its own batch
+(seed + rank); no collective on the data path (weak scaling). Timing uses CUDA
+events between barriers; the max over ranks is taken with an NCCL all-reduce.
+
+--impl reference: the reference's own CPU relm_mp library
+(``oracle/_ref/relm_mp_ref.so``, built from the reference sources) on the
+host cores, on a bounded edge sample of the same workload; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from relmo_b200 import workloads  # noqa: E402
+
+METRIC = "fanin/fanout GB/s vs HBM peak"
+UNIT = "GB/s"
+OPS = ("fanout_fwd", "fanout_bwd", "fanin_sum_fwd", "fanin_sum_bwd", "fanin_lse_fwd", "fanin_lse_bwd")
+REF_LIB = ROOT / "oracle" / "_ref" / "relm_mp_ref.so"
+
+
+# ---- helpers ---------------------------------------------------------------------------
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        try:
+            d = json.loads(p.read_text())
+            return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+        except Exception:
+            pass
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def ncu_traffic() -> dict:
+    """Per-launch DRAM bytes of each op's main kernel from a committed ncu summary, if any."""
+
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    if p.is_file():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            return {}
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    QUERY = (
+        "index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+        "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap"
+    )
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+
+    def start(self) -> None:
+        try:
+            self.path.parent.mkdir(parents=True, exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"],
+                stdout=self.fh, stderr=subprocess.DEVNULL,
+            )
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_workload(name: str, seed: int, device, dtype: torch.dtype) -> workloads.FanWorkload:
+    if name == "cfg2-unsorted":
+        return workloads.cfg2(seed=seed, device=device, sorted_dst=False, dtype=dtype)
+    if name == "cfg2-sorted":
+        return workloads.cfg2(seed=seed, device=device, sorted_dst=True, dtype=dtype)
+    if name == "cfg5":
+        return workloads.cfg5(seed=seed, device=device).to(device, dtype)
+    if name == "cfg1":
+        return workloads.cfg1(seed=seed, device=device).to(device, dtype)
+    raise ValueError(name)
+
+
+def op_bytes(wl: workloads.FanWorkload) -> dict[str, int]:
+    s = wl.x.element_size()
+    return {op: workloads.algorithmic_bytes(op, wl, s) for op in OPS}
+
+
+def run_ops(ops, wl: workloads.FanWorkload) -> dict[str, torch.Tensor]:
+    """The six ops of one step, as the autograd wrappers call them."""
+
+    out = {}
+    out["fanout_fwd"] = ops.fanout_scatter(wl.x, wl.src, wl.flat_dst, wl.out_rows)
+    out["fanout_bwd"] = ops.fanout_scatter_backward(wl.grad_slots, wl.src, wl.flat_dst, wl.x.size(0))
+    out["fanin_sum_fwd"] = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 0)
+    out["fanin_sum_bwd"] = ops.fanin_reduce_sum_backward(wl.grad_nodes, wl.flat_src, wl.dst, wl.msgs.size(0))
+    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+    out["fanin_lse_fwd"] = lse
+    out["fanin_lse_bwd"] = ops.fanin_reduce_logsumexp_backward(
+        wl.grad_nodes, wl.msgs, wl.flat_src, wl.dst, lse, wl.msgs.size(0)
+    )
+    return out
+
+
+def run_one_op(ops, wl, op: str, lse=None):
+    if op == "fanout_fwd":
+        return ops.fanout_scatter(wl.x, wl.src, wl.flat_dst, wl.out_rows)
+    if op == "fanout_bwd":
+        return ops.fanout_scatter_backward(wl.grad_slots, wl.src, wl.flat_dst, wl.x.size(0))
+    if op == "fanin_sum_fwd":
+        return ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 0)
+    if op == "fanin_lse_fwd":
+        return ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+    if op == "fanin_sum_bwd":
+        return ops.fanin_reduce_sum_backward(wl.grad_nodes, wl.flat_src, wl.dst, wl.msgs.size(0))
+    if op == "fanin_lse_bwd":
+        return ops.fanin_reduce_logsumexp_backward(wl.grad_nodes, wl.msgs, wl.flat_src, wl.dst, lse, wl.msgs.size(0))
+    raise ValueError(op)
+
+
+# ---- CPU baselines -------------------------------------------------------------------------
+
+
+def cpu_sample(workload: str, edges: int, seed: int = 0) -> workloads.FanWorkload:
+    """A bounded sample of the workload: the same node count, dimension and index
+    distributions, `edges` messages (generated on the CPU)."""
+
+    if workload.startswith("cfg2"):
+        return workloads.cfg2(seed=seed, device="cpu", sorted_dst=workload.endswith("sorted") and "un" not in workload,
+                              edges=edges)
+    if workload == "cfg5":
+        frac = edges / (1 << 26)
+        return workloads.cfg5(seed=seed, device="cpu", edges=edges, per_hub=max(1, int(100_000 * frac)))
+    return workloads.cfg1(seed=seed)
+
+
+def time_oracle_port(wl: workloads.FanWorkload, repeats: int = 1) -> tuple[float, int]:
+    """Seconds per step of the C oracle (single thread) on `wl`; returns (s, bytes)."""
+
+    from oracle import oracle
+
+    x, msgs = wl.x.float().numpy(), wl.msgs.float().numpy()
+    gs, gn = wl.grad_slots.float().numpy(), wl.grad_nodes.float().numpy()
+    src, fdst, fsrc, dst = wl.src.numpy(), wl.flat_dst.numpy(), wl.flat_src.numpy(), wl.dst.numpy()
+    best = math.inf
+    for _ in range(repeats):
+        t0 = time.perf_counter()
+        oracle.fanout_scatter(x, src, fdst, wl.out_rows)
+        oracle.fanout_scatter_backward(gs, src, fdst, x.shape[0])
+        oracle.fanin_reduce(msgs, fsrc, dst, wl.dim_size, 0)
+        oracle.fanin_reduce_sum_backward(gn, fsrc, dst, msgs.shape[0])
+        lse = oracle.fanin_reduce(msgs, fsrc, dst, wl.dim_size, 1)
+        oracle.fanin_reduce_logsumexp_backward(gn, msgs, fsrc, dst, lse, msgs.shape[0])
+        best = min(best, time.perf_counter() - t0)
+    return best, sum(op_bytes(wl).values())
+
+
+def reference_arm(args) -> None:
+    """--impl reference: the reference's CPU ops on the host cores."""
+
+    rank = env_int("RANK", 0)
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    edges = args.cpu_edges
+    wl = cpu_sample(args.workload, edges)
+    kind = "port"
+    if REF_LIB.is_file():
+        torch.ops.load_library(str(REF_LIB))
+        ops = torch.ops.relm_mp
+        kind = "reference"
+    nbytes = sum(op_bytes(wl).values())
+    times = []
+    for i in range(args.warmup + args.steps):
+        if kind == "reference":
+            t0 = time.perf_counter()
+            run_ops(ops, wl)
+            dt = time.perf_counter() - t0
+        else:
+            dt, _ = time_oracle_port(wl)
+        if i >= args.warmup:
+            times.append(dt)
+    step = sum(times) / len(times)
+    value = nbytes / step / 1e9
+    sample = (f"{args.workload} with E={edges} messages (of {1 << 24 if args.workload.startswith('cfg2') else 'n/a'}),"
+              f" same N, D and index distributions; 6 ops per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": args.workload, "edges_sample": edges, "nodes": int(wl.dim_size), "emb": wl.emb},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads if kind == "reference" else 1,
+                         "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---- B200 arm -------------------------------------------------------------------------------
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    parser.add_argument("--workload", default="cfg2-unsorted",
+                        choices=["cfg2-unsorted", "cfg2-sorted", "cfg5", "cfg1"])
+    parser.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
+    parser.add_argument("--cpu-edges", type=int, default=1 << 22, help="edge sample of the reference arm")
+    parser.add_argument("--port-edges", type=int, default=1 << 20, help="edge sample of the cpu_baseline leg")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-e2e", action="store_true")
+    parser.add_argument("--e2e-steps", type=int, default=2)
+    parser.add_argument("--ops-only", action="store_true", help="per-op kernel timing only (profiling runs)")
+    args = parser.parse_args()
+
+    if args.impl == "reference":
+        reference_arm(args)
+        return 0
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local_rank))
+    else:
+        torch.cuda.set_device(0)
+    device = torch.device("cuda", torch.cuda.current_device())
+
+    from relmo_b200 import capi
+    from relmo_b200.ops import mp, mp_runtime
+
+    assert mp.available(), "relm_mp library not loadable"
+    ops = torch.ops.relm_mp
+    dtype = torch.float32 if args.dtype == "float32" else torch.bfloat16
+    wl = make_workload(args.workload, seed=rank, device=device, dtype=dtype)
+    nbytes = op_bytes(wl)
+    step_bytes = sum(nbytes.values())
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def step():
+        mp.clear_plan_cache()
+        return run_ops(ops, wl)
+
+    # ---- per-op kernel timing (plans cached): roofline of each op -------------------------
+    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+    per_op = {}
+    stream = torch.cuda.current_stream()
+    for op in OPS:
+        for _ in range(2):
+            run_one_op(ops, wl, op, lse)
+        reps = 5
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            run_one_op(ops, wl, op, lse)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        per_op[op] = {"ms": round(ms, 4), "gbs": round(nbytes[op] / ms / 1e6, 1), "bytes": nbytes[op]}
+    if args.ops_only:
+        if rank == 0:
+            print(json.dumps({"per_op": per_op}), flush=True)
+        return 0
+
+    # ---- the timed region ----------------------------------------------------------------
+    for _ in range(max(args.warmup, 3)):
+        step()
+    sampler = ClockSampler(device.index if world == 1 else local_rank)
+    launches0 = capi.lib().relm_mp_kernel_launches()
+    barrier()
+    sampler.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    launches = capi.lib().relm_mp_kernel_launches() - launches0
+    elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+    ms_per_step = elapsed / args.steps * 1e3
+    value = step_bytes * world * args.steps / elapsed / 1e9
+
+    # ---- plan build cost (separately) -----------------------------------------------------------
+    mp.clear_plan_cache()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for op in OPS:  # the first call of each op builds its plan (4 distinct index pairs)
+        run_one_op(ops, wl, op, lse)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    first_calls_ms = t0.elapsed_time(t1)
+    ops_ms = sum(v["ms"] for v in per_op.values())
+
+    # ---- end to end through the public API with host buffers ------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier)
+
+    peaks = measured_peaks()
+    dominant = max(per_op, key=lambda k: per_op[k]["ms"])
+    achieved = per_op[dominant]["gbs"]
+    traffic = ncu_traffic().get(args.workload, {}).get(dominant)
+    roofline = {
+        "bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+        "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
+        "algorithmic_bytes": nbytes[dominant], "peak_source": peaks["source"],
+    }
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = cpu_sample(args.workload, args.port_edges)
+        secs, sbytes = time_oracle_port(sample)
+        cpu = {"value": round(sbytes / secs / 1e9, 4), "unit": UNIT, "cores": 1, "kind": "port",
+               "sample": f"{args.workload} with E={args.port_edges} messages, same N, D and distributions; "
+                         f"the six ops once, C oracle, 1 thread"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32" if dtype == torch.float32 else "bf16",
+            "data": "synthetic",
+            "config": {
+                "workload": args.workload, "nodes": int(wl.dim_size), "edges": wl.num_edges, "emb": wl.emb,
+                "dst": "zipf(1.3)" if args.workload.startswith("cfg2") else args.workload,
+                "per_rank_batches": 1, "l2": "inputs larger than L2 (no flush needed)",
+                "step": "plan builds (cache cleared) + 6 ops", "parallelism": f"independent batches x{world}",
+            },
+            "roofline": roofline,
+            "cpu_baseline": cpu,
+            "e2e": e2e,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "per_op": per_op,
+            "plan_and_first_call_ms": round(first_calls_ms, 3),
+            "ops_only_ms": round(ops_ms, 3),
+            "ops_only_gbs": round(step_bytes / ops_ms / 1e6, 1),
+            "libs": mp_runtime.loaded_library_paths(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier) -> dict:
+    """Same step through torch.ops.relm_mp with the inputs copied in from pinned
+    host memory and every op output copied back, all inside the timed region."""
+
+    names_in = ["x", "src", "flat_dst", "msgs", "flat_src", "dst", "grad_slots", "grad_nodes"]
+    host = {n: getattr(wl, n).cpu().pin_memory() for n in names_in}
+    dev = {n: torch.empty_like(getattr(wl, n)) for n in names_in}
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    dwl = workloads.FanWorkload(
+        wl.name, dev["x"], dev["src"], dev["flat_dst"], wl.out_rows, dev["msgs"], dev["flat_src"], dev["dst"],
+        wl.dim_size, dev["grad_slots"], dev["grad_nodes"],
+    )
+    outs_host = None
+    stream = torch.cuda.current_stream()
+
+    def one():
+        nonlocal outs_host
+        for n in names_in:
+            dev[n].copy_(host[n], non_blocking=True)
+        outs = run_ops(ops, dwl)
+        if outs_host is None:
+            outs_host = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}
+        for k, v in outs.items():
+            outs_host[k].copy_(v, non_blocking=True)
+        return outs
+
+    one()
+    torch.cuda.synchronize()
+    d2h = sum(t.numel() * t.element_size() for t in outs_host.values())
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.e2e_steps):
+        one()
+    ev1.record(stream)
+    barrier()
+    elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+    step_bytes = sum(op_bytes(wl).values())
+    return {
+        "value": round(step_bytes * world * args.e2e_steps / elapsed / 1e9, 3), "unit": UNIT,
+        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        "ms_per_step": round(elapsed / args.e2e_steps * 1e3, 2), "steps": args.e2e_steps,
+    }
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,220 @@
+/*
+ * relm_mp.h - C ABI of the B200 (sm_100a) fan-out / fan-in message-passing
+ * library (librelm_mp_b200.so).
+ *
+ * The entry points replace the five hot ops of relmo's torch library
+ * `relm_mp` (maichmueller/relmo, src/_ops/mp/mp_ops.cpp). Each `relm_mp_<op>`
+ * function computes what `torch.ops.relm_mp.<op>` computes, with plain device
+ * pointers, sizes, a caller-provided workspace and a CUDA stream instead of
+ * torch tensors:
+ *
+ *   relm_mp_fanout_scatter            <- fanout_scatter            (mp_ops.cpp:3038-3101, schema 3760-3762)
+ *   relm_mp_fanout_scatter_backward   <- fanout_scatter_backward   (mp_ops.cpp:3103-3166, schema 3763-3765)
+ *   relm_mp_fanin_reduce              <- fanin_reduce, mode 0 / 1  (mp_ops.cpp:3327-3348, 3168-3222, 3005-3036;
+ *                                                                   schema 3766-3768)
+ *   relm_mp_fanin_reduce_sum_backward <- fanin_reduce_sum_backward (mp_ops.cpp:3224-3284, schema 3769-3771)
+ *   relm_mp_fanin_reduce_logsumexp_backward
+ *                                     <- fanin_reduce_logsumexp_backward (mp_ops.cpp:3286-3325, schema 3772-3774)
+ *   relm_mp_build_info                <- build_info                (mp_ops.cpp:3745-3749)
+ *
+ * Conventions shared by every entry point:
+ *  - All array pointers are device pointers on the current CUDA device; value
+ *    arrays are dense row-major [rows, emb]; index arrays are int64.
+ *  - `stream` is a cudaStream_t passed as void*. Work is enqueued on it.
+ *  - Outputs are fully written (rows nothing maps to get 0, or -inf for
+ *    logsumexp), like the reference's at::zeros / at::full(-inf) outputs.
+ *  - `workspace` is device memory of at least the size the matching
+ *    `*_workspace_bytes` function returns (256-byte aligned). The library never
+ *    allocates device memory itself.
+ *  - Index arrays are validated before any output is written. An out-of-range
+ *    index returns RELM_MP_ERR_INDEX_OUT_OF_RANGE with a message such as
+ *    "flat_dst index out of bounds: 3 not in [0, 3)." (the reference CPU
+ *    message, mp_ops.cpp:59-64). Validation reads a few bytes back to the host,
+ *    so every call synchronizes `stream` once.
+ *  - Return value 0 (RELM_MP_OK) or a relm_mp_status code; relm_mp_last_error()
+ *    holds the message of the last failing call on the calling thread.
+ *  - Limits: num_edges + rows < 2^31 for every index space.
+ *  - Deterministic: the same inputs give bit-identical outputs; there are no
+ *    floating-point atomics.
+ */
+#ifndef RELM_MP_H
+#define RELM_MP_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define RELM_MP_ABI_VERSION 1
+
+#if defined(_WIN32)
+#define RELM_MP_API __declspec(dllexport)
+#else
+#define RELM_MP_API __attribute__((visibility("default")))
+#endif
+
+typedef enum relm_mp_dtype {
+   RELM_MP_FLOAT32 = 0,
+   RELM_MP_FLOAT64 = 1,
+   RELM_MP_BFLOAT16 = 2, /* stored bf16, accumulated in fp32 */
+   RELM_MP_FLOAT16 = 3   /* stored fp16, accumulated in fp32 */
+} relm_mp_dtype;
+
+typedef enum relm_mp_status {
+   RELM_MP_OK = 0,
+   RELM_MP_ERR_INVALID_ARGUMENT = 1,
+   RELM_MP_ERR_INDEX_OUT_OF_RANGE = 2,
+   RELM_MP_ERR_WORKSPACE_TOO_SMALL = 3,
+   RELM_MP_ERR_UNSUPPORTED = 4,
+   RELM_MP_ERR_CUDA = 5
+} relm_mp_status;
+
+/* fanin_reduce modes, as relmo.ops.mp_constants MODE_SUM / MODE_LOGSUMEXP. */
+#define RELM_MP_MODE_SUM 0
+#define RELM_MP_MODE_LOGSUMEXP 1
+/* Only for relm_mp_plan_reduce_scratch_bytes: scratch of relm_mp_plan_logsumexp_backward. */
+#define RELM_MP_MODE_LOGSUMEXP_BACKWARD 2
+
+/* Static strings: status name; "key=value;..." build metadata. */
+RELM_MP_API const char* relm_mp_status_string(int status);
+RELM_MP_API const char* relm_mp_build_info(void);
+/* Message of the last failing call on the calling thread ("" if none). */
+RELM_MP_API const char* relm_mp_last_error(void);
+/* Number of kernels this library has launched in the process (its own
+ * kernels; the radix-sort and scan kernels of the plan build come from CUB and
+ * are not counted). */
+RELM_MP_API unsigned long long relm_mp_kernel_launches(void);
+
+/* ---------------------------------------------------------------------------
+ * Op-level entry points (one call = one reference op call).
+ * ------------------------------------------------------------------------- */
+
+/* fanout_scatter: out[out_rows, emb] = 0; out[flat_dst[e]] = x_cat[src_global_idx[e]].
+ * With repeated flat_dst values the highest edge index wins, as the
+ * reference CPU loop (mp_ops.cpp:2815-2836) leaves it. */
+RELM_MP_API size_t relm_mp_fanout_scatter_workspace_bytes(int64_t num_edges, int64_t out_rows, int64_t emb,
+                                              relm_mp_dtype dtype);
+RELM_MP_API int relm_mp_fanout_scatter(relm_mp_dtype dtype, const void* x_cat, int64_t x_rows, int64_t emb,
+                           const int64_t* src_global_idx, const int64_t* flat_dst,
+                           int64_t num_edges, int64_t out_rows, void* out, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
+/* fanout_scatter_backward: grad_x[x_rows, emb] = 0;
+ * grad_x[src_global_idx[e]] += grad_out[flat_dst[e]]. */
+RELM_MP_API size_t relm_mp_fanout_scatter_backward_workspace_bytes(int64_t num_edges, int64_t x_rows,
+                                                       int64_t emb, relm_mp_dtype dtype);
+RELM_MP_API int relm_mp_fanout_scatter_backward(relm_mp_dtype dtype, const void* grad_out,
+                                    int64_t grad_out_rows, int64_t emb,
+                                    const int64_t* src_global_idx, const int64_t* flat_dst,
+                                    int64_t num_edges, int64_t x_rows, void* grad_x,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* fanin_reduce: mode 0: out[dim_size, emb] = 0; out[dst_idx[e]] += rel_flat[flat_src[e]].
+ * mode 1: out[n] = log(sum over edges into n of exp(rel_flat[flat_src[e]])),
+ * -inf for rows without edges, computed in one pass with a running
+ * (max, sum-exp) pair per column. */
+RELM_MP_API size_t relm_mp_fanin_reduce_workspace_bytes(int64_t num_edges, int64_t dim_size, int64_t emb,
+                                            relm_mp_dtype dtype, int mode);
+RELM_MP_API int relm_mp_fanin_reduce(relm_mp_dtype dtype, const void* rel_flat, int64_t rel_rows, int64_t emb,
+                         const int64_t* flat_src, const int64_t* dst_idx, int64_t num_edges,
+                         int64_t dim_size, int mode, void* out, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* fanin_reduce_sum_backward: grad_rel[rel_rows, emb] = 0;
+ * grad_rel[flat_src[e]] += grad_out[dst_idx[e]]. */
+RELM_MP_API size_t relm_mp_fanin_reduce_sum_backward_workspace_bytes(int64_t num_edges, int64_t rel_rows,
+                                                         int64_t emb, relm_mp_dtype dtype);
+RELM_MP_API int relm_mp_fanin_reduce_sum_backward(relm_mp_dtype dtype, const void* grad_out,
+                                      int64_t grad_out_rows, int64_t emb, const int64_t* flat_src,
+                                      const int64_t* dst_idx, int64_t num_edges, int64_t rel_rows,
+                                      void* grad_rel, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
+/* fanin_reduce_logsumexp_backward: grad_rel[rel_rows, emb] = 0;
+ * grad_rel[flat_src[e]] += grad_out[dst_idx[e]] * exp(rel_flat[flat_src[e]] - out[dst_idx[e]]).
+ * grad_out and out are [dim_size, emb]; rel_flat is [rel_table_rows, emb]. */
+RELM_MP_API size_t relm_mp_fanin_reduce_logsumexp_backward_workspace_bytes(int64_t num_edges,
+                                                               int64_t rel_rows, int64_t emb,
+                                                               relm_mp_dtype dtype);
+RELM_MP_API int relm_mp_fanin_reduce_logsumexp_backward(relm_mp_dtype dtype, const void* grad_out,
+                                            const void* rel_flat, int64_t rel_table_rows,
+                                            const void* out, int64_t dim_size, int64_t emb,
+                                            const int64_t* flat_src, const int64_t* dst_idx,
+                                            int64_t num_edges, int64_t rel_rows, void* grad_rel,
+                                            void* workspace, size_t workspace_bytes,
+                                            void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Plans: the CSR of one index pair, reusable across calls.
+ *
+ * A plan orders the edges by an output index (stable: equal output rows keep
+ * edge order) and records, per output row, its edge range and, per edge, the
+ * row of the gathered table. Every op above builds one plan and runs one
+ * planned kernel; callers that apply the same indices many times (the layers
+ * of one RelationalGNN forward and its backward) build the plan once and call
+ * the planned entry points. The plan lives in caller memory (`plan_mem`,
+ * relm_mp_plan_bytes) and must not be freed while in use; `scratch`
+ * (relm_mp_plan_scratch_bytes) is only used during the build.
+ * ------------------------------------------------------------------------- */
+
+#define RELM_MP_PLAN_SORTED_INPUT 1u /* out_index was already non-decreasing */
+
+typedef struct relm_mp_plan {
+   int64_t num_edges;
+   int64_t num_rows;        /* output rows */
+   int64_t gather_rows;     /* rows of the gathered table */
+   int64_t num_tiles;       /* merge-path tiles over num_rows + num_edges items */
+   int32_t tile_items;      /* items per tile */
+   uint32_t flags;          /* RELM_MP_PLAN_* */
+   const int32_t* row_ptr;  /* device [num_rows + 1]: edges of row r are [row_ptr[r], row_ptr[r+1]) */
+   const int32_t* gidx;     /* device [num_edges]: gathered row of the j-th edge in row order */
+   const int32_t* tile_row; /* device [num_tiles + 1]: first row of each tile */
+   const int32_t* tile_edge;/* device [num_tiles + 1]: first edge of each tile */
+} relm_mp_plan;
+
+RELM_MP_API size_t relm_mp_plan_bytes(int64_t num_edges, int64_t num_rows);
+RELM_MP_API size_t relm_mp_plan_scratch_bytes(int64_t num_edges, int64_t num_rows);
+/* Validates out_index in [0, num_rows) and gather_index in [0, gather_rows)
+ * (names are used in error messages; NULL gives "out_index"/"gather_index"),
+ * then builds the plan. Synchronizes `stream` once. */
+RELM_MP_API int relm_mp_plan_build(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                       int64_t num_rows, int64_t gather_rows, const char* out_index_name,
+                       const char* gather_index_name, void* plan_mem, size_t plan_bytes,
+                       void* scratch, size_t scratch_bytes, void* stream, relm_mp_plan* plan);
+
+/* As relm_mp_plan_build, with a separate validation bound for out_index
+ * (out_bound <= num_rows: rows >= out_bound exist but receive no edges) and
+ * the order in which the two indices are checked at the same edge
+ * (gather_checked_first != 0: gather_index first), which decides the error
+ * message when one edge has both out of range. */
+RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* gather_index,
+                                      int64_t num_edges, int64_t num_rows, int64_t out_bound,
+                                      int64_t gather_rows, const char* out_index_name,
+                                      const char* gather_index_name, int gather_checked_first,
+                                      void* plan_mem, size_t plan_bytes, void* scratch,
+                                      size_t scratch_bytes, void* stream, relm_mp_plan* plan);
+
+/* Scratch for the planned reductions (partials of rows that span tiles). */
+RELM_MP_API size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, int64_t emb,
+                                         relm_mp_dtype dtype, int mode);
+
+/* out[r] = table[gidx[last edge of r]] or 0 for rows without edges (fanout forward). */
+RELM_MP_API int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
+                             int64_t emb, void* out, void* stream);
+/* mode 0: out[r] = sum of table[gidx[j]] over the edges j of r;
+ * mode 1: out[r] = log(sum of exp(table[gidx[j]])), -inf when r has no edges. */
+RELM_MP_API int relm_mp_plan_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int mode, const void* table,
+                        int64_t emb, void* out, void* scratch, size_t scratch_bytes, void* stream);
+/* grad_rel[r] = sum over edges j of r of grad_out[gidx[j]] * exp(rel[r] - lse_out[gidx[j]]). */
+RELM_MP_API int relm_mp_plan_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtype,
+                                    const void* grad_out, const void* lse_out, const void* rel,
+                                    int64_t emb, void* grad_rel, void* scratch,
+                                    size_t scratch_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RELM_MP_H */

@@ -1,0 +1,286 @@
+"""ctypes binding of the C ABI (``include/relm_mp.h``, ``librelm_mp_b200.so``).
+
+This is the binding a non-torch host (or a test) uses: plain device pointers,
+sizes, a caller-allocated workspace and a CUDA stream. The helpers at the
+bottom take torch CUDA tensors for convenience, allocate outputs and the
+workspace with torch, and call the C entry points on the current stream.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "librelm_mp_b200.so"
+
+FLOAT32, FLOAT64, BFLOAT16, FLOAT16 = 0, 1, 2, 3
+MODE_SUM, MODE_LOGSUMEXP, MODE_LOGSUMEXP_BACKWARD = 0, 1, 2
+STATUS_NAMES = {
+    0: "RELM_MP_OK",
+    1: "RELM_MP_ERR_INVALID_ARGUMENT",
+    2: "RELM_MP_ERR_INDEX_OUT_OF_RANGE",
+    3: "RELM_MP_ERR_WORKSPACE_TOO_SMALL",
+    4: "RELM_MP_ERR_UNSUPPORTED",
+    5: "RELM_MP_ERR_CUDA",
+}
+
+# Every symbol the header declares, with (restype, argtypes).
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_SZ = ctypes.c_size_t
+_INT = ctypes.c_int
+_STR = ctypes.c_char_p
+
+
+class Plan(ctypes.Structure):
+    _fields_ = [
+        ("num_edges", ctypes.c_int64),
+        ("num_rows", ctypes.c_int64),
+        ("gather_rows", ctypes.c_int64),
+        ("num_tiles", ctypes.c_int64),
+        ("tile_items", ctypes.c_int32),
+        ("flags", ctypes.c_uint32),
+        ("row_ptr", ctypes.c_void_p),
+        ("gidx", ctypes.c_void_p),
+        ("tile_row", ctypes.c_void_p),
+        ("tile_edge", ctypes.c_void_p),
+    ]
+
+
+_PLANP = ctypes.POINTER(Plan)
+
+SIGNATURES: dict[str, tuple] = {
+    "relm_mp_status_string": (_STR, [_INT]),
+    "relm_mp_build_info": (_STR, []),
+    "relm_mp_last_error": (_STR, []),
+    "relm_mp_kernel_launches": (ctypes.c_ulonglong, []),
+    "relm_mp_fanout_scatter_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT]),
+    "relm_mp_fanout_scatter": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_fanout_scatter_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT]),
+    "relm_mp_fanout_scatter_backward": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_fanin_reduce_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT, _INT]),
+    "relm_mp_fanin_reduce": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _INT, _P, _P, _SZ, _P]),
+    "relm_mp_fanin_reduce_sum_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT]),
+    "relm_mp_fanin_reduce_sum_backward": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_fanin_reduce_logsumexp_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT]),
+    "relm_mp_fanin_reduce_logsumexp_backward": (
+        _INT,
+        [_INT, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P],
+    ),
+    "relm_mp_plan_bytes": (_SZ, [_I64, _I64]),
+    "relm_mp_plan_scratch_bytes": (_SZ, [_I64, _I64]),
+    "relm_mp_plan_build": (_INT, [_P, _P, _I64, _I64, _I64, _STR, _STR, _P, _SZ, _P, _SZ, _P, _PLANP]),
+    "relm_mp_plan_build_ex": (
+        _INT,
+        [_P, _P, _I64, _I64, _I64, _I64, _STR, _STR, _INT, _P, _SZ, _P, _SZ, _P, _PLANP],
+    ),
+    "relm_mp_plan_reduce_scratch_bytes": (_SZ, [_PLANP, _I64, _INT, _INT]),
+    "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
+    "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_plan_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
+}
+
+_LIB: ctypes.CDLL | None = None
+
+
+class RelmMpError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        self.status = status
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {message}")
+
+
+def lib() -> ctypes.CDLL:
+    """Load the library (RTLD_GLOBAL not needed) and declare every signature."""
+
+    global _LIB
+    if _LIB is None:
+        if not LIB_PATH.is_file():
+            raise FileNotFoundError(f"{LIB_PATH} missing: build it with `python -m relmo_b200.build`.")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = handle
+    return _LIB
+
+
+def check(status: int) -> None:
+    if status != 0:
+        raise RelmMpError(status, lib().relm_mp_last_error().decode())
+
+
+# ---- torch helpers -----------------------------------------------------------------
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def dtype_code(t) -> int:
+    torch = _torch()
+    codes = {torch.float32: FLOAT32, torch.float64: FLOAT64, torch.bfloat16: BFLOAT16, torch.float16: FLOAT16}
+    if t.dtype not in codes:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return codes[t.dtype]
+
+
+def _ptr(t) -> int | None:
+    return t.data_ptr() if t is not None and t.numel() > 0 else None
+
+
+def _stream(device) -> int:
+    return _torch().cuda.current_stream(device).cuda_stream
+
+
+def _workspace(nbytes: int, device):
+    return _torch().empty(max(int(nbytes), 1), dtype=_torch().uint8, device=device)
+
+
+def fanout_scatter(x, src, flat_dst, out_rows: int, out=None):
+    torch = _torch()
+    x, src, flat_dst = x.contiguous(), src.contiguous(), flat_dst.contiguous()
+    emb = x.size(1)
+    if out is None:
+        out = torch.empty((int(out_rows), emb), dtype=x.dtype, device=x.device)
+    ws = _workspace(lib().relm_mp_fanout_scatter_workspace_bytes(src.numel(), int(out_rows), emb, dtype_code(x)), x.device)
+    check(lib().relm_mp_fanout_scatter(
+        dtype_code(x), _ptr(x), x.size(0), emb, _ptr(src), _ptr(flat_dst), src.numel(), int(out_rows),
+        _ptr(out), ws.data_ptr(), ws.numel(), _stream(x.device),
+    ))
+    return out
+
+
+def fanout_scatter_backward(grad_out, src, flat_dst, x_rows: int):
+    torch = _torch()
+    g, src, flat_dst = grad_out.contiguous(), src.contiguous(), flat_dst.contiguous()
+    emb = g.size(1)
+    out = torch.empty((int(x_rows), emb), dtype=g.dtype, device=g.device)
+    ws = _workspace(
+        lib().relm_mp_fanout_scatter_backward_workspace_bytes(src.numel(), int(x_rows), emb, dtype_code(g)), g.device
+    )
+    check(lib().relm_mp_fanout_scatter_backward(
+        dtype_code(g), _ptr(g), g.size(0), emb, _ptr(src), _ptr(flat_dst), src.numel(), int(x_rows),
+        _ptr(out), ws.data_ptr(), ws.numel(), _stream(g.device),
+    ))
+    return out
+
+
+def fanin_reduce(rel, flat_src, dst, dim_size: int, mode: int):
+    torch = _torch()
+    rel, flat_src, dst = rel.contiguous(), flat_src.contiguous(), dst.contiguous()
+    emb = rel.size(1)
+    out = torch.empty((int(dim_size), emb), dtype=rel.dtype, device=rel.device)
+    ws = _workspace(
+        lib().relm_mp_fanin_reduce_workspace_bytes(flat_src.numel(), int(dim_size), emb, dtype_code(rel), int(mode)),
+        rel.device,
+    )
+    check(lib().relm_mp_fanin_reduce(
+        dtype_code(rel), _ptr(rel), rel.size(0), emb, _ptr(flat_src), _ptr(dst), flat_src.numel(), int(dim_size),
+        int(mode), _ptr(out), ws.data_ptr(), ws.numel(), _stream(rel.device),
+    ))
+    return out
+
+
+def fanin_reduce_sum_backward(grad_out, flat_src, dst, rel_rows: int):
+    torch = _torch()
+    g, flat_src, dst = grad_out.contiguous(), flat_src.contiguous(), dst.contiguous()
+    emb = g.size(1)
+    out = torch.empty((int(rel_rows), emb), dtype=g.dtype, device=g.device)
+    ws = _workspace(
+        lib().relm_mp_fanin_reduce_sum_backward_workspace_bytes(flat_src.numel(), int(rel_rows), emb, dtype_code(g)),
+        g.device,
+    )
+    check(lib().relm_mp_fanin_reduce_sum_backward(
+        dtype_code(g), _ptr(g), g.size(0), emb, _ptr(flat_src), _ptr(dst), flat_src.numel(), int(rel_rows),
+        _ptr(out), ws.data_ptr(), ws.numel(), _stream(g.device),
+    ))
+    return out
+
+
+def fanin_reduce_logsumexp_backward(grad_out, rel, flat_src, dst, lse_out, rel_rows: int):
+    torch = _torch()
+    g, rel, o = grad_out.contiguous(), rel.contiguous(), lse_out.contiguous()
+    flat_src, dst = flat_src.contiguous(), dst.contiguous()
+    emb = g.size(1)
+    out = torch.empty((int(rel_rows), emb), dtype=g.dtype, device=g.device)
+    ws = _workspace(
+        lib().relm_mp_fanin_reduce_logsumexp_backward_workspace_bytes(flat_src.numel(), int(rel_rows), emb, dtype_code(g)),
+        g.device,
+    )
+    check(lib().relm_mp_fanin_reduce_logsumexp_backward(
+        dtype_code(g), _ptr(g), _ptr(rel), rel.size(0), _ptr(o), o.size(0), emb, _ptr(flat_src), _ptr(dst),
+        flat_src.numel(), int(rel_rows), _ptr(out), ws.data_ptr(), ws.numel(), _stream(g.device),
+    ))
+    return out
+
+
+class PlanHandle:
+    """A plan built through the C ABI, owning its device memory (torch)."""
+
+    def __init__(self, out_index, gather_index, num_rows: int, gather_rows: int):
+        torch = _torch()
+        out_index, gather_index = out_index.contiguous(), gather_index.contiguous()
+        e = out_index.numel()
+        self.memory = _workspace(lib().relm_mp_plan_bytes(e, int(num_rows)), out_index.device)
+        scratch = _workspace(lib().relm_mp_plan_scratch_bytes(e, int(num_rows)), out_index.device)
+        self.plan = Plan()
+        self.device = out_index.device
+        check(lib().relm_mp_plan_build(
+            _ptr(out_index), _ptr(gather_index), e, int(num_rows), int(gather_rows), None, None,
+            self.memory.data_ptr(), self.memory.numel(), scratch.data_ptr(), scratch.numel(),
+            _stream(out_index.device), ctypes.byref(self.plan),
+        ))
+        del torch
+
+    def row_ptr(self):
+        """row_ptr of the plan as a CPU int64 tensor."""
+
+        return _device_int32(self.plan.row_ptr, self.plan.num_rows + 1, self.device).cpu().long()
+
+    def gidx(self):
+        """Gathered row of each edge in output-row order, as a CPU int64 tensor."""
+
+        return _device_int32(self.plan.gidx, self.plan.num_edges, self.device).cpu().long()
+
+    def reduce(self, table, mode: int):
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        out = torch.empty((self.plan.num_rows, emb), dtype=table.dtype, device=table.device)
+        scratch = _workspace(
+            lib().relm_mp_plan_reduce_scratch_bytes(ctypes.byref(self.plan), emb, dtype_code(table), int(mode)),
+            table.device,
+        )
+        check(lib().relm_mp_plan_reduce(
+            ctypes.byref(self.plan), dtype_code(table), int(mode), _ptr(table), emb, _ptr(out),
+            scratch.data_ptr(), scratch.numel(), _stream(table.device),
+        ))
+        return out
+
+    def gather_last(self, table):
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        out = torch.empty((self.plan.num_rows, emb), dtype=table.dtype, device=table.device)
+        check(lib().relm_mp_plan_gather_last(
+            ctypes.byref(self.plan), dtype_code(table), _ptr(table), emb, _ptr(out), _stream(table.device)
+        ))
+        return out
+
+
+class _DeviceArray:
+    def __init__(self, ptr: int, n: int, typestr: str):
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": typestr, "data": (int(ptr), True), "version": 3}
+
+
+def _device_int32(ptr: int, n: int, device):
+    """A torch view of `n` int32 values at device address `ptr` (no copy)."""
+
+    torch = _torch()
+    torch.cuda.current_stream(device).synchronize()
+    if n == 0:
+        return torch.empty(0, dtype=torch.int32, device=device)
+    return torch.as_tensor(_DeviceArray(ptr, n, "<i4"), device=device)

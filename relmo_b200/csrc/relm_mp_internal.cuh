@@ -1,0 +1,61 @@
+// Internal declarations shared by the relm_mp CUDA sources.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <string>
+
+#include "relm_mp.h"
+
+namespace relm_mp {
+
+// Items (output rows + edges) per merge-path tile. One warp owns one tile.
+constexpr int kTileItems = 256;
+// Tiles with a head partial whose row spans more than this many tiles are
+// combined by the block-wide long-row fixup instead of a single warp.
+constexpr int kLongRowTiles = 64;
+constexpr int kThreads = 256;
+
+// Alignment of every sub-buffer carved out of a workspace.
+constexpr size_t kAlign = 256;
+
+inline size_t align_up(size_t v, size_t a = kAlign) { return (v + a - 1) / a * a; }
+
+// Thread-local error message; returns `status` for convenient `return fail(...)`.
+int fail(int status, const std::string& message);
+int check_cuda(cudaError_t err, const char* what);
+int check_launch(const char* what);
+
+// Carves consecutive aligned sub-buffers out of one workspace.
+struct Carver {
+   char* base;
+   size_t used = 0;
+   explicit Carver(void* p) : base(static_cast<char*>(p)) {}
+   template <typename T>
+   T* take(size_t count)
+   {
+      T* p = reinterpret_cast<T*>(base ? base + used : nullptr);
+      used += align_up(count * sizeof(T));
+      return p;
+   }
+};
+
+// Builds a plan with a separate validation bound for the output index
+// (`out_bound` <= num_rows; rows >= out_bound may exist but receive no edges).
+int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                       int64_t num_rows, int64_t out_bound, int64_t gather_rows,
+                       const char* out_name, const char* gather_name, bool gather_checked_first,
+                       void* plan_mem, size_t plan_bytes, void* scratch, size_t scratch_bytes,
+                       cudaStream_t stream, relm_mp_plan* plan);
+
+int64_t plan_num_tiles(int64_t num_edges, int64_t num_rows);
+
+// Element-wise fill of `count` elements of dtype with 0 or -inf.
+int fill_rows(relm_mp_dtype dtype, void* out, int64_t count, bool neg_inf, cudaStream_t stream);
+
+size_t dtype_size(relm_mp_dtype dtype);
+
+}  // namespace relm_mp

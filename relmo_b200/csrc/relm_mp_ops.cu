@@ -1,0 +1,540 @@
+// C-ABI entry points of librelm_mp_b200.so (declared in include/relm_mp.h).
+//
+// Each op-level entry point reproduces one reference op of
+// maichmueller/relmo src/_ops/mp/mp_ops.cpp (argument checks, early returns,
+// output initialisation, error text) and runs it as:
+//   plan build (relm_mp_plan.cu) -> one planned kernel (relm_mp_segment.cuh).
+// The workspace holds the plan; the plan-build scratch and the reduction
+// scratch share the space after it.
+#include <atomic>
+#include <cstdio>
+#include <string>
+
+#include "relm_mp_internal.cuh"
+#include "relm_mp_segment.cuh"
+
+#ifndef RELM_MP_KERNEL_CUDA_VERSION
+#define RELM_MP_KERNEL_CUDA_VERSION "unknown"
+#endif
+
+namespace relm_mp {
+
+namespace {
+thread_local std::string g_last_error;
+std::atomic< unsigned long long > g_launches{0};
+
+__global__ void k_fill_f32(float* out, int64_t n, float v)
+{
+   for(int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+      out[i] = v;
+}
+__global__ void k_fill_f64(double* out, int64_t n, double v)
+{
+   for(int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+      out[i] = v;
+}
+__global__ void k_fill_u16(unsigned short* out, int64_t n, unsigned short v)
+{
+   for(int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+      out[i] = v;
+}
+
+bool aligned(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes) == 0; }
+
+struct Shape {
+   int vb;
+   int chmax;
+   int lpr;
+   int ch;
+   int col_blocks;
+   int64_t block_cols;
+};
+
+// Widest per-lane vector that divides the row and every pointer's alignment,
+// then lanes per row and chunks per lane.
+Shape choose_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
+{
+   Shape s{};
+   const int64_t row_bytes = emb * es;
+   int vb = 16;
+   while(vb > es) {
+      bool ok = row_bytes % vb == 0;
+      for(int i = 0; ok && i < nptrs; ++i) ok = ptrs[i] == nullptr || aligned(ptrs[i], vb);
+      if(ok) break;
+      vb >>= 1;
+   }
+   if(vb < es) vb = es;
+   int64_t nvec = row_bytes / vb;
+   if(nvec > 32 && vb != 16 && vb != es) {
+      // intermediate widths only come with one chunk per lane
+      vb = es;
+      nvec = row_bytes / vb;
+   }
+   s.vb = vb;
+   const int vn = vb / es;
+   if(nvec <= 32) {
+      int lpr = 1;
+      while(lpr < nvec) lpr <<= 1;
+      s.lpr = lpr < 1 ? 1 : lpr;
+      s.chmax = 1;
+      s.ch = 1;
+      s.block_cols = (int64_t)s.lpr * vn;
+      s.col_blocks = 1;
+   } else {
+      s.lpr = 32;
+      s.chmax = 4;
+      const int64_t need = (nvec + 31) / 32;
+      s.ch = need < 4 ? (int)need : 4;
+      s.block_cols = (int64_t)32 * s.ch * vn;
+      s.col_blocks = (int)((emb + s.block_cols - 1) / s.block_cols);
+   }
+   return s;
+}
+
+struct ReduceScratch {
+   void* head_val;
+   void* tail_val;
+   void* head_aux;
+   void* tail_aux;
+   int32_t* head_row;
+   int32_t* tail_row;
+   int32_t* long_count;
+   int32_t* long_list;
+   int64_t max_long;
+   size_t bytes;
+};
+
+int64_t max_long_rows(int64_t num_tiles)
+{
+   return num_tiles / (kLongRowTiles + 1) + 1;
+}
+
+ReduceScratch reduce_layout(void* mem, int64_t num_tiles, int64_t emb, int acc_bytes, int mode)
+{
+   Carver c(mem);
+   ReduceScratch r{};
+   const size_t vals = (size_t)num_tiles * (size_t)emb * (size_t)acc_bytes;
+   r.head_val = c.take< char >(vals);
+   r.tail_val = c.take< char >(vals);
+   r.head_aux = mode == RELM_MP_MODE_LOGSUMEXP ? c.take< char >(vals) : nullptr;
+   r.tail_aux = mode == RELM_MP_MODE_LOGSUMEXP ? c.take< char >(vals) : nullptr;
+   r.head_row = c.take< int32_t >((size_t)num_tiles);
+   r.tail_row = c.take< int32_t >((size_t)num_tiles);
+   r.max_long = max_long_rows(num_tiles);
+   r.long_count = c.take< int32_t >(1);
+   r.long_list = c.take< int32_t >((size_t)r.max_long);
+   r.bytes = c.used;
+   return r;
+}
+
+int acc_bytes_of(relm_mp_dtype d) { return d == RELM_MP_FLOAT64 ? 8 : 4; }
+
+bool valid_dtype(relm_mp_dtype d)
+{
+   return d == RELM_MP_FLOAT32 || d == RELM_MP_FLOAT64 || d == RELM_MP_BFLOAT16 || d == RELM_MP_FLOAT16;
+}
+
+SegParams base_params(const relm_mp_plan* plan, int64_t emb, const Shape& s)
+{
+   SegParams p{};
+   p.row_ptr = plan->row_ptr;
+   p.gidx = plan->gidx;
+   p.tile_row = plan->tile_row;
+   p.tile_edge = plan->tile_edge;
+   p.num_tiles = plan->num_tiles;
+   p.num_rows = plan->num_rows;
+   p.emb = emb;
+   p.lpr = s.lpr;
+   p.ch = s.ch;
+   p.col_blocks = s.col_blocks;
+   p.block_cols = s.block_cols;
+   return p;
+}
+
+int dispatch_gather(relm_mp_dtype dtype, const SegParams& p, const Shape& s, cudaStream_t st)
+{
+   switch(dtype) {
+      case RELM_MP_FLOAT32: return launch_gather_last< float >(p, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT64: return launch_gather_last< double >(p, s.vb, s.chmax, st);
+      case RELM_MP_BFLOAT16: return launch_gather_last< __nv_bfloat16 >(p, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT16: return launch_gather_last< __half >(p, s.vb, s.chmax, st);
+   }
+   return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
+int dispatch_reduce(relm_mp_dtype dtype, const SegParams& p, int mode, const Shape& s, cudaStream_t st)
+{
+   switch(dtype) {
+      case RELM_MP_FLOAT32: return launch_seg_reduce< float >(p, mode, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT64: return launch_seg_reduce< double >(p, mode, s.vb, s.chmax, st);
+      case RELM_MP_BFLOAT16: return launch_seg_reduce< __nv_bfloat16 >(p, mode, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT16: return launch_seg_reduce< __half >(p, mode, s.vb, s.chmax, st);
+   }
+   return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
+// Planned reduction shared by relm_mp_plan_reduce / relm_mp_plan_logsumexp_backward.
+int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, const void* table,
+                   const void* table2, const void* own, int64_t emb, void* out, void* scratch,
+                   size_t scratch_bytes, cudaStream_t stream)
+{
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
+   if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
+   const int64_t es = (int64_t)dtype_size(dtype);
+   if(plan->num_rows == 0 || emb == 0) return RELM_MP_OK;
+   const int scratch_mode = seg_mode == kLse ? RELM_MP_MODE_LOGSUMEXP : RELM_MP_MODE_SUM;
+   const ReduceScratch rs = reduce_layout(scratch, plan->num_tiles, emb, acc_bytes_of(dtype), scratch_mode);
+   if(!scratch || scratch_bytes < rs.bytes)
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "reduce scratch is smaller than relm_mp_plan_reduce_scratch_bytes().");
+   if(plan->num_edges == 0) {
+      return fill_rows(dtype, out, plan->num_rows * emb, seg_mode == kLse, stream);
+   }
+   const void* ptrs[4] = {table, table2, own, out};
+   const Shape s = choose_shape(emb, (int)es, ptrs, 4);
+   SegParams p = base_params(plan, emb, s);
+   p.table = table;
+   p.table2 = table2;
+   p.own = own;
+   p.out = out;
+   p.head_val = rs.head_val;
+   p.tail_val = rs.tail_val;
+   p.head_aux = rs.head_aux;
+   p.tail_aux = rs.tail_aux;
+   p.head_row = rs.head_row;
+   p.tail_row = rs.tail_row;
+   p.long_count = rs.long_count;
+   p.long_list = rs.long_list;
+   p.max_long = rs.max_long;
+   int rc = check_cuda(cudaMemsetAsync(rs.long_count, 0, sizeof(int32_t), stream), "long_count memset");
+   if(rc) return rc;
+   return dispatch_reduce(dtype, p, seg_mode, s, stream);
+}
+
+}  // namespace
+
+int fail(int status, const std::string& message)
+{
+   g_last_error = message;
+   return status;
+}
+
+int check_cuda(cudaError_t err, const char* what)
+{
+   if(err == cudaSuccess) return RELM_MP_OK;
+   return fail(RELM_MP_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(err));
+}
+
+int check_launch(const char* what)
+{
+   g_launches.fetch_add(1, std::memory_order_relaxed);
+   return check_cuda(cudaGetLastError(), what);
+}
+
+size_t dtype_size(relm_mp_dtype dtype)
+{
+   switch(dtype) {
+      case RELM_MP_FLOAT32: return 4;
+      case RELM_MP_FLOAT64: return 8;
+      case RELM_MP_BFLOAT16: return 2;
+      case RELM_MP_FLOAT16: return 2;
+   }
+   return 0;
+}
+
+int fill_rows(relm_mp_dtype dtype, void* out, int64_t count, bool neg_inf, cudaStream_t stream)
+{
+   if(count <= 0) return RELM_MP_OK;
+   if(!neg_inf) return check_cuda(cudaMemsetAsync(out, 0, (size_t)count * dtype_size(dtype), stream), "zero fill");
+   int64_t blocks = (count + kThreads - 1) / kThreads;
+   if(blocks > 148 * 32) blocks = 148 * 32;
+   switch(dtype) {
+      case RELM_MP_FLOAT32: k_fill_f32<<< (unsigned)blocks, kThreads, 0, stream >>>((float*)out, count, -INFINITY); break;
+      case RELM_MP_FLOAT64: k_fill_f64<<< (unsigned)blocks, kThreads, 0, stream >>>((double*)out, count, -INFINITY); break;
+      // -inf bit patterns: bf16 0xff80, fp16 0xfc00
+      case RELM_MP_BFLOAT16: k_fill_u16<<< (unsigned)blocks, kThreads, 0, stream >>>((unsigned short*)out, count, 0xff80); break;
+      case RELM_MP_FLOAT16: k_fill_u16<<< (unsigned)blocks, kThreads, 0, stream >>>((unsigned short*)out, count, 0xfc00); break;
+   }
+   return check_launch("fill");
+}
+
+}  // namespace relm_mp
+
+using namespace relm_mp;
+
+namespace {
+
+// Workspace of one op call: the plan, then the larger of the plan-build scratch
+// and the reduction scratch (they are never live at the same time).
+size_t op_workspace(int64_t num_edges, int64_t num_rows, int64_t emb, relm_mp_dtype dtype, int scratch_mode,
+                    bool reduces)
+{
+   if(num_edges < 0 || num_rows < 0 || emb < 0) return 0;
+   const size_t plan = relm_mp_plan_bytes(num_edges, num_rows);
+   size_t scratch = relm_mp_plan_scratch_bytes(num_edges, num_rows);
+   if(reduces) {
+      const int64_t tiles = plan_num_tiles(num_edges, num_rows);
+      const size_t red = reduce_layout(nullptr, tiles, emb, acc_bytes_of(dtype), scratch_mode).bytes;
+      if(red > scratch) scratch = red;
+   }
+   return plan + scratch;
+}
+
+struct OpMem {
+   void* plan_mem;
+   size_t plan_bytes;
+   void* scratch;
+   size_t scratch_bytes;
+};
+
+int split_workspace(void* ws, size_t ws_bytes, size_t need, int64_t num_edges, int64_t num_rows, OpMem& m)
+{
+   if(!ws || ws_bytes < need) {
+      char msg[160];
+      snprintf(msg, sizeof msg, "workspace too small: %zu bytes given, %zu needed.", ws_bytes, need);
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, msg);
+   }
+   m.plan_mem = ws;
+   m.plan_bytes = relm_mp_plan_bytes(num_edges, num_rows);
+   m.scratch = static_cast< char* >(ws) + m.plan_bytes;
+   m.scratch_bytes = ws_bytes - m.plan_bytes;
+   return RELM_MP_OK;
+}
+
+int check_common(relm_mp_dtype dtype, int64_t emb, int64_t num_edges)
+{
+   if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
+   if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
+   if(num_edges < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "num_edges must be >= 0.");
+   return RELM_MP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* relm_mp_status_string(int status)
+{
+   switch(status) {
+      case RELM_MP_OK: return "RELM_MP_OK";
+      case RELM_MP_ERR_INVALID_ARGUMENT: return "RELM_MP_ERR_INVALID_ARGUMENT";
+      case RELM_MP_ERR_INDEX_OUT_OF_RANGE: return "RELM_MP_ERR_INDEX_OUT_OF_RANGE";
+      case RELM_MP_ERR_WORKSPACE_TOO_SMALL: return "RELM_MP_ERR_WORKSPACE_TOO_SMALL";
+      case RELM_MP_ERR_UNSUPPORTED: return "RELM_MP_ERR_UNSUPPORTED";
+      case RELM_MP_ERR_CUDA: return "RELM_MP_ERR_CUDA";
+   }
+   return "RELM_MP_ERR_UNKNOWN";
+}
+
+const char* relm_mp_build_info(void)
+{
+   return "lib=relm_mp_b200;arch=sm_100a;kernel_cuda=" RELM_MP_KERNEL_CUDA_VERSION ";abi=1";
+}
+
+const char* relm_mp_last_error(void) { return g_last_error.c_str(); }
+
+unsigned long long relm_mp_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, int64_t emb, relm_mp_dtype dtype, int mode)
+{
+   if(!plan || emb < 0) return 0;
+   return reduce_layout(nullptr, plan->num_tiles, emb, acc_bytes_of(dtype), mode).bytes;
+}
+
+int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
+                             void* out, void* stream)
+{
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
+   if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(plan->num_rows == 0 || emb == 0) return RELM_MP_OK;
+   if(plan->num_edges == 0) return fill_rows(dtype, out, plan->num_rows * emb, false, st);
+   const void* ptrs[2] = {table, out};
+   const Shape s = choose_shape(emb, (int)dtype_size(dtype), ptrs, 2);
+   SegParams p = base_params(plan, emb, s);
+   p.table = table;
+   p.out = out;
+   return dispatch_gather(dtype, p, s, st);
+}
+
+int relm_mp_plan_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int mode, const void* table, int64_t emb,
+                        void* out, void* scratch, size_t scratch_bytes, void* stream)
+{
+   if(mode != RELM_MP_MODE_SUM && mode != RELM_MP_MODE_LOGSUMEXP)
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "Unsupported fanin_reduce mode. Supported: 0=sum, 1=logsumexp.");
+   return planned_reduce(
+      plan, dtype, mode == RELM_MP_MODE_SUM ? kSum : kLse, table, nullptr, nullptr, emb, out, scratch,
+      scratch_bytes, static_cast< cudaStream_t >(stream)
+   );
+}
+
+int relm_mp_plan_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* grad_out,
+                                    const void* lse_out, const void* rel, int64_t emb, void* grad_rel,
+                                    void* scratch, size_t scratch_bytes, void* stream)
+{
+   return planned_reduce(
+      plan, dtype, kLseBwd, grad_out, lse_out, rel, emb, grad_rel, scratch, scratch_bytes,
+      static_cast< cudaStream_t >(stream)
+   );
+}
+
+// ---- fanout_scatter (mp_ops.cpp:3038-3101) ---------------------------------
+
+size_t relm_mp_fanout_scatter_workspace_bytes(int64_t num_edges, int64_t out_rows, int64_t emb, relm_mp_dtype dtype)
+{
+   return op_workspace(num_edges, out_rows, emb, dtype, RELM_MP_MODE_SUM, false);
+}
+
+int relm_mp_fanout_scatter(relm_mp_dtype dtype, const void* x_cat, int64_t x_rows, int64_t emb,
+                           const int64_t* src_global_idx, const int64_t* flat_dst, int64_t num_edges,
+                           int64_t out_rows, void* out, void* workspace, size_t workspace_bytes, void* stream)
+{
+   int rc;
+   if((rc = check_common(dtype, emb, num_edges))) return rc;
+   if(out_rows < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_rows must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(num_edges == 0 || out_rows == 0) return fill_rows(dtype, out, out_rows * emb, false, st);
+   OpMem m;
+   const size_t need = relm_mp_fanout_scatter_workspace_bytes(num_edges, out_rows, emb, dtype);
+   if((rc = split_workspace(workspace, workspace_bytes, need, num_edges, out_rows, m))) return rc;
+   relm_mp_plan plan;
+   // The reference loop checks src_global_idx before flat_dst at each edge.
+   if((rc = plan_build_bounded(
+          flat_dst, src_global_idx, num_edges, out_rows, out_rows, x_rows, "flat_dst", "src_global_idx", true,
+          m.plan_mem, m.plan_bytes, m.scratch, m.scratch_bytes, st, &plan
+       )))
+      return rc;
+   return relm_mp_plan_gather_last(&plan, dtype, x_cat, emb, out, stream);
+}
+
+// ---- fanout_scatter_backward (mp_ops.cpp:3103-3166) ------------------------
+
+size_t relm_mp_fanout_scatter_backward_workspace_bytes(int64_t num_edges, int64_t x_rows, int64_t emb,
+                                                       relm_mp_dtype dtype)
+{
+   return op_workspace(num_edges, x_rows, emb, dtype, RELM_MP_MODE_SUM, true);
+}
+
+int relm_mp_fanout_scatter_backward(relm_mp_dtype dtype, const void* grad_out, int64_t grad_out_rows, int64_t emb,
+                                    const int64_t* src_global_idx, const int64_t* flat_dst, int64_t num_edges,
+                                    int64_t x_rows, void* grad_x, void* workspace, size_t workspace_bytes,
+                                    void* stream)
+{
+   int rc;
+   if((rc = check_common(dtype, emb, num_edges))) return rc;
+   if(x_rows < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "x_rows must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(num_edges == 0 || x_rows == 0) return fill_rows(dtype, grad_x, x_rows * emb, false, st);
+   OpMem m;
+   const size_t need = relm_mp_fanout_scatter_backward_workspace_bytes(num_edges, x_rows, emb, dtype);
+   if((rc = split_workspace(workspace, workspace_bytes, need, num_edges, x_rows, m))) return rc;
+   relm_mp_plan plan;
+   if((rc = plan_build_bounded(
+          src_global_idx, flat_dst, num_edges, x_rows, x_rows, grad_out_rows, "src_global_idx", "flat_dst", false,
+          m.plan_mem, m.plan_bytes, m.scratch, m.scratch_bytes, st, &plan
+       )))
+      return rc;
+   return planned_reduce(&plan, dtype, kSum, grad_out, nullptr, nullptr, emb, grad_x, m.scratch, m.scratch_bytes, st);
+}
+
+// ---- fanin_reduce (mp_ops.cpp:3327-3348 -> 3168-3222 / 3005-3036) ----------
+
+size_t relm_mp_fanin_reduce_workspace_bytes(int64_t num_edges, int64_t dim_size, int64_t emb, relm_mp_dtype dtype,
+                                            int mode)
+{
+   return op_workspace(num_edges, dim_size, emb, dtype, mode, true);
+}
+
+int relm_mp_fanin_reduce(relm_mp_dtype dtype, const void* rel_flat, int64_t rel_rows, int64_t emb,
+                         const int64_t* flat_src, const int64_t* dst_idx, int64_t num_edges, int64_t dim_size,
+                         int mode, void* out, void* workspace, size_t workspace_bytes, void* stream)
+{
+   int rc;
+   if((rc = check_common(dtype, emb, num_edges))) return rc;
+   if(dim_size < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "dim_size must be >= 0.");
+   if(mode != RELM_MP_MODE_SUM && mode != RELM_MP_MODE_LOGSUMEXP)
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "Unsupported fanin_reduce mode. Supported: 0=sum, 1=logsumexp.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(num_edges == 0 || dim_size == 0)
+      return fill_rows(dtype, out, dim_size * emb, mode == RELM_MP_MODE_LOGSUMEXP, st);
+   OpMem m;
+   const size_t need = relm_mp_fanin_reduce_workspace_bytes(num_edges, dim_size, emb, dtype, mode);
+   if((rc = split_workspace(workspace, workspace_bytes, need, num_edges, dim_size, m))) return rc;
+   relm_mp_plan plan;
+   if((rc = plan_build_bounded(
+          dst_idx, flat_src, num_edges, dim_size, dim_size, rel_rows, "dst_idx", "flat_src", true, m.plan_mem,
+          m.plan_bytes, m.scratch, m.scratch_bytes, st, &plan
+       )))
+      return rc;
+   return planned_reduce(
+      &plan, dtype, mode == RELM_MP_MODE_SUM ? kSum : kLse, rel_flat, nullptr, nullptr, emb, out, m.scratch,
+      m.scratch_bytes, st
+   );
+}
+
+// ---- fanin_reduce_sum_backward (mp_ops.cpp:3224-3284) ----------------------
+
+size_t relm_mp_fanin_reduce_sum_backward_workspace_bytes(int64_t num_edges, int64_t rel_rows, int64_t emb,
+                                                         relm_mp_dtype dtype)
+{
+   return op_workspace(num_edges, rel_rows, emb, dtype, RELM_MP_MODE_SUM, true);
+}
+
+int relm_mp_fanin_reduce_sum_backward(relm_mp_dtype dtype, const void* grad_out, int64_t grad_out_rows, int64_t emb,
+                                      const int64_t* flat_src, const int64_t* dst_idx, int64_t num_edges,
+                                      int64_t rel_rows, void* grad_rel, void* workspace, size_t workspace_bytes,
+                                      void* stream)
+{
+   int rc;
+   if((rc = check_common(dtype, emb, num_edges))) return rc;
+   if(rel_rows < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "rel_rows must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(num_edges == 0 || rel_rows == 0) return fill_rows(dtype, grad_rel, rel_rows * emb, false, st);
+   OpMem m;
+   const size_t need = relm_mp_fanin_reduce_sum_backward_workspace_bytes(num_edges, rel_rows, emb, dtype);
+   if((rc = split_workspace(workspace, workspace_bytes, need, num_edges, rel_rows, m))) return rc;
+   relm_mp_plan plan;
+   if((rc = plan_build_bounded(
+          flat_src, dst_idx, num_edges, rel_rows, rel_rows, grad_out_rows, "flat_src", "dst_idx", false,
+          m.plan_mem, m.plan_bytes, m.scratch, m.scratch_bytes, st, &plan
+       )))
+      return rc;
+   return planned_reduce(&plan, dtype, kSum, grad_out, nullptr, nullptr, emb, grad_rel, m.scratch, m.scratch_bytes, st);
+}
+
+// ---- fanin_reduce_logsumexp_backward (mp_ops.cpp:3286-3325, 2981-3003) -----
+
+size_t relm_mp_fanin_reduce_logsumexp_backward_workspace_bytes(int64_t num_edges, int64_t rel_rows, int64_t emb,
+                                                               relm_mp_dtype dtype)
+{
+   return op_workspace(num_edges, rel_rows, emb, dtype, RELM_MP_MODE_SUM, true);
+}
+
+int relm_mp_fanin_reduce_logsumexp_backward(relm_mp_dtype dtype, const void* grad_out, const void* rel_flat,
+                                            int64_t rel_table_rows, const void* out, int64_t dim_size, int64_t emb,
+                                            const int64_t* flat_src, const int64_t* dst_idx, int64_t num_edges,
+                                            int64_t rel_rows, void* grad_rel, void* workspace,
+                                            size_t workspace_bytes, void* stream)
+{
+   int rc;
+   if((rc = check_common(dtype, emb, num_edges))) return rc;
+   if(rel_rows < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "rel_rows must be >= 0.");
+   if(rel_table_rows < 0 || dim_size < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "sizes must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(num_edges == 0 || rel_rows == 0) return fill_rows(dtype, grad_rel, rel_rows * emb, false, st);
+   OpMem m;
+   const size_t need = relm_mp_fanin_reduce_logsumexp_backward_workspace_bytes(num_edges, rel_rows, emb, dtype);
+   if((rc = split_workspace(workspace, workspace_bytes, need, num_edges, rel_rows, m))) return rc;
+   relm_mp_plan plan;
+   // flat_src indexes both rel_flat and grad_rel, so it is bounded by the smaller of the two.
+   const int64_t bound = rel_table_rows < rel_rows ? rel_table_rows : rel_rows;
+   if((rc = plan_build_bounded(
+          flat_src, dst_idx, num_edges, rel_rows, bound, dim_size, "flat_src", "dst_idx", false, m.plan_mem,
+          m.plan_bytes, m.scratch, m.scratch_bytes, st, &plan
+       )))
+      return rc;
+   return planned_reduce(&plan, dtype, kLseBwd, grad_out, out, rel_flat, emb, grad_rel, m.scratch, m.scratch_bytes, st);
+}
+
+}  // extern "C"

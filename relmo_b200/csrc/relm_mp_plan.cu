@@ -1,0 +1,372 @@
+// Plan build: validate an (output index, gather index) pair and lay it out as
+// a CSR over the output rows, plus merge-path tile boundaries.
+//
+// The reference kernels (mp_cuda_kernels.cu:412-649) run one thread per
+// (edge, column) and resolve collisions with float atomics. Here every op is a
+// segment reduction over output rows instead, so the indices are laid out
+// once:
+//   1. k_validate   - bounds of both indices (first offending edge, as the
+//                     reference CPU loop reports it), sortedness of the output
+//                     index, int32 copies of both.
+//   2. radix sort   - stable sort of (output row, gathered row) pairs by output
+//                     row, only over the bits num_rows needs (skipped when the
+//                     output index is already non-decreasing).
+//   3. k_mark_ends + inclusive max-scan - row_ptr without atomics: the end of
+//                     each non-empty segment is written at row+1, the max-scan
+//                     carries it over empty rows.
+//   4. k_partition  - merge-path split of the (num_rows + num_edges) items into
+//                     equal tiles, so one hub row spreads over many warps and
+//                     runs of empty rows cost what their output bytes cost.
+#include <cub/device/device_radix_sort.cuh>
+#include <cub/device/device_scan.cuh>
+
+#include <climits>
+#include <cstdio>
+#include <string>
+
+#include "relm_mp_internal.cuh"
+
+namespace relm_mp {
+
+namespace {
+
+struct PlanStats {
+   unsigned long long out_bad;     // first edge with an out-of-range output index
+   unsigned long long gather_bad;  // first edge with an out-of-range gather index
+   unsigned int descents;          // warps that saw out_index[e] > out_index[e+1]
+   unsigned int pad;
+};
+
+__global__ void k_init_stats(PlanStats* st)
+{
+   st->out_bad = ULLONG_MAX;
+   st->gather_bad = ULLONG_MAX;
+   st->descents = 0;
+   st->pad = 0;
+}
+
+__global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict__ key,
+                                                       const int64_t* __restrict__ gat, int64_t n,
+                                                       int64_t key_bound, int64_t gat_bound,
+                                                       uint32_t* __restrict__ key32,
+                                                       int32_t* __restrict__ gat32,
+                                                       PlanStats* __restrict__ st)
+{
+   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+   bool descent = false;
+   if(e < n) {
+      const int64_t k = key[e];
+      const int64_t g = gat[e];
+      if(k < 0 || k >= key_bound) atomicMin(&st->out_bad, (unsigned long long)e);
+      if(g < 0 || g >= gat_bound) atomicMin(&st->gather_bad, (unsigned long long)e);
+      key32[e] = (uint32_t)k;
+      gat32[e] = (int32_t)g;
+      if(e + 1 < n) descent = key[e + 1] < k;
+   }
+   const unsigned any = __ballot_sync(0xffffffffu, descent);
+   if(any && (threadIdx.x & 31) == 0) atomicAdd(&st->descents, 1u);
+}
+
+// mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys).
+__global__ void __launch_bounds__(kThreads) k_mark_ends(const uint32_t* __restrict__ keys,
+                                                        int64_t n, int32_t* __restrict__ mark)
+{
+   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+   if(e >= n) return;
+   const uint32_t k = keys[e];
+   if(e == n - 1 || keys[e + 1] != k) mark[(int64_t)k + 1] = (int32_t)(e + 1);
+}
+
+// Merge-path search: the split of diagonal d between the row-end list
+// (row_ptr[1..num_rows]) and the edge list (0..num_edges-1). Row ends are
+// consumed before an edge with the same position, so a split (i, j) means rows
+// [0, i) have ended and edges [0, j) are consumed.
+__global__ void __launch_bounds__(kThreads) k_partition(const int32_t* __restrict__ row_ptr,
+                                                        int64_t num_rows, int64_t num_edges,
+                                                        int64_t num_tiles, int tile_items,
+                                                        int32_t* __restrict__ tile_row,
+                                                        int32_t* __restrict__ tile_edge)
+{
+   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+   if(t > num_tiles) return;
+   const int64_t total = num_rows + num_edges;
+   int64_t d = t * (int64_t)tile_items;
+   if(d > total) d = total;
+   int64_t lo = d - num_edges > 0 ? d - num_edges : 0;
+   int64_t hi = d < num_rows ? d : num_rows;
+   while(lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      if((int64_t)row_ptr[mid + 1] <= d - mid - 1)
+         lo = mid + 1;
+      else
+         hi = mid;
+   }
+   tile_row[t] = (int32_t)lo;
+   tile_edge[t] = (int32_t)(d - lo);
+}
+
+struct MaxOp {
+   __device__ __forceinline__ int32_t operator()(int32_t a, int32_t b) const { return a > b ? a : b; }
+};
+
+int end_bit_for(int64_t num_rows)
+{
+   int bits = 1;
+   while(bits < 32 && ((int64_t)1 << bits) < num_rows) ++bits;
+   return bits;
+}
+
+size_t sort_temp_bytes(int64_t num_edges)
+{
+   size_t bytes = 0;
+   cub::DoubleBuffer< uint32_t > keys(nullptr, nullptr);
+   cub::DoubleBuffer< int32_t > vals(nullptr, nullptr);
+   cub::DeviceRadixSort::SortPairs(nullptr, bytes, keys, vals, (int)num_edges, 0, 32);
+   return bytes;
+}
+
+size_t scan_temp_bytes(int64_t num_rows)
+{
+   size_t bytes = 0;
+   cub::DeviceScan::InclusiveScan(
+      nullptr, bytes, (const int32_t*)nullptr, (int32_t*)nullptr, MaxOp(), (int)(num_rows + 1)
+   );
+   return bytes;
+}
+
+struct PlanLayout {
+   int32_t* gidx;
+   int32_t* row_ptr;
+   int32_t* tile_row;
+   int32_t* tile_edge;
+   size_t bytes;
+};
+
+PlanLayout plan_layout(void* mem, int64_t num_edges, int64_t num_rows)
+{
+   Carver c(mem);
+   PlanLayout l;
+   const int64_t tiles = plan_num_tiles(num_edges, num_rows);
+   l.gidx = c.take< int32_t >((size_t)num_edges);
+   l.row_ptr = c.take< int32_t >((size_t)num_rows + 1);
+   l.tile_row = c.take< int32_t >((size_t)tiles + 1);
+   l.tile_edge = c.take< int32_t >((size_t)tiles + 1);
+   l.bytes = c.used;
+   return l;
+}
+
+struct ScratchLayout {
+   PlanStats* stats;
+   uint32_t* key_in;
+   uint32_t* key_alt;
+   int32_t* val_alt;
+   int32_t* mark;
+   void* sort_temp;
+   size_t sort_bytes;
+   void* scan_temp;
+   size_t scan_bytes;
+   size_t bytes;
+};
+
+ScratchLayout scratch_layout(void* mem, int64_t num_edges, int64_t num_rows)
+{
+   Carver c(mem);
+   ScratchLayout l;
+   l.stats = c.take< PlanStats >(1);
+   l.key_in = c.take< uint32_t >((size_t)num_edges);
+   l.key_alt = c.take< uint32_t >((size_t)num_edges);
+   l.val_alt = c.take< int32_t >((size_t)num_edges);
+   l.mark = c.take< int32_t >((size_t)num_rows + 1);
+   l.sort_bytes = sort_temp_bytes(num_edges);
+   l.sort_temp = c.take< char >(l.sort_bytes);
+   l.scan_bytes = scan_temp_bytes(num_rows);
+   l.scan_temp = c.take< char >(l.scan_bytes);
+   l.bytes = c.used;
+   return l;
+}
+
+unsigned grid_for(int64_t n, int threads = kThreads)
+{
+   return (unsigned)((n + threads - 1) / threads);
+}
+
+}  // namespace
+
+int64_t plan_num_tiles(int64_t num_edges, int64_t num_rows)
+{
+   return (num_edges + num_rows + kTileItems - 1) / kTileItems;
+}
+
+int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                       int64_t num_rows, int64_t out_bound, int64_t gather_rows,
+                       const char* out_name, const char* gather_name, bool gather_checked_first,
+                       void* plan_mem, size_t plan_bytes, void* scratch, size_t scratch_bytes,
+                       cudaStream_t stream, relm_mp_plan* plan)
+{
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   if(num_edges < 0 || num_rows < 0 || gather_rows < 0)
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan sizes must be >= 0.");
+   if(num_edges + num_rows >= (int64_t)INT32_MAX || gather_rows >= (int64_t)INT32_MAX)
+      return fail(
+         RELM_MP_ERR_UNSUPPORTED, "relm_mp supports num_edges + num_rows < 2^31 and < 2^31 gathered rows."
+      );
+   if(num_edges > 0 && (!out_index || !gather_index))
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "index pointers must not be NULL.");
+   const PlanLayout pl = plan_layout(plan_mem, num_edges, num_rows);
+   const ScratchLayout sl = scratch_layout(scratch, num_edges, num_rows);
+   if(!plan_mem || plan_bytes < pl.bytes)
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "plan memory is smaller than relm_mp_plan_bytes().");
+   if(!scratch || scratch_bytes < sl.bytes)
+      return fail(
+         RELM_MP_ERR_WORKSPACE_TOO_SMALL, "plan scratch is smaller than relm_mp_plan_scratch_bytes()."
+      );
+   const char* oname = out_name ? out_name : "out_index";
+   const char* gname = gather_name ? gather_name : "gather_index";
+
+   const int64_t tiles = plan_num_tiles(num_edges, num_rows);
+   *plan = relm_mp_plan{};
+   plan->num_edges = num_edges;
+   plan->num_rows = num_rows;
+   plan->gather_rows = gather_rows;
+   plan->num_tiles = tiles;
+   plan->tile_items = kTileItems;
+   plan->row_ptr = pl.row_ptr;
+   plan->gidx = pl.gidx;
+   plan->tile_row = pl.tile_row;
+   plan->tile_edge = pl.tile_edge;
+
+   int rc;
+   k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
+   if((rc = check_launch("k_init_stats"))) return rc;
+   if(num_edges > 0) {
+      k_validate<<< grid_for(num_edges), kThreads, 0, stream >>>(
+         out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, pl.gidx, sl.stats
+      );
+      if((rc = check_launch("k_validate"))) return rc;
+   }
+   PlanStats host{};
+   if((rc = check_cuda(
+          cudaMemcpyAsync(&host, sl.stats, sizeof(PlanStats), cudaMemcpyDeviceToHost, stream),
+          "plan stats copy"
+       )))
+      return rc;
+   if((rc = check_cuda(cudaStreamSynchronize(stream), "plan stats sync"))) return rc;
+
+   if(host.out_bad != ULLONG_MAX || host.gather_bad != ULLONG_MAX) {
+      bool use_gather;
+      if(host.out_bad == host.gather_bad)
+         use_gather = gather_checked_first;
+      else
+         use_gather = host.gather_bad < host.out_bad;
+      const unsigned long long pos = use_gather ? host.gather_bad : host.out_bad;
+      const int64_t* arr = use_gather ? gather_index : out_index;
+      int64_t value = 0;
+      if((rc = check_cuda(
+             cudaMemcpy(&value, arr + pos, sizeof(int64_t), cudaMemcpyDeviceToHost), "bad index copy"
+          )))
+         return rc;
+      char msg[256];
+      snprintf(
+         msg,
+         sizeof msg,
+         "%s index out of bounds: %lld not in [0, %lld).",
+         use_gather ? gname : oname,
+         (long long)value,
+         (long long)(use_gather ? gather_rows : out_bound)
+      );
+      return fail(RELM_MP_ERR_INDEX_OUT_OF_RANGE, msg);
+   }
+
+   const uint32_t* sorted_keys = sl.key_in;
+   if(host.descents == 0) {
+      plan->flags |= RELM_MP_PLAN_SORTED_INPUT;
+   } else {
+      cub::DoubleBuffer< uint32_t > keys(sl.key_in, sl.key_alt);
+      cub::DoubleBuffer< int32_t > vals(pl.gidx, sl.val_alt);
+      size_t temp = sl.sort_bytes;
+      if((rc = check_cuda(
+             cub::DeviceRadixSort::SortPairs(
+                sl.sort_temp, temp, keys, vals, (int)num_edges, 0, end_bit_for(num_rows), stream
+             ),
+             "radix sort"
+          )))
+         return rc;
+      sorted_keys = keys.Current();
+      if(vals.Current() != pl.gidx) {
+         if((rc = check_cuda(
+                cudaMemcpyAsync(
+                   pl.gidx, vals.Current(), (size_t)num_edges * sizeof(int32_t),
+                   cudaMemcpyDeviceToDevice, stream
+                ),
+                "gidx copy"
+             )))
+            return rc;
+      }
+   }
+
+   if((rc = check_cuda(
+          cudaMemsetAsync(sl.mark, 0, ((size_t)num_rows + 1) * sizeof(int32_t), stream), "mark memset"
+       )))
+      return rc;
+   if(num_edges > 0) {
+      k_mark_ends<<< grid_for(num_edges), kThreads, 0, stream >>>(sorted_keys, num_edges, sl.mark);
+      if((rc = check_launch("k_mark_ends"))) return rc;
+   }
+   size_t scan_temp = sl.scan_bytes;
+   if((rc = check_cuda(
+          cub::DeviceScan::InclusiveScan(
+             sl.scan_temp, scan_temp, sl.mark, pl.row_ptr, MaxOp(), (int)(num_rows + 1), stream
+          ),
+          "row_ptr scan"
+       )))
+      return rc;
+   k_partition<<< grid_for(tiles + 1), kThreads, 0, stream >>>(
+      pl.row_ptr, num_rows, num_edges, tiles, kTileItems, pl.tile_row, pl.tile_edge
+   );
+   if((rc = check_launch("k_partition"))) return rc;
+   return RELM_MP_OK;
+}
+
+}  // namespace relm_mp
+
+extern "C" {
+
+size_t relm_mp_plan_bytes(int64_t num_edges, int64_t num_rows)
+{
+   if(num_edges < 0 || num_rows < 0) return 0;
+   return relm_mp::plan_layout(nullptr, num_edges, num_rows).bytes;
+}
+
+size_t relm_mp_plan_scratch_bytes(int64_t num_edges, int64_t num_rows)
+{
+   if(num_edges < 0 || num_rows < 0) return 0;
+   return relm_mp::scratch_layout(nullptr, num_edges, num_rows).bytes;
+}
+
+int relm_mp_plan_build(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                       int64_t num_rows, int64_t gather_rows, const char* out_index_name,
+                       const char* gather_index_name, void* plan_mem, size_t plan_bytes,
+                       void* scratch, size_t scratch_bytes, void* stream, relm_mp_plan* plan)
+{
+   return relm_mp::plan_build_bounded(
+      out_index, gather_index, num_edges, num_rows, num_rows, gather_rows, out_index_name,
+      gather_index_name, false, plan_mem, plan_bytes, scratch, scratch_bytes,
+      static_cast< cudaStream_t >(stream), plan
+   );
+}
+
+int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                          int64_t num_rows, int64_t out_bound, int64_t gather_rows, const char* out_index_name,
+                          const char* gather_index_name, int gather_checked_first, void* plan_mem,
+                          size_t plan_bytes, void* scratch, size_t scratch_bytes, void* stream, relm_mp_plan* plan)
+{
+   if(out_bound < 0 || out_bound > num_rows)
+      return relm_mp::fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_bound must be in [0, num_rows].");
+   return relm_mp::plan_build_bounded(
+      out_index, gather_index, num_edges, num_rows, out_bound, gather_rows, out_index_name,
+      gather_index_name, gather_checked_first != 0, plan_mem, plan_bytes, scratch, scratch_bytes,
+      static_cast< cudaStream_t >(stream), plan
+   );
+}
+
+}  // extern "C"

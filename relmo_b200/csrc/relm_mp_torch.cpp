@@ -1,0 +1,637 @@
+// torch.ops.relm_mp registration of the B200 library.
+//
+// Registers the reference's schemas (maichmueller/relmo
+// src/_ops/mp/mp_ops.cpp:3754-3838) for the hot path and the pack ops its call
+// sites use, with:
+//   - CUDA kernels for fanout_scatter, fanout_scatter_backward, fanin_reduce,
+//     fanin_reduce_sum_backward, fanin_reduce_logsumexp_backward, all running
+//     through librelm_mp_b200.so (include/relm_mp.h). There is no CPU or ATen
+//     fallback for CUDA tensors: an unsupported dtype raises.
+//   - Meta kernels (shapes only) so the ops trace under torch.compile / fake
+//     tensors.
+//   - CompositeImplicitAutograd pack ops (index arithmetic + cat, as
+//     mp_ops.cpp:412-570 and 2511-2773) and build_info.
+// CPU tensors are not handled by this library (the Python facade keeps the
+// reference's ATen formulas for them).
+//
+// Plans (relm_mp_plan) are cached per (output index, gather index) pair. The
+// key holds weak references to both index storages plus their version
+// counters, offsets, lengths and the bounds, so a freed, reallocated or
+// in-place-modified index never hits a stale plan. One model forward reuses
+// the same routing indices in every layer and in the backward, so each
+// distinct index pair pays the sort once.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <c10/util/intrusive_ptr.h>
+#include <torch/library.h>
+
+#include <cstdint>
+#include <limits>
+#include <list>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "relm_mp.h"
+
+#ifndef RELM_MP_BUILD_TORCH_VERSION
+#define RELM_MP_BUILD_TORCH_VERSION "unknown"
+#endif
+#ifndef RELM_MP_BUILD_CUDA_TAG
+#define RELM_MP_BUILD_CUDA_TAG "unknown"
+#endif
+#ifndef RELM_MP_ABI_TARGET
+#define RELM_MP_ABI_TARGET "unknown"
+#endif
+
+namespace relm_b200 {
+
+using at::Tensor;
+
+constexpr int64_t kModeSum = 0;
+constexpr int64_t kModeLogSumExp = 1;
+
+// ---- validation, as mp_ops.cpp:38-71 --------------------------------------
+
+void check_rank(const Tensor& t, int64_t expected, const char* name)
+{
+   TORCH_CHECK(t.dim() == expected, name, " must be rank ", expected, ", got rank ", t.dim(), ".");
+}
+
+void check_int64_index(const Tensor& t, const char* name)
+{
+   check_rank(t, 1, name);
+   TORCH_CHECK(t.scalar_type() == at::kLong, name, " must have dtype torch.int64.");
+}
+
+void check_same_device(const Tensor& a, const Tensor& b, const char* an, const char* bn)
+{
+   TORCH_CHECK(
+      a.device() == b.device(), an, " and ", bn, " must be on the same CUDA device, got ", a.device(), " and ",
+      b.device(), "."
+   );
+}
+
+relm_mp_dtype to_dtype(const Tensor& t, const char* op)
+{
+   switch(t.scalar_type()) {
+      case at::kFloat: return RELM_MP_FLOAT32;
+      case at::kDouble: return RELM_MP_FLOAT64;
+      case at::kBFloat16: return RELM_MP_BFLOAT16;
+      case at::kHalf: return RELM_MP_FLOAT16;
+      default: break;
+   }
+   TORCH_CHECK(false, op, ": unsupported dtype ", t.scalar_type(), " (float32, float64, bfloat16, float16).");
+   return RELM_MP_FLOAT32;
+}
+
+void check_status(int rc, const char* op)
+{
+   if(rc == RELM_MP_OK) return;
+   TORCH_CHECK(false, relm_mp_last_error(), rc == RELM_MP_ERR_INDEX_OUT_OF_RANGE ? "" : " (",
+               rc == RELM_MP_ERR_INDEX_OUT_OF_RANGE ? "" : op, rc == RELM_MP_ERR_INDEX_OUT_OF_RANGE ? "" : ")");
+}
+
+cudaStream_t stream_of(const Tensor& t)
+{
+   return at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+Tensor byte_buffer(size_t bytes, const Tensor& like)
+{
+   return at::empty({(int64_t)std::max< size_t >(bytes, 1)}, like.options().dtype(at::kByte));
+}
+
+// ---- plan cache -------------------------------------------------------------
+
+struct IndexKey {
+   c10::weak_intrusive_ptr< c10::StorageImpl > storage;
+   const c10::StorageImpl* impl = nullptr;
+   int64_t offset = 0;
+   int64_t numel = 0;
+   uint32_t version = 0;
+
+   static IndexKey of(const Tensor& t)
+   {
+      IndexKey k{c10::weak_intrusive_ptr< c10::StorageImpl >(t.storage().getWeakStorageImpl())};
+      k.impl = t.storage().unsafeGetStorageImpl();
+      k.offset = t.storage_offset();
+      k.numel = t.numel();
+      k.version = t.unsafeGetTensorImpl()->version_counter().current_version();
+      return k;
+   }
+   bool alive() const { return !storage.expired(); }
+   bool same(const IndexKey& o) const
+   {
+      return impl == o.impl && offset == o.offset && numel == o.numel && version == o.version;
+   }
+};
+
+struct PlanEntry {
+   IndexKey out_key;
+   IndexKey gather_key;
+   int64_t num_rows;
+   int64_t out_bound;
+   int64_t gather_rows;
+   int gather_first;
+   Tensor memory;  // owns the plan arrays
+   relm_mp_plan plan;
+};
+
+class PlanCache {
+ public:
+   static PlanCache& get()
+   {
+      static PlanCache cache;
+      return cache;
+   }
+
+   // Returns the plan for (out_index, gather_index); builds it on a miss.
+   relm_mp_plan lookup(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
+                       int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first,
+                       Tensor* keep_alive)
+   {
+      const IndexKey ok = IndexKey::of(out_index);
+      const IndexKey gk = IndexKey::of(gather_index);
+      {
+         std::lock_guard< std::mutex > lock(mu_);
+         evict_dead_locked();
+         for(auto it = entries_.begin(); it != entries_.end(); ++it) {
+            if(it->out_key.same(ok) && it->gather_key.same(gk) && it->num_rows == num_rows
+               && it->out_bound == out_bound && it->gather_rows == gather_rows
+               && it->gather_first == (int)gather_first && it->memory.device() == out_index.device()) {
+               entries_.splice(entries_.begin(), entries_, it);
+               ++hits_;
+               *keep_alive = entries_.front().memory;
+               return entries_.front().plan;
+            }
+         }
+      }
+      const int64_t num_edges = out_index.numel();
+      Tensor memory = byte_buffer(relm_mp_plan_bytes(num_edges, num_rows), out_index);
+      Tensor scratch = byte_buffer(relm_mp_plan_scratch_bytes(num_edges, num_rows), out_index);
+      relm_mp_plan plan;
+      const int rc = relm_mp_plan_build_ex(
+         out_index.data_ptr< int64_t >(), gather_index.data_ptr< int64_t >(), num_edges, num_rows, out_bound,
+         gather_rows, out_name, gather_name, gather_first ? 1 : 0, memory.data_ptr(), (size_t)memory.numel(),
+         scratch.data_ptr(), (size_t)scratch.numel(), stream_of(out_index), &plan
+      );
+      check_status(rc, "plan build");
+      *keep_alive = memory;
+      std::lock_guard< std::mutex > lock(mu_);
+      ++builds_;
+      entries_.push_front(PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan});
+      while(entries_.size() > capacity_) entries_.pop_back();
+      return plan;
+   }
+
+   void clear()
+   {
+      std::lock_guard< std::mutex > lock(mu_);
+      entries_.clear();
+   }
+
+   std::vector< int64_t > stats()
+   {
+      std::lock_guard< std::mutex > lock(mu_);
+      evict_dead_locked();
+      int64_t bytes = 0;
+      for(const auto& e : entries_) bytes += e.memory.numel();
+      return {(int64_t)entries_.size(), hits_, builds_, bytes, (int64_t)capacity_};
+   }
+
+   void set_capacity(int64_t cap)
+   {
+      std::lock_guard< std::mutex > lock(mu_);
+      capacity_ = (size_t)std::max< int64_t >(cap, 0);
+      while(entries_.size() > capacity_) entries_.pop_back();
+   }
+
+ private:
+   void evict_dead_locked()
+   {
+      for(auto it = entries_.begin(); it != entries_.end();) {
+         if(!it->out_key.alive() || !it->gather_key.alive())
+            it = entries_.erase(it);
+         else
+            ++it;
+      }
+   }
+
+   std::mutex mu_;
+   std::list< PlanEntry > entries_;
+   size_t capacity_ = 16;
+   int64_t hits_ = 0;
+   int64_t builds_ = 0;
+};
+
+relm_mp_plan get_plan(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
+                      int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first,
+                      Tensor* keep_alive)
+{
+   return PlanCache::get().lookup(
+      out_index, gather_index, num_rows, out_bound, gather_rows, out_name, gather_name, gather_first, keep_alive
+   );
+}
+
+Tensor contig(const Tensor& t) { return t.is_contiguous() ? t : t.contiguous(); }
+
+// ---- CUDA kernels of the hot ops ------------------------------------------------
+
+// mp_ops.cpp:3038-3101
+Tensor fanout_scatter_cuda(const Tensor& x_cat, const Tensor& src_global_idx, const Tensor& flat_dst, int64_t out_rows)
+{
+   check_rank(x_cat, 2, "x_cat");
+   check_int64_index(src_global_idx, "src_global_idx");
+   check_int64_index(flat_dst, "flat_dst");
+   TORCH_CHECK(src_global_idx.size(0) == flat_dst.size(0), "src_global_idx and flat_dst must have equal length.");
+   TORCH_CHECK(out_rows >= 0, "out_rows must be >= 0.");
+   check_same_device(x_cat, src_global_idx, "x_cat", "src_global_idx");
+   check_same_device(x_cat, flat_dst, "x_cat", "flat_dst");
+   c10::cuda::CUDAGuard guard(x_cat.device());
+   const relm_mp_dtype dt = to_dtype(x_cat, "fanout_scatter");
+   const int64_t emb = x_cat.size(1);
+   if(src_global_idx.numel() == 0 || out_rows == 0) return at::zeros({out_rows, emb}, x_cat.options());
+   Tensor out = at::empty({out_rows, emb}, x_cat.options());
+   const Tensor x = contig(x_cat);
+   const Tensor src = contig(src_global_idx);
+   const Tensor dst = contig(flat_dst);
+   Tensor keep;
+   const relm_mp_plan plan = get_plan(dst, src, out_rows, out_rows, x.size(0), "flat_dst", "src_global_idx", true, &keep);
+   check_status(relm_mp_plan_gather_last(&plan, dt, x.data_ptr(), emb, out.data_ptr(), stream_of(x)), "fanout_scatter");
+   return out;
+}
+
+Tensor planned_sum(const relm_mp_plan& plan, relm_mp_dtype dt, const Tensor& table, int64_t emb, Tensor& out,
+                   int mode, const char* op)
+{
+   Tensor scratch = byte_buffer(relm_mp_plan_reduce_scratch_bytes(&plan, emb, dt, mode), table);
+   check_status(
+      relm_mp_plan_reduce(&plan, dt, mode, table.data_ptr(), emb, out.data_ptr(), scratch.data_ptr(),
+                          (size_t)scratch.numel(), stream_of(table)),
+      op
+   );
+   return out;
+}
+
+// mp_ops.cpp:3103-3166
+Tensor fanout_scatter_backward_cuda(const Tensor& grad_out, const Tensor& src_global_idx, const Tensor& flat_dst,
+                                    int64_t x_rows)
+{
+   check_rank(grad_out, 2, "grad_out");
+   check_int64_index(src_global_idx, "src_global_idx");
+   check_int64_index(flat_dst, "flat_dst");
+   TORCH_CHECK(src_global_idx.size(0) == flat_dst.size(0), "src_global_idx and flat_dst must have equal length.");
+   TORCH_CHECK(x_rows >= 0, "x_rows must be >= 0.");
+   check_same_device(grad_out, src_global_idx, "grad_out", "src_global_idx");
+   check_same_device(grad_out, flat_dst, "grad_out", "flat_dst");
+   c10::cuda::CUDAGuard guard(grad_out.device());
+   const relm_mp_dtype dt = to_dtype(grad_out, "fanout_scatter_backward");
+   const int64_t emb = grad_out.size(1);
+   if(src_global_idx.numel() == 0 || x_rows == 0) return at::zeros({x_rows, emb}, grad_out.options());
+   Tensor grad_x = at::empty({x_rows, emb}, grad_out.options());
+   const Tensor g = contig(grad_out);
+   const Tensor src = contig(src_global_idx);
+   const Tensor dst = contig(flat_dst);
+   Tensor keep;
+   const relm_mp_plan plan = get_plan(src, dst, x_rows, x_rows, g.size(0), "src_global_idx", "flat_dst", false, &keep);
+   return planned_sum(plan, dt, g, emb, grad_x, RELM_MP_MODE_SUM, "fanout_scatter_backward");
+}
+
+// mp_ops.cpp:3327-3348 with 3168-3222 (sum) and 3005-3036 (logsumexp)
+Tensor fanin_reduce_cuda(const Tensor& rel_flat, const Tensor& flat_src, const Tensor& dst_idx, int64_t dim_size,
+                         int64_t mode)
+{
+   check_rank(rel_flat, 2, "rel_flat");
+   check_int64_index(flat_src, "flat_src");
+   check_int64_index(dst_idx, "dst_idx");
+   TORCH_CHECK(flat_src.size(0) == dst_idx.size(0), "flat_src and dst_idx must have equal length.");
+   TORCH_CHECK(dim_size >= 0, "dim_size must be >= 0.");
+   if(mode != kModeSum && mode != kModeLogSumExp)
+      throw std::invalid_argument("Unsupported fanin_reduce mode. Supported: 0=sum, 1=logsumexp.");
+   check_same_device(rel_flat, flat_src, "rel_flat", "flat_src");
+   check_same_device(rel_flat, dst_idx, "rel_flat", "dst_idx");
+   c10::cuda::CUDAGuard guard(rel_flat.device());
+   const relm_mp_dtype dt = to_dtype(rel_flat, "fanin_reduce");
+   const int64_t emb = rel_flat.size(1);
+   if(flat_src.numel() == 0 || dim_size == 0) {
+      if(mode == kModeSum) return at::zeros({dim_size, emb}, rel_flat.options());
+      return at::full({dim_size, emb}, -std::numeric_limits< double >::infinity(), rel_flat.options());
+   }
+   Tensor out = at::empty({dim_size, emb}, rel_flat.options());
+   const Tensor rel = contig(rel_flat);
+   const Tensor src = contig(flat_src);
+   const Tensor dst = contig(dst_idx);
+   Tensor keep;
+   const relm_mp_plan plan = get_plan(dst, src, dim_size, dim_size, rel.size(0), "dst_idx", "flat_src", true, &keep);
+   return planned_sum(plan, dt, rel, emb, out, (int)mode, "fanin_reduce");
+}
+
+// mp_ops.cpp:3224-3284
+Tensor fanin_reduce_sum_backward_cuda(const Tensor& grad_out, const Tensor& flat_src, const Tensor& dst_idx,
+                                      int64_t rel_rows)
+{
+   check_rank(grad_out, 2, "grad_out");
+   check_int64_index(flat_src, "flat_src");
+   check_int64_index(dst_idx, "dst_idx");
+   TORCH_CHECK(flat_src.size(0) == dst_idx.size(0), "flat_src and dst_idx must have equal length.");
+   TORCH_CHECK(rel_rows >= 0, "rel_rows must be >= 0.");
+   check_same_device(grad_out, flat_src, "grad_out", "flat_src");
+   check_same_device(grad_out, dst_idx, "grad_out", "dst_idx");
+   c10::cuda::CUDAGuard guard(grad_out.device());
+   const relm_mp_dtype dt = to_dtype(grad_out, "fanin_reduce_sum_backward");
+   const int64_t emb = grad_out.size(1);
+   if(flat_src.numel() == 0 || rel_rows == 0) return at::zeros({rel_rows, emb}, grad_out.options());
+   Tensor grad_rel = at::empty({rel_rows, emb}, grad_out.options());
+   const Tensor g = contig(grad_out);
+   const Tensor src = contig(flat_src);
+   const Tensor dst = contig(dst_idx);
+   Tensor keep;
+   const relm_mp_plan plan = get_plan(src, dst, rel_rows, rel_rows, g.size(0), "flat_src", "dst_idx", false, &keep);
+   return planned_sum(plan, dt, g, emb, grad_rel, RELM_MP_MODE_SUM, "fanin_reduce_sum_backward");
+}
+
+// mp_ops.cpp:3286-3325
+Tensor fanin_reduce_logsumexp_backward_cuda(const Tensor& grad_out, const Tensor& rel_flat, const Tensor& flat_src,
+                                            const Tensor& dst_idx, const Tensor& out, int64_t rel_rows)
+{
+   check_rank(grad_out, 2, "grad_out");
+   check_rank(rel_flat, 2, "rel_flat");
+   check_int64_index(flat_src, "flat_src");
+   check_int64_index(dst_idx, "dst_idx");
+   check_rank(out, 2, "out");
+   TORCH_CHECK(flat_src.size(0) == dst_idx.size(0), "flat_src and dst_idx must have equal length.");
+   TORCH_CHECK(rel_flat.size(1) == grad_out.size(1), "rel_flat and grad_out must share embedding dim.");
+   TORCH_CHECK(out.size(0) == grad_out.size(0), "out and grad_out must share dim_size.");
+   TORCH_CHECK(out.size(1) == grad_out.size(1), "out and grad_out must share embedding dim.");
+   TORCH_CHECK(rel_rows >= 0, "rel_rows must be >= 0.");
+   check_same_device(grad_out, rel_flat, "grad_out", "rel_flat");
+   check_same_device(grad_out, flat_src, "grad_out", "flat_src");
+   check_same_device(grad_out, dst_idx, "grad_out", "dst_idx");
+   check_same_device(grad_out, out, "grad_out", "out");
+   TORCH_CHECK(
+      grad_out.scalar_type() == rel_flat.scalar_type() && grad_out.scalar_type() == out.scalar_type(),
+      "grad_out, rel_flat, and out must share dtype."
+   );
+   c10::cuda::CUDAGuard guard(grad_out.device());
+   const relm_mp_dtype dt = to_dtype(grad_out, "fanin_reduce_logsumexp_backward");
+   const int64_t emb = grad_out.size(1);
+   if(flat_src.numel() == 0 || rel_rows == 0) return at::zeros({rel_rows, emb}, rel_flat.options());
+   Tensor grad_rel = at::empty({rel_rows, emb}, rel_flat.options());
+   const Tensor g = contig(grad_out);
+   const Tensor rel = contig(rel_flat);
+   const Tensor o = contig(out);
+   const Tensor src = contig(flat_src);
+   const Tensor dst = contig(dst_idx);
+   Tensor keep;
+   const int64_t bound = std::min(rel_rows, rel.size(0));
+   const relm_mp_plan plan = get_plan(src, dst, rel_rows, bound, g.size(0), "flat_src", "dst_idx", false, &keep);
+   Tensor scratch = byte_buffer(relm_mp_plan_reduce_scratch_bytes(&plan, emb, dt, RELM_MP_MODE_LOGSUMEXP_BACKWARD), g);
+   check_status(
+      relm_mp_plan_logsumexp_backward(&plan, dt, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb,
+                                      grad_rel.data_ptr(), scratch.data_ptr(), (size_t)scratch.numel(), stream_of(g)),
+      "fanin_reduce_logsumexp_backward"
+   );
+   return grad_rel;
+}
+
+// ---- Meta (shape) kernels ------------------------------------------------------
+
+Tensor fanout_scatter_meta(const Tensor& x_cat, const Tensor&, const Tensor&, int64_t out_rows)
+{
+   return at::empty({out_rows, x_cat.size(1)}, x_cat.options());
+}
+Tensor fanout_scatter_backward_meta(const Tensor& grad_out, const Tensor&, const Tensor&, int64_t x_rows)
+{
+   return at::empty({x_rows, grad_out.size(1)}, grad_out.options());
+}
+Tensor fanin_reduce_meta(const Tensor& rel_flat, const Tensor&, const Tensor&, int64_t dim_size, int64_t)
+{
+   return at::empty({dim_size, rel_flat.size(1)}, rel_flat.options());
+}
+Tensor fanin_reduce_sum_backward_meta(const Tensor& grad_out, const Tensor&, const Tensor&, int64_t rel_rows)
+{
+   return at::empty({rel_rows, grad_out.size(1)}, grad_out.options());
+}
+Tensor fanin_reduce_logsumexp_backward_meta(const Tensor& grad_out, const Tensor& rel_flat, const Tensor&,
+                                            const Tensor&, const Tensor&, int64_t rel_rows)
+{
+   return at::empty({rel_rows, grad_out.size(1)}, rel_flat.options());
+}
+
+// ---- pack ops (index arithmetic; mp_ops.cpp:412-570, 2511-2773) ------------------
+
+Tensor cat_or_single(const std::vector< Tensor >& parts)
+{
+   return parts.size() == 1 ? parts[0] : at::cat(parts, 0);
+}
+
+Tensor empty_index_like(const Tensor& ref) { return at::empty({0}, ref.options().dtype(at::kLong)); }
+
+std::tuple< Tensor, Tensor, Tensor > pack_multi(const std::vector< Tensor >& value_parts,
+                                                const std::vector< Tensor >& first_idx_parts,
+                                                const std::vector< Tensor >& second_idx_parts, const char* op,
+                                                const char* what, const char* first_name, const char* second_name)
+{
+   TORCH_CHECK(!value_parts.empty(), op, " requires at least one ", what, ".");
+   TORCH_CHECK(
+      value_parts.size() == first_idx_parts.size() && value_parts.size() == second_idx_parts.size(), op,
+      " expects matching sequence lengths."
+   );
+   std::vector< Tensor > firsts;
+   int64_t offset = 0;
+   check_rank(value_parts[0], 2, what);
+   for(size_t i = 0; i < value_parts.size(); ++i) {
+      check_rank(value_parts[i], 2, what);
+      TORCH_CHECK(
+         value_parts[i].device() == value_parts[0].device() && value_parts[i].scalar_type() == value_parts[0].scalar_type()
+            && value_parts[i].size(1) == value_parts[0].size(1),
+         op, " expects every ", what, " on one device with one dtype and embedding dim. Mismatch at part ", i, "."
+      );
+      check_int64_index(first_idx_parts[i], first_name);
+      check_int64_index(second_idx_parts[i], second_name);
+      TORCH_CHECK(
+         first_idx_parts[i].numel() == second_idx_parts[i].numel(), op, " expects ", first_name, " and ",
+         second_name, " lengths to match per part."
+      );
+      firsts.push_back(first_idx_parts[i] + offset);
+      offset += value_parts[i].size(0);
+   }
+   return {cat_or_single(value_parts), cat_or_single(firsts), cat_or_single(second_idx_parts)};
+}
+
+std::tuple< Tensor, Tensor, Tensor > fanout_pack_multi(at::TensorList x_parts, at::TensorList src_idx_parts,
+                                                       at::TensorList flat_dst_parts)
+{
+   return pack_multi(x_parts.vec(), src_idx_parts.vec(), flat_dst_parts.vec(), "fanout_pack_multi", "source tensor",
+                     "src_idx", "flat_dst");
+}
+
+std::tuple< Tensor, Tensor, Tensor > fanin_pack_multi(at::TensorList rel_parts, at::TensorList flat_src_parts,
+                                                      at::TensorList dst_idx_parts)
+{
+   return pack_multi(rel_parts.vec(), flat_src_parts.vec(), dst_idx_parts.vec(), "fanin_pack_multi",
+                     "relation tensor", "flat_src", "dst_idx");
+}
+
+std::tuple< Tensor, Tensor, Tensor > fanout_pack_from_edges(at::TensorList x_parts, at::TensorList edge_src_parts,
+                                                            at::TensorList edge_dst_parts, at::IntArrayRef src_part_ids,
+                                                            at::IntArrayRef arity_parts, at::IntArrayRef pos_parts,
+                                                            at::IntArrayRef slot_offset_parts)
+{
+   const char* op = "fanout_pack_from_edges";
+   TORCH_CHECK(!x_parts.empty(), op, " requires at least one source tensor.");
+   const size_t n = edge_src_parts.size();
+   TORCH_CHECK(
+      edge_dst_parts.size() == n && src_part_ids.size() == n && arity_parts.size() == n && pos_parts.size() == n
+         && slot_offset_parts.size() == n,
+      op, " expects matching sequence lengths."
+   );
+   std::vector< int64_t > offsets;
+   int64_t offset = 0;
+   for(const auto& x : x_parts) {
+      check_rank(x, 2, "source tensor");
+      offsets.push_back(offset);
+      offset += x.size(0);
+   }
+   std::vector< Tensor > srcs, dsts;
+   for(size_t i = 0; i < n; ++i) {
+      check_int64_index(edge_src_parts[i], "edge_src");
+      check_int64_index(edge_dst_parts[i], "edge_dst");
+      TORCH_CHECK(edge_src_parts[i].numel() == edge_dst_parts[i].numel(), op, " expects edge src/dst lengths to match.");
+      const int64_t part = src_part_ids[i];
+      TORCH_CHECK(part >= 0 && part < (int64_t)x_parts.size(), op, " src_part_ids out of range: ", part, ".");
+      const int64_t arity = arity_parts[i];
+      TORCH_CHECK(arity > 0, op, " expects arity > 0.");
+      const int64_t pos = pos_parts[i];
+      TORCH_CHECK(pos >= 0 && pos < arity, op, " expects pos in [0, arity), got pos=", pos, " arity=", arity, ".");
+      srcs.push_back(edge_src_parts[i] + offsets[part]);
+      dsts.push_back(edge_dst_parts[i] * arity + (slot_offset_parts[i] + pos));
+   }
+   const Tensor x_cat = cat_or_single(x_parts.vec());
+   if(n == 0) return {x_cat, empty_index_like(x_parts[0]), empty_index_like(x_parts[0])};
+   return {x_cat, cat_or_single(srcs), cat_or_single(dsts)};
+}
+
+std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_parts, at::TensorList edge_src_parts,
+                                                           at::TensorList edge_dst_parts, at::IntArrayRef rel_part_ids,
+                                                           at::IntArrayRef arity_parts, at::IntArrayRef pos_parts,
+                                                           int64_t mode)
+{
+   const char* op = "fanin_pack_from_edges";
+   TORCH_CHECK(!rel_parts.empty(), op, " requires at least one relation tensor.");
+   const size_t n = edge_src_parts.size();
+   TORCH_CHECK(
+      edge_dst_parts.size() == n && rel_part_ids.size() == n && arity_parts.size() == n && pos_parts.size() == n,
+      op, " expects matching sequence lengths."
+   );
+   TORCH_CHECK(mode == 0 || mode == 1, op, " expects mode in {0,1}, got ", mode, ".");
+   std::vector< int64_t > offsets;
+   int64_t offset = 0;
+   for(const auto& r : rel_parts) {
+      check_rank(r, 2, "relation tensor");
+      offsets.push_back(offset);
+      offset += r.size(0);
+   }
+   std::vector< Tensor > srcs, dsts;
+   for(size_t i = 0; i < n; ++i) {
+      check_int64_index(edge_src_parts[i], "edge_src");
+      check_int64_index(edge_dst_parts[i], "edge_dst");
+      TORCH_CHECK(edge_src_parts[i].numel() == edge_dst_parts[i].numel(), op, " expects edge src/dst lengths to match.");
+      const int64_t part = rel_part_ids[i];
+      TORCH_CHECK(part >= 0 && part < (int64_t)rel_parts.size(), op, " rel_part_ids out of range: ", part, ".");
+      Tensor local = edge_src_parts[i];
+      if(mode != 1) {
+         const int64_t arity = arity_parts[i];
+         TORCH_CHECK(arity > 0, op, " expects arity > 0.");
+         const int64_t pos = pos_parts[i];
+         TORCH_CHECK(pos >= 0 && pos < arity, op, " expects pos in [0, arity), got pos=", pos, " arity=", arity, ".");
+         local = local * arity + pos;
+      }
+      srcs.push_back(local + offsets[part]);
+      dsts.push_back(edge_dst_parts[i]);
+   }
+   const Tensor rel_cat = cat_or_single(rel_parts.vec());
+   if(n == 0) return {rel_cat, empty_index_like(rel_parts[0]), empty_index_like(rel_parts[0])};
+   return {rel_cat, cat_or_single(srcs), cat_or_single(dsts)};
+}
+
+// build_torch / build_cuda_tag describe the torch this layer was compiled
+// against (what the reference loader checks, mp_runtime.py:175-228); the
+// kernel library's own metadata follows.
+std::string build_info()
+{
+   return std::string("build_torch=") + RELM_MP_BUILD_TORCH_VERSION + ";build_cuda_tag=" + RELM_MP_BUILD_CUDA_TAG
+          + ";abi_target=" + RELM_MP_ABI_TARGET + ";abi_lane=nonstable;" + relm_mp_build_info();
+}
+
+void clear_plan_cache() { PlanCache::get().clear(); }
+std::vector< int64_t > plan_cache_stats() { return PlanCache::get().stats(); }
+void set_plan_cache_capacity(int64_t cap) { PlanCache::get().set_capacity(cap); }
+
+}  // namespace relm_b200
+
+TORCH_LIBRARY(relm_mp, m)
+{
+   m.def(
+      "fanout_pack_multi(Tensor[] x_parts, Tensor[] src_idx_parts, Tensor[] flat_dst_parts) -> (Tensor, Tensor, Tensor)"
+   );
+   m.def(
+      "fanout_pack_from_edges(Tensor[] x_parts, Tensor[] edge_src_parts, Tensor[] edge_dst_parts, int[] src_part_ids, "
+      "int[] arity_parts, int[] pos_parts, int[] slot_offset_parts) -> (Tensor, Tensor, Tensor)"
+   );
+   m.def("fanout_scatter(Tensor x_cat, Tensor src_global_idx, Tensor flat_dst, int out_rows) -> Tensor");
+   m.def("fanout_scatter_backward(Tensor grad_out, Tensor src_global_idx, Tensor flat_dst, int x_rows) -> Tensor");
+   m.def("fanin_reduce(Tensor rel_flat, Tensor flat_src, Tensor dst_idx, int dim_size, int mode) -> Tensor");
+   m.def("fanin_reduce_sum_backward(Tensor grad_out, Tensor flat_src, Tensor dst_idx, int rel_rows) -> Tensor");
+   m.def(
+      "fanin_reduce_logsumexp_backward(Tensor grad_out, Tensor rel_flat, Tensor flat_src, Tensor dst_idx, Tensor out, "
+      "int rel_rows) -> Tensor"
+   );
+   m.def(
+      "fanin_pack_multi(Tensor[] rel_parts, Tensor[] flat_src_parts, Tensor[] dst_idx_parts) -> (Tensor, Tensor, Tensor)"
+   );
+   m.def(
+      "fanin_pack_from_edges(Tensor[] rel_parts, Tensor[] edge_src_parts, Tensor[] edge_dst_parts, int[] rel_part_ids, "
+      "int[] arity_parts, int[] pos_parts, int mode) -> (Tensor, Tensor, Tensor)"
+   );
+   m.def("build_info() -> str");
+}
+
+TORCH_LIBRARY_IMPL(relm_mp, CUDA, m)
+{
+   m.impl("fanout_scatter", relm_b200::fanout_scatter_cuda);
+   m.impl("fanout_scatter_backward", relm_b200::fanout_scatter_backward_cuda);
+   m.impl("fanin_reduce", relm_b200::fanin_reduce_cuda);
+   m.impl("fanin_reduce_sum_backward", relm_b200::fanin_reduce_sum_backward_cuda);
+   m.impl("fanin_reduce_logsumexp_backward", relm_b200::fanin_reduce_logsumexp_backward_cuda);
+}
+
+TORCH_LIBRARY_IMPL(relm_mp, Meta, m)
+{
+   m.impl("fanout_scatter", relm_b200::fanout_scatter_meta);
+   m.impl("fanout_scatter_backward", relm_b200::fanout_scatter_backward_meta);
+   m.impl("fanin_reduce", relm_b200::fanin_reduce_meta);
+   m.impl("fanin_reduce_sum_backward", relm_b200::fanin_reduce_sum_backward_meta);
+   m.impl("fanin_reduce_logsumexp_backward", relm_b200::fanin_reduce_logsumexp_backward_meta);
+}
+
+TORCH_LIBRARY_IMPL(relm_mp, CompositeImplicitAutograd, m)
+{
+   m.impl("fanout_pack_multi", relm_b200::fanout_pack_multi);
+   m.impl("fanout_pack_from_edges", relm_b200::fanout_pack_from_edges);
+   m.impl("fanin_pack_multi", relm_b200::fanin_pack_multi);
+   m.impl("fanin_pack_from_edges", relm_b200::fanin_pack_from_edges);
+   m.impl("build_info", relm_b200::build_info);
+}
+
+// Plan-cache control, outside the reference namespace.
+TORCH_LIBRARY(relm_mp_b200, m)
+{
+   m.def("clear_plan_cache() -> ()", relm_b200::clear_plan_cache);
+   m.def("plan_cache_stats() -> int[]", relm_b200::plan_cache_stats);
+   m.def("set_plan_cache_capacity(int capacity) -> ()", relm_b200::set_plan_cache_capacity);
+}

@@ -1,0 +1,139 @@
+"""Public facade of the relational message-passing ops (mirrors ``relmo.ops.mp``).
+
+Same functions, arguments and return values as relmo's ``src/relmo/ops/mp.py``
+for the fan-out / fan-in path (``fanout_scatter`` 43-52, ``fanin_reduce`` 55-70,
+the four pack helpers, ``available``, ``assert_runtime_compat``, ``__all__``
+528-544):
+
+- CUDA tensors run the B200 kernels through ``torch.ops.relm_mp`` with the
+  reference's autograd wrappers. There is no GPU fallback: if the library is
+  missing or disabled the call raises.
+- CPU tensors, and fanin modes other than sum/logsumexp, use the reference's
+  ATen formulas (``mp_pack``), as relmo's Python fallback does.
+
+The fused block/program and LGAN ops of relmo are a different model family and
+are not part of this package.
+"""
+
+from __future__ import annotations
+
+from .mp_autograd import _FaninReduceLogSumExpFunction, _FaninReduceSumFunction, _FanoutScatterFunction
+from .mp_constants import MODE_LOGSUMEXP, MODE_MEAN, MODE_SUM
+from .mp_dispatch import dispatch_namespace_op, is_cuda, require_gpu_custom
+from .mp_pack import (
+    fanin_pack_from_edges_python,
+    fanin_pack_multi_python,
+    fanin_reduce_python,
+    fanout_pack_from_edges_python,
+    fanout_pack_multi_python,
+    fanout_scatter_python,
+)
+from .mp_runtime import TORCH_IMPORT_ERROR, assert_runtime_compat, available, ops_namespace, require_torch, torch
+
+
+def fanout_scatter(x_cat, src_global_idx, flat_dst, out_rows: int):
+    """``out = zeros(out_rows, D); out[flat_dst[e]] = x_cat[src_global_idx[e]]``."""
+
+    require_torch("fanout_scatter")
+    if is_cuda(x_cat):
+        require_gpu_custom("fanout_scatter")
+        return _FanoutScatterFunction.apply(x_cat, src_global_idx, flat_dst, int(out_rows))
+    return fanout_scatter_python(x_cat, src_global_idx, flat_dst, int(out_rows))
+
+
+def fanin_reduce(rel_flat, flat_src, dst_idx, dim_size: int, mode: int):
+    """Reduce ``rel_flat[flat_src[e]]`` into row ``dst_idx[e]``: mode 0 sum,
+    mode 1 logsumexp (-inf for rows without messages)."""
+
+    require_torch("fanin_reduce")
+    mode_int = int(mode)
+    if mode_int not in (MODE_SUM, MODE_LOGSUMEXP):
+        return fanin_reduce_python(rel_flat, flat_src, dst_idx, int(dim_size), mode_int)
+    if is_cuda(rel_flat):
+        require_gpu_custom("fanin_reduce")
+        if mode_int == MODE_SUM:
+            return _FaninReduceSumFunction.apply(rel_flat, flat_src, dst_idx, int(dim_size))
+        return _FaninReduceLogSumExpFunction.apply(rel_flat, flat_src, dst_idx, int(dim_size))
+    return fanin_reduce_python(rel_flat, flat_src, dst_idx, int(dim_size), mode_int)
+
+
+def fanout_pack_multi(x_parts, src_idx_parts, flat_dst_parts):
+    require_torch("fanout_pack_multi")
+    return dispatch_namespace_op(
+        "fanout_pack_multi", x_parts, src_idx_parts, flat_dst_parts, fallback=fanout_pack_multi_python
+    )
+
+
+def fanin_pack_multi(rel_parts, flat_src_parts, dst_idx_parts):
+    require_torch("fanin_pack_multi")
+    return dispatch_namespace_op(
+        "fanin_pack_multi", rel_parts, flat_src_parts, dst_idx_parts, fallback=fanin_pack_multi_python
+    )
+
+
+def fanout_pack_from_edges(x_parts, edge_src_parts, edge_dst_parts, src_part_ids, arity_parts, pos_parts, slot_offset_parts):
+    require_torch("fanout_pack_from_edges")
+    return dispatch_namespace_op(
+        "fanout_pack_from_edges",
+        x_parts,
+        edge_src_parts,
+        edge_dst_parts,
+        [int(v) for v in src_part_ids],
+        [int(v) for v in arity_parts],
+        [int(v) for v in pos_parts],
+        [int(v) for v in slot_offset_parts],
+        fallback=fanout_pack_from_edges_python,
+    )
+
+
+def fanin_pack_from_edges(rel_parts, edge_src_parts, edge_dst_parts, rel_part_ids, arity_parts, pos_parts, mode: int):
+    require_torch("fanin_pack_from_edges")
+    return dispatch_namespace_op(
+        "fanin_pack_from_edges",
+        rel_parts,
+        edge_src_parts,
+        edge_dst_parts,
+        [int(v) for v in rel_part_ids],
+        [int(v) for v in arity_parts],
+        [int(v) for v in pos_parts],
+        int(mode),
+        fallback=fanin_pack_from_edges_python,
+    )
+
+
+def clear_plan_cache() -> None:
+    """Drop every cached index plan (they are rebuilt on the next call)."""
+
+    require_gpu_custom("clear_plan_cache")
+    torch.ops.relm_mp_b200.clear_plan_cache()
+
+
+def plan_cache_stats() -> dict[str, int]:
+    """Entries, hits, builds, bytes and capacity of the index-plan cache."""
+
+    require_gpu_custom("plan_cache_stats")
+    entries, hits, builds, nbytes, capacity = torch.ops.relm_mp_b200.plan_cache_stats()
+    return {"entries": entries, "hits": hits, "builds": builds, "bytes": nbytes, "capacity": capacity}
+
+
+def set_plan_cache_capacity(capacity: int) -> None:
+    require_gpu_custom("set_plan_cache_capacity")
+    torch.ops.relm_mp_b200.set_plan_cache_capacity(int(capacity))
+
+
+__all__ = [
+    "fanout_scatter",
+    "fanin_reduce",
+    "fanout_pack_multi",
+    "fanin_pack_multi",
+    "fanout_pack_from_edges",
+    "fanin_pack_from_edges",
+    "available",
+    "assert_runtime_compat",
+    "clear_plan_cache",
+    "plan_cache_stats",
+    "set_plan_cache_capacity",
+    "MODE_SUM",
+    "MODE_LOGSUMEXP",
+    "MODE_MEAN",
+]

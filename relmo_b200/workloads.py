@@ -1,0 +1,194 @@
+"""Seeded synthetic workloads for the fan-out / fan-in path.
+
+The reference publishes no dataset for these ops; its op benchmark
+(``scripts/benchmark_mp_ops.py:203-258``) draws seeded random inputs. These
+generators produce the shapes and value distributions of the five benchmark
+configurations:
+
+* ``cfg1`` - parity micro-workload: N=2000 nodes, D=32, E=20000 messages.
+* ``cfg2`` - large op benchmark: N=2**20, E=2**24, D=64, truncated Zipf(1.3)
+  destinations, sorted or unsorted.
+* ``cfg5`` - skewed stress test: N=2**22, E=2**26, D=32, 64 hub destinations
+  with 100k messages each, the rest uniform.
+
+Everything is drawn from one ``torch.Generator`` per call in a fixed order, so a
+seed fully determines a workload on a given device type.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+
+@dataclass
+class FanWorkload:
+    """Inputs of one fan-out + fan-in pass.
+
+    Fan-out: ``x[x_rows, D]`` gathered by ``src`` into ``out_rows`` slot rows at
+    ``flat_dst``. Fan-in: ``msgs[E, D]`` rows ``flat_src`` reduced into
+    ``dim_size`` destination rows ``dst``. ``grad_slots`` / ``grad_nodes`` are
+    upstream gradients for the backward ops.
+    """
+
+    name: str
+    x: torch.Tensor
+    src: torch.Tensor
+    flat_dst: torch.Tensor
+    out_rows: int
+    msgs: torch.Tensor
+    flat_src: torch.Tensor
+    dst: torch.Tensor
+    dim_size: int
+    grad_slots: torch.Tensor
+    grad_nodes: torch.Tensor
+
+    @property
+    def num_edges(self) -> int:
+        return int(self.src.numel())
+
+    @property
+    def emb(self) -> int:
+        return int(self.x.size(1))
+
+    def to(self, device, dtype: torch.dtype | None = None) -> "FanWorkload":
+        def v(t: torch.Tensor) -> torch.Tensor:
+            return t.to(device=device, dtype=dtype) if dtype is not None else t.to(device)
+
+        return FanWorkload(
+            self.name, v(self.x), self.src.to(device), self.flat_dst.to(device), self.out_rows,
+            v(self.msgs), self.flat_src.to(device), self.dst.to(device), self.dim_size,
+            v(self.grad_slots), v(self.grad_nodes),
+        )
+
+
+def _gen(device, seed: int) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(int(seed))
+    return g
+
+
+def cfg1(seed: int = 0, device="cpu", n: int = 2000, emb: int = 32, edges: int = 20000) -> FanWorkload:
+    """Parity micro-workload. Draw order: X=randn(N,D); src=randint(N,(E,));
+    dst=randint(N,(E,)); msgs=randn(E,D)*sqrt(2); flat_dst=randperm(E);
+    grad_slots=randn(E,D); grad_nodes=randn(N,D). flat_src=arange(E)."""
+
+    g = _gen(device, seed)
+    kw = dict(device=device, generator=g)
+    x = torch.randn(n, emb, dtype=torch.float32, **kw)
+    src = torch.randint(0, n, (edges,), dtype=torch.int64, **kw)
+    dst = torch.randint(0, n, (edges,), dtype=torch.int64, **kw)
+    msgs = torch.randn(edges, emb, dtype=torch.float32, **kw) * math.sqrt(2.0)
+    flat_dst = torch.randperm(edges, dtype=torch.int64, **kw)
+    grad_slots = torch.randn(edges, emb, dtype=torch.float32, **kw)
+    grad_nodes = torch.randn(n, emb, dtype=torch.float32, **kw)
+    flat_src = torch.arange(edges, dtype=torch.int64, device=device)
+    return FanWorkload("cfg1", x, src, flat_dst, edges, msgs, flat_src, dst, n, grad_slots, grad_nodes)
+
+
+def zipf_destinations(n: int, edges: int, alpha: float, g: torch.Generator, device) -> torch.Tensor:
+    """Truncated Zipf(alpha) node ids: rank k in [1, n] with P(k) ~ k**-alpha,
+    sampled with replacement, mapped to node ids through a random permutation."""
+
+    ranks = torch.arange(1, n + 1, dtype=torch.float64, device=device)
+    weights = ranks.pow(-float(alpha)).to(torch.float32)
+    out = torch.empty(edges, dtype=torch.int64, device=device)
+    chunk = 1 << 22  # torch.multinomial caps the sample count per call
+    for start in range(0, edges, chunk):
+        stop = min(edges, start + chunk)
+        out[start:stop] = torch.multinomial(weights, stop - start, replacement=True, generator=g)
+    node_of_rank = torch.randperm(n, dtype=torch.int64, device=device, generator=g)
+    return node_of_rank[out]
+
+
+def cfg2(
+    seed: int = 0,
+    device="cpu",
+    sorted_dst: bool = False,
+    dtype: torch.dtype = torch.float32,
+    n: int = 1 << 20,
+    edges: int = 1 << 24,
+    emb: int = 64,
+    alpha: float = 1.3,
+) -> FanWorkload:
+    """Large op benchmark: uniform ``src``, Zipf(1.3) ``dst``, values ~N(0,1).
+
+    ``sorted_dst`` stable-sorts the fan-in edges by destination and permutes the
+    message rows with them (``flat_src`` stays ``arange``) so segments are
+    contiguous; the fan-out slots become ``arange`` (in-order slots). bf16 data
+    is generated in float32 and cast.
+    """
+
+    g = _gen(device, seed)
+    kw = dict(device=device, generator=g)
+    x = torch.randn(n, emb, dtype=torch.float32, **kw)
+    src = torch.randint(0, n, (edges,), dtype=torch.int64, **kw)
+    dst = zipf_destinations(n, edges, alpha, g, device)
+    msgs = torch.randn(edges, emb, dtype=torch.float32, **kw)
+    flat_dst = torch.randperm(edges, dtype=torch.int64, **kw)
+    grad_slots = torch.randn(edges, emb, dtype=torch.float32, **kw)
+    grad_nodes = torch.randn(n, emb, dtype=torch.float32, **kw)
+    flat_src = torch.arange(edges, dtype=torch.int64, device=device)
+    if sorted_dst:
+        dst, perm = torch.sort(dst, stable=True)
+        msgs = msgs[perm]
+        flat_dst = torch.arange(edges, dtype=torch.int64, device=device)
+    wl = FanWorkload(
+        "cfg2-sorted" if sorted_dst else "cfg2-unsorted",
+        x, src, flat_dst, edges, msgs, flat_src, dst, n, grad_slots, grad_nodes,
+    )
+    return wl.to(device, dtype) if dtype != torch.float32 else wl
+
+
+def cfg5(
+    seed: int = 0,
+    device="cpu",
+    n: int = 1 << 22,
+    edges: int = 1 << 26,
+    emb: int = 32,
+    hubs: int = 64,
+    per_hub: int = 100_000,
+) -> FanWorkload:
+    """Skewed-degree stress test: 64 hub nodes (seeded ``randperm``) receive
+    100 000 messages each, the remaining messages pick uniform destinations;
+    the destination order is shuffled. Messages ~N(0, 4)."""
+
+    g = _gen(device, seed)
+    kw = dict(device=device, generator=g)
+    x = torch.randn(n, emb, dtype=torch.float32, **kw)
+    src = torch.randint(0, n, (edges,), dtype=torch.int64, **kw)
+    hub_ids = torch.randperm(n, dtype=torch.int64, **kw)[:hubs]
+    rest = edges - hubs * per_hub
+    dst = torch.cat([hub_ids.repeat_interleave(per_hub), torch.randint(0, n, (rest,), dtype=torch.int64, **kw)])
+    dst = dst[torch.randperm(edges, dtype=torch.int64, **kw)]
+    msgs = torch.randn(edges, emb, dtype=torch.float32, **kw) * 2.0
+    flat_dst = torch.randperm(edges, dtype=torch.int64, **kw)
+    grad_slots = torch.randn(edges, emb, dtype=torch.float32, **kw)
+    grad_nodes = torch.randn(n, emb, dtype=torch.float32, **kw)
+    flat_src = torch.arange(edges, dtype=torch.int64, device=device)
+    return FanWorkload("cfg5", x, src, flat_dst, edges, msgs, flat_src, dst, n, grad_slots, grad_nodes)
+
+
+def algorithmic_bytes(op: str, wl: FanWorkload, elem_bytes: int | None = None) -> int:
+    """Compulsory HBM traffic of one op call: each referenced input row read
+    once, every int64 index read once, each output row written once. Sort or
+    CSR-build traffic is not counted."""
+
+    s = elem_bytes if elem_bytes is not None else wl.x.element_size()
+    d = wl.emb
+    e = wl.num_edges
+    if op == "fanout_fwd":
+        ux = int(torch.unique(wl.src).numel())
+        return ux * d * s + 16 * e + wl.out_rows * d * s
+    if op == "fanout_bwd":
+        return e * d * s + 16 * e + int(wl.x.size(0)) * d * s
+    if op in ("fanin_sum_fwd", "fanin_lse_fwd"):
+        return e * d * s + 16 * e + wl.dim_size * d * s
+    ud = int(torch.unique(wl.dst).numel())
+    if op == "fanin_sum_bwd":
+        return ud * d * s + 16 * e + e * d * s
+    if op == "fanin_lse_bwd":
+        return 2 * e * d * s + 2 * ud * d * s + 16 * e
+    raise ValueError(op)

@@ -1,0 +1,205 @@
+"""Generate golden vectors from the reference's own CPU op library.
+
+Run in a process of its own (the reference library registers the ``relm_mp``
+torch namespace, the same one ``relmo_b200`` registers):
+
+    python oracle/build_ref.py          # builds oracle/_ref/relm_mp_ref.so
+    python tests/golden/make_golden.py  # writes tests/golden/*.npz
+
+Inputs come from the reference's own test fixtures
+(``tests/python/test_mp_ops.py:171-347`` of maichmueller/relmo: the literal index
+vectors, with seeded values instead of unseeded ``randn``), a set of edge cases
+(empty inputs, zero rows, duplicate slots, non-finite values, out-of-range
+indices) and the cfg1 parity workload. Outputs are what
+``torch.ops.relm_mp.*`` of the reference returns on CPU.
+
+Files:
+* ``ref_cases.npz`` - small cases, inputs and outputs stored in full.
+* ``ref_cfg1.npz`` - cfg1 (N=2000, D=32, E=20000, seed 0). Inputs are regenerated
+  from the seed and pinned by SHA-256; outputs stored in full when they are
+  [N, D], by SHA-256 when bit-exact [E, D], and by a row sample plus float64
+  checksums for the [E, D] logsumexp gradient.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+sys.path.insert(0, str(ROOT))
+
+from relmo_b200 import workloads  # noqa: E402  (pure-python module, loads no library)
+
+REF_LIB = ROOT / "oracle" / "_ref" / "relm_mp_ref.so"
+
+
+def sha(t: torch.Tensor) -> str:
+    return hashlib.sha256(t.detach().contiguous().cpu().numpy().tobytes()).hexdigest()
+
+
+def load_reference():
+    if not REF_LIB.is_file():
+        raise SystemExit(f"{REF_LIB} missing: run python oracle/build_ref.py first")
+    torch.ops.load_library(str(REF_LIB))
+    return torch.ops.relm_mp
+
+
+def small_cases():
+    """(name, op, args) with the reference test fixtures and edge cases."""
+
+    g = torch.Generator().manual_seed(1234)
+
+    def randn(*shape, dtype=torch.float32):
+        return torch.randn(*shape, generator=g, dtype=torch.float64).to(dtype)
+
+    def idx(*v):
+        return torch.tensor(v, dtype=torch.int64)
+
+    cases = []
+    # test_mp_ops.py:171-188 (python fallback fixture)
+    cases.append(("fallback_fanout", "fanout_scatter", [randn(6, 3), idx(0, 4, 1), idx(3, 0, 1), 5]))
+    for mode in (0, 1):
+        cases.append((f"fallback_fanin_m{mode}", "fanin_reduce",
+                      [randn(8, 3), idx(0, 2, 4, 1), idx(2, 0, 1, 0), 4, mode]))
+    # test_mp_ops.py:191-207
+    cases.append(("parity_fanout", "fanout_scatter", [randn(7, 5), idx(0, 3, 5, 2, 3), idx(4, 1, 0, 2, 3), 6]))
+    # test_mp_ops.py:210-230: grad of out.sum() -> grad_out = ones
+    cases.append(("grad_fanout_bwd", "fanout_scatter_backward",
+                  [torch.ones(5, 4), idx(0, 5, 2, 6), idx(1, 0, 3, 2), 8]))
+    # test_mp_ops.py:233-252 (empty destination row 3)
+    for mode in (0, 1):
+        cases.append((f"parity_fanin_m{mode}", "fanin_reduce",
+                      [randn(10, 4), idx(0, 2, 7, 5, 2, 1), idx(1, 0, 2, 2, 1, 0), 4, mode]))
+    # test_mp_ops.py:255-281 (dim_size 5 with two empty rows) forward and backward
+    rel = randn(12, 3)
+    fs, di = idx(0, 1, 8, 4, 9, 10), idx(2, 0, 1, 1, 0, 2)
+    cases.append(("grad_fanin_m0_fwd", "fanin_reduce", [rel, fs, di, 5, 0]))
+    cases.append(("grad_fanin_m0_bwd", "fanin_reduce_sum_backward", [torch.ones(5, 3), fs, di, 12]))
+    cases.append(("grad_fanin_m1_fwd", "fanin_reduce", [rel, fs, di, 5, 1]))
+    cases.append(("grad_fanin_m1_bwd", "fanin_reduce_logsumexp_backward",
+                  [torch.ones(5, 3), rel, fs, di, "@grad_fanin_m1_fwd", 12]))
+    # test_mp_ops.py:302-347 gradcheck fixtures, in float64, with random upstream grads
+    cases.append(("f64_fanout", "fanout_scatter", [randn(6, 3, dtype=torch.float64), idx(0, 5, 2, 1), idx(1, 0, 3, 2), 5]))
+    cases.append(("f64_fanout_bwd", "fanout_scatter_backward",
+                  [randn(5, 3, dtype=torch.float64), idx(0, 5, 2, 1), idx(1, 0, 3, 2), 6]))
+    rel64 = randn(8, 4, dtype=torch.float64)
+    cases.append(("f64_sum", "fanin_reduce", [rel64, idx(0, 2, 5, 7, 1), idx(1, 0, 3, 2, 0), 5, 0]))
+    cases.append(("f64_sum_bwd", "fanin_reduce_sum_backward",
+                  [randn(5, 4, dtype=torch.float64), idx(0, 2, 5, 7, 1), idx(1, 0, 3, 2, 0), 8]))
+    fs6, di6 = idx(0, 2, 5, 7, 1, 3), idx(1, 0, 3, 2, 0, 1)
+    cases.append(("f64_lse", "fanin_reduce", [rel64, fs6, di6, 4, 1]))
+    cases.append(("f64_lse_bwd", "fanin_reduce_logsumexp_backward",
+                  [randn(4, 4, dtype=torch.float64), rel64, fs6, di6, "@f64_lse", 8]))
+    # edge cases
+    e0 = torch.empty(0, dtype=torch.int64)
+    cases.append(("empty_edges_fanout", "fanout_scatter", [randn(4, 3), e0, e0, 3]))
+    cases.append(("empty_edges_sum", "fanin_reduce", [randn(4, 3), e0, e0, 3, 0]))
+    cases.append(("empty_edges_lse", "fanin_reduce", [randn(4, 3), e0, e0, 3, 1]))
+    cases.append(("zero_rows_fanout", "fanout_scatter", [randn(4, 3), idx(1, 2), idx(0, 1), 0]))
+    cases.append(("zero_dim_lse", "fanin_reduce", [randn(4, 3), idx(1, 2), idx(0, 1), 0, 1]))
+    cases.append(("dup_slots_fanout", "fanout_scatter",
+                  [randn(6, 4), idx(0, 1, 2, 3, 4, 5), idx(2, 0, 2, 1, 2, 0), 4]))
+    cases.append(("dup_src_sum_bwd", "fanin_reduce_sum_backward",
+                  [randn(3, 4), idx(1, 1, 0, 1, 3), idx(0, 2, 1, 1, 2), 5]))
+    nf = randn(5, 3)
+    nf[1, 0] = float("nan")
+    nf[2, 1] = float("inf")
+    nf[3, 2] = float("-inf")
+    nf[4, :] = float("-inf")
+    cases.append(("nonfinite_lse", "fanin_reduce", [nf, idx(0, 1, 2, 3, 4, 4), idx(0, 0, 1, 1, 2, 3), 4, 1]))
+    cases.append(("nonfinite_sum", "fanin_reduce", [nf, idx(0, 1, 2, 3, 4, 4), idx(0, 0, 1, 1, 2, 3), 4, 0]))
+    cases.append(("wide_emb_sum", "fanin_reduce",
+                  [randn(40, 300), torch.randint(0, 40, (90,), generator=g), torch.randint(0, 17, (90,), generator=g), 17, 0]))
+    cases.append(("wide_emb_lse", "fanin_reduce",
+                  [randn(40, 300), torch.randint(0, 40, (90,), generator=g), torch.randint(0, 17, (90,), generator=g), 17, 1]))
+    # out-of-range indices: the reference CPU op raises
+    cases.append(("oob_fanout_src", "fanout_scatter", [randn(4, 3), idx(0, 4), idx(0, 1), 3]))
+    cases.append(("oob_fanout_dst", "fanout_scatter", [randn(4, 3), idx(0, 1), idx(0, 3), 3]))
+    cases.append(("oob_fanout_neg", "fanout_scatter", [randn(4, 3), idx(-1, 1), idx(0, 1), 3]))
+    cases.append(("oob_sum_dst", "fanin_reduce", [randn(4, 3), idx(0, 1), idx(0, 5), 3, 0]))
+    cases.append(("oob_sum_src", "fanin_reduce", [randn(4, 3), idx(0, 9), idx(0, 1), 3, 0]))
+    cases.append(("oob_lse_dst", "fanin_reduce", [randn(4, 3), idx(0, 1), idx(0, 5), 3, 1]))
+    cases.append(("oob_fanout_bwd_src", "fanout_scatter_backward", [randn(3, 3), idx(0, 7), idx(0, 1), 4]))
+    cases.append(("oob_sum_bwd_dst", "fanin_reduce_sum_backward", [randn(3, 3), idx(0, 1), idx(0, 3), 4]))
+    return cases
+
+
+def run_small(ops) -> dict[str, np.ndarray]:
+    arrays: dict[str, np.ndarray] = {}
+    meta: dict[str, dict] = {}
+    results: dict[str, torch.Tensor] = {}
+    for name, op, args in small_cases():
+        call_args = [results[a[1:]] if isinstance(a, str) and a.startswith("@") else a for a in args]
+        entry = {"op": op, "args": []}
+        for i, a in enumerate(call_args):
+            if isinstance(a, torch.Tensor):
+                key = f"{name}__arg{i}"
+                arrays[key] = a.numpy()
+                entry["args"].append({"tensor": key})
+            else:
+                entry["args"].append({"int": int(a)})
+        try:
+            out = getattr(ops, op)(*call_args)
+            results[name] = out
+            arrays[f"{name}__out"] = out.numpy()
+            entry["raises"] = None
+        except Exception as exc:  # the reference raises for out-of-range indices
+            entry["raises"] = type(exc).__name__
+            entry["message"] = str(exc).splitlines()[0]
+        meta[name] = entry
+    arrays["__meta__"] = np.frombuffer(json.dumps(meta, sort_keys=True).encode(), dtype=np.uint8)
+    return arrays
+
+
+def run_cfg1(ops) -> dict[str, np.ndarray]:
+    wl = workloads.cfg1(seed=0)
+    arrays: dict[str, np.ndarray] = {}
+    inputs = {
+        "x": wl.x, "src": wl.src, "dst": wl.dst, "msgs": wl.msgs, "flat_dst": wl.flat_dst,
+        "grad_slots": wl.grad_slots, "grad_nodes": wl.grad_nodes,
+    }
+    meta = {"input_sha256": {k: sha(v) for k, v in inputs.items()}}
+    fan = ops.fanout_scatter(wl.x, wl.src, wl.flat_dst, wl.out_rows)
+    fan_bwd = ops.fanout_scatter_backward(wl.grad_slots, wl.src, wl.flat_dst, wl.x.size(0))
+    fsum = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 0)
+    flse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+    sum_bwd = ops.fanin_reduce_sum_backward(wl.grad_nodes, wl.flat_src, wl.dst, wl.msgs.size(0))
+    lse_bwd = ops.fanin_reduce_logsumexp_backward(
+        wl.grad_nodes, wl.msgs, wl.flat_src, wl.dst, flse, wl.msgs.size(0)
+    )
+    meta["out_sha256"] = {"fanout_fwd": sha(fan), "fanin_sum_bwd": sha(sum_bwd)}
+    arrays["fanout_bwd"] = fan_bwd.numpy()
+    arrays["fanin_sum_fwd"] = fsum.numpy()
+    arrays["fanin_lse_fwd"] = flse.numpy()
+    rows = np.arange(0, lse_bwd.size(0), 10)
+    arrays["fanin_lse_bwd_rows"] = rows
+    arrays["fanin_lse_bwd_sample"] = lse_bwd.numpy()[rows]
+    d = lse_bwd.double()
+    meta["fanin_lse_bwd_checksum"] = {"sum": float(d.sum()), "sumsq": float((d * d).sum())}
+    arrays["__meta__"] = np.frombuffer(json.dumps(meta, sort_keys=True).encode(), dtype=np.uint8)
+    return arrays
+
+
+def main() -> int:
+    torch.set_num_threads(1)
+    ops = load_reference()
+    info = ops.build_info()
+    small = run_small(ops)
+    small["__build_info__"] = np.frombuffer(info.encode(), dtype=np.uint8)
+    np.savez_compressed(HERE / "ref_cases.npz", **small)
+    cfg = run_cfg1(ops)
+    cfg["__build_info__"] = np.frombuffer(info.encode(), dtype=np.uint8)
+    np.savez_compressed(HERE / "ref_cfg1.npz", **cfg)
+    print("wrote", HERE / "ref_cases.npz", HERE / "ref_cfg1.npz", "from", info)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
