@@ -143,13 +143,18 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_workload(name: str, seed: int, device, dtype: torch.dtype) -> workloads.FanWorkload:
+def make_workload(name: str, seed: int, device, dtype: torch.dtype, nodes=None, edges=None) -> workloads.FanWorkload:
+    size = {}
+    if nodes is not None:
+        size["n"] = int(nodes)
+    if edges is not None:
+        size["edges"] = int(edges)
     if name == "cfg2-unsorted":
-        return workloads.cfg2(seed=seed, device=device, sorted_dst=False, dtype=dtype)
+        return workloads.cfg2(seed=seed, device=device, sorted_dst=False, dtype=dtype, **size)
     if name == "cfg2-sorted":
-        return workloads.cfg2(seed=seed, device=device, sorted_dst=True, dtype=dtype)
+        return workloads.cfg2(seed=seed, device=device, sorted_dst=True, dtype=dtype, **size)
     if name == "cfg5":
-        return workloads.cfg5(seed=seed, device=device).to(device, dtype)
+        return workloads.cfg5(seed=seed, device=device, **size).to(device, dtype)
     if name == "cfg1":
         return workloads.cfg1(seed=seed, device=device).to(device, dtype)
     raise ValueError(name)
@@ -289,6 +294,10 @@ def main() -> int:
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--e2e-steps", type=int, default=2)
     parser.add_argument("--ops-only", action="store_true", help="per-op kernel timing only (profiling runs)")
+    parser.add_argument("--ops", default=",".join(OPS), help="ops timed by --ops-only (comma list)")
+    parser.add_argument("--reps", type=int, default=5, help="timed repetitions per op in the per-op timing")
+    parser.add_argument("--nodes", type=int, default=None, help="override the workload's node count (profiling)")
+    parser.add_argument("--edges", type=int, default=None, help="override the workload's edge count (profiling)")
     args = parser.parse_args()
 
     if args.impl == "reference":
@@ -313,7 +322,7 @@ def main() -> int:
     assert mp.available(), "relm_mp library not loadable"
     ops = torch.ops.relm_mp
     dtype = torch.float32 if args.dtype == "float32" else torch.bfloat16
-    wl = make_workload(args.workload, seed=rank, device=device, dtype=dtype)
+    wl = make_workload(args.workload, seed=rank, device=device, dtype=dtype, nodes=args.nodes, edges=args.edges)
     nbytes = op_bytes(wl)
     step_bytes = sum(nbytes.values())
     torch.cuda.synchronize()
@@ -342,10 +351,11 @@ def main() -> int:
     lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
     per_op = {}
     stream = torch.cuda.current_stream()
-    for op in OPS:
+    timed_ops = OPS if not args.ops_only else tuple(o for o in args.ops.split(",") if o)
+    for op in timed_ops:
         for _ in range(2):
             run_one_op(ops, wl, op, lse)
-        reps = 5
+        reps = args.reps
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
         ev0.record(stream)

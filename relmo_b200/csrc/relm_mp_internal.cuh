@@ -12,8 +12,14 @@
 
 namespace relm_mp {
 
-// Items (output rows + edges) per merge-path tile. One warp owns one tile.
-constexpr int kTileItems = 256;
+// Merge-path tiles: one warp owns one tile of `items` (output rows + edges).
+// The tile size is chosen from the problem size alone, aiming at about
+// kTargetTiles tiles (4 resident waves of 32 warps on each of the B200's 148
+// SMs), within [kMinTileItems, kMaxTileItems].
+constexpr int64_t kTargetTiles = 148 * 128;
+constexpr int kMinTileItems = 128;
+constexpr int kMaxTileItems = 4096;
+int plan_tile_items(int64_t num_edges, int64_t num_rows);
 // Tiles with a head partial whose row spans more than this many tiles are
 // combined by the block-wide long-row fixup instead of a single warp.
 constexpr int kLongRowTiles = 64;

@@ -44,44 +44,45 @@ bool aligned(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes
 struct Shape {
    int vb;
    int chmax;
-   int lpr;
+   int lanes;
    int ch;
    int col_blocks;
    int64_t block_cols;
 };
 
-// Widest per-lane vector that divides the row and every pointer's alignment,
-// then lanes per row and chunks per lane.
+// One warp load moves one row: the narrowest vector width that still covers the
+// row with <= 32 lanes, among the widths that divide the row size and every
+// pointer's alignment. Rows wider than 32 x 16 bytes take several chunks per
+// lane (the 16-byte or scalar width) and, past 4 chunks, several column blocks.
 Shape choose_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
 {
    Shape s{};
    const int64_t row_bytes = emb * es;
-   int vb = 16;
-   while(vb > es) {
-      bool ok = row_bytes % vb == 0;
-      for(int i = 0; ok && i < nptrs; ++i) ok = ptrs[i] == nullptr || aligned(ptrs[i], vb);
-      if(ok) break;
-      vb >>= 1;
+   auto valid = [&](int vb) {
+      if(vb < es || row_bytes % vb != 0) return false;
+      for(int i = 0; i < nptrs; ++i)
+         if(ptrs[i] != nullptr && !aligned(ptrs[i], vb)) return false;
+      return true;
+   };
+   int vb = 0;
+   for(int w = es; w <= 16; w <<= 1) {
+      if(valid(w) && row_bytes / w <= 32) {
+         vb = w;
+         break;
+      }
    }
-   if(vb < es) vb = es;
-   int64_t nvec = row_bytes / vb;
-   if(nvec > 32 && vb != 16 && vb != es) {
-      // intermediate widths only come with one chunk per lane
-      vb = es;
-      nvec = row_bytes / vb;
-   }
+   if(vb == 0) vb = valid(16) ? 16 : es;  // wide row: several chunks per lane
    s.vb = vb;
    const int vn = vb / es;
+   const int64_t nvec = row_bytes / vb;
    if(nvec <= 32) {
-      int lpr = 1;
-      while(lpr < nvec) lpr <<= 1;
-      s.lpr = lpr < 1 ? 1 : lpr;
+      s.lanes = (int)(nvec < 1 ? 1 : nvec);
       s.chmax = 1;
       s.ch = 1;
-      s.block_cols = (int64_t)s.lpr * vn;
+      s.block_cols = (int64_t)32 * vn;
       s.col_blocks = 1;
    } else {
-      s.lpr = 32;
+      s.lanes = 32;
       s.chmax = 4;
       const int64_t need = (nvec + 31) / 32;
       s.ch = need < 4 ? (int)need : 4;
@@ -104,9 +105,11 @@ struct ReduceScratch {
    size_t bytes;
 };
 
+// A long row spans more than kLongRowTiles tiles and neighbouring long rows
+// share at most one tile, so there are at most num_tiles / kLongRowTiles + 1.
 int64_t max_long_rows(int64_t num_tiles)
 {
-   return num_tiles / (kLongRowTiles + 1) + 1;
+   return num_tiles / kLongRowTiles + 1;
 }
 
 ReduceScratch reduce_layout(void* mem, int64_t num_tiles, int64_t emb, int acc_bytes, int mode)
@@ -143,8 +146,10 @@ SegParams base_params(const relm_mp_plan* plan, int64_t emb, const Shape& s)
    p.tile_edge = plan->tile_edge;
    p.num_tiles = plan->num_tiles;
    p.num_rows = plan->num_rows;
+   p.num_edges = plan->num_edges;
+   p.tile_items = plan->tile_items;
    p.emb = emb;
-   p.lpr = s.lpr;
+   p.lanes = s.lanes;
    p.ch = s.ch;
    p.col_blocks = s.col_blocks;
    p.block_cols = s.block_cols;

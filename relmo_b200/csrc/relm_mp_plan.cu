@@ -63,8 +63,10 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       gat32[e] = (int32_t)g;
       if(e + 1 < n) descent = key[e + 1] < k;
    }
-   const unsigned any = __ballot_sync(0xffffffffu, descent);
-   if(any && (threadIdx.x & 31) == 0) atomicAdd(&st->descents, 1u);
+   // One flag write per block at most, and none once the flag is set: a single
+   // counter hit by every warp of an unsorted index serialises at L2.
+   if(__syncthreads_or(descent) && threadIdx.x == 0 && *((volatile unsigned*)&st->descents) == 0u)
+      atomicExch(&st->descents, 1u);
 }
 
 // mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys).
@@ -192,9 +194,20 @@ unsigned grid_for(int64_t n, int threads = kThreads)
 
 }  // namespace
 
+int plan_tile_items(int64_t num_edges, int64_t num_rows)
+{
+   const int64_t total = num_edges + num_rows;
+   int64_t items = (total + kTargetTiles - 1) / kTargetTiles;
+   items = (items + 31) / 32 * 32;
+   if(items < kMinTileItems) items = kMinTileItems;
+   if(items > kMaxTileItems) items = kMaxTileItems;
+   return (int)items;
+}
+
 int64_t plan_num_tiles(int64_t num_edges, int64_t num_rows)
 {
-   return (num_edges + num_rows + kTileItems - 1) / kTileItems;
+   const int items = plan_tile_items(num_edges, num_rows);
+   return (num_edges + num_rows + items - 1) / items;
 }
 
 int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
@@ -229,7 +242,7 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    plan->num_rows = num_rows;
    plan->gather_rows = gather_rows;
    plan->num_tiles = tiles;
-   plan->tile_items = kTileItems;
+   plan->tile_items = plan_tile_items(num_edges, num_rows);
    plan->row_ptr = pl.row_ptr;
    plan->gidx = pl.gidx;
    plan->tile_row = pl.tile_row;
@@ -321,7 +334,7 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
        )))
       return rc;
    k_partition<<< grid_for(tiles + 1), kThreads, 0, stream >>>(
-      pl.row_ptr, num_rows, num_edges, tiles, kTileItems, pl.tile_row, pl.tile_edge
+      pl.row_ptr, num_rows, num_edges, tiles, plan->tile_items, pl.tile_row, pl.tile_edge
    );
    if((rc = check_launch("k_partition"))) return rc;
    return RELM_MP_OK;

@@ -26,7 +26,7 @@ int launch_fixups(const SegParams& p, cudaStream_t stream)
    int rc = check_launch("k_fixup");
    if(rc) return rc;
    if(p.max_long > 0) {
-      k_fixup_long< T, MODE ><<< (unsigned)p.max_long, kThreads, 0, stream >>>(p);
+      k_fixup_long< T, MODE ><<< (unsigned)p.max_long, kLongThreads, 0, stream >>>(p);
       rc = check_launch("k_fixup_long");
    }
    return rc;
@@ -35,9 +35,10 @@ int launch_fixups(const SegParams& p, cudaStream_t stream)
 template < typename T, int VB, int CH >
 int launch_gather_shape(const SegParams& p, cudaStream_t stream)
 {
-   const int epw = 32 / p.lpr;
-   const int64_t warps_needed = (p.num_rows + (int64_t)epw * 4 - 1) / ((int64_t)epw * 4);
-   int64_t blocks = (warps_needed * 32 + kThreads - 1) / kThreads;
+   const int64_t groups = (p.num_rows + 31) / 32;
+   int64_t blocks = (groups * 32 + kThreads - 1) / kThreads;
+   const int64_t cap = (int64_t)148 * 16;
+   if(blocks > cap) blocks = cap;
    if(blocks < 1) blocks = 1;
    k_gather_last< T, VB, CH ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    return check_launch("k_gather_last");

@@ -31,6 +31,11 @@ DEV = "cuda"
 CASES = load_cases()
 
 
+@pytest.fixture(autouse=True, scope="module")
+def _load_library():
+    assert mp.available(), "relm_mp library not loadable"
+
+
 def _t(a, device=DEV):
     if isinstance(a, np.ndarray):
         return torch.from_numpy(np.ascontiguousarray(a)).to(device)
