@@ -172,6 +172,8 @@ typedef struct relm_mp_plan {
    const int32_t* gidx;     /* device [num_edges]: gathered row of the j-th edge in row order */
    const int32_t* tile_row; /* device [num_tiles + 1]: first row of each tile */
    const int32_t* tile_edge;/* device [num_tiles + 1]: first edge of each tile */
+   const int32_t* device_flags; /* device [1]: nonzero when some row has more than one
+                                   edge; kernels read it on the device (no host copy) */
 } relm_mp_plan;
 
 RELM_MP_API size_t relm_mp_plan_bytes(int64_t num_edges, int64_t num_rows);

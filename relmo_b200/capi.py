@@ -44,6 +44,7 @@ class Plan(ctypes.Structure):
         ("gidx", ctypes.c_void_p),
         ("tile_row", ctypes.c_void_p),
         ("tile_edge", ctypes.c_void_p),
+        ("device_flags", ctypes.c_void_p),
     ]
 
 

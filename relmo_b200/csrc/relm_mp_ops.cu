@@ -50,13 +50,14 @@ struct Shape {
    int64_t block_cols;
 };
 
+Shape shape_for(int64_t emb, int es, int vb);
+
 // One warp load moves one row: the narrowest vector width that still covers the
 // row with <= 32 lanes, among the widths that divide the row size and every
 // pointer's alignment. Rows wider than 32 x 16 bytes take several chunks per
 // lane (the 16-byte or scalar width) and, past 4 chunks, several column blocks.
 Shape choose_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
 {
-   Shape s{};
    const int64_t row_bytes = emb * es;
    auto valid = [&](int vb) {
       if(vb < es || row_bytes % vb != 0) return false;
@@ -72,6 +73,82 @@ Shape choose_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
       }
    }
    if(vb == 0) vb = valid(16) ? 16 : es;  // wide row: several chunks per lane
+   return shape_for(emb, es, vb);
+}
+
+// For the segment reduction: the widest vector width (16 bytes when the row
+// size and pointers allow), lanes per row a power of two, so one load
+// instruction moves 32 / lanes rows.
+Shape choose_reduce_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
+{
+   const int64_t row_bytes = emb * es;
+   int vb = 16;
+   while(vb > es) {
+      bool ok = row_bytes % vb == 0;
+      for(int i = 0; ok && i < nptrs; ++i) ok = ptrs[i] == nullptr || aligned(ptrs[i], vb);
+      if(ok) break;
+      vb >>= 1;
+   }
+   if(vb < es) vb = es;
+   if(row_bytes / vb > 32 && vb != 16) vb = es;  // chunked rows use the 16-byte or scalar width
+   Shape s = shape_for(emb, es, vb);
+   if(s.chmax == 1) {
+      int l = 1;
+      while(l < s.lanes) l <<= 1;
+      s.lanes = l;
+      s.block_cols = (int64_t)l * (vb / es);
+   }
+   return s;
+}
+
+// Shared-memory pipeline shape: rows of 16-byte multiples with 16-byte aligned
+// tables, in column blocks of up to 1 KB; PB bytes per lane (4..32), B rows per
+// 4 KB stage. Returns pb = 0 when the row does not fit the pipeline.
+struct StreamShape {
+   int pb;
+   int lanes;
+   int rows_per_stage;
+   int col_blocks;
+   int64_t block_cols;  // elements
+};
+
+StreamShape choose_stream_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
+{
+   StreamShape s{};
+   const int64_t row_bytes = emb * es;
+   if(row_bytes <= 0 || row_bytes % 16 != 0) return s;
+   for(int i = 0; i < nptrs; ++i)
+      if(ptrs[i] != nullptr && !aligned(ptrs[i], 16)) return s;
+   int64_t cbw;
+   if(row_bytes <= 1024) {
+      cbw = row_bytes;
+      s.col_blocks = 1;
+   } else if(row_bytes % 1024 == 0) {
+      cbw = 1024;
+      s.col_blocks = (int)(row_bytes / 1024);
+   } else {
+      return s;
+   }
+   int pb = 0;
+   for(int w = 4; w <= 32; w <<= 1) {
+      if(w >= es && 32 * w >= cbw && cbw % w == 0) {
+         pb = w;
+         break;
+      }
+   }
+   if(pb == 0 || ((cbw / 16) & (cbw / 16 - 1)) != 0) return s;  // 16-byte chunks per row: a power of two
+   s.pb = pb;
+   s.lanes = (int)(cbw / pb);
+   const int64_t rows = 4096 / cbw;
+   s.rows_per_stage = (int)(rows > 32 ? 32 : (rows < 1 ? 1 : rows));
+   s.block_cols = cbw / es;
+   return s;
+}
+
+Shape shape_for(int64_t emb, int es, int vb)
+{
+   Shape s{};
+   const int64_t row_bytes = emb * es;
    s.vb = vb;
    const int vn = vb / es;
    const int64_t nvec = row_bytes / vb;
@@ -144,6 +221,7 @@ SegParams base_params(const relm_mp_plan* plan, int64_t emb, const Shape& s)
    p.gidx = plan->gidx;
    p.tile_row = plan->tile_row;
    p.tile_edge = plan->tile_edge;
+   p.has_dups = plan->device_flags;
    p.num_tiles = plan->num_tiles;
    p.num_rows = plan->num_rows;
    p.num_edges = plan->num_edges;
@@ -159,21 +237,35 @@ SegParams base_params(const relm_mp_plan* plan, int64_t emb, const Shape& s)
 int dispatch_gather(relm_mp_dtype dtype, const SegParams& p, const Shape& s, cudaStream_t st)
 {
    switch(dtype) {
-      case RELM_MP_FLOAT32: return launch_gather_last< float >(p, s.vb, s.chmax, st);
-      case RELM_MP_FLOAT64: return launch_gather_last< double >(p, s.vb, s.chmax, st);
-      case RELM_MP_BFLOAT16: return launch_gather_last< __nv_bfloat16 >(p, s.vb, s.chmax, st);
-      case RELM_MP_FLOAT16: return launch_gather_last< __half >(p, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT32: return launch_row_map< float >(p, kCopyLast, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT64: return launch_row_map< double >(p, kCopyLast, s.vb, s.chmax, st);
+      case RELM_MP_BFLOAT16: return launch_row_map< __nv_bfloat16 >(p, kCopyLast, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT16: return launch_row_map< __half >(p, kCopyLast, s.vb, s.chmax, st);
    }
    return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
 }
 
-int dispatch_reduce(relm_mp_dtype dtype, const SegParams& p, int mode, const Shape& s, cudaStream_t st)
+int dispatch_reduce(relm_mp_dtype dtype, const SegParams& pm, const Shape& sm, const SegParams& pr,
+                    const Shape& sr, int mode, cudaStream_t st)
 {
    switch(dtype) {
-      case RELM_MP_FLOAT32: return launch_seg_reduce< float >(p, mode, s.vb, s.chmax, st);
-      case RELM_MP_FLOAT64: return launch_seg_reduce< double >(p, mode, s.vb, s.chmax, st);
-      case RELM_MP_BFLOAT16: return launch_seg_reduce< __nv_bfloat16 >(p, mode, s.vb, s.chmax, st);
-      case RELM_MP_FLOAT16: return launch_seg_reduce< __half >(p, mode, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT32: return launch_seg_reduce< float >(pm, sm.vb, sm.chmax, pr, sr.vb, sr.chmax, mode, st);
+      case RELM_MP_FLOAT64: return launch_seg_reduce< double >(pm, sm.vb, sm.chmax, pr, sr.vb, sr.chmax, mode, st);
+      case RELM_MP_BFLOAT16:
+         return launch_seg_reduce< __nv_bfloat16 >(pm, sm.vb, sm.chmax, pr, sr.vb, sr.chmax, mode, st);
+      case RELM_MP_FLOAT16: return launch_seg_reduce< __half >(pm, sm.vb, sm.chmax, pr, sr.vb, sr.chmax, mode, st);
+   }
+   return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
+int dispatch_stream(relm_mp_dtype dtype, const SegParams& pm, const Shape& sm, const SegParams& pst, int pb, int mode,
+                    cudaStream_t st)
+{
+   switch(dtype) {
+      case RELM_MP_FLOAT32: return launch_seg_stream< float >(pm, sm.vb, sm.chmax, pst, pb, mode, st);
+      case RELM_MP_FLOAT64: return launch_seg_stream< double >(pm, sm.vb, sm.chmax, pst, pb, mode, st);
+      case RELM_MP_BFLOAT16: return launch_seg_stream< __nv_bfloat16 >(pm, sm.vb, sm.chmax, pst, pb, mode, st);
+      case RELM_MP_FLOAT16: return launch_seg_stream< __half >(pm, sm.vb, sm.chmax, pst, pb, mode, st);
    }
    return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
 }
@@ -197,6 +289,7 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    }
    const void* ptrs[4] = {table, table2, own, out};
    const Shape s = choose_shape(emb, (int)es, ptrs, 4);
+   const Shape sr = choose_reduce_shape(emb, (int)es, ptrs, 4);
    SegParams p = base_params(plan, emb, s);
    p.table = table;
    p.table2 = table2;
@@ -213,7 +306,21 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    p.max_long = rs.max_long;
    int rc = check_cuda(cudaMemsetAsync(rs.long_count, 0, sizeof(int32_t), stream), "long_count memset");
    if(rc) return rc;
-   return dispatch_reduce(dtype, p, seg_mode, s, stream);
+   const StreamShape ss = choose_stream_shape(emb, (int)es, ptrs, 4);
+   if(ss.pb > 0) {
+      SegParams pst = p;
+      pst.lanes = ss.lanes;
+      pst.ch = ss.rows_per_stage;
+      pst.col_blocks = ss.col_blocks;
+      pst.block_cols = ss.block_cols;
+      return dispatch_stream(dtype, p, s, pst, ss.pb, seg_mode, stream);
+   }
+   SegParams pr = p;
+   pr.lanes = sr.lanes;
+   pr.ch = sr.ch;
+   pr.col_blocks = sr.col_blocks;
+   pr.block_cols = sr.block_cols;
+   return dispatch_reduce(dtype, p, s, pr, sr, seg_mode, stream);
 }
 
 }  // namespace

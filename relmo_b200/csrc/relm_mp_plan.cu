@@ -69,14 +69,21 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       atomicExch(&st->descents, 1u);
 }
 
-// mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys).
+// mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys);
+// *has_dups becomes nonzero if some row holds more than one edge.
 __global__ void __launch_bounds__(kThreads) k_mark_ends(const uint32_t* __restrict__ keys,
-                                                        int64_t n, int32_t* __restrict__ mark)
+                                                        int64_t n, int32_t* __restrict__ mark,
+                                                        int32_t* __restrict__ has_dups)
 {
    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-   if(e >= n) return;
-   const uint32_t k = keys[e];
-   if(e == n - 1 || keys[e + 1] != k) mark[(int64_t)k + 1] = (int32_t)(e + 1);
+   bool dup = false;
+   if(e < n) {
+      const uint32_t k = keys[e];
+      const bool last = e == n - 1 || keys[e + 1] != k;
+      if(last) mark[(int64_t)k + 1] = (int32_t)(e + 1);
+      dup = !last;
+   }
+   if(__syncthreads_or(dup) && threadIdx.x == 0 && *((volatile int32_t*)has_dups) == 0) *has_dups = 1;
 }
 
 // Merge-path search: the split of diagonal d between the row-end list
@@ -137,6 +144,7 @@ size_t scan_temp_bytes(int64_t num_rows)
 }
 
 struct PlanLayout {
+   int32_t* flags;
    int32_t* gidx;
    int32_t* row_ptr;
    int32_t* tile_row;
@@ -149,6 +157,7 @@ PlanLayout plan_layout(void* mem, int64_t num_edges, int64_t num_rows)
    Carver c(mem);
    PlanLayout l;
    const int64_t tiles = plan_num_tiles(num_edges, num_rows);
+   l.flags = c.take< int32_t >(1);
    l.gidx = c.take< int32_t >((size_t)num_edges);
    l.row_ptr = c.take< int32_t >((size_t)num_rows + 1);
    l.tile_row = c.take< int32_t >((size_t)tiles + 1);
@@ -247,6 +256,7 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    plan->gidx = pl.gidx;
    plan->tile_row = pl.tile_row;
    plan->tile_edge = pl.tile_edge;
+   plan->device_flags = pl.flags;
 
    int rc;
    k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
@@ -321,8 +331,9 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
           cudaMemsetAsync(sl.mark, 0, ((size_t)num_rows + 1) * sizeof(int32_t), stream), "mark memset"
        )))
       return rc;
+   if((rc = check_cuda(cudaMemsetAsync(pl.flags, 0, sizeof(int32_t), stream), "flags memset"))) return rc;
    if(num_edges > 0) {
-      k_mark_ends<<< grid_for(num_edges), kThreads, 0, stream >>>(sorted_keys, num_edges, sl.mark);
+      k_mark_ends<<< grid_for(num_edges), kThreads, 0, stream >>>(sorted_keys, num_edges, sl.mark, pl.flags);
       if((rc = check_launch("k_mark_ends"))) return rc;
    }
    size_t scan_temp = sl.scan_bytes;

@@ -33,15 +33,22 @@ int launch_fixups(const SegParams& p, cudaStream_t stream)
 }
 
 template < typename T, int VB, int CH >
-int launch_gather_shape(const SegParams& p, cudaStream_t stream)
+int launch_map_shape(const SegParams& p, int mode, cudaStream_t stream)
 {
    const int64_t groups = (p.num_rows + 31) / 32;
    int64_t blocks = (groups * 32 + kThreads - 1) / kThreads;
    const int64_t cap = (int64_t)148 * 16;
    if(blocks > cap) blocks = cap;
    if(blocks < 1) blocks = 1;
-   k_gather_last< T, VB, CH ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
-   return check_launch("k_gather_last");
+   if(mode == kCopyLast)
+      k_row_map< T, VB, CH, kCopyLast ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kSum)
+      k_row_map< T, VB, CH, kSum ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kLse)
+      k_row_map< T, VB, CH, kLse ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else
+      k_row_map< T, VB, CH, kLseBwd ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   return check_launch("k_row_map");
 }
 
 // VB choices per storage type: the element size (scalar path) and 16 bytes are
@@ -63,17 +70,73 @@ int launch_gather_shape(const SegParams& p, cudaStream_t stream)
    } while(0)
 
 template < typename T >
-int launch_gather_last(const SegParams& p, int vb, int chmax, cudaStream_t stream)
+int launch_row_map(const SegParams& p, int mode, int vb, int chmax, cudaStream_t stream)
 {
-   RELM_MP_SHAPE_DISPATCH(T, launch_gather_shape, p, stream);
+   RELM_MP_SHAPE_DISPATCH(T, launch_map_shape, p, mode, stream);
 }
 
 template < typename T >
-int launch_seg_reduce(const SegParams& p, int mode, int vb, int chmax, cudaStream_t stream)
+int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int vb, int chmax, int mode,
+                      cudaStream_t stream)
 {
+   // Plans whose rows hold at most one edge are served by the row map; the
+   // merge-path kernels return at once for them (and vice versa), decided on
+   // the device from the plan's has_dups flag.
    int rc;
+   if((rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
    auto run = [&]() -> int { RELM_MP_SHAPE_DISPATCH(T, launch_reduce_shape, p, mode, stream); };
    if((rc = run())) return rc;
+   if(mode == kSum) return launch_fixups< T, kSum >(p, stream);
+   if(mode == kLse) return launch_fixups< T, kLse >(p, stream);
+   return launch_fixups< T, kLseBwd >(p, stream);
+}
+
+template < typename T, int PB, int MODE >
+int launch_stream_shape(const SegParams& p, cudaStream_t stream)
+{
+   constexpr int NT = (MODE == kLseBwd) ? 2 : 1;
+   const size_t smem = (size_t)kStreamWarps * stream_warp_bytes(NT);
+   static bool configured = false;  // one attribute call per instantiation (per process)
+   if(!configured) {
+      const int rc = check_cuda(
+         cudaFuncSetAttribute(k_seg_stream< T, PB, MODE >, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+         "k_seg_stream smem attribute"
+      );
+      if(rc) return rc;
+      configured = true;
+   }
+   const unsigned grid = (unsigned)((p.num_tiles + kStreamWarps - 1) / kStreamWarps);
+   k_seg_stream< T, PB, MODE ><<< grid, kStreamThreads, smem, stream >>>(p);
+   return check_launch("k_seg_stream");
+}
+
+template < typename T, int PB >
+int launch_stream_mode(const SegParams& p, int mode, cudaStream_t stream)
+{
+   if(mode == kSum) return launch_stream_shape< T, PB, kSum >(p, stream);
+   if(mode == kLse) return launch_stream_shape< T, PB, kLse >(p, stream);
+   return launch_stream_shape< T, PB, kLseBwd >(p, stream);
+}
+
+template < typename T >
+int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int pb, int mode,
+                      cudaStream_t stream)
+{
+   int rc;
+   if((rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
+   constexpr int ES = (int)sizeof(T);
+   if(pb == 4 && ES <= 4) {
+      rc = launch_stream_mode< T, (ES <= 4 ? 4 : 8) >(p, mode, stream);
+   } else if(pb == 8) {
+      rc = launch_stream_mode< T, 8 >(p, mode, stream);
+   } else if(pb == 16) {
+      rc = launch_stream_mode< T, 16 >(p, mode, stream);
+   } else if(pb == 32) {
+      rc = launch_stream_mode< T, 32 >(p, mode, stream);
+   } else {
+      return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported stream chunk width");
+   }
+   if(rc) return rc;
    if(mode == kSum) return launch_fixups< T, kSum >(p, stream);
    if(mode == kLse) return launch_fixups< T, kLse >(p, stream);
    return launch_fixups< T, kLseBwd >(p, stream);
@@ -83,6 +146,7 @@ int launch_seg_reduce(const SegParams& p, int mode, int vb, int chmax, cudaStrea
 
 #define RELM_MP_INSTANTIATE(T)                                                                  \
    namespace relm_mp {                                                                          \
-   template int launch_gather_last< T >(const SegParams&, int, int, cudaStream_t);              \
-   template int launch_seg_reduce< T >(const SegParams&, int, int, int, cudaStream_t);          \
+   template int launch_row_map< T >(const SegParams&, int, int, int, cudaStream_t);             \
+   template int launch_seg_reduce< T >(const SegParams&, int, int, const SegParams&, int, int, int, cudaStream_t); \
+   template int launch_seg_stream< T >(const SegParams&, int, int, const SegParams&, int, int, cudaStream_t);     \
    }

@@ -1,5 +1,6 @@
 // Segment kernels over a plan (CSR of output rows):
-//   k_gather_last - out[r] = table[gidx[last edge of r]] (fanout forward)
+//   k_row_map     - one gathered row per output row: fanout forward, and the
+//                   reductions of plans whose rows hold at most one edge
 //   k_seg_reduce  - merge-path segment reduction, one warp per tile, with
 //                   partials for rows that cross tile boundaries
 //                   (SUM: fanin sum forward, both sum backwards;
@@ -22,7 +23,7 @@
 
 namespace relm_mp {
 
-enum SegMode : int { kSum = 0, kLse = 1, kLseBwd = 2 };
+enum SegMode : int { kSum = 0, kLse = 1, kLseBwd = 2, kCopyLast = 3 };
 
 template < typename T >
 struct AccOf {
@@ -103,25 +104,36 @@ __device__ __forceinline__ void store_vec(T* p, const typename AccOf< T >::type 
 
 __device__ __forceinline__ float nanmax(float a, float b) { return (a != a || a > b) ? a : b; }
 __device__ __forceinline__ double nanmax(double a, double b) { return (a != a || a > b) ? a : b; }
-__device__ __forceinline__ float exp_acc(float v) { return expf(v); }
-__device__ __forceinline__ double exp_acc(double v) { return exp(v); }
+// e^x = 2^(x * log2(e)): one scale and the hardware base-2 exponential.
+constexpr double kLog2E = 1.4426950408889634073599246810019;
+__device__ __forceinline__ float exp_acc(float v) { return exp2f(v * (float)kLog2E); }
+__device__ __forceinline__ double exp_acc(double v) { return exp2(v * kLog2E); }
 __device__ __forceinline__ float log_acc(float v) { return logf(v); }
 __device__ __forceinline__ double log_acc(double v) { return log(v); }
 
-// (m, s) of a running log-sum-exp: value = log(s) + m. The empty state is
-// (-inf, 0); a state that saw only -inf values has s = NaN, which is what the
-// reference's exp(-inf - (-inf)) gives.
+// (m, s) of a running log-sum-exp: value = log(s) + m. States:
+//   empty                      (-inf, +0)  -> -inf
+//   values seen, all -inf      (-inf, -0)  -> NaN (the reference's max is -inf
+//                                             and exp(-inf - (-inf)) is NaN)
+//   otherwise                  (max, sum of exp(x - max)); a +inf or NaN value
+//                              makes s NaN, as exp(inf - inf) does in the reference.
+// The sign of a zero s carries "values seen" so that a partial holding only
+// -inf values merges as a zero contribution into a row with finite values.
 template < typename A >
-__device__ __forceinline__ bool lse_empty(A m, A s)
+__device__ __forceinline__ A lse_value(A m, A s)
 {
-   return s == A(0) && m == -(A)INFINITY;
+   if(m == -(A)INFINITY && s == A(0)) return signbit(s) ? (A)NAN : -(A)INFINITY;
+   return log_acc(s) + m;
 }
 
 template < typename A >
 __device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2)
 {
-   if(lse_empty(m2, s2)) return;
-   if(lse_empty(m, s)) {
+   if(m2 == -(A)INFINITY && s2 == A(0)) {  // nothing but -inf (or nothing) on the right
+      if(m == -(A)INFINITY && signbit(s2)) s = -fabs(s);
+      return;
+   }
+   if(m == -(A)INFINITY && s == A(0)) {
       m = m2;
       s = s2;
       return;
@@ -129,6 +141,22 @@ __device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2)
    const A mn = nanmax(m, m2);
    s = s * exp_acc(m - mn) + s2 * exp_acc(m2 - mn);
    m = mn;
+}
+
+// Folds one value v into (m, s) with a single exp: the smaller of the two
+// exponents is always the one evaluated, and every case is a select (no
+// divergence). A +inf or NaN value turns s into NaN through (v - v); a -inf
+// value only marks an all--inf state.
+template < typename A >
+__device__ __forceinline__ void lse_push(A& m, A& s, A v)
+{
+   const A d = v - m;
+   const bool gt = d > A(0);
+   const A e = exp_acc(-fabs(d));
+   const A s_up = s * e + ((v - v) + A(1));
+   const A s_keep = (v == -(A)INFINITY) ? ((m == -(A)INFINITY) ? -fabs(s) : s) : s + e;
+   s = gt ? s_up : s_keep;
+   m = gt ? v : m;
 }
 
 struct SegParams {
@@ -158,6 +186,7 @@ struct SegParams {
    int32_t* long_count;
    int32_t* long_list;
    int64_t max_long;
+   const int32_t* has_dups;  // device flag of the plan: some row holds more than one edge
 };
 
 // Entries of gidx / row ends a warp stages in shared memory at a time.
@@ -179,61 +208,120 @@ struct Cols {
    }
 };
 
-// fanout forward: out[r] = table[gidx[last edge of r]], 0 for rows without
-// edges. A warp owns groups of 32 consecutive rows: the lanes fetch the
-// group's row_ptr / gidx entries with coalesced loads (prefetched one group
-// ahead), then the whole warp copies one row per load, U rows in flight.
+// 32-bit registers one lane spends on one gathered value (VB bytes per chunk,
+// CH chunks, held in the accumulator type).
 template < typename T, int VB, int CH >
-__global__ void __launch_bounds__(kThreads) k_gather_last(SegParams p)
+__host__ __device__ constexpr int value_regs()
+{
+   return (VB / (int)sizeof(T)) * CH * (int)(sizeof(typename AccOf< T >::type) / 4);
+}
+
+// Loads in flight per lane group: about 16 registers of values (8 with the
+// three loads per edge of the logsumexp backward).
+template < typename T, int VB, int CH, int MODE >
+__host__ __device__ constexpr int unroll_for()
+{
+   constexpr int budget = (MODE == kLseBwd) ? 8 : 16;
+   constexpr int u = budget / value_regs< T, VB, CH >();
+   return u < 1 ? 1 : (u > 8 ? 8 : u);
+}
+
+// Gathered row of output row g * 32 + lane: its last (or first) edge's gidx,
+// -1 for rows without edges or past the end.
+template < bool LAST >
+__device__ __forceinline__ int32_t row_source(const SegParams& p, int64_t g, int64_t groups, int lane)
+{
+   const int64_t r = g * 32 + lane;
+   int32_t src = -1;
+   if(g < groups && r < p.num_rows) {
+      const int32_t e0 = p.row_ptr[r];
+      const int32_t e1 = p.row_ptr[r + 1];
+      if(e1 > e0) src = p.gidx[LAST ? e1 - 1 : e0];
+   }
+   return src;
+}
+
+// Row map: one gathered row per output row.
+//   kCopyLast: out[r] = table[gidx[last edge of r]], 0 without edges (fanout
+//              forward; repeated slots keep the highest edge, as the reference
+//              CPU loop leaves them).
+//   kSum / kLse / kLseBwd: the same reductions as k_seg_reduce for plans whose
+//              rows hold at most one edge (the kernel returns at once when the
+//              plan's has_dups flag is set; k_seg_reduce runs instead).
+// A warp owns groups of 32 consecutive rows: the lanes fetch the group's
+// row_ptr / gidx entries with coalesced loads, prefetched one group ahead, then
+// the whole warp moves one row per load with U rows in flight.
+template < typename T, int VB, int CH, int MODE >
+__global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
 {
    using A = typename AccOf< T >::type;
    constexpr int VN = VB / (int)sizeof(T);
-   constexpr int U = (VB * CH <= 16) ? 8 : 4;
+   constexpr int U = unroll_for< T, VB, CH, (MODE == kLseBwd) ? kLseBwd : kSum >();
+   if(MODE != kCopyLast && *p.has_dups) return;
    const int lane = threadIdx.x & 31;
    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
    const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
    const T* table = static_cast< const T* >(p.table);
+   const T* table2 = static_cast< const T* >(p.table2);
+   const T* own = static_cast< const T* >(p.own);
    T* out = static_cast< T* >(p.out);
    const int64_t groups = (p.num_rows + 31) / 32;
-
-   auto fetch_src = [&](int64_t g) -> int32_t {
-      const int64_t r = g * 32 + lane;
-      int32_t src = -1;
-      if(g < groups && r < p.num_rows) {
-         const int32_t e0 = p.row_ptr[r];
-         const int32_t e1 = p.row_ptr[r + 1];
-         if(e1 > e0) src = p.gidx[e1 - 1];
-      }
-      return src;
-   };
+   const A ninf = -(A)INFINITY;
 
    int64_t g = warp;
-   int32_t src_cur = fetch_src(g);
+   int32_t src_cur = row_source< MODE == kCopyLast >(p, g, groups, lane);
    for(; g < groups; g += nwarps) {
-      const int32_t src_next = fetch_src(g + nwarps);
+      const int32_t src_next = row_source< MODE == kCopyLast >(p, g + nwarps, groups, lane);
       const int64_t r0 = g * 32;
       const int nrows = (int)((p.num_rows - r0) < 32 ? (p.num_rows - r0) : 32);
       for(int cb = 0; cb < p.col_blocks; ++cb) {
          const Cols< CH > cols(p, cb, lane, VN);
          for(int base = 0; base < nrows; base += U) {
             A v[U][CH][VN];
+            A w[(MODE == kLseBwd) ? U : 1][CH][VN];
+            A o[(MODE == kLseBwd) ? U : 1][CH][VN];
+            int32_t src[U];
 #pragma unroll
             for(int u = 0; u < U; ++u) {
-               const int32_t src = __shfl_sync(0xffffffffu, src_cur, (base + u) & 31);
+               src[u] = __shfl_sync(0xffffffffu, src_cur, (base + u) & 31);
+               const bool live = base + u < nrows && src[u] >= 0;
 #pragma unroll
                for(int c = 0; c < CH; ++c) {
-#pragma unroll
-                  for(int k = 0; k < VN; ++k) v[u][c][k] = A(0);
-                  if(base + u < nrows && src >= 0 && cols.ok[c])
-                     load_vec< T, VB >(table + (int64_t)src * p.emb + cols.col[c], v[u][c]);
+                  if(live && cols.ok[c]) {
+                     load_vec< T, VB >(table + (int64_t)src[u] * p.emb + cols.col[c], v[u][c]);
+                     if(MODE == kLseBwd) {
+                        const int ui = (MODE == kLseBwd) ? u : 0;
+                        load_vec< T, VB >(table2 + (int64_t)src[u] * p.emb + cols.col[c], w[ui][c]);
+                        load_vec< T, VB >(own + (r0 + base + u) * p.emb + cols.col[c], o[ui][c]);
+                     }
+                  }
                }
             }
 #pragma unroll
             for(int u = 0; u < U; ++u) {
-               if(base + u >= nrows) break;
 #pragma unroll
-               for(int c = 0; c < CH; ++c)
-                  if(cols.ok[c]) store_vec< T, VB >(out + (r0 + base + u) * p.emb + cols.col[c], v[u][c]);
+               for(int c = 0; c < CH; ++c) {
+                  if(base + u >= nrows || !cols.ok[c]) continue;
+                  A res[VN];
+#pragma unroll
+                  for(int k = 0; k < VN; ++k) {
+                     if(src[u] < 0) {
+                        res[k] = (MODE == kLse) ? ninf : A(0);
+                     } else if(MODE == kCopyLast) {
+                        res[k] = v[u][c][k];
+                     } else if(MODE == kSum) {
+                        res[k] = A(0) + v[u][c][k];
+                     } else if(MODE == kLse) {
+                        A m = ninf, sacc = A(0);
+                        lse_push(m, sacc, v[u][c][k]);
+                        res[k] = lse_value(m, sacc);
+                     } else {
+                        const int ui = (MODE == kLseBwd) ? u : 0;
+                        res[k] = A(0) + v[u][c][k] * exp_acc(o[ui][c][k] - w[ui][c][k]);
+                     }
+                  }
+                  store_vec< T, VB >(out + (r0 + base + u) * p.emb + cols.col[c], res);
+               }
             }
          }
       }
@@ -243,25 +331,33 @@ __global__ void __launch_bounds__(kThreads) k_gather_last(SegParams p)
 
 // Segment reduction over one merge-path tile per warp.
 //
-// The tile's edges are consumed as one stream, U at a time, whatever the row
-// lengths: the warp first resolves the row of each of the next U edges from
-// the staged row ends (shared memory), issues the U gathered row loads (one
-// full row per warp load), then folds them into the running accumulator,
-// finishing rows as the stream crosses their ends. Rows that began in an
-// earlier tile are written as a head partial, the row still open at the end of
-// the tile as a tail partial; k_fixup combines them in tile order.
+// A row is covered by `lanes` lanes (VB bytes each, 16 when possible), so the
+// warp holds G = 32 / lanes lane groups and one load instruction moves G
+// gathered rows. The tile's edges are consumed as one stream, G * U at a time
+// whatever the row lengths: group g takes edges j + g, j + g + G, ... The warp
+// first resolves the row of every edge of the batch from the staged row ends
+// (shared memory, uniform walk), issues the loads, then folds the values into
+// the per-group accumulators in edge order, finishing rows as the stream
+// crosses their ends (a finished row folds its G group accumulators with
+// shuffles). Rows that began in an earlier tile are written as a head partial,
+// the row still open at the end of the tile as a tail partial; k_fixup
+// combines them in tile order.
 template < typename T, int VB, int CH, int MODE >
-__global__ void __launch_bounds__(kThreads) k_seg_reduce(SegParams p)
+__global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3 : 2) k_seg_reduce(SegParams p)
 {
    using A = typename AccOf< T >::type;
    constexpr int VN = VB / (int)sizeof(T);
-   constexpr int U = (MODE == kLseBwd) ? ((VB * CH <= 16) ? 4 : 2) : ((VB * CH <= 16) ? 8 : 4);
+   constexpr int U = unroll_for< T, VB, CH, MODE >();
    __shared__ int32_t s_gidx[kWarps][kStage];
    __shared__ int32_t s_rend[kWarps][kStage];
    const int wib = threadIdx.x >> 5;
    const int64_t tile = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-   if(tile >= p.num_tiles) return;
+   if(tile >= p.num_tiles || !*p.has_dups) return;
    const int lane = threadIdx.x & 31;
+   const int L = p.lanes;
+   const int G = 32 / L;
+   const int grp = lane / L;
+   const int sub = lane % L;
    int32_t* sg = s_gidx[wib];
    int32_t* sr = s_rend[wib];
    const int r_begin = p.tile_row[tile];
@@ -282,11 +378,17 @@ __global__ void __launch_bounds__(kThreads) k_seg_reduce(SegParams p)
    int tail_row = -1;
 
    for(int cb = 0; cb < p.col_blocks; ++cb) {
-      const Cols< CH > cols(p, cb, lane, VN);
+      int64_t col[CH];
+      bool ok[CH];
+#pragma unroll
+      for(int c = 0; c < CH; ++c) {
+         col[c] = cb * p.block_cols + (int64_t)(c * L + sub) * VN;
+         ok[c] = c < p.ch && col[c] < p.emb;
+      }
       int gbase = j_begin, gcount = 0;
       int rbase = r_begin, rcount = 0;
       // End (exclusive edge index) of row R < r_end, from the staged row ends.
-      auto row_end = [&](int R) -> int {
+      auto row_end = [&](int R) __attribute__((always_inline)) -> int {
          if(R - rbase >= rcount) {
             __syncwarp();
             rbase = R;
@@ -298,7 +400,7 @@ __global__ void __launch_bounds__(kThreads) k_seg_reduce(SegParams p)
       };
       A acc[CH][VN];
       A aux[CH][VN];
-      auto reset = [&]() {
+      auto reset = [&]() __attribute__((always_inline)) {
 #pragma unroll
          for(int c = 0; c < CH; ++c)
 #pragma unroll
@@ -307,37 +409,75 @@ __global__ void __launch_bounds__(kThreads) k_seg_reduce(SegParams p)
                aux[c][k] = A(0);
             }
       };
-      // Finishes row R: final output, or the head partial when it began earlier.
-      auto flush = [&](int R) {
-         const bool head = (R == r_begin) && began_before;
+      // Folds the G group accumulators of the open row (every lane ends up
+      // with the row's total).
+      auto fold = [&]() __attribute__((always_inline)) {
+         for(int off = L; off < 32; off <<= 1) {
 #pragma unroll
-         for(int c = 0; c < CH; ++c) {
-            if(!cols.ok[c]) continue;
-            if(head) {
-               const int64_t off = tile * p.emb + cols.col[c];
+            for(int c = 0; c < CH; ++c)
 #pragma unroll
                for(int k = 0; k < VN; ++k) {
-                  head_val[off + k] = acc[c][k];
-                  if(MODE == kLse) head_aux[off + k] = aux[c][k];
+                  const A om = __shfl_xor_sync(0xffffffffu, acc[c][k], off);
+                  if(MODE == kLse) {
+                     const A os = __shfl_xor_sync(0xffffffffu, aux[c][k], off);
+                     lse_merge(acc[c][k], aux[c][k], om, os);
+                  } else {
+                     acc[c][k] += om;
+                  }
                }
-            } else {
-               A fin[VN];
+         }
+      };
+      // Finishes row R: final output, or the head partial when it began earlier.
+      auto flush = [&](int R) __attribute__((always_inline)) {
+         fold();
+         const bool head = (R == r_begin) && began_before;
+         if(grp == 0) {
 #pragma unroll
-               for(int k = 0; k < VN; ++k) fin[k] = (MODE == kLse) ? log_acc(aux[c][k]) + acc[c][k] : acc[c][k];
-               store_vec< T, VB >(out + (int64_t)R * p.emb + cols.col[c], fin);
+            for(int c = 0; c < CH; ++c) {
+               if(!ok[c]) continue;
+               if(head) {
+                  const int64_t off = tile * p.emb + col[c];
+#pragma unroll
+                  for(int k = 0; k < VN; ++k) {
+                     head_val[off + k] = acc[c][k];
+                     if(MODE == kLse) head_aux[off + k] = aux[c][k];
+                  }
+               } else {
+                  A fin[VN];
+#pragma unroll
+                  for(int k = 0; k < VN; ++k)
+                     fin[k] = (MODE == kLse) ? lse_value(acc[c][k], aux[c][k]) : acc[c][k];
+                  store_vec< T, VB >(out + (int64_t)R * p.emb + col[c], fin);
+               }
             }
          }
          if(head) head_row = R;
          reset();
       };
+      auto fold_in = [&](const A (&val)[CH][VN], const A (&w2)[CH][VN], const A (&o2)[CH][VN]) {
+#pragma unroll
+         for(int c = 0; c < CH; ++c) {
+            if(!ok[c]) continue;
+#pragma unroll
+            for(int k = 0; k < VN; ++k) {
+               if(MODE == kSum)
+                  acc[c][k] += val[c][k];
+               else if(MODE == kLse)
+                  lse_push(acc[c][k], aux[c][k], val[c][k]);
+               else
+                  acc[c][k] += val[c][k] * exp_acc(o2[c][k] - w2[c][k]);
+            }
+         }
+      };
 
       reset();
-      int R = r_begin;   // next row to finish
-      int Rw = r_begin;  // row of the next edge
+      int R = r_begin;   // open row (all rows before it are finished)
+      int Rw = r_begin;  // walker: row of the next edge
       int rend_w = (Rw < r_end) ? row_end(Rw) : INT_MAX;
-      int pending = 0;   // edges folded into acc since the last flush
-      for(int j = j_begin; j < j_end; j += U) {
-         const int nb = (j_end - j) < U ? (j_end - j) : U;
+      bool pending = false;  // the open row holds edges of this tile
+      const int step = G * U;
+      for(int j = j_begin; j < j_end; j += step) {
+         const int nb = (j_end - j) < step ? (j_end - j) : step;
          if(j + nb > gbase + gcount) {
             __syncwarp();
             gbase = j;
@@ -345,16 +485,23 @@ __global__ void __launch_bounds__(kThreads) k_seg_reduce(SegParams p)
             for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j + i];
             __syncwarp();
          }
+         // Row of this group's edges (rr) and of the last edge of each sub-batch (rl).
          int rr[U];
+         int rl[U];
 #pragma unroll
          for(int u = 0; u < U; ++u) {
-            rr[u] = Rw;
-            if(u < nb) {
-               while(rend_w <= j + u) {
-                  ++Rw;
-                  rend_w = (Rw < r_end) ? row_end(Rw) : INT_MAX;
+            rr[u] = INT_MAX;
+            rl[u] = Rw;
+            for(int g = 0; g < G; ++g) {
+               const int e = u * G + g;
+               if(e < nb) {
+                  while(rend_w <= j + e) {
+                     ++Rw;
+                     rend_w = (Rw < r_end) ? row_end(Rw) : INT_MAX;
+                  }
+                  if(g == grp) rr[u] = Rw;
+                  rl[u] = Rw;
                }
-               rr[u] = Rw;
             }
          }
          A v[U][CH][VN];
@@ -362,60 +509,361 @@ __global__ void __launch_bounds__(kThreads) k_seg_reduce(SegParams p)
          A o[(MODE == kLseBwd) ? U : 1][CH][VN];
 #pragma unroll
          for(int u = 0; u < U; ++u) {
-            const int32_t g = (u < nb) ? sg[j + u - gbase] : 0;
+            const int e = u * G + grp;
+            const int32_t g = (e < nb) ? sg[j + e - gbase] : 0;
 #pragma unroll
             for(int c = 0; c < CH; ++c) {
-               if(u < nb && cols.ok[c]) {
-                  load_vec< T, VB >(table + (int64_t)g * p.emb + cols.col[c], v[u][c]);
+               if(e < nb && ok[c]) {
+                  load_vec< T, VB >(table + (int64_t)g * p.emb + col[c], v[u][c]);
                   if(MODE == kLseBwd) {
-                     load_vec< T, VB >(table2 + (int64_t)g * p.emb + cols.col[c], w[(MODE == kLseBwd) ? u : 0][c]);
-                     load_vec< T, VB >(own + (int64_t)rr[u] * p.emb + cols.col[c], o[(MODE == kLseBwd) ? u : 0][c]);
+                     const int ui = (MODE == kLseBwd) ? u : 0;
+                     load_vec< T, VB >(table2 + (int64_t)g * p.emb + col[c], w[ui][c]);
+                     load_vec< T, VB >(own + (int64_t)rr[u] * p.emb + col[c], o[ui][c]);
                   }
                }
             }
          }
 #pragma unroll
          for(int u = 0; u < U; ++u) {
-            if(u >= nb) break;
-            while(R < rr[u]) {
-               flush(R);
-               pending = 0;
-               ++R;
+            if(u * G >= nb) continue;
+            const int ui = (MODE == kLseBwd) ? u : 0;
+            bool added = false;
+            if(rr[u] == R) {
+               fold_in(v[u], w[ui], o[ui]);
+               added = true;
             }
-            ++pending;
-#pragma unroll
-            for(int c = 0; c < CH; ++c) {
-               if(!cols.ok[c]) continue;
-#pragma unroll
-               for(int k = 0; k < VN; ++k) {
-                  if(MODE == kSum) {
-                     acc[c][k] += v[u][c][k];
-                  } else if(MODE == kLse) {
-                     const A mn = nanmax(acc[c][k], v[u][c][k]);
-                     aux[c][k] = aux[c][k] * exp_acc(acc[c][k] - mn) + exp_acc(v[u][c][k] - mn);
-                     acc[c][k] = mn;
-                  } else {
-                     const int ui = (MODE == kLseBwd) ? u : 0;
-                     acc[c][k] += v[u][c][k] * exp_acc(o[ui][c][k] - w[ui][c][k]);
-                  }
+            while(R < rl[u]) {
+               flush(R);
+               ++R;
+               if(!added && rr[u] == R) {
+                  fold_in(v[u], w[ui], o[ui]);
+                  added = true;
                }
             }
+            pending = true;
          }
       }
       while(R < r_end) {
          flush(R);
-         pending = 0;
+         pending = false;
          ++R;
       }
-      if(pending > 0) {
+      if(pending) {
+         fold();
+         if(grp == 0) {
 #pragma unroll
-         for(int c = 0; c < CH; ++c) {
-            if(!cols.ok[c]) continue;
-            const int64_t off = tile * p.emb + cols.col[c];
+            for(int c = 0; c < CH; ++c) {
+               if(!ok[c]) continue;
+               const int64_t off = tile * p.emb + col[c];
+#pragma unroll
+               for(int k = 0; k < VN; ++k) {
+                  tail_val[off + k] = acc[c][k];
+                  if(MODE == kLse) tail_aux[off + k] = aux[c][k];
+               }
+            }
+         }
+         tail_row = r_end;
+      }
+      __syncwarp();
+   }
+   if(lane == 0) {
+      p.head_row[tile] = head_row;
+      p.tail_row[tile] = tail_row;
+   }
+}
+
+// ---- shared-memory gather pipeline ---------------------------------------------
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem)
+{
+   const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template < int N >
+__device__ __forceinline__ void cp_async_wait()
+{
+   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// PB bytes of T (PB in {2, 4, 8, 16, 32}) <-> accumulator values.
+template < typename T, int PB >
+__device__ __forceinline__ void load_chunk(const T* p, typename AccOf< T >::type (&out)[PB / sizeof(T)])
+{
+   constexpr int W = PB < 16 ? PB : 16;
+   constexpr int per = W / (int)sizeof(T);
+#pragma unroll
+   for(int i = 0; i < PB / W; ++i) {
+      using R = typename Raw< W >::type;
+      const R r = *reinterpret_cast< const R* >(p + i * per);
+      const T* e = reinterpret_cast< const T* >(&r);
+#pragma unroll
+      for(int k = 0; k < per; ++k) out[i * per + k] = to_acc(e[k]);
+   }
+}
+
+template < typename T, int PB >
+__device__ __forceinline__ void load_chunk_global(const T* p, typename AccOf< T >::type (&out)[PB / sizeof(T)])
+{
+   constexpr int W = PB < 16 ? PB : 16;
+   constexpr int per = W / (int)sizeof(T);
+#pragma unroll
+   for(int i = 0; i < PB / W; ++i) {
+      typename AccOf< T >::type part[per];
+      load_vec< T, W >(p + i * per, part);
+#pragma unroll
+      for(int k = 0; k < per; ++k) out[i * per + k] = part[k];
+   }
+}
+
+template < typename T, int PB >
+__device__ __forceinline__ void store_chunk(T* p, const typename AccOf< T >::type (&in)[PB / sizeof(T)])
+{
+   constexpr int W = PB < 16 ? PB : 16;
+   constexpr int per = W / (int)sizeof(T);
+#pragma unroll
+   for(int i = 0; i < PB / W; ++i) {
+      typename AccOf< T >::type part[per];
+#pragma unroll
+      for(int k = 0; k < per; ++k) part[k] = in[i * per + k];
+      store_vec< T, W >(p + i * per, part);
+   }
+}
+
+constexpr int kStreamWarps = 4;
+constexpr int kStreamThreads = kStreamWarps * 32;
+constexpr int kStreamStages = 3;
+constexpr int kStreamStageBytes = 4096;  // per warp, stage and gathered table
+constexpr int kStreamMeta = 192;         // staged gidx / row-end entries per warp
+
+__host__ __device__ constexpr int stream_warp_bytes(int tables)
+{
+   return tables * kStreamStages * kStreamStageBytes + 2 * kStreamMeta * 4;
+}
+
+// Segment reduction over one merge-path tile per warp, with the gathered rows
+// brought into shared memory by cp.async ahead of use.
+//
+// A column block of CBW bytes of each gathered row (the whole row up to 1 KB)
+// is split over `lanes` lanes of PB bytes. The tile's edges are fetched B rows
+// per stage, kStreamStages - 1 stages ahead of the one being folded: the copies
+// need no registers, so the bytes in flight per SM no longer depend on register
+// pressure, and folding an edge costs one shared load and the arithmetic. The
+// fold walks the edges in order, finishing rows as it crosses their ends; rows
+// that began in an earlier tile go out as head partials, the row still open at
+// the end as the tail partial (combined by k_fixup in tile order).
+template < typename T, int PB, int MODE >
+__global__ void __launch_bounds__(kStreamThreads) k_seg_stream(SegParams p)
+{
+   using A = typename AccOf< T >::type;
+   constexpr int VN = PB / (int)sizeof(T);
+   constexpr int NT = (MODE == kLseBwd) ? 2 : 1;
+   extern __shared__ __align__(16) unsigned char smem[];
+   const int wib = threadIdx.x >> 5;
+   const int lane = threadIdx.x & 31;
+   const int64_t tile = (int64_t)blockIdx.x * kStreamWarps + wib;
+   if(tile >= p.num_tiles || !*p.has_dups) return;
+   unsigned char* wbase = smem + (size_t)wib * stream_warp_bytes(NT);
+   int32_t* sg = reinterpret_cast< int32_t* >(wbase + NT * kStreamStages * kStreamStageBytes);
+   int32_t* sr = sg + kStreamMeta;
+   const int CBW = (int)p.block_cols * (int)sizeof(T);  // bytes of a column block
+   const int B = p.ch;                                   // rows per stage
+   const bool lane_ok = lane < p.lanes;
+   const int64_t row_bytes = p.emb * (int64_t)sizeof(T);
+   const int r_begin = p.tile_row[tile];
+   const int j_begin = p.tile_edge[tile];
+   const int r_end = p.tile_row[tile + 1];
+   const int j_end = p.tile_edge[tile + 1];
+   const bool began_before = p.row_ptr[r_begin] < j_begin;
+   const char* table = static_cast< const char* >(p.table);
+   const char* table2 = static_cast< const char* >(p.table2);
+   const T* own = static_cast< const T* >(p.own);
+   T* out = static_cast< T* >(p.out);
+   A* head_val = static_cast< A* >(p.head_val);
+   A* tail_val = static_cast< A* >(p.tail_val);
+   A* head_aux = static_cast< A* >(p.head_aux);
+   A* tail_aux = static_cast< A* >(p.tail_aux);
+   const A ninf = -(A)INFINITY;
+   const int nbatches = (j_end - j_begin + B - 1) / B;
+   const int chunks = CBW / 16;
+   int head_row = -1;
+   int tail_row = -1;
+
+   for(int cb = 0; cb < p.col_blocks; ++cb) {
+      const int64_t cbyte = (int64_t)cb * CBW;
+      const int64_t col = (cbyte + (int64_t)lane * PB) / (int64_t)sizeof(T);
+      int gbase = j_begin, gcount = 0;
+      int rbase = r_begin, rcount = 0;
+      auto row_end = [&](int R) __attribute__((always_inline)) -> int {
+         if(R - rbase >= rcount) {
+            __syncwarp();
+            rbase = R;
+            rcount = (r_end - R) < kStreamMeta ? (r_end - R) : kStreamMeta;
+            for(int i = lane; i < rcount; i += 32) sr[i] = p.row_ptr[R + 1 + i];
+            __syncwarp();
+         }
+         return sr[R - rbase];
+      };
+      // Copies batch k (rows j_begin + k*B ...) into stage k % kStreamStages.
+      // Lane l copies 16-byte chunk (l mod chunks) of rows l / chunks, + 32 / chunks, ...
+      // (chunks is a power of two; wider rows give a lane several chunks).
+      auto issue = [&](int k) __attribute__((always_inline)) {
+         if(k < nbatches) {
+            const int j0 = j_begin + k * B;
+            const int nb = (j_end - j0) < B ? (j_end - j0) : B;
+            if(j0 + nb > gbase + gcount) {
+               __syncwarp();
+               gbase = j0;
+               gcount = (j_end - j0) < kStreamMeta ? (j_end - j0) : kStreamMeta;
+               for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j0 + i];
+               __syncwarp();
+            }
+            unsigned char* st = wbase + (k % kStreamStages) * kStreamStageBytes;
+            const int32_t* sgb = sg + (j0 - gbase);
+            if(chunks <= 32) {
+               const int c = lane & (chunks - 1);
+               const int rpi = 32 / chunks;
+               for(int b = lane / chunks; b < nb; b += rpi) {
+                  const int64_t off = (int64_t)sgb[b] * row_bytes + cbyte + c * 16;
+                  cp_async16(st + b * CBW + c * 16, table + off);
+                  if(NT == 2) cp_async16(st + kStreamStages * kStreamStageBytes + b * CBW + c * 16, table2 + off);
+               }
+            } else {
+               for(int b = 0; b < nb; ++b) {
+                  const int64_t roff = (int64_t)sgb[b] * row_bytes + cbyte;
+                  for(int c = lane; c < chunks; c += 32) {
+                     cp_async16(st + b * CBW + c * 16, table + roff + c * 16);
+                     if(NT == 2)
+                        cp_async16(st + kStreamStages * kStreamStageBytes + b * CBW + c * 16, table2 + roff + c * 16);
+                  }
+               }
+            }
+         }
+         cp_async_commit();
+      };
+      A acc[VN];
+      A aux[VN];
+      A ownv[VN];
+#define RELM_MP_STREAM_RESET()                                  \
+   do {                                                         \
+      _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_)          \
+      {                                                         \
+         acc[k_] = (MODE == kLse) ? ninf : A(0);                \
+         aux[k_] = A(0);                                        \
+      }                                                         \
+   } while(0)
+      // Finishes row R_: final output, or the head partial when it began earlier.
+#define RELM_MP_STREAM_FLUSH(R_)                                                                 \
+   do {                                                                                         \
+      const bool head_ = ((R_) == r_begin) && began_before;                                     \
+      if(lane_ok) {                                                                             \
+         if(head_) {                                                                            \
+            const int64_t off_ = tile * p.emb + col;                                            \
+            _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_)                                    \
+            {                                                                                   \
+               head_val[off_ + k_] = acc[k_];                                                   \
+               if(MODE == kLse) head_aux[off_ + k_] = aux[k_];                                  \
+            }                                                                                   \
+         } else {                                                                               \
+            A fin_[VN];                                                                         \
+            _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_) fin_[k_] =                         \
+               (MODE == kLse) ? lse_value(acc[k_], aux[k_]) : acc[k_];                          \
+            store_chunk< T, PB >(out + (int64_t)(R_)*p.emb + col, fin_);                         \
+         }                                                                                      \
+      }                                                                                         \
+      if(head_) head_row = (R_);                                                                \
+      RELM_MP_STREAM_RESET();                                                                   \
+   } while(0)
+
+#pragma unroll
+      for(int s = 0; s < kStreamStages - 1; ++s) issue(s);
+      RELM_MP_STREAM_RESET();
+      int R = r_begin;
+      int rend = (R < r_end) ? row_end(R) : INT_MAX;
+      int own_row = -1;
+      bool pending = false;
+      for(int k = 0; k < nbatches; ++k) {
+         issue(k + kStreamStages - 1);
+         cp_async_wait< kStreamStages - 1 >();
+         __syncwarp();
+         const int j0 = j_begin + k * B;
+         const int nb = (j_end - j0) < B ? (j_end - j0) : B;
+         const unsigned char* st = wbase + (k % kStreamStages) * kStreamStageBytes;
+         int b = 0;
+         while(b < nb) {
+            while(rend <= j0 + b) {
+               RELM_MP_STREAM_FLUSH(R);
+               ++R;
+               rend = (R < r_end) ? row_end(R) : INT_MAX;
+            }
+            // Edges [b, b + run) of this batch all belong to the open row R.
+            const int run = (nb - b) < (rend - (j0 + b)) ? (nb - b) : (rend - (j0 + b));
+            if(lane_ok) {
+               const unsigned char* src = st + b * CBW + lane * PB;
+               if(MODE == kLseBwd) {
+                  if(own_row != R) {
+                     load_chunk_global< T, PB >(own + (int64_t)R * p.emb + col, ownv);
+                     own_row = R;
+                  }
+                  for(int q = 0; q < run; ++q) {
+                     A v[VN], w[VN];
+                     load_chunk< T, PB >(reinterpret_cast< const T* >(src + q * CBW), v);
+                     load_chunk< T, PB >(
+                        reinterpret_cast< const T* >(src + kStreamStages * kStreamStageBytes + q * CBW), w
+                     );
+#pragma unroll
+                     for(int x = 0; x < VN; ++x) acc[x] += v[x] * exp_acc(ownv[x] - w[x]);
+                  }
+               } else {
+                  int q = 0;
+                  for(; q + 4 <= run; q += 4) {
+                     A v[4][VN];
+#pragma unroll
+                     for(int i = 0; i < 4; ++i)
+                        load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q + i) * CBW), v[i]);
+#pragma unroll
+                     for(int i = 0; i < 4; ++i)
+#pragma unroll
+                        for(int x = 0; x < VN; ++x) {
+                           if(MODE == kSum)
+                              acc[x] += v[i][x];
+                           else
+                              lse_push(acc[x], aux[x], v[i][x]);
+                        }
+                  }
+                  for(; q < run; ++q) {
+                     A v[VN];
+                     load_chunk< T, PB >(reinterpret_cast< const T* >(src + q * CBW), v);
+#pragma unroll
+                     for(int x = 0; x < VN; ++x) {
+                        if(MODE == kSum)
+                           acc[x] += v[x];
+                        else
+                           lse_push(acc[x], aux[x], v[x]);
+                     }
+                  }
+               }
+            }
+            b += run;
+         }
+         pending = true;
+         __syncwarp();
+      }
+      cp_async_wait< 0 >();
+      if(R < r_end) pending = false;
+      while(R < r_end) {
+         RELM_MP_STREAM_FLUSH(R);
+         ++R;
+      }
+#undef RELM_MP_STREAM_FLUSH
+#undef RELM_MP_STREAM_RESET
+      if(pending) {
+         if(lane_ok) {
+            const int64_t off = tile * p.emb + col;
 #pragma unroll
             for(int k = 0; k < VN; ++k) {
-               tail_val[off + k] = acc[c][k];
-               if(MODE == kLse) tail_aux[off + k] = aux[c][k];
+               tail_val[off + k] = acc[k];
+               if(MODE == kLse) tail_aux[off + k] = aux[k];
             }
          }
          tail_row = r_end;
@@ -474,7 +922,7 @@ __device__ __forceinline__ void fixup_finish(const SegParams& p, int64_t R, int6
    A res;
    if(MODE == kLse) {
       lse_merge(m, s, head_val[off], head_aux[off]);
-      res = log_acc(s) + m;
+      res = lse_value(m, s);
    } else {
       res = m + head_val[off];
    }
@@ -489,7 +937,7 @@ __global__ void __launch_bounds__(kThreads) k_fixup(SegParams p)
 {
    using A = typename AccOf< T >::type;
    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-   if(t >= p.num_tiles) return;
+   if(t >= p.num_tiles || !*p.has_dups) return;
    const int lane = threadIdx.x & 31;
    const int R = p.head_row[t];
    if(R < 0) return;
@@ -521,6 +969,7 @@ __global__ void __launch_bounds__(kLongThreads) k_fixup_long(SegParams p)
    __shared__ A sm_m[W][32];
    __shared__ A sm_s[W][32];
    const int64_t b = blockIdx.x;
+   if(!*p.has_dups) return;
    const int count = *p.long_count;
    if(b >= count || b >= p.max_long) return;
    const int64_t t = p.long_list[b];
@@ -557,8 +1006,14 @@ __global__ void __launch_bounds__(kLongThreads) k_fixup_long(SegParams p)
 
 // Launchers, one set per storage type (instantiated in relm_mp_seg_<dtype>.cu).
 template < typename T >
-int launch_gather_last(const SegParams& p, int vb, int chmax, cudaStream_t stream);
+int launch_row_map(const SegParams& p, int mode, int vb, int chmax, cudaStream_t stream);
 template < typename T >
-int launch_seg_reduce(const SegParams& p, int mode, int vb, int chmax, cudaStream_t stream);
+int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int vb, int chmax, int mode,
+                      cudaStream_t stream);
+// Shared-memory pipeline variant (rows of 16-byte multiples, 16-byte aligned):
+// pb = bytes per lane, p.block_cols = column block in elements, p.ch = rows per stage.
+template < typename T >
+int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int pb, int mode,
+                      cudaStream_t stream);
 
 }  // namespace relm_mp

@@ -170,7 +170,7 @@ def _random_problem(seed: int, n_src: int, n_dst: int, edges: int, emb: int, hub
     return vals, src, dst
 
 
-EMBS = [1, 3, 5, 8, 31, 32, 33, 64, 100, 128, 256, 300, 513, 1030]
+EMBS = [1, 3, 4, 5, 8, 16, 31, 32, 33, 64, 100, 128, 256, 300, 512, 513, 1024, 1030]
 
 
 @pytest.mark.parametrize("emb", EMBS)
