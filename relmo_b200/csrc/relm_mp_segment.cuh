@@ -102,23 +102,37 @@ __device__ __forceinline__ void store_vec(T* p, const typename AccOf< T >::type 
    *reinterpret_cast< R* >(p) = r;
 }
 
-__device__ __forceinline__ float nanmax(float a, float b) { return (a != a || a > b) ? a : b; }
+__device__ __forceinline__ float nanmax(float a, float b)
+{
+   float r;
+   asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+   return r;
+}
 __device__ __forceinline__ double nanmax(double a, double b) { return (a != a || a > b) ? a : b; }
-// e^x = 2^(x * log2(e)): one scale and the hardware base-2 exponential.
+// e^x = 2^(x * log2(e)); base-2 exponential of the hardware (ex2.approx.ftz:
+// about 2 ulp, results below 2^-126 flush to zero, which only drops terms far
+// below the sum they are added to).
 constexpr double kLog2E = 1.4426950408889634073599246810019;
-__device__ __forceinline__ float exp_acc(float v) { return exp2f(v * (float)kLog2E); }
-__device__ __forceinline__ double exp_acc(double v) { return exp2(v * kLog2E); }
+__device__ __forceinline__ float exp2_fast(float x)
+{
+   float r;
+   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+   return r;
+}
+__device__ __forceinline__ double exp2_fast(double x) { return exp2(x); }
+__device__ __forceinline__ float exp_acc(float v) { return exp2_fast(v * (float)kLog2E); }
+__device__ __forceinline__ double exp_acc(double v) { return exp2_fast(v * kLog2E); }
 __device__ __forceinline__ float log_acc(float v) { return logf(v); }
 __device__ __forceinline__ double log_acc(double v) { return log(v); }
 
-// (m, s) of a running log-sum-exp: value = log(s) + m. States:
-//   empty                      (-inf, +0)  -> -inf
-//   values seen, all -inf      (-inf, -0)  -> NaN (the reference's max is -inf
-//                                             and exp(-inf - (-inf)) is NaN)
-//   otherwise                  (max, sum of exp(x - max)); a +inf or NaN value
-//                              makes s NaN, as exp(inf - inf) does in the reference.
-// The sign of a zero s carries "values seen" so that a partial holding only
-// -inf values merges as a zero contribution into a row with finite values.
+// Running log-sum-exp (m, s), value = m + log(s):
+//   m  running maximum, NaN as soon as a NaN was seen
+//   s  sum of exp(x - m); NaN once a NaN or +inf value was seen (exp(inf - inf)
+//      is NaN in the reference too)
+// and, when nothing but -inf has been seen (m = -inf, s = 0), the sign of the
+// zero tells "no value" (+0 -> -inf) from "only -inf values" (-0 -> NaN, the
+// reference's exp(-inf - (-inf))). A block of -inf values inside a row with
+// finite values therefore merges as the zero contribution it is.
 template < typename A >
 __device__ __forceinline__ A lse_value(A m, A s)
 {
@@ -129,8 +143,8 @@ __device__ __forceinline__ A lse_value(A m, A s)
 template < typename A >
 __device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2)
 {
-   if(m2 == -(A)INFINITY && s2 == A(0)) {  // nothing but -inf (or nothing) on the right
-      if(m == -(A)INFINITY && signbit(s2)) s = -fabs(s);
+   if(m2 == -(A)INFINITY && s2 == A(0)) {
+      if(signbit(s2) && m == -(A)INFINITY && s == A(0)) s = -A(0);
       return;
    }
    if(m == -(A)INFINITY && s == A(0)) {
@@ -143,20 +157,31 @@ __device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2)
    m = mn;
 }
 
-// Folds one value v into (m, s) with a single exp: the smaller of the two
-// exponents is always the one evaluated, and every case is a select (no
-// divergence). A +inf or NaN value turns s into NaN through (v - v); a -inf
-// value only marks an all--inf state.
+// Folds n <= N values into (m, s): one max pass, one rescale of s and one
+// exponential per value, all as selects (no divergence between lanes).
+template < typename A, int N >
+__device__ __forceinline__ void lse_fold(A& m, A& s, const A (&v)[N], int n)
+{
+   A mr = m;
+#pragma unroll
+   for(int i = 0; i < N; ++i)
+      if(i < n) mr = nanmax(mr, v[i]);
+   // (x - mr) is exact for the maximum itself, so a row's largest value
+   // contributes exactly 1 and a single-value row returns that value.
+   A t = s * exp_acc(m - mr);
+#pragma unroll
+   for(int i = 0; i < N; ++i)
+      if(i < n) t += exp_acc(v[i] - mr);
+   const bool only_ninf = mr == -(A)INFINITY;  // every value so far is -inf
+   s = only_ninf ? ((n > 0) ? -fabs(s) : s) : t;
+   m = mr;
+}
+
 template < typename A >
 __device__ __forceinline__ void lse_push(A& m, A& s, A v)
 {
-   const A d = v - m;
-   const bool gt = d > A(0);
-   const A e = exp_acc(-fabs(d));
-   const A s_up = s * e + ((v - v) + A(1));
-   const A s_keep = (v == -(A)INFINITY) ? ((m == -(A)INFINITY) ? -fabs(s) : s) : s + e;
-   s = gt ? s_up : s_keep;
-   m = gt ? v : m;
+   const A one[1] = {v};
+   lse_fold< A, 1 >(m, s, one, 1);
 }
 
 struct SegParams {
@@ -822,14 +847,14 @@ __global__ void __launch_bounds__(kStreamThreads) k_seg_stream(SegParams p)
                      for(int i = 0; i < 4; ++i)
                         load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q + i) * CBW), v[i]);
 #pragma unroll
-                     for(int i = 0; i < 4; ++i)
-#pragma unroll
-                        for(int x = 0; x < VN; ++x) {
-                           if(MODE == kSum)
-                              acc[x] += v[i][x];
-                           else
-                              lse_push(acc[x], aux[x], v[i][x]);
+                     for(int x = 0; x < VN; ++x) {
+                        if(MODE == kSum) {
+                           acc[x] += v[0][x] + v[1][x] + v[2][x] + v[3][x];
+                        } else {
+                           const A vx[4] = {v[0][x], v[1][x], v[2][x], v[3][x]};
+                           lse_fold< A, 4 >(acc[x], aux[x], vx, 4);
                         }
+                     }
                   }
                   for(; q < run; ++q) {
                      A v[VN];
