@@ -93,9 +93,11 @@ RELM_MP_API unsigned long long relm_mp_kernel_launches(void);
 
 /* fanout_scatter: out[out_rows, emb] = 0; out[flat_dst[e]] = x_cat[src_global_idx[e]].
  * With repeated flat_dst values the highest edge index wins, as the
- * reference CPU loop (mp_ops.cpp:2815-2836) leaves it. */
-RELM_MP_API size_t relm_mp_fanout_scatter_workspace_bytes(int64_t num_edges, int64_t out_rows, int64_t emb,
-                                              relm_mp_dtype dtype);
+ * reference CPU loop (mp_ops.cpp:2815-2836) leaves it. When every slot is
+ * written at most once (the model's routing) the op runs in source-row order
+ * and reads each x row once; otherwise it orders by slot. */
+RELM_MP_API size_t relm_mp_fanout_scatter_workspace_bytes(int64_t num_edges, int64_t x_rows, int64_t out_rows,
+                                                          int64_t emb, relm_mp_dtype dtype);
 RELM_MP_API int relm_mp_fanout_scatter(relm_mp_dtype dtype, const void* x_cat, int64_t x_rows, int64_t emb,
                            const int64_t* src_global_idx, const int64_t* flat_dst,
                            int64_t num_edges, int64_t out_rows, void* out, void* workspace,
@@ -202,6 +204,17 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
 RELM_MP_API size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, int64_t emb,
                                          relm_mp_dtype dtype, int mode);
 
+/* Coverage of the plan's gather index over [0, gather_rows): cover[g] = number
+ * of edges whose gather row is g (device int32 [gather_rows]); *has_dups = 1
+ * when some row is covered more than once. Synchronizes `stream` once. */
+RELM_MP_API int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has_dups,
+                                          void* stream);
+/* Scatter in plan-row order, for a gather index that covers each row at most
+ * once: out[gidx[j]] = table[r] for every edge j of plan row r, and 0 in the
+ * out rows `cover` marks as uncovered. fanout forward through the source plan
+ * (plan rows = x rows, gather index = flat_dst): every x row is read once. */
+RELM_MP_API int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
+                                          int64_t emb, const int32_t* cover, void* out, void* stream);
 /* out[r] = table[gidx[last edge of r]] or 0 for rows without edges (fanout forward). */
 RELM_MP_API int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
                              int64_t emb, void* out, void* stream);

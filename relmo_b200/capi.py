@@ -55,7 +55,7 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_build_info": (_STR, []),
     "relm_mp_last_error": (_STR, []),
     "relm_mp_kernel_launches": (ctypes.c_ulonglong, []),
-    "relm_mp_fanout_scatter_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT]),
+    "relm_mp_fanout_scatter_workspace_bytes": (_SZ, [_I64, _I64, _I64, _I64, _INT]),
     "relm_mp_fanout_scatter": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P]),
     "relm_mp_fanout_scatter_backward_workspace_bytes": (_SZ, [_I64, _I64, _I64, _INT]),
     "relm_mp_fanout_scatter_backward": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P]),
@@ -77,6 +77,8 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "relm_mp_plan_reduce_scratch_bytes": (_SZ, [_PLANP, _I64, _INT, _INT]),
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
+    "relm_mp_plan_gather_cover": (_INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), _P]),
+    "relm_mp_plan_scatter_rows": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
     "relm_mp_plan_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
 }
@@ -146,7 +148,9 @@ def fanout_scatter(x, src, flat_dst, out_rows: int, out=None):
     emb = x.size(1)
     if out is None:
         out = torch.empty((int(out_rows), emb), dtype=x.dtype, device=x.device)
-    ws = _workspace(lib().relm_mp_fanout_scatter_workspace_bytes(src.numel(), int(out_rows), emb, dtype_code(x)), x.device)
+    ws = _workspace(
+        lib().relm_mp_fanout_scatter_workspace_bytes(src.numel(), x.size(0), int(out_rows), emb, dtype_code(x)), x.device
+    )
     check(lib().relm_mp_fanout_scatter(
         dtype_code(x), _ptr(x), x.size(0), emb, _ptr(src), _ptr(flat_dst), src.numel(), int(out_rows),
         _ptr(out), ws.data_ptr(), ws.numel(), _stream(x.device),

@@ -41,6 +41,16 @@ __global__ void k_fill_u16(unsigned short* out, int64_t n, unsigned short v)
 
 bool aligned(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes) == 0; }
 
+// cover[g] += 1 for the gather row g of every edge; *dups = 1 once a row is hit twice.
+__global__ void k_cover(const int32_t* __restrict__ gidx, int64_t n, int32_t* __restrict__ cover,
+                        int32_t* __restrict__ dups)
+{
+   bool dup = false;
+   for(int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
+      dup |= atomicAdd(&cover[gidx[j]], 1) > 0;
+   if(__syncthreads_or(dup) && threadIdx.x == 0 && *((volatile int32_t*)dups) == 0) *dups = 1;
+}
+
 struct Shape {
    int vb;
    int chmax;
@@ -241,6 +251,18 @@ int dispatch_gather(relm_mp_dtype dtype, const SegParams& p, const Shape& s, cud
       case RELM_MP_FLOAT64: return launch_row_map< double >(p, kCopyLast, s.vb, s.chmax, st);
       case RELM_MP_BFLOAT16: return launch_row_map< __nv_bfloat16 >(p, kCopyLast, s.vb, s.chmax, st);
       case RELM_MP_FLOAT16: return launch_row_map< __half >(p, kCopyLast, s.vb, s.chmax, st);
+   }
+   return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
+int dispatch_scatter(relm_mp_dtype dtype, const SegParams& p, const Shape& s, const int32_t* cover, int64_t rows,
+                     cudaStream_t st)
+{
+   switch(dtype) {
+      case RELM_MP_FLOAT32: return launch_scatter_rows< float >(p, cover, rows, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT64: return launch_scatter_rows< double >(p, cover, rows, s.vb, s.chmax, st);
+      case RELM_MP_BFLOAT16: return launch_scatter_rows< __nv_bfloat16 >(p, cover, rows, s.vb, s.chmax, st);
+      case RELM_MP_FLOAT16: return launch_scatter_rows< __half >(p, cover, rows, s.vb, s.chmax, st);
    }
    return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
 }
@@ -470,6 +492,48 @@ int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, cons
    return dispatch_gather(dtype, p, s, st);
 }
 
+int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has_dups, void* stream)
+{
+   if(!plan || !cover || !has_dups) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan, cover and has_dups must not be NULL.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   int rc;
+   // The last int of the cover buffer's allocation is not ours: keep the flag
+   // in the plan's own device flags word (bit 1), cleared first.
+   int32_t* flag = const_cast< int32_t* >(plan->device_flags) + 1;
+   if((rc = check_cuda(cudaMemsetAsync(cover, 0, (size_t)plan->gather_rows * sizeof(int32_t), st), "cover memset")))
+      return rc;
+   if((rc = check_cuda(cudaMemsetAsync(flag, 0, sizeof(int32_t), st), "cover flag memset"))) return rc;
+   if(plan->num_edges > 0) {
+      int64_t blocks = (plan->num_edges + kThreads - 1) / kThreads;
+      if(blocks > 148 * 16) blocks = 148 * 16;
+      k_cover<<< (unsigned)blocks, kThreads, 0, st >>>(plan->gidx, plan->num_edges, cover, flag);
+      if((rc = check_launch("k_cover"))) return rc;
+   }
+   int32_t host = 0;
+   if((rc = check_cuda(cudaMemcpyAsync(&host, flag, sizeof(int32_t), cudaMemcpyDeviceToHost, st), "cover flag copy")))
+      return rc;
+   if((rc = check_cuda(cudaStreamSynchronize(st), "cover sync"))) return rc;
+   *has_dups = host != 0;
+   return RELM_MP_OK;
+}
+
+int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
+                              const int32_t* cover, void* out, void* stream)
+{
+   if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
+   if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
+   if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(plan->gather_rows == 0 || emb == 0) return RELM_MP_OK;
+   if(plan->num_edges == 0) return fill_rows(dtype, out, plan->gather_rows * emb, false, st);
+   const void* ptrs[2] = {table, out};
+   const Shape s = choose_shape(emb, (int)dtype_size(dtype), ptrs, 2);
+   SegParams p = base_params(plan, emb, s);
+   p.table = table;
+   p.out = out;
+   return dispatch_scatter(dtype, p, s, cover, plan->gather_rows, st);
+}
+
 int relm_mp_plan_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int mode, const void* table, int64_t emb,
                         void* out, void* scratch, size_t scratch_bytes, void* stream)
 {
@@ -493,9 +557,27 @@ int relm_mp_plan_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtyp
 
 // ---- fanout_scatter (mp_ops.cpp:3038-3101) ---------------------------------
 
-size_t relm_mp_fanout_scatter_workspace_bytes(int64_t num_edges, int64_t out_rows, int64_t emb, relm_mp_dtype dtype)
+// fanout_scatter runs through the source plan (rows = x rows, gather index =
+// flat_dst) when flat_dst covers every slot at most once; otherwise (repeated
+// slots, last writer wins) through the slot plan. Workspace: source plan,
+// cover counts, then the larger of the source plan's build scratch and the
+// slot plan with its build scratch.
+size_t fanout_workspace(int64_t num_edges, int64_t x_rows, int64_t out_rows)
 {
-   return op_workspace(num_edges, out_rows, emb, dtype, RELM_MP_MODE_SUM, false);
+   if(num_edges < 0 || x_rows < 0 || out_rows < 0) return 0;
+   const size_t src_plan = relm_mp_plan_bytes(num_edges, x_rows);
+   const size_t cover = align_up((size_t)out_rows * sizeof(int32_t));
+   const size_t a = relm_mp_plan_scratch_bytes(num_edges, x_rows);
+   const size_t b = relm_mp_plan_bytes(num_edges, out_rows) + relm_mp_plan_scratch_bytes(num_edges, out_rows);
+   return src_plan + cover + (a > b ? a : b);
+}
+
+size_t relm_mp_fanout_scatter_workspace_bytes(int64_t num_edges, int64_t x_rows, int64_t out_rows, int64_t emb,
+                                              relm_mp_dtype dtype)
+{
+   (void)emb;
+   (void)dtype;
+   return fanout_workspace(num_edges, x_rows, out_rows);
 }
 
 int relm_mp_fanout_scatter(relm_mp_dtype dtype, const void* x_cat, int64_t x_rows, int64_t emb,
@@ -507,17 +589,36 @@ int relm_mp_fanout_scatter(relm_mp_dtype dtype, const void* x_cat, int64_t x_row
    if(out_rows < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_rows must be >= 0.");
    cudaStream_t st = static_cast< cudaStream_t >(stream);
    if(num_edges == 0 || out_rows == 0) return fill_rows(dtype, out, out_rows * emb, false, st);
-   OpMem m;
-   const size_t need = relm_mp_fanout_scatter_workspace_bytes(num_edges, out_rows, emb, dtype);
-   if((rc = split_workspace(workspace, workspace_bytes, need, num_edges, out_rows, m))) return rc;
+   if(x_rows < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "x_rows must be >= 0.");
+   const size_t need = fanout_workspace(num_edges, x_rows, out_rows);
+   if(!workspace || workspace_bytes < need) {
+      char msg[160];
+      snprintf(msg, sizeof msg, "workspace too small: %zu bytes given, %zu needed.", workspace_bytes, need);
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, msg);
+   }
+   char* ws = static_cast< char* >(workspace);
+   const size_t src_plan_bytes = relm_mp_plan_bytes(num_edges, x_rows);
+   int32_t* cover = reinterpret_cast< int32_t* >(ws + src_plan_bytes);
+   char* rest = ws + src_plan_bytes + align_up((size_t)out_rows * sizeof(int32_t));
+   const size_t rest_bytes = workspace_bytes - (size_t)(rest - ws);
    relm_mp_plan plan;
    // The reference loop checks src_global_idx before flat_dst at each edge.
    if((rc = plan_build_bounded(
-          flat_dst, src_global_idx, num_edges, out_rows, out_rows, x_rows, "flat_dst", "src_global_idx", true,
-          m.plan_mem, m.plan_bytes, m.scratch, m.scratch_bytes, st, &plan
+          src_global_idx, flat_dst, num_edges, x_rows, x_rows, out_rows, "src_global_idx", "flat_dst", false, ws,
+          src_plan_bytes, rest, rest_bytes, st, &plan
        )))
       return rc;
-   return relm_mp_plan_gather_last(&plan, dtype, x_cat, emb, out, stream);
+   int dups = 0;
+   if((rc = relm_mp_plan_gather_cover(&plan, cover, &dups, stream))) return rc;
+   if(!dups) return relm_mp_plan_scatter_rows(&plan, dtype, x_cat, emb, cover, out, stream);
+   relm_mp_plan slot_plan;
+   const size_t slot_bytes = relm_mp_plan_bytes(num_edges, out_rows);
+   if((rc = plan_build_bounded(
+          flat_dst, src_global_idx, num_edges, out_rows, out_rows, x_rows, "flat_dst", "src_global_idx", true, rest,
+          slot_bytes, rest + slot_bytes, rest_bytes - slot_bytes, st, &slot_plan
+       )))
+      return rc;
+   return relm_mp_plan_gather_last(&slot_plan, dtype, x_cat, emb, out, stream);
 }
 
 // ---- fanout_scatter_backward (mp_ops.cpp:3103-3166) ------------------------

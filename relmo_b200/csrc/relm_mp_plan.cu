@@ -157,7 +157,7 @@ PlanLayout plan_layout(void* mem, int64_t num_edges, int64_t num_rows)
    Carver c(mem);
    PlanLayout l;
    const int64_t tiles = plan_num_tiles(num_edges, num_rows);
-   l.flags = c.take< int32_t >(1);
+   l.flags = c.take< int32_t >(2);  // [0] has_dups of the output index, [1] gather-cover scratch flag
    l.gidx = c.take< int32_t >((size_t)num_edges);
    l.row_ptr = c.take< int32_t >((size_t)num_rows + 1);
    l.tile_row = c.take< int32_t >((size_t)tiles + 1);

@@ -354,6 +354,126 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
    }
 }
 
+// Scatter in plan-row order (fanout forward through the source plan): the
+// warp walks its merge-path tile, loads each plan row's table row once (the
+// next row's load is issued before the current row's stores) and stores it to
+// out[gidx[j]] for every edge j of the row in the tile. No reduction, so rows
+// that span tiles need no partials: each tile reloads the row it starts with.
+template < typename T, int VB, int CH >
+__global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
+{
+   using A = typename AccOf< T >::type;
+   constexpr int VN = VB / (int)sizeof(T);
+   __shared__ int32_t s_gidx[kWarps][kStage];
+   __shared__ int32_t s_rend[kWarps][kStage];
+   const int wib = threadIdx.x >> 5;
+   const int64_t tile = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+   if(tile >= p.num_tiles) return;
+   const int lane = threadIdx.x & 31;
+   int32_t* sg = s_gidx[wib];
+   int32_t* sr = s_rend[wib];
+   const int r_begin = p.tile_row[tile];
+   const int j_begin = p.tile_edge[tile];
+   const int r_end = p.tile_row[tile + 1];
+   const int j_end = p.tile_edge[tile + 1];
+   if(j_begin == j_end) return;
+   const T* table = static_cast< const T* >(p.table);
+   T* out = static_cast< T* >(p.out);
+   for(int cb = 0; cb < p.col_blocks; ++cb) {
+      const Cols< CH > cols(p, cb, lane, VN);
+      int gbase = j_begin, gcount = 0;
+      int rbase = r_begin, rcount = 0;
+      auto row_end = [&](int R) __attribute__((always_inline)) -> int {
+         if(R >= r_end) return j_end;
+         if(R - rbase >= rcount) {
+            __syncwarp();
+            rbase = R;
+            rcount = (r_end - R) < kStage ? (r_end - R) : kStage;
+            for(int i = lane; i < rcount; i += 32) sr[i] = p.row_ptr[R + 1 + i];
+            __syncwarp();
+         }
+         const int e = sr[R - rbase];
+         return e < j_end ? e : j_end;
+      };
+      auto load_row = [&](int R, A (&v)[CH][VN]) __attribute__((always_inline)) {
+#pragma unroll
+         for(int c = 0; c < CH; ++c)
+            if(cols.ok[c]) load_vec< T, VB >(table + (int64_t)R * p.emb + cols.col[c], v[c]);
+      };
+      int R = r_begin;
+      int j = j_begin;
+      int e_end = row_end(R);
+      while(e_end <= j) {  // rows that end before the tile's first edge (empty here)
+         ++R;
+         e_end = row_end(R);
+      }
+      A cur[CH][VN];
+      load_row(R, cur);
+      while(j < j_end) {
+         // next row with edges in this tile, and its data, before storing this one
+         int Rn = R + 1;
+         int e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
+         while(Rn <= r_end && e_next <= e_end) {
+            ++Rn;
+            e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
+         }
+         A nxt[CH][VN];
+         const bool has_next = e_end < j_end;
+         if(has_next) load_row(Rn, nxt);
+         for(; j < e_end; ++j) {
+            if(j >= gbase + gcount) {
+               __syncwarp();
+               gbase = j;
+               gcount = (j_end - j) < kStage ? (j_end - j) : kStage;
+               for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j + i];
+               __syncwarp();
+            }
+            const int64_t dst = sg[j - gbase];
+#pragma unroll
+            for(int c = 0; c < CH; ++c)
+               if(cols.ok[c]) store_vec< T, VB >(out + dst * p.emb + cols.col[c], cur[c]);
+         }
+         if(!has_next) break;
+#pragma unroll
+         for(int c = 0; c < CH; ++c)
+#pragma unroll
+            for(int k = 0; k < VN; ++k) cur[c][k] = nxt[c][k];
+         R = Rn;
+         e_end = e_next;
+      }
+      __syncwarp();
+   }
+}
+
+// Zero rows of `out` that the cover count marks as uncovered.
+template < typename T, int VB, int CH >
+__global__ void __launch_bounds__(kThreads) k_zero_uncovered(SegParams p, const int32_t* __restrict__ cover,
+                                                             int64_t rows)
+{
+   using A = typename AccOf< T >::type;
+   constexpr int VN = VB / (int)sizeof(T);
+   const int lane = threadIdx.x & 31;
+   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+   T* out = static_cast< T* >(p.out);
+   A zero[VN];
+#pragma unroll
+   for(int k = 0; k < VN; ++k) zero[k] = A(0);
+   for(int64_t base = warp * 32; base < rows; base += nwarps * 32) {
+      const int64_t r = base + lane;
+      const unsigned todo = __ballot_sync(0xffffffffu, r < rows && cover[r] == 0);
+      for(unsigned m = todo; m; m &= m - 1) {
+         const int64_t row = base + __ffs(m) - 1;
+         for(int cb = 0; cb < p.col_blocks; ++cb) {
+            const Cols< CH > cols(p, cb, lane, VN);
+#pragma unroll
+            for(int c = 0; c < CH; ++c)
+               if(cols.ok[c]) store_vec< T, VB >(out + row * p.emb + cols.col[c], zero);
+         }
+      }
+   }
+}
+
 // Segment reduction over one merge-path tile per warp.
 //
 // A row is covered by `lanes` lanes (VB bytes each, 16 when possible), so the
@@ -1035,6 +1155,9 @@ int launch_row_map(const SegParams& p, int mode, int vb, int chmax, cudaStream_t
 template < typename T >
 int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int vb, int chmax, int mode,
                       cudaStream_t stream);
+template < typename T >
+int launch_scatter_rows(const SegParams& p, const int32_t* cover, int64_t out_rows, int vb, int chmax,
+                        cudaStream_t stream);
 // Shared-memory pipeline variant (rows of 16-byte multiples, 16-byte aligned):
 // pb = bytes per lane, p.block_cols = column block in elements, p.ch = rows per stage.
 template < typename T >

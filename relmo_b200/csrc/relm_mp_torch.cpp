@@ -29,6 +29,7 @@
 #include <cstdint>
 #include <limits>
 #include <list>
+#include <memory>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -139,7 +140,10 @@ struct PlanEntry {
    int gather_first;
    Tensor memory;  // owns the plan arrays
    relm_mp_plan plan;
+   Tensor cover;         // gather-index coverage counts, computed on first use
+   int cover_dups = -1;  // -1 unknown, 0 each gather row at most once, 1 repeats
 };
+using PlanPtr = std::shared_ptr< PlanEntry >;
 
 class PlanCache {
  public:
@@ -150,9 +154,8 @@ class PlanCache {
    }
 
    // Returns the plan for (out_index, gather_index); builds it on a miss.
-   relm_mp_plan lookup(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
-                       int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first,
-                       Tensor* keep_alive)
+   PlanPtr lookup(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
+                  int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first)
    {
       const IndexKey ok = IndexKey::of(out_index);
       const IndexKey gk = IndexKey::of(gather_index);
@@ -160,13 +163,13 @@ class PlanCache {
          std::lock_guard< std::mutex > lock(mu_);
          evict_dead_locked();
          for(auto it = entries_.begin(); it != entries_.end(); ++it) {
-            if(it->out_key.same(ok) && it->gather_key.same(gk) && it->num_rows == num_rows
-               && it->out_bound == out_bound && it->gather_rows == gather_rows
-               && it->gather_first == (int)gather_first && it->memory.device() == out_index.device()) {
+            const PlanEntry& e = **it;
+            if(e.out_key.same(ok) && e.gather_key.same(gk) && e.num_rows == num_rows && e.out_bound == out_bound
+               && e.gather_rows == gather_rows && e.gather_first == (int)gather_first
+               && e.memory.device() == out_index.device()) {
                entries_.splice(entries_.begin(), entries_, it);
                ++hits_;
-               *keep_alive = entries_.front().memory;
-               return entries_.front().plan;
+               return entries_.front();
             }
          }
       }
@@ -180,12 +183,27 @@ class PlanCache {
          scratch.data_ptr(), (size_t)scratch.numel(), stream_of(out_index), &plan
       );
       check_status(rc, "plan build");
-      *keep_alive = memory;
+      auto entry = std::make_shared< PlanEntry >(
+         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1}
+      );
       std::lock_guard< std::mutex > lock(mu_);
       ++builds_;
-      entries_.push_front(PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan});
+      entries_.push_front(entry);
       while(entries_.size() > capacity_) entries_.pop_back();
-      return plan;
+      return entry;
+   }
+
+   // Coverage of the entry's gather index (computed once per plan).
+   void ensure_cover(const PlanPtr& e, const Tensor& like)
+   {
+      std::lock_guard< std::mutex > lock(cover_mu_);
+      if(e->cover_dups >= 0) return;
+      Tensor cover = at::empty({std::max< int64_t >(e->gather_rows, 1)}, like.options().dtype(at::kInt));
+      int dups = 0;
+      check_status(relm_mp_plan_gather_cover(&e->plan, cover.data_ptr< int32_t >(), &dups, stream_of(like)),
+                   "gather cover");
+      e->cover = cover;
+      e->cover_dups = dups;
    }
 
    void clear()
@@ -199,7 +217,7 @@ class PlanCache {
       std::lock_guard< std::mutex > lock(mu_);
       evict_dead_locked();
       int64_t bytes = 0;
-      for(const auto& e : entries_) bytes += e.memory.numel();
+      for(const auto& e : entries_) bytes += e->memory.numel() + (e->cover.defined() ? e->cover.numel() * 4 : 0);
       return {(int64_t)entries_.size(), hits_, builds_, bytes, (int64_t)capacity_};
    }
 
@@ -214,7 +232,7 @@ class PlanCache {
    void evict_dead_locked()
    {
       for(auto it = entries_.begin(); it != entries_.end();) {
-         if(!it->out_key.alive() || !it->gather_key.alive())
+         if(!(*it)->out_key.alive() || !(*it)->gather_key.alive())
             it = entries_.erase(it);
          else
             ++it;
@@ -222,7 +240,8 @@ class PlanCache {
    }
 
    std::mutex mu_;
-   std::list< PlanEntry > entries_;
+   std::mutex cover_mu_;
+   std::list< PlanPtr > entries_;
    size_t capacity_ = 16;
    int64_t hits_ = 0;
    int64_t builds_ = 0;
@@ -232,9 +251,11 @@ relm_mp_plan get_plan(const Tensor& out_index, const Tensor& gather_index, int64
                       int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first,
                       Tensor* keep_alive)
 {
-   return PlanCache::get().lookup(
-      out_index, gather_index, num_rows, out_bound, gather_rows, out_name, gather_name, gather_first, keep_alive
+   const PlanPtr e = PlanCache::get().lookup(
+      out_index, gather_index, num_rows, out_bound, gather_rows, out_name, gather_name, gather_first
    );
+   *keep_alive = e->memory;
+   return e->plan;
 }
 
 Tensor contig(const Tensor& t) { return t.is_contiguous() ? t : t.contiguous(); }
@@ -259,6 +280,19 @@ Tensor fanout_scatter_cuda(const Tensor& x_cat, const Tensor& src_global_idx, co
    const Tensor x = contig(x_cat);
    const Tensor src = contig(src_global_idx);
    const Tensor dst = contig(flat_dst);
+   // Source plan (shared with fanout_scatter_backward): each x row is read once
+   // and stored into its slots, when every slot is written at most once.
+   const PlanPtr sp = PlanCache::get().lookup(
+      src, dst, x.size(0), x.size(0), out_rows, "src_global_idx", "flat_dst", false
+   );
+   PlanCache::get().ensure_cover(sp, x);
+   if(sp->cover_dups == 0) {
+      check_status(relm_mp_plan_scatter_rows(&sp->plan, dt, x.data_ptr(), emb, sp->cover.data_ptr< int32_t >(),
+                                             out.data_ptr(), stream_of(x)),
+                   "fanout_scatter");
+      return out;
+   }
+   // Repeated slots: order by slot, the highest edge of each slot wins.
    Tensor keep;
    const relm_mp_plan plan = get_plan(dst, src, out_rows, out_rows, x.size(0), "flat_dst", "src_global_idx", true, &keep);
    check_status(relm_mp_plan_gather_last(&plan, dt, x.data_ptr(), emb, out.data_ptr(), stream_of(x)), "fanout_scatter");

@@ -73,7 +73,7 @@ def test_workspace_queries_without_gpu() -> None:
     assert plan >= 4 * e + 4 * (n + 1)
     ws = lib.relm_mp_fanin_reduce_workspace_bytes(e, n, d, capi.FLOAT32, 1)
     assert ws > plan
-    assert lib.relm_mp_fanout_scatter_workspace_bytes(-1, n, d, capi.FLOAT32) == 0
+    assert lib.relm_mp_fanout_scatter_workspace_bytes(-1, n, n, d, capi.FLOAT32) == 0
 
 
 def test_torch_library_registers_reference_schemas() -> None:
