@@ -148,6 +148,23 @@ RELM_MP_API int relm_mp_fanin_reduce_logsumexp_backward(relm_mp_dtype dtype, con
                                             void* workspace, size_t workspace_bytes,
                                             void* stream);
 
+/* fanin_reduce for callers that cannot allocate device memory where they call
+ * it (their device memory belongs to another allocator, or they cannot afford
+ * cudaMalloc's implicit device synchronization while other work is in
+ * flight). No counterpart in the reference library: it is relm_mp_fanin_reduce
+ * with its workspace taken from a static device array of
+ * RELM_MP_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit. The call allocates nothing. Problems whose workspace
+ * (relm_mp_fanin_reduce_workspace_bytes) exceeds that size are rejected with
+ * RELM_MP_ERR_WORKSPACE_TOO_SMALL. The first call on a device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU race. */
+#define RELM_MP_NOALLOC_SCRATCH_BYTES (16u << 20)
+RELM_MP_API int relm_mp_fanin_reduce_noalloc(relm_mp_dtype dtype, const void* rel_flat, int64_t rel_rows,
+                                             int64_t emb, const int64_t* flat_src, const int64_t* dst_idx,
+                                             int64_t num_edges, int64_t dim_size, int mode, void* out,
+                                             void* stream);
+
 /* ---------------------------------------------------------------------------
  * Plans: the CSR of one index pair, reusable across calls.
  *

@@ -68,6 +68,7 @@ SIGNATURES: dict[str, tuple] = {
         _INT,
         [_INT, _P, _P, _I64, _P, _I64, _I64, _P, _P, _I64, _I64, _P, _P, _SZ, _P],
     ),
+    "relm_mp_fanin_reduce_noalloc": (_INT, [_INT, _P, _I64, _I64, _P, _P, _I64, _I64, _INT, _P, _P]),
     "relm_mp_plan_bytes": (_SZ, [_I64, _I64]),
     "relm_mp_plan_scratch_bytes": (_SZ, [_I64, _I64]),
     "relm_mp_plan_build": (_INT, [_P, _P, _I64, _I64, _I64, _STR, _STR, _P, _SZ, _P, _SZ, _P, _PLANP]),
@@ -218,6 +219,25 @@ def fanin_reduce_logsumexp_backward(grad_out, rel, flat_src, dst, lse_out, rel_r
     check(lib().relm_mp_fanin_reduce_logsumexp_backward(
         dtype_code(g), _ptr(g), _ptr(rel), rel.size(0), _ptr(o), o.size(0), emb, _ptr(flat_src), _ptr(dst),
         flat_src.numel(), int(rel_rows), _ptr(out), ws.data_ptr(), ws.numel(), _stream(g.device),
+    ))
+    return out
+
+
+NOALLOC_SCRATCH_BYTES = 16 << 20
+
+
+def fanin_reduce_noalloc(rel, flat_src, dst, dim_size: int, mode: int, out=None):
+    """fanin_reduce through the entry point that takes its scratch from the
+    library's static device array (no workspace argument)."""
+
+    torch = _torch()
+    rel, flat_src, dst = rel.contiguous(), flat_src.contiguous(), dst.contiguous()
+    emb = rel.size(1)
+    if out is None:
+        out = torch.empty((int(dim_size), emb), dtype=rel.dtype, device=rel.device)
+    check(lib().relm_mp_fanin_reduce_noalloc(
+        dtype_code(rel), _ptr(rel), rel.size(0), emb, _ptr(flat_src), _ptr(dst), flat_src.numel(), int(dim_size),
+        int(mode), _ptr(out), _stream(rel.device),
     ))
     return out
 
