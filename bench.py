@@ -20,6 +20,15 @@ ranks of the step time (which does include the plan builds).
 (seed + rank); no collective on the data path (weak scaling). Timing uses CUDA
 events between barriers; the max over ranks is taken with an NCCL all-reduce.
 
+RelationalGNN train steps (``rgnn_train`` in the line; ``--workload cfg3|cfg4``
+prints them as the headline instead): cfg3 = CentralizedRelationalGNN, emb 32,
+10 layers, smoothed logsumexp, 256 states; cfg4 = decentralized RelationalGNN,
+emb 128, 30 layers, sum, bf16 autocast, global batch 4096 states split evenly
+over the ranks (strong scaling) and into micro-batches with gradient
+accumulation, DDP gradient all-reduce over NCCL. One step = forward, loss,
+backward and AdamW over the whole global batch; states/s = global states per
+step / max-over-ranks step time.
+
 --impl reference: the reference's own CPU relm_mp library
 (``oracle/_ref/relm_mp_ref.so``, built from the reference sources) on the
 host cores, on a bounded edge sample of the same workload; rank 0 only.
@@ -46,6 +55,7 @@ sys.path.insert(0, str(ROOT))
 from relmo_b200 import workloads  # noqa: E402
 
 METRIC = "fanin/fanout GB/s vs HBM peak"
+MODEL_METRIC = "RGNN train states/s"
 UNIT = "GB/s"
 OPS = ("fanout_fwd", "fanout_bwd", "fanin_sum_fwd", "fanin_sum_bwd", "fanin_lse_fwd", "fanin_lse_bwd")
 REF_LIB = ROOT / "oracle" / "_ref" / "relm_mp_ref.so"
@@ -286,7 +296,7 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--workload", default="cfg2-unsorted",
-                        choices=["cfg2-unsorted", "cfg2-sorted", "cfg5", "cfg1"])
+                        choices=["cfg2-unsorted", "cfg2-sorted", "cfg5", "cfg1", "cfg3", "cfg4"])
     parser.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
     parser.add_argument("--cpu-edges", type=int, default=1 << 22, help="edge sample of the reference arm")
     parser.add_argument("--port-edges", type=int, default=1 << 20, help="edge sample of the cpu_baseline leg")
@@ -298,6 +308,12 @@ def main() -> int:
     parser.add_argument("--reps", type=int, default=5, help="timed repetitions per op in the per-op timing")
     parser.add_argument("--nodes", type=int, default=None, help="override the workload's node count (profiling)")
     parser.add_argument("--edges", type=int, default=None, help="override the workload's edge count (profiling)")
+    parser.add_argument("--models", default="cfg3,cfg4",
+                        help="RGNN train-step workloads added to the cfg2 line ('' for none)")
+    parser.add_argument("--model-steps", type=int, default=2, help="timed train steps per model workload")
+    parser.add_argument("--model-warmup", type=int, default=3)
+    parser.add_argument("--model-states", type=int, default=None, help="override the global batch (states)")
+    parser.add_argument("--micro-states", type=int, default=None, help="states per micro-batch (cfg4 default 512)")
     args = parser.parse_args()
 
     if args.impl == "reference":
@@ -320,6 +336,8 @@ def main() -> int:
     from relmo_b200.ops import mp, mp_runtime
 
     assert mp.available(), "relm_mp library not loadable"
+    if args.workload in ("cfg3", "cfg4"):
+        return model_main(args, device, rank, world, local_rank)
     ops = torch.ops.relm_mp
     dtype = torch.float32 if args.dtype == "float32" else torch.bfloat16
     wl = make_workload(args.workload, seed=rank, device=device, dtype=dtype, nodes=args.nodes, edges=args.edges)
@@ -416,6 +434,12 @@ def main() -> int:
         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,
         "algorithmic_bytes": nbytes[dominant], "peak_source": peaks["source"],
     }
+    rgnn = {}
+    for name in [m for m in args.models.split(",") if m]:
+        if name == "cfg3" and world > 1:
+            continue  # single-GPU configuration
+        rgnn[name] = model_bench(name, args, device, rank, world, max_over_ranks, barrier,
+                                 steps=args.model_steps, warmup=args.model_warmup)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = cpu_sample(args.workload, args.port_edges)
@@ -441,9 +465,132 @@ def main() -> int:
             "gpu_launches": int(launches),
             "clocks": clocks,
             "per_op": per_op,
+            "rgnn_train": rgnn or None,
             "plan_and_first_call_ms": round(first_calls_ms, 3),
             "ops_only_ms": round(ops_ms, 3),
             "ops_only_gbs": round(step_bytes / ops_ms / 1e6, 1),
+            "libs": mp_runtime.loaded_library_paths(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def model_bench(name, args, device, rank, world, max_over_ranks, barrier, *, steps: int, warmup: int,
+                e2e: bool = False) -> dict:
+    """Train steps of one RGNN workload over all ranks (see the module docstring).
+    With ``e2e`` the batch lives in pinned host memory and every step copies its
+    index tensors to the device and reads the loss back."""
+
+    from relmo_b200 import capi, model_train
+
+    cfg = model_train.CONFIGS[name]
+    states = int(args.model_states or cfg.global_states)
+    lo, hi = model_train.shard_states(states, rank, world)
+    host_batch = cfg.batch(seed=0, device="cpu", states=states).state_slice(lo, hi)
+    per_rank = hi - lo
+    micro = int(args.micro_states or (min(per_rank, 512) if name == "cfg4" else per_rank))
+    host_micro = model_train.micro_batches(host_batch, micro)
+    dev_micro = [b.to(device) for b in host_micro]
+    model = model_train.model_for(cfg, seed=0, device=device)
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+
+        model = DDP(model, device_ids=[device.index], gradient_as_bucket_view=True)
+    opt = model_train.make_optimizer(model)
+    pinned = [model_train.RelationalBatch(b.num_objects, b.num_states,
+                                          {p: a.pin_memory() for p, a in b.relations.items()},
+                                          b.object_state.pin_memory()) for b in host_micro]
+    loss_host = torch.empty((), dtype=torch.float32, pin_memory=True)
+    h2d = sum(a.numel() * a.element_size() for b in pinned for a in [*b.relations.values(), b.object_state])
+
+    def step(from_host: bool):
+        batches = [b.to(device, non_blocking=True) for b in pinned] if from_host else dev_micro
+        loss = model_train.train_step(model, opt, batches, autocast=cfg.autocast)
+        if from_host:
+            loss_host.copy_(loss, non_blocking=True)
+        return loss
+
+    for _ in range(max(warmup, 3)):
+        step(False)
+    stream = torch.cuda.current_stream()
+    result = {}
+    for mode in ("device", "e2e") if e2e else ("device",):
+        launches0 = capi.lib().relm_mp_kernel_launches()
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(steps):
+            loss = step(mode == "e2e")
+        ev1.record(stream)
+        barrier()
+        elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+        result[mode] = {"states_per_s": round(states * steps / elapsed, 2),
+                        "ms_per_step": round(elapsed / steps * 1e3, 2),
+                        "relm_mp_launches_per_step": (capi.lib().relm_mp_kernel_launches() - launches0) // steps}
+    loss_value = float(loss)
+    finite = math.isfinite(loss_value)
+    out = {
+        "workload": name, "model": cfg.kind, "emb": cfg.embedding_size, "layers": cfg.num_layers,
+        "aggregation": cfg.aggregation, "dtype": "bf16 autocast, fp32 accumulation" if cfg.autocast else "f32",
+        "global_states": states, "per_rank_states": per_rank, "micro_states": micro,
+        "micro_batches": len(dev_micro), "steps": steps, "warmup": max(warmup, 3),
+        "parallelism": f"ddp{world}" if world > 1 else "single", "scaling": "strong",
+        "states_per_s": result["device"]["states_per_s"], "ms_per_step": result["device"]["ms_per_step"],
+        "relm_mp_launches_per_step": result["device"]["relm_mp_launches_per_step"],
+        "loss": round(loss_value, 6) if finite else None, "loss_finite": finite, "optimizer": "AdamW (fused)",
+    }
+    if e2e:
+        out["e2e"] = {"value": result["e2e"]["states_per_s"], "unit": "states/s", "h2d_bytes_per_step": h2d,
+                      "d2h_bytes_per_step": 4, "ms_per_step": result["e2e"]["ms_per_step"]}
+    return out
+
+
+def model_main(args, device, rank, world, local_rank) -> int:
+    """--workload cfg3|cfg4: the RGNN train step as the headline line."""
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    from relmo_b200 import capi
+    from relmo_b200.ops import mp_runtime
+
+    sampler = ClockSampler(local_rank)
+    launches0 = capi.lib().relm_mp_kernel_launches()
+    sampler.start()
+    r = model_bench(args.workload, args, device, rank, world, max_over_ranks, barrier, steps=args.steps,
+                    warmup=args.warmup, e2e=not args.no_e2e)
+    clocks = sampler.stop()
+    launches = capi.lib().relm_mp_kernel_launches() - launches0
+    if rank == 0:
+        line = {
+            "metric": MODEL_METRIC, "value": r["states_per_s"], "unit": "states/s", "n_gpus": world,
+            "steps": args.steps, "warmup": r["warmup"], "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16" if "bf16" in r["dtype"] else "f32",
+            "data": "synthetic",
+            "config": {k: r[k] for k in ("workload", "model", "emb", "layers", "aggregation", "global_states",
+                                         "per_rank_states", "micro_states", "micro_batches", "parallelism")}
+            | {"l2": "activations far larger than L2 (no flush needed)"},
+            "roofline": None, "cpu_baseline": None, "e2e": r.get("e2e"),
+            "gpu_launches": int(r["relm_mp_launches_per_step"] * args.steps),
+            "relm_mp_launches_all_phases": int(launches), "clocks": clocks, "loss": r["loss"],
+            "loss_finite": r["loss_finite"],
             "libs": mp_runtime.loaded_library_paths(),
         }
         print(json.dumps(line), flush=True)

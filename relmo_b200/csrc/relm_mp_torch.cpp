@@ -164,9 +164,10 @@ class PlanCache {
          evict_dead_locked();
          for(auto it = entries_.begin(); it != entries_.end(); ++it) {
             const PlanEntry& e = **it;
+            // gather_first only orders the error checks of a build; a cached plan
+            // passed both, so fan-out and fan-in over the same pair share it.
             if(e.out_key.same(ok) && e.gather_key.same(gk) && e.num_rows == num_rows && e.out_bound == out_bound
-               && e.gather_rows == gather_rows && e.gather_first == (int)gather_first
-               && e.memory.device() == out_index.device()) {
+               && e.gather_rows == gather_rows && e.memory.device() == out_index.device()) {
                entries_.splice(entries_.begin(), entries_, it);
                ++hits_;
                return entries_.front();

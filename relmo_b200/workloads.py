@@ -192,3 +192,84 @@ def algorithmic_bytes(op: str, wl: FanWorkload, elem_bytes: int | None = None) -
     if op == "fanin_lse_bwd":
         return 2 * e * d * s + 2 * ud * d * s + 16 * e
     raise ValueError(op)
+
+
+# ---- relational batches (RelationalGNN workloads) ------------------------------------
+
+
+@dataclass
+class RelationalBatch:
+    """A batch of planning states as one disjoint-union relational graph.
+
+    ``relations[p]`` holds the ground atoms of predicate ``p`` as int64
+    ``[n_atoms, arity]`` global object ids (arity 0: ``[n_atoms, 0]``); objects
+    of state ``s`` are ``object_state == s``. This is the information relmo
+    reads from a PyG ``HeteroData`` batch: the edge types
+    ``(object, str(pos), predicate)`` / ``(predicate, str(pos), object)`` are
+    column ``pos`` of ``relations[predicate]``.
+    """
+
+    num_objects: int
+    num_states: int
+    relations: dict
+    object_state: torch.Tensor
+
+    @property
+    def arities(self) -> dict:
+        return {p: int(a.size(1)) for p, a in self.relations.items()}
+
+    def to(self, device, non_blocking: bool = False) -> "RelationalBatch":
+        return RelationalBatch(self.num_objects, self.num_states,
+                               {p: a.to(device, non_blocking=non_blocking) for p, a in self.relations.items()},
+                               self.object_state.to(device, non_blocking=non_blocking))
+
+    def state_slice(self, lo: int, hi: int) -> "RelationalBatch":
+        """States ``[lo, hi)`` as a batch of their own (objects renumbered from 0).
+        Objects are stored state-major (``object_state`` non-decreasing) and every
+        atom's arguments belong to one state."""
+
+        bounds = torch.searchsorted(self.object_state, torch.tensor([lo, hi], device=self.object_state.device))
+        o_lo, o_hi = (int(v) for v in bounds.tolist())
+        relations = {}
+        for p, args in self.relations.items():
+            if args.size(1) == 0:
+                relations[p] = args[:0]
+                continue
+            first = args[:, 0]
+            keep = (first >= o_lo) & (first < o_hi)
+            relations[p] = args[keep] - o_lo
+        return RelationalBatch(o_hi - o_lo, hi - lo, relations, self.object_state[o_lo:o_hi] - lo)
+
+
+def relational_batch(num_states: int, objects_per_state: int, arities: dict, atoms_per_predicate: int,
+                     seed: int = 0, device="cpu") -> RelationalBatch:
+    """Synthetic states: every predicate gets ``atoms_per_predicate`` atoms per
+    state whose arguments are objects of that state drawn uniformly (seeded)."""
+
+    g = _gen("cpu", seed)
+    base = (torch.arange(num_states, dtype=torch.int64) * objects_per_state).view(-1, 1, 1)
+    relations = {}
+    for pred in sorted(arities):
+        k = int(arities[pred])
+        args = torch.randint(0, objects_per_state, (num_states, atoms_per_predicate, k), dtype=torch.int64, generator=g)
+        relations[pred] = (args + base).reshape(num_states * atoms_per_predicate, k).to(device)
+    object_state = torch.arange(num_states, dtype=torch.int64).repeat_interleave(objects_per_state).to(device)
+    return RelationalBatch(num_states * objects_per_state, num_states, relations, object_state)
+
+
+CFG3_ARITIES = {"p0": 0, "p1": 1, "p2": 1, "p3": 2, "p4": 2, "p5": 2, "p6": 3, "p7": 3}
+CFG4_ARITIES = {f"p{i:02d}": 1 + (i % 3) for i in range(12)}
+
+
+def cfg3_batch(seed: int = 0, device="cpu", states: int = 256) -> RelationalBatch:
+    """CentralizedRelationalGNN workload: 256 states x 50 objects, 8 predicates of
+    arity {0,1,1,2,2,2,3,3}, 50 atoms per predicate (400 ground atoms per state)."""
+
+    return relational_batch(states, 50, CFG3_ARITIES, 50, seed, device)
+
+
+def cfg4_batch(seed: int = 0, device="cpu", states: int = 4096) -> RelationalBatch:
+    """Decentralized RelationalGNN workload: states x 100 objects, 12 predicates of
+    arity 1-3 (four each), 125 atoms per predicate (1500 ground atoms per state)."""
+
+    return relational_batch(states, 100, CFG4_ARITIES, 125, seed, device)

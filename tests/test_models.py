@@ -1,0 +1,309 @@
+"""Model call sites: routing, the smoothed logsumexp, the two RelationalGNN lanes,
+gradient accumulation and data-parallel training.
+
+CPU tests check the host logic (routing against per-atom loops, the beta-scaled
+logsumexp against relmo's LogSumExpAggregation formula, micro-batch and DDP
+equivalence on gloo). GPU tests run the models with the relm_mp kernels and with
+relmo's torch formulas (the path relmo takes with its kernel flags off) on the
+same weights and batch, and compare outputs and every parameter gradient:
+fp32 within 1e-4 relative / 1e-5 absolute after 10 layers (each layer adds
+rounding of reordered sums), bf16 autocast by relative Frobenius error against
+the fp32 model.
+"""
+
+from __future__ import annotations
+
+import math
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as tmp
+
+from relmo_b200 import hetero_mp, model_train, workloads
+from relmo_b200.ops import mp
+from relmo_b200.relational_gnn import CentralizedRelationalGNN, RelationalGNN, train_loss
+
+
+def small_batch(states=3, objects=7, seed=1, device="cpu"):
+    arities = {"a": 0, "b": 1, "c": 2, "d": 3, "e": 2}
+    b = workloads.relational_batch(states, objects, arities, 5, seed=seed, device=device)
+    # one predicate without atoms and one object without any edge
+    b.relations["e"] = b.relations["e"][:0]
+    return b, arities
+
+
+# ---- routing ---------------------------------------------------------------------------------
+
+
+def test_fused_routing_matches_atom_loop():
+    b, arities = small_batch()
+    cond = {p: i for i, p in enumerate(arities)}
+    rel_ar = {p: a for p, a in arities.items() if a > 0}
+    r = hetero_mp.build_fused_routing(b, rel_ar, cond, 3, torch.float32)
+    assert r.order == ["b", "c", "d"]
+    row = 0
+    exp_obj, exp_slot, exp_cond = [], [], []
+    for p in r.order:
+        args = b.relations[p]
+        assert r.offsets[p] == row
+        for atom in range(args.size(0)):
+            exp_cond.append(cond[p])
+            for pos in range(args.size(1)):
+                exp_obj.append(int(args[atom, pos]))
+                exp_slot.append((row + atom) * 3 + pos)
+            assert r.slot_mask[row + atom].tolist() == [1.0] * args.size(1) + [0.0] * (3 - args.size(1))
+        row += args.size(0)
+    assert r.total_atoms == row
+    got = sorted(zip(r.slot.tolist(), r.obj.tolist()))
+    assert got == sorted(zip(exp_slot, exp_obj))
+    assert r.cond_index.tolist() == exp_cond
+    used = set(exp_obj)
+    assert r.empty_objects.tolist() == [o not in used for o in range(b.num_objects)]
+
+
+def test_batched_routing_matches_atom_loop():
+    b, arities = small_batch()
+    rel_ar = {p: a for p, a in arities.items() if a > 0}
+    r = hetero_mp.build_batched_routing(b, rel_ar)
+    start = 0
+    for p, s, n, k in r.pred_meta:
+        assert s == start and k == arities[p] and n == b.relations[p].size(0)
+        assert torch.equal(r.obj[s : s + n * k], b.relations[p].reshape(-1))
+        start += n * k
+    assert [m[0] for m in r.pred_meta] == ["b", "c", "d"]
+    assert torch.equal(r.slot, torch.arange(start))
+
+
+def test_state_slice_renumbers_objects():
+    b = workloads.cfg4_batch(states=6)
+    s = b.state_slice(2, 4)
+    assert s.num_objects == 200 and s.num_states == 2
+    for p, args in s.relations.items():
+        assert torch.equal(args, b.relations[p][2 * 125 : 4 * 125] - 200)
+    assert torch.equal(s.object_state, torch.arange(2).repeat_interleave(100))
+
+
+# ---- smoothed logsumexp ------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+def test_smoothed_logsumexp_kernel_formula(dtype):
+    g = torch.Generator().manual_seed(3)
+    msgs = (torch.randn(40, 6, generator=g) * 3).to(dtype).requires_grad_(True)
+    flat = torch.randperm(40, generator=g)
+    dst = torch.randint(0, 9, (40,), generator=g)
+    dst[dst == 4] = 5  # row 4 empty
+    empty = hetero_mp._empty_rows(dst, 9)
+    assert empty[4]
+    ref = hetero_mp.smoothed_logsumexp_reference(msgs.index_select(0, flat), dst, 9)
+    got = hetero_mp.fanin(msgs, flat, dst, 9, "logsumexp", True, empty)
+    tol = dict(rtol=1e-6, atol=1e-6) if dtype == torch.float32 else dict(rtol=1e-12, atol=1e-12)
+    torch.testing.assert_close(got, ref, **tol)
+    assert torch.allclose(got[4], torch.full((6,), math.log(1e-16) / 12.0, dtype=dtype))
+    w = torch.randn(9, 6, generator=g).to(dtype)
+    (gr,) = torch.autograd.grad((ref * w).sum(), msgs)
+    (gk,) = torch.autograd.grad((got * w).sum(), msgs)
+    torch.testing.assert_close(gk, gr, **tol)
+
+
+def test_fanin_rejects_unknown_aggregation():
+    x = torch.zeros(2, 2)
+    with pytest.raises(ValueError, match="aggregation"):
+        hetero_mp.fanin(x, torch.arange(2), torch.arange(2), 2, "mean", False)
+
+
+# ---- whole models on CPU (ops facade vs torch formulas) ------------------------------------
+
+
+def _grads(model):
+    return {n: p.grad.detach().clone() for n, p in model.named_parameters() if p.grad is not None}
+
+
+def _run(model, batch):
+    model.zero_grad(set_to_none=True)
+    out = model(batch)
+    train_loss(out).backward()
+    return out[0].detach(), _grads(model)
+
+
+def _pair(kind, aggr, emb, layers, arities, device):
+    torch.manual_seed(0)
+    a = model_train.build_model(kind, emb, layers, aggr, arities, use_kernels=True).to(device)
+    torch.manual_seed(0)
+    b = model_train.build_model(kind, emb, layers, aggr, arities, use_kernels=False).to(device)
+    b.load_state_dict(a.state_dict())
+    return a, b
+
+
+@pytest.mark.parametrize("kind,aggr", [("centralized", "logsumexp"), ("centralized", "sum"),
+                                       ("decentralized", "sum"), ("decentralized", "logsumexp")])
+def test_models_cpu_facade_matches_torch_path(kind, aggr):
+    batch, arities = small_batch()
+    a, b = _pair(kind, aggr, 8, 3, arities, "cpu")
+    xa, ga = _run(a, batch)
+    xb, gb = _run(b, batch)
+    torch.testing.assert_close(xa, xb, rtol=1e-5, atol=1e-6)
+    assert ga.keys() == gb.keys() and len(ga) > 0
+    for n in ga:
+        torch.testing.assert_close(ga[n], gb[n], rtol=1e-4, atol=1e-6, msg=n)
+
+
+def test_central_default_modules_build_and_step():
+    batch, arities = small_batch()
+    for cond in ("film", "concat"):
+        for pos in ("pre", "post"):
+            torch.manual_seed(0)
+            m = CentralizedRelationalGNN(8, 2, "logsumexp", arities, central_conditioning=cond,
+                                         condition_position=pos)
+            out = m(batch)
+            assert out[0].shape == (batch.num_objects, 8)
+            train_loss(out).backward()
+            assert m.relation_condition_embedding.weight.grad is not None
+
+
+def test_micro_batches_equal_full_batch_step():
+    cfg = model_train.ModelConfig("cfg4", "decentralized", 8, 2, "sum", workloads.CFG4_ARITIES, 8, None)
+    batch = cfg.batch(states=8)
+    params = []
+    for micro in (0, 2):
+        m = model_train.model_for(cfg, seed=0)
+        opt = torch.optim.AdamW(m.parameters(), lr=1e-3)
+        loss = model_train.train_step(m, opt, model_train.micro_batches(batch, micro))
+        params.append(([p.detach().clone() for p in m.parameters()], float(loss)))
+    assert params[0][1] == pytest.approx(params[1][1], rel=1e-6)
+    for p, q in zip(params[0][0], params[1][0]):
+        torch.testing.assert_close(p, q, rtol=1e-5, atol=1e-7)
+
+
+# ---- data parallel (gloo, world size 2) ------------------------------------------------------
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _ddp_worker(rank, world, port, out_path):
+    import torch.distributed as dist
+    from torch.nn.parallel import DistributedDataParallel as DDP
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        cfg = model_train.ModelConfig("cfg4", "decentralized", 8, 2, "sum", workloads.CFG4_ARITIES, 8, None)
+        batch = cfg.batch(states=8)
+        lo, hi = model_train.shard_states(8, rank, world)
+        model = DDP(model_train.model_for(cfg, seed=0))
+        opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+        model_train.train_step(model, opt, model_train.micro_batches(batch.state_slice(lo, hi), 2))
+        if rank == 0:
+            torch.save([p.detach() for p in model.module.parameters()], out_path)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_ddp_gloo_two_ranks_equal_single_process(tmp_path):
+    out = tmp_path / "ddp.pt"
+    tmp.spawn(_ddp_worker, args=(2, _free_port(), str(out)), nprocs=2, join=True)
+    ddp_params = torch.load(out)
+    cfg = model_train.ModelConfig("cfg4", "decentralized", 8, 2, "sum", workloads.CFG4_ARITIES, 8, None)
+    m = model_train.model_for(cfg, seed=0)
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-3)
+    model_train.train_step(m, opt, [cfg.batch(states=8)])
+    for p, q in zip(ddp_params, m.parameters()):
+        torch.testing.assert_close(p, q.detach(), rtol=1e-5, atol=1e-7)
+
+
+# ---- GPU: kernels vs torch formulas --------------------------------------------------------
+
+
+@pytest.fixture()
+def _lib():
+    assert mp.available(), "relm_mp library not loadable"
+
+
+def _launches():
+    from relmo_b200 import capi
+
+    return int(capi.lib().relm_mp_kernel_launches())
+
+
+def _rel(a, b):
+    return float((a.double() - b.double()).norm() / b.double().norm().clamp_min(1e-300))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,aggr,layers", [("centralized", "logsumexp", 10), ("decentralized", "sum", 4),
+                                              ("centralized", "sum", 4), ("decentralized", "logsumexp", 4)])
+def test_models_gpu_kernels_match_torch_path(_lib, kind, aggr, layers):
+    """fp64: kernels and torch formulas agree to 1e-10 (relative Frobenius) on the
+    output and every gradient. fp32: the kernel path's error against the fp64
+    result is at most twice the torch path's own fp32 error (both reorder sums)."""
+
+    cfg_ar = workloads.CFG3_ARITIES if kind == "centralized" else workloads.CFG4_ARITIES
+    batch = (workloads.cfg3_batch(states=16) if kind == "centralized" else workloads.cfg4_batch(states=4)).to("cuda")
+    emb = 32 if kind == "centralized" else 64
+    a, b = _pair(kind, aggr, emb, layers, cfg_ar, "cuda")
+    a64, b64 = _pair(kind, aggr, emb, layers, cfg_ar, "cuda")
+    a64.double()
+    b64.double()
+    before = _launches()
+    xa, ga = _run(a, batch)
+    torch.cuda.synchronize()
+    assert _launches() > before, "relm_mp kernels did not run"
+    xb, gb = _run(b, batch)
+    xa64, ga64 = _run(a64, batch)
+    xb64, gb64 = _run(b64, batch)
+    assert ga.keys() == gb.keys() == ga64.keys() == gb64.keys() and len(ga) > 0
+    assert _rel(xa64, xb64) < 1e-10
+    for n in ga:
+        assert _rel(ga64[n], gb64[n]) < 1e-10, n
+    assert _rel(xa, xb64) <= 2 * _rel(xb, xb64) + 1e-6
+    torch.testing.assert_close(xa, xb, rtol=1e-3, atol=1e-4)
+    for n in ga:
+        assert _rel(ga[n], gb64[n]) <= 2 * _rel(gb[n], gb64[n]) + 1e-6, n
+
+
+@pytest.mark.gpu
+def test_model_forward_builds_one_plan_per_routing(_lib):
+    batch = workloads.cfg4_batch(states=4).to("cuda")
+    torch.manual_seed(0)
+    m = RelationalGNN(32, 5, "sum", workloads.CFG4_ARITIES).cuda()
+    mp.clear_plan_cache()
+    s0 = mp.plan_cache_stats()
+    train_loss(m(batch)).backward()
+    torch.cuda.synchronize()
+    s1 = mp.plan_cache_stats()
+    # fan-out and fan-in of all layers, forward and backward, share the routing's plans
+    assert s1["builds"] - s0["builds"] <= 2
+    assert s1["hits"] - s0["hits"] >= 2 * 5 - 2
+
+
+@pytest.mark.gpu
+def test_decentralized_bf16_autocast(_lib):
+    batch = workloads.cfg4_batch(states=4).to("cuda")
+    torch.manual_seed(0)
+    ref = model_train.build_model("decentralized", 64, 4, "sum", workloads.CFG4_ARITIES, use_kernels=False).cuda()
+    torch.manual_seed(0)
+    kern = model_train.build_model("decentralized", 64, 4, "sum", workloads.CFG4_ARITIES).cuda()
+    x32 = ref(batch)[0].detach()
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        xk = kern(batch)[0].detach().float()
+        xt = ref(batch)[0].detach().float()
+    err_k = (xk - x32).norm() / x32.norm()
+    err_t = (xt - x32).norm() / x32.norm()
+    assert err_k < 2e-2, float(err_k)
+    assert err_k <= 1.5 * err_t + 1e-3, (float(err_k), float(err_t))
+
+
+@pytest.mark.gpu
+def test_train_step_cfg3_runs_and_loss_finite(_lib):
+    cfg = model_train.CFG3
+    batch = cfg.batch(states=32, device="cuda")
+    m = model_train.model_for(cfg, device="cuda")
+    opt = model_train.make_optimizer(m)
+    losses = [float(model_train.train_step(m, opt, [batch])) for _ in range(3)]
+    assert all(math.isfinite(v) for v in losses)
