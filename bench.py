@@ -58,6 +58,13 @@ METRIC = "fanin/fanout GB/s vs HBM peak"
 MODEL_METRIC = "RGNN train states/s"
 UNIT = "GB/s"
 OPS = ("fanout_fwd", "fanout_bwd", "fanin_sum_fwd", "fanin_sum_bwd", "fanin_lse_fwd", "fanin_lse_bwd")
+FANIN_OPS = ("fanin_sum_fwd", "fanin_sum_bwd", "fanin_lse_fwd", "fanin_lse_bwd")
+
+
+def ops_of(workload: str) -> tuple[str, ...]:
+    """cfg5 is the fan-in stress test (sum and logsumexp, forward and backward)."""
+
+    return FANIN_OPS if workload == "cfg5" else OPS
 REF_LIB = ROOT / "oracle" / "_ref" / "relm_mp_ref.so"
 
 
@@ -170,25 +177,37 @@ def make_workload(name: str, seed: int, device, dtype: torch.dtype, nodes=None, 
     raise ValueError(name)
 
 
-def op_bytes(wl: workloads.FanWorkload) -> dict[str, int]:
+def op_bytes(wl: workloads.FanWorkload, op_list=OPS) -> dict[str, int]:
     s = wl.x.element_size()
-    return {op: workloads.algorithmic_bytes(op, wl, s) for op in OPS}
+    return {op: workloads.algorithmic_bytes(op, wl, s) for op in op_list}
 
 
-def run_ops(ops, wl: workloads.FanWorkload) -> dict[str, torch.Tensor]:
-    """The six ops of one step, as the autograd wrappers call them."""
+def run_ops(ops, wl: workloads.FanWorkload, op_list=OPS) -> dict[str, torch.Tensor]:
+    """The ops of one step, as the autograd wrappers call them (the logsumexp
+    backward takes the forward's output)."""
 
-    out = {}
-    out["fanout_fwd"] = ops.fanout_scatter(wl.x, wl.src, wl.flat_dst, wl.out_rows)
-    out["fanout_bwd"] = ops.fanout_scatter_backward(wl.grad_slots, wl.src, wl.flat_dst, wl.x.size(0))
-    out["fanin_sum_fwd"] = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 0)
-    out["fanin_sum_bwd"] = ops.fanin_reduce_sum_backward(wl.grad_nodes, wl.flat_src, wl.dst, wl.msgs.size(0))
-    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
-    out["fanin_lse_fwd"] = lse
-    out["fanin_lse_bwd"] = ops.fanin_reduce_logsumexp_backward(
-        wl.grad_nodes, wl.msgs, wl.flat_src, wl.dst, lse, wl.msgs.size(0)
-    )
+    out, lse = {}, None
+    for op in op_list:
+        if op == "fanin_lse_bwd" and lse is None:
+            lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+        out[op] = run_one_op(ops, wl, op, lse)
+        if op == "fanin_lse_fwd":
+            lse = out[op]
     return out
+
+
+def shard_workload(wl: workloads.FanWorkload, rank: int, world: int) -> workloads.FanWorkload:
+    """The rank's part of a fan-in workload under the destination-range partition
+    (its edges, the message rows they read, its output rows)."""
+
+    from relmo_b200 import partition
+
+    sh = partition.shard_by_destination(wl.flat_src, wl.dst, wl.dim_size, rank, world)
+    none = torch.empty(0, dtype=torch.int64, device=wl.dst.device)
+    return workloads.FanWorkload(
+        wl.name, wl.x[:0], none, none, 0, wl.msgs.index_select(0, sh.rel_rows), sh.flat_src, sh.dst, sh.dim_size,
+        wl.grad_slots[:0], wl.grad_nodes[sh.row_lo : sh.row_hi].contiguous(),
+    )
 
 
 def run_one_op(ops, wl, op: str, lse=None):
@@ -223,7 +242,7 @@ def cpu_sample(workload: str, edges: int, seed: int = 0) -> workloads.FanWorkloa
     return workloads.cfg1(seed=seed)
 
 
-def time_oracle_port(wl: workloads.FanWorkload, repeats: int = 1) -> tuple[float, int]:
+def time_oracle_port(wl: workloads.FanWorkload, repeats: int = 1, op_list=OPS) -> tuple[float, int]:
     """Seconds per step of the C oracle (single thread) on `wl`; returns (s, bytes)."""
 
     from oracle import oracle
@@ -234,14 +253,15 @@ def time_oracle_port(wl: workloads.FanWorkload, repeats: int = 1) -> tuple[float
     best = math.inf
     for _ in range(repeats):
         t0 = time.perf_counter()
-        oracle.fanout_scatter(x, src, fdst, wl.out_rows)
-        oracle.fanout_scatter_backward(gs, src, fdst, x.shape[0])
+        if "fanout_fwd" in op_list:
+            oracle.fanout_scatter(x, src, fdst, wl.out_rows)
+            oracle.fanout_scatter_backward(gs, src, fdst, x.shape[0])
         oracle.fanin_reduce(msgs, fsrc, dst, wl.dim_size, 0)
         oracle.fanin_reduce_sum_backward(gn, fsrc, dst, msgs.shape[0])
         lse = oracle.fanin_reduce(msgs, fsrc, dst, wl.dim_size, 1)
         oracle.fanin_reduce_logsumexp_backward(gn, msgs, fsrc, dst, lse, msgs.shape[0])
         best = min(best, time.perf_counter() - t0)
-    return best, sum(op_bytes(wl).values())
+    return best, sum(op_bytes(wl, op_list).values())
 
 
 def reference_arm(args) -> None:
@@ -259,21 +279,22 @@ def reference_arm(args) -> None:
         torch.ops.load_library(str(REF_LIB))
         ops = torch.ops.relm_mp
         kind = "reference"
-    nbytes = sum(op_bytes(wl).values())
+    op_list = ops_of(args.workload)
+    nbytes = sum(op_bytes(wl, op_list).values())
     times = []
     for i in range(args.warmup + args.steps):
         if kind == "reference":
             t0 = time.perf_counter()
-            run_ops(ops, wl)
+            run_ops(ops, wl, op_list)
             dt = time.perf_counter() - t0
         else:
-            dt, _ = time_oracle_port(wl)
+            dt, _ = time_oracle_port(wl, op_list=op_list)
         if i >= args.warmup:
             times.append(dt)
     step = sum(times) / len(times)
     value = nbytes / step / 1e9
     sample = (f"{args.workload} with E={edges} messages (of {1 << 24 if args.workload.startswith('cfg2') else 'n/a'}),"
-              f" same N, D and index distributions; 6 ops per step")
+              f" same N, D and index distributions; {len(op_list)} ops per step")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step * 1e3, 3), "higher_is_better": True,
@@ -304,7 +325,7 @@ def main() -> int:
     parser.add_argument("--no-e2e", action="store_true")
     parser.add_argument("--e2e-steps", type=int, default=2)
     parser.add_argument("--ops-only", action="store_true", help="per-op kernel timing only (profiling runs)")
-    parser.add_argument("--ops", default=",".join(OPS), help="ops timed by --ops-only (comma list)")
+    parser.add_argument("--ops", default=None, help="ops timed by --ops-only (comma list; default: the workload's)")
     parser.add_argument("--reps", type=int, default=5, help="timed repetitions per op in the per-op timing")
     parser.add_argument("--nodes", type=int, default=None, help="override the workload's node count (profiling)")
     parser.add_argument("--edges", type=int, default=None, help="override the workload's edge count (profiling)")
@@ -340,8 +361,16 @@ def main() -> int:
         return model_main(args, device, rank, world, local_rank)
     ops = torch.ops.relm_mp
     dtype = torch.float32 if args.dtype == "float32" else torch.bfloat16
-    wl = make_workload(args.workload, seed=rank, device=device, dtype=dtype, nodes=args.nodes, edges=args.edges)
-    nbytes = op_bytes(wl)
+    op_list = ops_of(args.workload)
+    partitioned = args.workload == "cfg5" and world > 1
+    # weak scaling: an independent batch per rank; cfg5: one global workload split by destination range
+    wl = make_workload(args.workload, seed=0 if partitioned else rank, device=device, dtype=dtype,
+                       nodes=args.nodes, edges=args.edges)
+    global_nodes, global_edges = int(wl.dim_size), wl.num_edges
+    if partitioned:
+        wl = shard_workload(wl, rank, world)
+        torch.cuda.empty_cache()
+    nbytes = op_bytes(wl, op_list)
     step_bytes = sum(nbytes.values())
     torch.cuda.synchronize()
 
@@ -361,15 +390,24 @@ def main() -> int:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def sum_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        return float(t.item())
+
     def step():
         mp.clear_plan_cache()
-        return run_ops(ops, wl)
+        return run_ops(ops, wl, op_list)
 
     # ---- per-op kernel timing (plans cached): roofline of each op -------------------------
     lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
     per_op = {}
     stream = torch.cuda.current_stream()
-    timed_ops = OPS if not args.ops_only else tuple(o for o in args.ops.split(",") if o)
+    timed_ops = op_list if not (args.ops_only and args.ops) else tuple(o for o in args.ops.split(",") if o)
     for op in timed_ops:
         for _ in range(2):
             run_one_op(ops, wl, op, lse)
@@ -405,7 +443,8 @@ def main() -> int:
     launches = capi.lib().relm_mp_kernel_launches() - launches0
     elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
     ms_per_step = elapsed / args.steps * 1e3
-    value = step_bytes * world * args.steps / elapsed / 1e9
+    job_bytes = sum_over_ranks(step_bytes)
+    value = job_bytes * args.steps / elapsed / 1e9
 
     # ---- plan build cost (separately) -----------------------------------------------------------
     mp.clear_plan_cache()
@@ -413,7 +452,7 @@ def main() -> int:
     t0 = torch.cuda.Event(enable_timing=True)
     t1 = torch.cuda.Event(enable_timing=True)
     t0.record(stream)
-    for op in OPS:  # the first call of each op builds its plan (4 distinct index pairs)
+    for op in op_list:  # the first call of each op builds its plan
         run_one_op(ops, wl, op, lse)
     t1.record(stream)
     torch.cuda.synchronize()
@@ -423,7 +462,7 @@ def main() -> int:
     # ---- end to end through the public API with host buffers ------------------------------------
     e2e = None
     if not args.no_e2e:
-        e2e = end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier)
+        e2e = end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier, op_list, sum_over_ranks)
 
     peaks = measured_peaks()
     dominant = max(per_op, key=lambda k: per_op[k]["ms"])
@@ -443,21 +482,23 @@ def main() -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = cpu_sample(args.workload, args.port_edges)
-        secs, sbytes = time_oracle_port(sample)
+        secs, sbytes = time_oracle_port(sample, op_list=op_list)
         cpu = {"value": round(sbytes / secs / 1e9, 4), "unit": UNIT, "cores": 1, "kind": "port",
                "sample": f"{args.workload} with E={args.port_edges} messages, same N, D and distributions; "
-                         f"the six ops once, C oracle, 1 thread"}
+                         f"the {len(op_list)} ops once, C oracle, 1 thread"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32" if dtype == torch.float32 else "bf16",
-            "data": "synthetic",
+            "scaling": "strong" if partitioned else "weak", "vs_baseline": None,
+            "dtype": "f32" if dtype == torch.float32 else "bf16", "data": "synthetic",
             "config": {
-                "workload": args.workload, "nodes": int(wl.dim_size), "edges": wl.num_edges, "emb": wl.emb,
+                "workload": args.workload, "nodes": global_nodes, "edges": global_edges, "emb": wl.emb,
                 "dst": "zipf(1.3)" if args.workload.startswith("cfg2") else args.workload,
                 "per_rank_batches": 1, "l2": "inputs larger than L2 (no flush needed)",
-                "step": "plan builds (cache cleared) + 6 ops", "parallelism": f"independent batches x{world}",
+                "step": f"plan builds (cache cleared) + {len(op_list)} ops",
+                "parallelism": (f"destination-range partition x{world}, no collective" if partitioned
+                                else f"independent batches x{world}"),
             },
             "roofline": roofline,
             "cpu_baseline": cpu,
@@ -601,7 +642,7 @@ def model_main(args, device, rank, world, local_rank) -> int:
     return 0
 
 
-def end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier) -> dict:
+def end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier, op_list=OPS, sum_over_ranks=None) -> dict:
     """Same step through torch.ops.relm_mp with the inputs copied in from pinned
     host memory and every op output copied back, all inside the timed region."""
 
@@ -620,7 +661,7 @@ def end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier) -> dic
         nonlocal outs_host
         for n in names_in:
             dev[n].copy_(host[n], non_blocking=True)
-        outs = run_ops(ops, dwl)
+        outs = run_ops(ops, dwl, op_list)
         if outs_host is None:
             outs_host = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in outs.items()}
         for k, v in outs.items():
@@ -638,9 +679,10 @@ def end_to_end(ops, mp, wl, args, device, world, max_over_ranks, barrier) -> dic
     ev1.record(stream)
     barrier()
     elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
-    step_bytes = sum(op_bytes(wl).values())
+    step_bytes = sum(op_bytes(wl, op_list).values())
+    job_bytes = sum_over_ranks(step_bytes) if sum_over_ranks is not None else step_bytes * world
     return {
-        "value": round(step_bytes * world * args.e2e_steps / elapsed / 1e9, 3), "unit": UNIT,
+        "value": round(job_bytes * args.e2e_steps / elapsed / 1e9, 3), "unit": UNIT,
         "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
         "ms_per_step": round(elapsed / args.e2e_steps * 1e3, 2), "steps": args.e2e_steps,
     }

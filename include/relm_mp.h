@@ -226,6 +226,10 @@ RELM_MP_API size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, i
  * when some row is covered more than once. Synchronizes `stream` once. */
 RELM_MP_API int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has_dups,
                                           void* stream);
+/* Number of the plan's output rows that hold at least one edge (counted by
+ * the plan build on the device). Synchronizes `stream` once. No counterpart in
+ * the reference (its ops keep no plans). */
+RELM_MP_API int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* rows, void* stream);
 /* Scatter in plan-row order, for a gather index that covers each row at most
  * once: out[gidx[j]] = table[r] for every edge j of plan row r, and 0 in the
  * out rows `cover` marks as uncovered. fanout forward through the source plan

@@ -79,6 +79,7 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_reduce_scratch_bytes": (_SZ, [_PLANP, _I64, _INT, _INT]),
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
     "relm_mp_plan_gather_cover": (_INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), _P]),
+    "relm_mp_plan_nonempty_rows": (_INT, [_PLANP, ctypes.POINTER(_I64), _P]),
     "relm_mp_plan_scatter_rows": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
     "relm_mp_plan_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
@@ -292,6 +293,35 @@ class PlanHandle:
         out = torch.empty((self.plan.num_rows, emb), dtype=table.dtype, device=table.device)
         check(lib().relm_mp_plan_gather_last(
             ctypes.byref(self.plan), dtype_code(table), _ptr(table), emb, _ptr(out), _stream(table.device)
+        ))
+        return out
+
+
+    def gather_cover(self):
+        """Coverage count of every gather row (int32 device tensor) and whether
+        any gather row is used more than once."""
+
+        torch = _torch()
+        cover = torch.empty(max(int(self.plan.gather_rows), 1), dtype=torch.int32, device=self.device)
+        dups = ctypes.c_int(0)
+        check(lib().relm_mp_plan_gather_cover(ctypes.byref(self.plan), _ptr(cover), ctypes.byref(dups),
+                                              _stream(self.device)))
+        return cover, bool(dups.value)
+
+    def nonempty_rows(self) -> int:
+        rows = ctypes.c_int64(0)
+        check(lib().relm_mp_plan_nonempty_rows(ctypes.byref(self.plan), ctypes.byref(rows), _stream(self.device)))
+        return int(rows.value)
+
+    def scatter_rows(self, table, cover):
+        """out[gidx[e]] = table[row of e] for every edge, zeros for uncovered gather rows."""
+
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        out = torch.empty((self.plan.gather_rows, emb), dtype=table.dtype, device=table.device)
+        check(lib().relm_mp_plan_scatter_rows(
+            ctypes.byref(self.plan), dtype_code(table), _ptr(table), emb, _ptr(cover), _ptr(out), _stream(table.device)
         ))
         return out
 

@@ -86,6 +86,26 @@ Shape choose_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
    return shape_for(emb, es, vb);
 }
 
+// Row map and scatter: the packed shape (16-byte vectors, several rows per
+// warp instruction) for rows of 16..256 bytes that are a power of two times 16
+// with 16-byte aligned pointers, else one row per warp instruction.
+Shape choose_map_shape(int64_t emb, int es, const void* const* ptrs, int nptrs)
+{
+   const int64_t row_bytes = emb * es;
+   const int64_t lanes = row_bytes / 16;
+   bool ok = row_bytes > 0 && row_bytes % 16 == 0 && lanes <= 16 && (lanes & (lanes - 1)) == 0;
+   for(int i = 0; ok && i < nptrs; ++i) ok = ptrs[i] == nullptr || aligned(ptrs[i], 16);
+   if(!ok) return choose_shape(emb, es, ptrs, nptrs);
+   Shape s{};
+   s.vb = 16;
+   s.chmax = kPackedCh;
+   s.lanes = (int)lanes;
+   s.ch = 1;
+   s.col_blocks = 1;
+   s.block_cols = emb;
+   return s;
+}
+
 // For the segment reduction: the widest vector width (16 bytes when the row
 // size and pointers allow), lanes per row a power of two, so one load
 // instruction moves 32 / lanes rows.
@@ -310,7 +330,7 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
       return fill_rows(dtype, out, plan->num_rows * emb, seg_mode == kLse, stream);
    }
    const void* ptrs[4] = {table, table2, own, out};
-   const Shape s = choose_shape(emb, (int)es, ptrs, 4);
+   const Shape s = choose_map_shape(emb, (int)es, ptrs, 4);
    const Shape sr = choose_reduce_shape(emb, (int)es, ptrs, 4);
    SegParams p = base_params(plan, emb, s);
    p.table = table;
@@ -485,7 +505,7 @@ int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, cons
    if(plan->num_rows == 0 || emb == 0) return RELM_MP_OK;
    if(plan->num_edges == 0) return fill_rows(dtype, out, plan->num_rows * emb, false, st);
    const void* ptrs[2] = {table, out};
-   const Shape s = choose_shape(emb, (int)dtype_size(dtype), ptrs, 2);
+   const Shape s = choose_map_shape(emb, (int)dtype_size(dtype), ptrs, 2);
    SegParams p = base_params(plan, emb, s);
    p.table = table;
    p.out = out;
@@ -498,7 +518,7 @@ int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has
    cudaStream_t st = static_cast< cudaStream_t >(stream);
    int rc;
    // The last int of the cover buffer's allocation is not ours: keep the flag
-   // in the plan's own device flags word (bit 1), cleared first.
+   // in the plan's own device flags word (index 1), cleared first.
    int32_t* flag = const_cast< int32_t* >(plan->device_flags) + 1;
    if((rc = check_cuda(cudaMemsetAsync(cover, 0, (size_t)plan->gather_rows * sizeof(int32_t), st), "cover memset")))
       return rc;
@@ -517,6 +537,20 @@ int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has
    return RELM_MP_OK;
 }
 
+int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* rows, void* stream)
+{
+   if(!plan || !rows) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and rows must not be NULL.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   int rc;
+   int32_t host = 0;
+   if((rc = check_cuda(cudaMemcpyAsync(&host, plan->device_flags + 2, sizeof(int32_t), cudaMemcpyDeviceToHost, st),
+                       "row count copy")))
+      return rc;
+   if((rc = check_cuda(cudaStreamSynchronize(st), "row count sync"))) return rc;
+   *rows = host;
+   return RELM_MP_OK;
+}
+
 int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
                               const int32_t* cover, void* out, void* stream)
 {
@@ -527,7 +561,7 @@ int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, con
    if(plan->gather_rows == 0 || emb == 0) return RELM_MP_OK;
    if(plan->num_edges == 0) return fill_rows(dtype, out, plan->gather_rows * emb, false, st);
    const void* ptrs[2] = {table, out};
-   const Shape s = choose_shape(emb, (int)dtype_size(dtype), ptrs, 2);
+   const Shape s = choose_map_shape(emb, (int)dtype_size(dtype), ptrs, 2);
    SegParams p = base_params(plan, emb, s);
    p.table = table;
    p.out = out;

@@ -70,20 +70,35 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
 }
 
 // mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys);
-// *has_dups becomes nonzero if some row holds more than one edge.
+// flags[0] (has_dups) becomes nonzero if some row holds more than one edge;
+// flags[2] counts the rows that hold edges.
 __global__ void __launch_bounds__(kThreads) k_mark_ends(const uint32_t* __restrict__ keys,
                                                         int64_t n, int32_t* __restrict__ mark,
-                                                        int32_t* __restrict__ has_dups)
+                                                        int32_t* __restrict__ flags)
 {
-   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
    bool dup = false;
-   if(e < n) {
+   int ends = 0;
+   for(int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
       const uint32_t k = keys[e];
       const bool last = e == n - 1 || keys[e + 1] != k;
-      if(last) mark[(int64_t)k + 1] = (int32_t)(e + 1);
-      dup = !last;
+      if(last) {
+         mark[(int64_t)k + 1] = (int32_t)(e + 1);
+         ++ends;
+      } else {
+         dup = true;
+      }
    }
-   if(__syncthreads_or(dup) && threadIdx.x == 0 && *((volatile int32_t*)has_dups) == 0) *has_dups = 1;
+   __shared__ int s_ends[kThreads / 32];
+#pragma unroll
+   for(int off = 16; off > 0; off >>= 1) ends += __shfl_down_sync(0xffffffffu, ends, off);
+   if((threadIdx.x & 31) == 0) s_ends[threadIdx.x >> 5] = ends;
+   const bool any_dup = __syncthreads_or(dup);
+   if(threadIdx.x == 0) {
+      int total = 0;
+      for(int w = 0; w < kThreads / 32; ++w) total += s_ends[w];
+      if(total) atomicAdd(&flags[2], total);
+      if(any_dup && *((volatile int32_t*)flags) == 0) flags[0] = 1;
+   }
 }
 
 // Merge-path search: the split of diagonal d between the row-end list
@@ -157,7 +172,8 @@ PlanLayout plan_layout(void* mem, int64_t num_edges, int64_t num_rows)
    Carver c(mem);
    PlanLayout l;
    const int64_t tiles = plan_num_tiles(num_edges, num_rows);
-   l.flags = c.take< int32_t >(2);  // [0] has_dups of the output index, [1] gather-cover scratch flag
+   // [0] has_dups of the output index, [1] gather-cover scratch flag, [2] rows with edges
+   l.flags = c.take< int32_t >(4);
    l.gidx = c.take< int32_t >((size_t)num_edges);
    l.row_ptr = c.take< int32_t >((size_t)num_rows + 1);
    l.tile_row = c.take< int32_t >((size_t)tiles + 1);
@@ -331,9 +347,11 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
           cudaMemsetAsync(sl.mark, 0, ((size_t)num_rows + 1) * sizeof(int32_t), stream), "mark memset"
        )))
       return rc;
-   if((rc = check_cuda(cudaMemsetAsync(pl.flags, 0, sizeof(int32_t), stream), "flags memset"))) return rc;
+   if((rc = check_cuda(cudaMemsetAsync(pl.flags, 0, 4 * sizeof(int32_t), stream), "flags memset"))) return rc;
    if(num_edges > 0) {
-      k_mark_ends<<< grid_for(num_edges), kThreads, 0, stream >>>(sorted_keys, num_edges, sl.mark, pl.flags);
+      unsigned grid = grid_for(num_edges);
+      if(grid > 148u * 8u) grid = 148u * 8u;
+      k_mark_ends<<< grid, kThreads, 0, stream >>>(sorted_keys, num_edges, sl.mark, pl.flags);
       if((rc = check_launch("k_mark_ends"))) return rc;
    }
    size_t scan_temp = sl.scan_bytes;

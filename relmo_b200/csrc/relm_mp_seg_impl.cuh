@@ -66,6 +66,40 @@ int launch_scatter_shape(const SegParams& p, const int32_t* cover, int64_t out_r
    return check_launch("k_zero_uncovered");
 }
 
+template < typename T >
+int launch_map_packed(const SegParams& p, int mode, cudaStream_t stream)
+{
+   const int64_t groups = (p.num_rows + 31) / 32;
+   int64_t blocks = (groups * 32 + kThreads - 1) / kThreads;
+   const int64_t cap = (int64_t)148 * 16;
+   if(blocks > cap) blocks = cap;
+   if(blocks < 1) blocks = 1;
+   if(mode == kCopyLast)
+      k_row_map_packed< T, kCopyLast ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kSum)
+      k_row_map_packed< T, kSum ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kLse)
+      k_row_map_packed< T, kLse ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else
+      k_row_map_packed< T, kLseBwd ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   return check_launch("k_row_map_packed");
+}
+
+template < typename T >
+int launch_scatter_packed(const SegParams& p, const int32_t* cover, int64_t out_rows, cudaStream_t stream)
+{
+   const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
+   k_scatter_rows_packed< T ><<< grid, kThreads, 0, stream >>>(p);
+   int rc = check_launch("k_scatter_rows_packed");
+   if(rc) return rc;
+   int64_t blocks = (out_rows + kThreads - 1) / kThreads;
+   const int64_t cap = (int64_t)148 * 8;
+   if(blocks > cap) blocks = cap;
+   if(blocks < 1) blocks = 1;
+   k_zero_uncovered< T, 16, 1 ><<< (unsigned)blocks, kThreads, 0, stream >>>(p, cover, out_rows);
+   return check_launch("k_zero_uncovered");
+}
+
 // VB choices per storage type: the element size (scalar path) and 16 bytes are
 // available with 1 or 4 chunks per lane; intermediate widths with 1 chunk.
 #define RELM_MP_SHAPE_DISPATCH(T, FN, ...)                                        \
@@ -87,6 +121,7 @@ int launch_scatter_shape(const SegParams& p, const int32_t* cover, int64_t out_r
 template < typename T >
 int launch_row_map(const SegParams& p, int mode, int vb, int chmax, cudaStream_t stream)
 {
+   if(chmax == kPackedCh) return launch_map_packed< T >(p, mode, stream);
    RELM_MP_SHAPE_DISPATCH(T, launch_map_shape, p, mode, stream);
 }
 
@@ -94,6 +129,7 @@ template < typename T >
 int launch_scatter_rows(const SegParams& p, const int32_t* cover, int64_t out_rows, int vb, int chmax,
                         cudaStream_t stream)
 {
+   if(chmax == kPackedCh) return launch_scatter_packed< T >(p, cover, out_rows, stream);
    RELM_MP_SHAPE_DISPATCH(T, launch_scatter_shape, p, cover, out_rows, stream);
 }
 

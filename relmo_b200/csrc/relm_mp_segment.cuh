@@ -354,6 +354,99 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
    }
 }
 
+// Packed shapes: rows of 16 to 256 bytes, a power of two times 16, with
+// 16-byte aligned tables. L = row bytes / 16 lanes cover a row with 16-byte
+// vectors and the warp's 32 / L lane groups work on different rows, so every
+// load and store instruction moves 512 bytes whatever the row width (the
+// narrow-vector shapes above move one row, 128 bytes for a 32-float or
+// 64-bf16 row). Launchers select them with chmax == kPackedCh.
+constexpr int kPackedCh = 0;
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast< const uint4* >(p)); }
+
+// Row map with packed rows; same results as k_row_map.
+template < typename T, int MODE >
+__global__ void __launch_bounds__(kThreads, (MODE == kLseBwd || MODE == kLse) ? 3 : 4) k_row_map_packed(SegParams p)
+{
+   using A = typename AccOf< T >::type;
+   constexpr int VN = 16 / (int)sizeof(T);
+   constexpr int U = (MODE == kLseBwd) ? 2 : 4;  // row loads in flight per lane group (x3 for kLseBwd)
+   constexpr int UL = (MODE == kLseBwd) ? U : 1;
+   if(MODE != kCopyLast && *p.has_dups) return;
+   const int lane = threadIdx.x & 31;
+   const int L = p.lanes;
+   const int RPI = 32 / L;  // rows per load instruction
+   const int sub = lane / L;
+   const int64_t col = (int64_t)(lane - sub * L) * VN;
+   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+   const T* table = static_cast< const T* >(p.table);
+   const T* table2 = static_cast< const T* >(p.table2);
+   const T* own = static_cast< const T* >(p.own);
+   T* out = static_cast< T* >(p.out);
+   const int64_t groups = (p.num_rows + 31) / 32;
+   const A ninf = -(A)INFINITY;
+
+   int64_t g = warp;
+   int32_t src_cur = row_source< MODE == kCopyLast >(p, g, groups, lane);
+   for(; g < groups; g += nwarps) {
+      const int32_t src_next = row_source< MODE == kCopyLast >(p, g + nwarps, groups, lane);
+      const int64_t r0 = g * 32;
+      const int nrows = (int)((p.num_rows - r0) < 32 ? (p.num_rows - r0) : 32);
+      for(int base = 0; base < nrows; base += RPI * U) {
+         uint4 v[U], w[UL], o[UL];
+         int32_t src[U];
+#pragma unroll
+         for(int u = 0; u < U; ++u) {
+            const int row = base + u * RPI + sub;
+            src[u] = __shfl_sync(0xffffffffu, src_cur, row & 31);
+            v[u] = make_uint4(0u, 0u, 0u, 0u);
+            if(MODE == kLseBwd) {
+               w[u % UL] = make_uint4(0u, 0u, 0u, 0u);
+               o[u % UL] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            if(row < nrows && src[u] >= 0) {
+               v[u] = ldg16(table + (int64_t)src[u] * p.emb + col);
+               if(MODE == kLseBwd) {
+                  w[u % UL] = ldg16(table2 + (int64_t)src[u] * p.emb + col);
+                  o[u % UL] = ldg16(own + (r0 + row) * p.emb + col);
+               }
+            }
+         }
+#pragma unroll
+         for(int u = 0; u < U; ++u) {
+            const int row = base + u * RPI + sub;
+            if(row >= nrows) continue;
+            const T* ev = reinterpret_cast< const T* >(&v[u]);
+            const T* ew = reinterpret_cast< const T* >(&w[u % UL]);
+            const T* eo = reinterpret_cast< const T* >(&o[u % UL]);
+            uint4 r;
+            T* er = reinterpret_cast< T* >(&r);
+#pragma unroll
+            for(int k = 0; k < VN; ++k) {
+               A res;
+               if(src[u] < 0) {
+                  res = (MODE == kLse) ? ninf : A(0);
+               } else if(MODE == kCopyLast) {
+                  res = to_acc(ev[k]);
+               } else if(MODE == kSum) {
+                  res = A(0) + to_acc(ev[k]);
+               } else if(MODE == kLse) {
+                  A m = ninf, sacc = A(0);
+                  lse_push(m, sacc, to_acc(ev[k]));
+                  res = lse_value(m, sacc);
+               } else {
+                  res = A(0) + to_acc(ev[k]) * exp_acc(to_acc(eo[k]) - to_acc(ew[k]));
+               }
+               er[k] = from_acc< T >(res);
+            }
+            *reinterpret_cast< uint4* >(out + (r0 + row) * p.emb + col) = r;
+         }
+      }
+      src_cur = src_next;
+   }
+}
+
 // Scatter in plan-row order (fanout forward through the source plan): the
 // warp walks its merge-path tile, loads each plan row's table row once (the
 // next row's load is issued before the current row's stores) and stores it to
@@ -443,6 +536,84 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
       }
       __syncwarp();
    }
+}
+
+// k_scatter_rows with packed rows: the lane groups store the current row to
+// 32 / L destinations per instruction.
+template < typename T >
+__global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
+{
+   constexpr int VN = 16 / (int)sizeof(T);
+   __shared__ int32_t s_gidx[kWarps][kStage];
+   __shared__ int32_t s_rend[kWarps][kStage];
+   const int wib = threadIdx.x >> 5;
+   const int64_t tile = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+   if(tile >= p.num_tiles) return;
+   const int lane = threadIdx.x & 31;
+   const int L = p.lanes;
+   const int RPI = 32 / L;  // destinations per store instruction
+   const int sub = lane / L;
+   const int64_t col = (int64_t)(lane - sub * L) * VN;
+   int32_t* sg = s_gidx[wib];
+   int32_t* sr = s_rend[wib];
+   const int r_begin = p.tile_row[tile];
+   const int j_begin = p.tile_edge[tile];
+   const int r_end = p.tile_row[tile + 1];
+   const int j_end = p.tile_edge[tile + 1];
+   if(j_begin == j_end) return;
+   const T* table = static_cast< const T* >(p.table);
+   T* out = static_cast< T* >(p.out);
+   int gbase = j_begin, gcount = 0;
+   int rbase = r_begin, rcount = 0;
+   auto row_end = [&](int R) __attribute__((always_inline)) -> int {
+      if(R >= r_end) return j_end;
+      if(R - rbase >= rcount) {
+         __syncwarp();
+         rbase = R;
+         rcount = (r_end - R) < kStage ? (r_end - R) : kStage;
+         for(int i = lane; i < rcount; i += 32) sr[i] = p.row_ptr[R + 1 + i];
+         __syncwarp();
+      }
+      const int e = sr[R - rbase];
+      return e < j_end ? e : j_end;
+   };
+   int R = r_begin;
+   int j = j_begin;
+   int e_end = row_end(R);
+   while(e_end <= j) {  // rows that end before the tile's first edge (empty here)
+      ++R;
+      e_end = row_end(R);
+   }
+   uint4 cur = ldg16(table + (int64_t)R * p.emb + col);
+   while(j < j_end) {
+      int Rn = R + 1;
+      int e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
+      while(Rn <= r_end && e_next <= e_end) {
+         ++Rn;
+         e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
+      }
+      const bool has_next = e_end < j_end;
+      uint4 nxt = cur;
+      if(has_next) nxt = ldg16(table + (int64_t)Rn * p.emb + col);
+      for(; j < e_end; j += RPI) {
+         const int need = (j + RPI) < e_end ? (j + RPI) : e_end;
+         if(need > gbase + gcount) {
+            __syncwarp();
+            gbase = j;
+            gcount = (j_end - j) < kStage ? (j_end - j) : kStage;
+            for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j + i];
+            __syncwarp();
+         }
+         const int jj = j + sub;
+         if(jj < e_end) *reinterpret_cast< uint4* >(out + (int64_t)sg[jj - gbase] * p.emb + col) = cur;
+      }
+      j = e_end;
+      if(!has_next) break;
+      cur = nxt;
+      R = Rn;
+      e_end = e_next;
+   }
+   __syncwarp();
 }
 
 // Zero rows of `out` that the cover count marks as uncovered.

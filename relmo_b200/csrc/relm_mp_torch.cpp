@@ -142,8 +142,13 @@ struct PlanEntry {
    relm_mp_plan plan;
    Tensor cover;         // gather-index coverage counts, computed on first use
    int cover_dups = -1;  // -1 unknown, 0 each gather row at most once, 1 repeats
+   int64_t nonempty_rows = -1;  // output rows holding edges, read on first use
 };
 using PlanPtr = std::shared_ptr< PlanEntry >;
+
+// Working set (bytes of gathered rows in use) above which a copy through a
+// destination-ordered plan beats the gather: about 3/4 of the 126 MB L2.
+constexpr int64_t kScatterWorkingSet = 96ll << 20;
 
 class PlanCache {
  public:
@@ -185,13 +190,39 @@ class PlanCache {
       );
       check_status(rc, "plan build");
       auto entry = std::make_shared< PlanEntry >(
-         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1}
+         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1, -1}
       );
       std::lock_guard< std::mutex > lock(mu_);
       ++builds_;
       entries_.push_front(entry);
       while(entries_.size() > capacity_) entries_.pop_back();
       return entry;
+   }
+
+   // The cached plan for the pair, or null (never builds).
+   PlanPtr peek(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
+                int64_t gather_rows)
+   {
+      const IndexKey ok = IndexKey::of(out_index);
+      const IndexKey gk = IndexKey::of(gather_index);
+      std::lock_guard< std::mutex > lock(mu_);
+      for(const auto& e : entries_)
+         if(e->out_key.same(ok) && e->gather_key.same(gk) && e->num_rows == num_rows && e->out_bound == out_bound
+            && e->gather_rows == gather_rows && e->memory.device() == out_index.device())
+            return e;
+      return nullptr;
+   }
+
+   // Output rows of the entry's plan that hold edges (read once per plan).
+   int64_t nonempty_rows(const PlanPtr& e, const Tensor& like)
+   {
+      std::lock_guard< std::mutex > lock(cover_mu_);
+      if(e->nonempty_rows < 0) {
+         int64_t rows = 0;
+         check_status(relm_mp_plan_nonempty_rows(&e->plan, &rows, stream_of(like)), "plan row count");
+         e->nonempty_rows = rows;
+      }
+      return e->nonempty_rows;
    }
 
    // Coverage of the entry's gather index (computed once per plan).
@@ -384,6 +415,26 @@ Tensor fanin_reduce_sum_backward_cuda(const Tensor& grad_out, const Tensor& flat
    const Tensor g = contig(grad_out);
    const Tensor src = contig(flat_src);
    const Tensor dst = contig(dst_idx);
+   // With flat_src repeating no row, grad_rel rows are copies of grad_out rows.
+   // When the grad_out rows in use outgrow L2, each is read once in destination
+   // order through the forward's plan and stored to its message rows (no
+   // re-reads from HBM); below that the per-message-row gather is faster.
+   const int64_t row_bytes = emb * (int64_t)g.element_size();
+   if(g.size(0) * row_bytes > kScatterWorkingSet) {
+      PlanCache& cache = PlanCache::get();
+      if(const PlanPtr fp = cache.peek(dst, src, g.size(0), g.size(0), rel_rows)) {
+         if(cache.nonempty_rows(fp, g) * row_bytes > kScatterWorkingSet) {
+            cache.ensure_cover(fp, g);
+            if(fp->cover_dups == 0) {
+               check_status(relm_mp_plan_scatter_rows(&fp->plan, dt, g.data_ptr(), emb,
+                                                      fp->cover.data_ptr< int32_t >(), grad_rel.data_ptr(),
+                                                      stream_of(g)),
+                            "fanin_reduce_sum_backward");
+               return grad_rel;
+            }
+         }
+      }
+   }
    Tensor keep;
    const relm_mp_plan plan = get_plan(src, dst, rel_rows, rel_rows, g.size(0), "flat_src", "dst_idx", false, &keep);
    return planned_sum(plan, dt, g, emb, grad_rel, RELM_MP_MODE_SUM, "fanin_reduce_sum_backward");

@@ -1,0 +1,101 @@
+"""Kernel-path selection on the GPU: every path an op can take gives the
+reference's result.
+
+* fanin_reduce_sum_backward with a working set above L2 and a cached forward
+  plan copies grad rows through the forward's destination-ordered plan; without
+  the forward (no cached plan), or with repeated message rows, it reduces over
+  the message-row plan. All three are checked against the index formula
+  (copies bit-exact, sums within 1e-5 relative / 1e-6 absolute plus 1e-5 of the
+  row's sum of |terms|).
+* Packed row shapes (rows of 16..256 bytes, several rows per warp load) and the
+  one-row-per-load shapes around them, for every storage type.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from relmo_b200.ops import mp
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _load_library():
+    assert mp.available(), "relm_mp library not loadable"
+
+
+def _big_fanin(seed=0, rows=1 << 20, edges=1 << 22, emb=32):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    dst = torch.randint(0, rows, (edges,), device="cuda", generator=g)
+    flat_src = torch.randperm(edges, device="cuda", generator=g)
+    grad = torch.randn(rows, emb, device="cuda", generator=g)
+    return dst, flat_src, grad
+
+
+def test_sum_backward_scatter_path_after_forward():
+    ops = torch.ops.relm_mp
+    dst, flat_src, grad = _big_fanin()
+    rel = torch.randn(flat_src.numel(), grad.size(1), device="cuda")
+    mp.clear_plan_cache()
+    cold = ops.fanin_reduce_sum_backward(grad, flat_src, dst, rel.size(0))  # no forward plan: gather path
+    ops.fanin_reduce(rel, flat_src, dst, grad.size(0), 0)  # caches the destination-ordered plan
+    warm = ops.fanin_reduce_sum_backward(grad, flat_src, dst, rel.size(0))
+    expect = torch.empty_like(rel)
+    expect[flat_src] = grad[dst]
+    assert torch.equal(cold, expect)
+    assert torch.equal(warm, expect)
+
+
+def test_sum_backward_repeated_message_rows_reduce():
+    ops = torch.ops.relm_mp
+    dst, _, grad = _big_fanin(seed=1)
+    rel_rows = dst.numel() // 2
+    flat_src = torch.randint(0, rel_rows, dst.shape, device="cuda")
+    rel = torch.randn(rel_rows, grad.size(1), device="cuda")
+    mp.clear_plan_cache()
+    ops.fanin_reduce(rel, flat_src, dst, grad.size(0), 0)
+    got = ops.fanin_reduce_sum_backward(grad, flat_src, dst, rel_rows)
+    terms = grad.index_select(0, dst)
+    expect = torch.zeros_like(rel).index_add_(0, flat_src, terms)
+    row_abs = torch.zeros_like(rel).index_add_(0, flat_src, terms.abs())
+    assert bool(((got - expect).abs() <= 1e-6 + 1e-5 * expect.abs() + 1e-5 * row_abs).all())
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16, torch.float64])
+@pytest.mark.parametrize("row_bytes", [16, 32, 48, 64, 128, 256, 272, 512])
+def test_row_map_and_scatter_shapes(dtype, row_bytes):
+    """Each gathered row used once (row map), fan-out through the source plan
+    (scatter), and their logsumexp / backward forms, around the packed sizes."""
+
+    ops = torch.ops.relm_mp
+    es = torch.empty((), dtype=dtype).element_size()
+    emb = row_bytes // es
+    g = torch.Generator(device="cuda").manual_seed(row_bytes)
+    n, e = 3000, 5000
+    x = torch.randn(n, emb, device="cuda", generator=g).to(dtype)
+    src = torch.randint(0, n, (e,), device="cuda", generator=g)
+    flat_dst = torch.randperm(e, device="cuda", generator=g)
+    out = ops.fanout_scatter(x, src, flat_dst, e + 7)
+    expect = torch.zeros(e + 7, emb, device="cuda", dtype=dtype)
+    expect[flat_dst] = x[src]
+    assert torch.equal(out, expect)
+    # one message per destination row: the row map serves fan-in and both backwards
+    rel = torch.randn(e, emb, device="cuda", generator=g).to(dtype)
+    dst = torch.randperm(e + 7, device="cuda", generator=g)[:e]
+    flat_src = torch.randperm(e, device="cuda", generator=g)
+    s = ops.fanin_reduce(rel, flat_src, dst, e + 7, 0)
+    s_expect = torch.zeros(e + 7, emb, device="cuda", dtype=dtype)
+    s_expect[dst] = rel[flat_src]
+    assert torch.equal(s, s_expect)
+    lse = ops.fanin_reduce(rel, flat_src, dst, e + 7, 1)
+    lse_expect = torch.full((e + 7, emb), float("-inf"), device="cuda", dtype=dtype)
+    lse_expect[dst] = rel[flat_src]
+    assert torch.equal(lse, lse_expect)
+    gout = torch.randn(e + 7, emb, device="cuda", generator=g).to(dtype)
+    gb = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, e)
+    gb_expect = torch.zeros(e, emb, device="cuda", dtype=torch.float64)
+    gb_expect[flat_src] = gout[dst].double() * torch.exp(rel[flat_src].double() - lse[dst].double())
+    tol = dict(rtol=1e-2, atol=1e-2) if es == 2 else dict(rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(gb.double(), gb_expect, **tol)
