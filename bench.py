@@ -127,6 +127,23 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
+    def settle(self, step, max_seconds: float = 3.0, samples: int = 2) -> None:
+        """Run untimed steps until the sampler has recorded a few samples, so the
+        samples taken around the (possibly short) timed region are under load."""
+
+        if self.proc is None:
+            return
+        t0 = time.perf_counter()
+        while time.perf_counter() - t0 < max_seconds:
+            step()
+            torch.cuda.synchronize()
+            self.fh.flush()
+            try:
+                if len(self.path.read_text().splitlines()) >= samples:
+                    return
+            except OSError:
+                return
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
@@ -430,9 +447,12 @@ def main() -> int:
     for _ in range(max(args.warmup, 3)):
         step()
     sampler = ClockSampler(device.index if world == 1 else local_rank)
+    sampler.start()
+    sampler.settle(step)
+    if world > 1:  # every rank ran a rank-local number of settle steps; line them up
+        barrier()
     launches0 = capi.lib().relm_mp_kernel_launches()
     barrier()
-    sampler.start()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     ev0.record(stream)
     for _ in range(args.steps):

@@ -221,10 +221,14 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
 RELM_MP_API size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, int64_t emb,
                                          relm_mp_dtype dtype, int mode);
 
-/* Coverage of the plan's gather index over [0, gather_rows): cover[g] = number
- * of edges whose gather row is g (device int32 [gather_rows]); *has_dups = 1
- * when some row is covered more than once. Synchronizes `stream` once. */
-RELM_MP_API int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has_dups,
+/* 32-bit words of a cover bitmap over `rows` rows. */
+static inline size_t relm_mp_cover_words(int64_t rows) { return rows > 0 ? (size_t)((rows + 31) / 32) : 1u; }
+
+/* Coverage of the plan's gather index over [0, gather_rows): bit g of the
+ * bitmap (word g / 32, bit g % 32; device uint32 [relm_mp_cover_words(gather_rows)])
+ * is set when some edge gathers row g; *has_dups = 1 when some row is gathered
+ * more than once. Synchronizes `stream` once. */
+RELM_MP_API int relm_mp_plan_gather_cover(const relm_mp_plan* plan, uint32_t* cover, int* has_dups,
                                           void* stream);
 /* Number of the plan's output rows that hold at least one edge (counted by
  * the plan build on the device). Synchronizes `stream` once. No counterpart in
@@ -235,7 +239,7 @@ RELM_MP_API int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* ro
  * out rows `cover` marks as uncovered. fanout forward through the source plan
  * (plan rows = x rows, gather index = flat_dst): every x row is read once. */
 RELM_MP_API int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
-                                          int64_t emb, const int32_t* cover, void* out, void* stream);
+                                          int64_t emb, const uint32_t* cover, void* out, void* stream);
 /* out[r] = table[gidx[last edge of r]] or 0 for rows without edges (fanout forward). */
 RELM_MP_API int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
                              int64_t emb, void* out, void* stream);

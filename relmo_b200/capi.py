@@ -298,11 +298,12 @@ class PlanHandle:
 
 
     def gather_cover(self):
-        """Coverage count of every gather row (int32 device tensor) and whether
-        any gather row is used more than once."""
+        """Coverage bitmap of the gather rows (int32 device tensor of 32-row
+        words) and whether any gather row is used more than once."""
 
         torch = _torch()
-        cover = torch.empty(max(int(self.plan.gather_rows), 1), dtype=torch.int32, device=self.device)
+        words = max((int(self.plan.gather_rows) + 31) // 32, 1)
+        cover = torch.empty(words, dtype=torch.int32, device=self.device)  # bitmap, 32 rows per word
         dups = ctypes.c_int(0)
         check(lib().relm_mp_plan_gather_cover(ctypes.byref(self.plan), _ptr(cover), ctypes.byref(dups),
                                               _stream(self.device)))

@@ -41,13 +41,18 @@ __global__ void k_fill_u16(unsigned short* out, int64_t n, unsigned short v)
 
 bool aligned(const void* p, int bytes) { return ((uintptr_t)p % (uintptr_t)bytes) == 0; }
 
-// cover[g] += 1 for the gather row g of every edge; *dups = 1 once a row is hit twice.
-__global__ void k_cover(const int32_t* __restrict__ gidx, int64_t n, int32_t* __restrict__ cover,
+// Sets bit g of the cover bitmap for the gather row g of every edge; *dups = 1
+// once a row is hit twice. One bit per row keeps the bitmap in L2 (2 MB for
+// 2^24 rows), where the atomics resolve.
+__global__ void k_cover(const int32_t* __restrict__ gidx, int64_t n, uint32_t* __restrict__ cover,
                         int32_t* __restrict__ dups)
 {
    bool dup = false;
-   for(int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
-      dup |= atomicAdd(&cover[gidx[j]], 1) > 0;
+   for(int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x) {
+      const uint32_t g = (uint32_t)gidx[j];
+      const uint32_t bit = 1u << (g & 31u);
+      dup |= (atomicOr(&cover[g >> 5], bit) & bit) != 0u;
+   }
    if(__syncthreads_or(dup) && threadIdx.x == 0 && *((volatile int32_t*)dups) == 0) *dups = 1;
 }
 
@@ -133,7 +138,7 @@ Shape choose_reduce_shape(int64_t emb, int es, const void* const* ptrs, int nptr
 
 // Shared-memory pipeline shape: rows of 16-byte multiples with 16-byte aligned
 // tables, in column blocks of up to 1 KB; PB bytes per lane (4..32), B rows per
-// 4 KB stage. Returns pb = 0 when the row does not fit the pipeline.
+// stage of kStreamStageBytes. Returns pb = 0 when the row does not fit the pipeline.
 struct StreamShape {
    int pb;
    int lanes;
@@ -169,7 +174,7 @@ StreamShape choose_stream_shape(int64_t emb, int es, const void* const* ptrs, in
    if(pb == 0 || ((cbw / 16) & (cbw / 16 - 1)) != 0) return s;  // 16-byte chunks per row: a power of two
    s.pb = pb;
    s.lanes = (int)(cbw / pb);
-   const int64_t rows = 4096 / cbw;
+   const int64_t rows = kStreamStageBytes / cbw;
    s.rows_per_stage = (int)(rows > 32 ? 32 : (rows < 1 ? 1 : rows));
    s.block_cols = cbw / es;
    return s;
@@ -275,7 +280,7 @@ int dispatch_gather(relm_mp_dtype dtype, const SegParams& p, const Shape& s, cud
    return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
 }
 
-int dispatch_scatter(relm_mp_dtype dtype, const SegParams& p, const Shape& s, const int32_t* cover, int64_t rows,
+int dispatch_scatter(relm_mp_dtype dtype, const SegParams& p, const Shape& s, const uint32_t* cover, int64_t rows,
                      cudaStream_t st)
 {
    switch(dtype) {
@@ -512,7 +517,7 @@ int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, cons
    return dispatch_gather(dtype, p, s, st);
 }
 
-int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has_dups, void* stream)
+int relm_mp_plan_gather_cover(const relm_mp_plan* plan, uint32_t* cover, int* has_dups, void* stream)
 {
    if(!plan || !cover || !has_dups) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan, cover and has_dups must not be NULL.");
    cudaStream_t st = static_cast< cudaStream_t >(stream);
@@ -520,7 +525,8 @@ int relm_mp_plan_gather_cover(const relm_mp_plan* plan, int32_t* cover, int* has
    // The last int of the cover buffer's allocation is not ours: keep the flag
    // in the plan's own device flags word (index 1), cleared first.
    int32_t* flag = const_cast< int32_t* >(plan->device_flags) + 1;
-   if((rc = check_cuda(cudaMemsetAsync(cover, 0, (size_t)plan->gather_rows * sizeof(int32_t), st), "cover memset")))
+   if((rc = check_cuda(cudaMemsetAsync(cover, 0, relm_mp_cover_words(plan->gather_rows) * sizeof(uint32_t), st),
+                       "cover memset")))
       return rc;
    if((rc = check_cuda(cudaMemsetAsync(flag, 0, sizeof(int32_t), st), "cover flag memset"))) return rc;
    if(plan->num_edges > 0) {
@@ -552,7 +558,7 @@ int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* rows, void* st
 }
 
 int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
-                              const int32_t* cover, void* out, void* stream)
+                              const uint32_t* cover, void* out, void* stream)
 {
    if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
    if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
@@ -600,7 +606,7 @@ size_t fanout_workspace(int64_t num_edges, int64_t x_rows, int64_t out_rows)
 {
    if(num_edges < 0 || x_rows < 0 || out_rows < 0) return 0;
    const size_t src_plan = relm_mp_plan_bytes(num_edges, x_rows);
-   const size_t cover = align_up((size_t)out_rows * sizeof(int32_t));
+   const size_t cover = align_up(relm_mp_cover_words(out_rows) * sizeof(uint32_t));
    const size_t a = relm_mp_plan_scratch_bytes(num_edges, x_rows);
    const size_t b = relm_mp_plan_bytes(num_edges, out_rows) + relm_mp_plan_scratch_bytes(num_edges, out_rows);
    return src_plan + cover + (a > b ? a : b);
@@ -632,7 +638,7 @@ int relm_mp_fanout_scatter(relm_mp_dtype dtype, const void* x_cat, int64_t x_row
    }
    char* ws = static_cast< char* >(workspace);
    const size_t src_plan_bytes = relm_mp_plan_bytes(num_edges, x_rows);
-   int32_t* cover = reinterpret_cast< int32_t* >(ws + src_plan_bytes);
+   uint32_t* cover = reinterpret_cast< uint32_t* >(ws + src_plan_bytes);
    char* rest = ws + src_plan_bytes + align_up((size_t)out_rows * sizeof(int32_t));
    const size_t rest_bytes = workspace_bytes - (size_t)(rest - ws);
    relm_mp_plan plan;

@@ -7,7 +7,10 @@
 // once:
 //   1. k_validate   - bounds of both indices (first offending edge, as the
 //                     reference CPU loop reports it), sortedness of the output
-//                     index, int32 copies of both.
+//                     index and whether it is the identity, int32 copies of
+//                     both. An identity output index (edge e writes row e, the
+//                     message-row index of a fan-in) skips steps 2 and 3:
+//                     k_identity_rows writes row_ptr directly.
 //   2. radix sort   - stable sort of (output row, gathered row) pairs by output
 //                     row, only over the bits num_rows needs (skipped when the
 //                     output index is already non-decreasing).
@@ -34,7 +37,7 @@ struct PlanStats {
    unsigned long long out_bad;     // first edge with an out-of-range output index
    unsigned long long gather_bad;  // first edge with an out-of-range gather index
    unsigned int descents;          // warps that saw out_index[e] > out_index[e+1]
-   unsigned int pad;
+   unsigned int not_identity;      // some out_index[e] != e
 };
 
 __global__ void k_init_stats(PlanStats* st)
@@ -42,7 +45,7 @@ __global__ void k_init_stats(PlanStats* st)
    st->out_bad = ULLONG_MAX;
    st->gather_bad = ULLONG_MAX;
    st->descents = 0;
-   st->pad = 0;
+   st->not_identity = 0;
 }
 
 __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict__ key,
@@ -54,6 +57,7 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
 {
    const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
    bool descent = false;
+   bool moved = false;
    if(e < n) {
       const int64_t k = key[e];
       const int64_t g = gat[e];
@@ -62,11 +66,25 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       key32[e] = (uint32_t)k;
       gat32[e] = (int32_t)g;
       if(e + 1 < n) descent = key[e + 1] < k;
+      moved = k != e;
    }
    // One flag write per block at most, and none once the flag is set: a single
    // counter hit by every warp of an unsorted index serialises at L2.
    if(__syncthreads_or(descent) && threadIdx.x == 0 && *((volatile unsigned*)&st->descents) == 0u)
       atomicExch(&st->descents, 1u);
+   if(__syncthreads_or(moved) && threadIdx.x == 0 && *((volatile unsigned*)&st->not_identity) == 0u)
+      atomicExch(&st->not_identity, 1u);
+}
+
+// Identity output index (out_index[e] == e): row r holds edge r alone for
+// r < num_edges, nothing after; flags[2] (rows with edges) = num_edges.
+__global__ void __launch_bounds__(kThreads) k_identity_rows(int32_t* __restrict__ row_ptr, int64_t num_rows,
+                                                            int64_t num_edges, int32_t* __restrict__ flags)
+{
+   for(int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r <= num_rows;
+       r += (int64_t)gridDim.x * blockDim.x)
+      row_ptr[r] = (int32_t)(r < num_edges ? r : num_edges);
+   if(blockIdx.x == 0 && threadIdx.x == 0) flags[2] = (int32_t)num_edges;
 }
 
 // mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys);
@@ -314,6 +332,19 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
          (long long)(use_gather ? gather_rows : out_bound)
       );
       return fail(RELM_MP_ERR_INDEX_OUT_OF_RANGE, msg);
+   }
+
+   if(host.not_identity == 0) {  // edge e is row e: no sort, no segment scan
+      plan->flags |= RELM_MP_PLAN_SORTED_INPUT;
+      if((rc = check_cuda(cudaMemsetAsync(pl.flags, 0, 4 * sizeof(int32_t), stream), "flags memset"))) return rc;
+      unsigned grid = grid_for(num_rows + 1);
+      if(grid > 148u * 8u) grid = 148u * 8u;
+      k_identity_rows<<< grid, kThreads, 0, stream >>>(pl.row_ptr, num_rows, num_edges, pl.flags);
+      if((rc = check_launch("k_identity_rows"))) return rc;
+      k_partition<<< grid_for(tiles + 1), kThreads, 0, stream >>>(
+         pl.row_ptr, num_rows, num_edges, tiles, plan->tile_items, pl.tile_row, pl.tile_edge
+      );
+      return check_launch("k_partition");
    }
 
    const uint32_t* sorted_keys = sl.key_in;

@@ -52,7 +52,7 @@ int launch_map_shape(const SegParams& p, int mode, cudaStream_t stream)
 }
 
 template < typename T, int VB, int CH >
-int launch_scatter_shape(const SegParams& p, const int32_t* cover, int64_t out_rows, cudaStream_t stream)
+int launch_scatter_shape(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream)
 {
    const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
    k_scatter_rows< T, VB, CH ><<< grid, kThreads, 0, stream >>>(p);
@@ -86,7 +86,7 @@ int launch_map_packed(const SegParams& p, int mode, cudaStream_t stream)
 }
 
 template < typename T >
-int launch_scatter_packed(const SegParams& p, const int32_t* cover, int64_t out_rows, cudaStream_t stream)
+int launch_scatter_packed(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream)
 {
    const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
    k_scatter_rows_packed< T ><<< grid, kThreads, 0, stream >>>(p);
@@ -126,7 +126,7 @@ int launch_row_map(const SegParams& p, int mode, int vb, int chmax, cudaStream_t
 }
 
 template < typename T >
-int launch_scatter_rows(const SegParams& p, const int32_t* cover, int64_t out_rows, int vb, int chmax,
+int launch_scatter_rows(const SegParams& p, const uint32_t* cover, int64_t out_rows, int vb, int chmax,
                         cudaStream_t stream)
 {
    if(chmax == kPackedCh) return launch_scatter_packed< T >(p, cover, out_rows, stream);
@@ -205,7 +205,7 @@ int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegPara
 #define RELM_MP_INSTANTIATE(T)                                                                  \
    namespace relm_mp {                                                                          \
    template int launch_row_map< T >(const SegParams&, int, int, int, cudaStream_t);             \
-   template int launch_scatter_rows< T >(const SegParams&, const int32_t*, int64_t, int, int, cudaStream_t); \
+   template int launch_scatter_rows< T >(const SegParams&, const uint32_t*, int64_t, int, int, cudaStream_t); \
    template int launch_seg_reduce< T >(const SegParams&, int, int, const SegParams&, int, int, int, cudaStream_t); \
    template int launch_seg_stream< T >(const SegParams&, int, int, const SegParams&, int, int, cudaStream_t);     \
    }

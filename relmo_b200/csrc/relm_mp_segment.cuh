@@ -616,9 +616,9 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
    __syncwarp();
 }
 
-// Zero rows of `out` that the cover count marks as uncovered.
+// Zero rows of `out` whose bit in the cover bitmap is clear.
 template < typename T, int VB, int CH >
-__global__ void __launch_bounds__(kThreads) k_zero_uncovered(SegParams p, const int32_t* __restrict__ cover,
+__global__ void __launch_bounds__(kThreads) k_zero_uncovered(SegParams p, const uint32_t* __restrict__ cover,
                                                              int64_t rows)
 {
    using A = typename AccOf< T >::type;
@@ -632,7 +632,7 @@ __global__ void __launch_bounds__(kThreads) k_zero_uncovered(SegParams p, const 
    for(int k = 0; k < VN; ++k) zero[k] = A(0);
    for(int64_t base = warp * 32; base < rows; base += nwarps * 32) {
       const int64_t r = base + lane;
-      const unsigned todo = __ballot_sync(0xffffffffu, r < rows && cover[r] == 0);
+      const unsigned todo = __ballot_sync(0xffffffffu, r < rows && ((cover[base >> 5] >> lane) & 1u) == 0u);
       for(unsigned m = todo; m; m &= m - 1) {
          const int64_t row = base + __ffs(m) - 1;
          for(int cb = 0; cb < p.col_blocks; ++cb) {
@@ -949,8 +949,8 @@ __device__ __forceinline__ void store_chunk(T* p, const typename AccOf< T >::typ
 constexpr int kStreamWarps = 4;
 constexpr int kStreamThreads = kStreamWarps * 32;
 constexpr int kStreamStages = 3;
-constexpr int kStreamStageBytes = 4096;  // per warp, stage and gathered table
-constexpr int kStreamMeta = 192;         // staged gidx / row-end entries per warp
+constexpr int kStreamStageBytes = 2048;  // per warp, stage and gathered table
+constexpr int kStreamMeta = 96;         // staged gidx / row-end entries per warp
 
 __host__ __device__ constexpr int stream_warp_bytes(int tables)
 {
@@ -1147,15 +1147,26 @@ __global__ void __launch_bounds__(kStreamThreads) k_seg_stream(SegParams p)
                         }
                      }
                   }
-                  for(; q < run; ++q) {
-                     A v[VN];
-                     load_chunk< T, PB >(reinterpret_cast< const T* >(src + q * CBW), v);
+                  if(q < run) {  // the last 1..3 edges of the run as one fold (one rescale)
+                     const int rem = run - q;
+                     A v[3][VN];
+#pragma unroll
+                     for(int i = 0; i < 3; ++i) {
+                        if(i < rem) {
+                           load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q + i) * CBW), v[i]);
+                        } else {
+#pragma unroll
+                           for(int x = 0; x < VN; ++x) v[i][x] = (MODE == kSum) ? A(0) : ninf;
+                        }
+                     }
 #pragma unroll
                      for(int x = 0; x < VN; ++x) {
-                        if(MODE == kSum)
-                           acc[x] += v[x];
-                        else
-                           lse_push(acc[x], aux[x], v[x]);
+                        if(MODE == kSum) {
+                           acc[x] += v[0][x] + v[1][x] + v[2][x];
+                        } else {
+                           const A vx[3] = {v[0][x], v[1][x], v[2][x]};
+                           lse_fold< A, 3 >(acc[x], aux[x], vx, rem);
+                        }
                      }
                   }
                }
@@ -1327,7 +1338,7 @@ template < typename T >
 int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int vb, int chmax, int mode,
                       cudaStream_t stream);
 template < typename T >
-int launch_scatter_rows(const SegParams& p, const int32_t* cover, int64_t out_rows, int vb, int chmax,
+int launch_scatter_rows(const SegParams& p, const uint32_t* cover, int64_t out_rows, int vb, int chmax,
                         cudaStream_t stream);
 // Shared-memory pipeline variant (rows of 16-byte multiples, 16-byte aligned):
 // pb = bytes per lane, p.block_cols = column block in elements, p.ch = rows per stage.

@@ -140,7 +140,7 @@ struct PlanEntry {
    int gather_first;
    Tensor memory;  // owns the plan arrays
    relm_mp_plan plan;
-   Tensor cover;         // gather-index coverage counts, computed on first use
+   Tensor cover;         // gather-index coverage bitmap (int32 words), computed on first use
    int cover_dups = -1;  // -1 unknown, 0 each gather row at most once, 1 repeats
    int64_t nonempty_rows = -1;  // output rows holding edges, read on first use
 };
@@ -230,9 +230,10 @@ class PlanCache {
    {
       std::lock_guard< std::mutex > lock(cover_mu_);
       if(e->cover_dups >= 0) return;
-      Tensor cover = at::empty({std::max< int64_t >(e->gather_rows, 1)}, like.options().dtype(at::kInt));
+      Tensor cover = at::empty({(int64_t)relm_mp_cover_words(e->gather_rows)}, like.options().dtype(at::kInt));
       int dups = 0;
-      check_status(relm_mp_plan_gather_cover(&e->plan, cover.data_ptr< int32_t >(), &dups, stream_of(like)),
+      check_status(relm_mp_plan_gather_cover(&e->plan, reinterpret_cast< uint32_t* >(cover.data_ptr< int32_t >()),
+                                             &dups, stream_of(like)),
                    "gather cover");
       e->cover = cover;
       e->cover_dups = dups;
@@ -279,6 +280,11 @@ class PlanCache {
    int64_t builds_ = 0;
 };
 
+const uint32_t* cover_bits(const PlanPtr& e)
+{
+   return reinterpret_cast< const uint32_t* >(e->cover.data_ptr< int32_t >());
+}
+
 relm_mp_plan get_plan(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
                       int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first,
                       Tensor* keep_alive)
@@ -319,7 +325,7 @@ Tensor fanout_scatter_cuda(const Tensor& x_cat, const Tensor& src_global_idx, co
    );
    PlanCache::get().ensure_cover(sp, x);
    if(sp->cover_dups == 0) {
-      check_status(relm_mp_plan_scatter_rows(&sp->plan, dt, x.data_ptr(), emb, sp->cover.data_ptr< int32_t >(),
+      check_status(relm_mp_plan_scatter_rows(&sp->plan, dt, x.data_ptr(), emb, cover_bits(sp),
                                              out.data_ptr(), stream_of(x)),
                    "fanout_scatter");
       return out;
@@ -427,7 +433,7 @@ Tensor fanin_reduce_sum_backward_cuda(const Tensor& grad_out, const Tensor& flat
             cache.ensure_cover(fp, g);
             if(fp->cover_dups == 0) {
                check_status(relm_mp_plan_scatter_rows(&fp->plan, dt, g.data_ptr(), emb,
-                                                      fp->cover.data_ptr< int32_t >(), grad_rel.data_ptr(),
+                                                      cover_bits(fp), grad_rel.data_ptr(),
                                                       stream_of(g)),
                             "fanin_reduce_sum_backward");
                return grad_rel;

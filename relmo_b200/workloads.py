@@ -178,7 +178,7 @@ def algorithmic_bytes(op: str, wl: FanWorkload, elem_bytes: int | None = None) -
 
     s = elem_bytes if elem_bytes is not None else wl.x.element_size()
     d = wl.emb
-    e = wl.num_edges
+    e = wl.num_edges if op.startswith("fanout") else int(wl.flat_src.numel())
     if op == "fanout_fwd":
         ux = int(torch.unique(wl.src).numel())
         return ux * d * s + 16 * e + wl.out_rows * d * s

@@ -99,3 +99,28 @@ def test_row_map_and_scatter_shapes(dtype, row_bytes):
     gb_expect[flat_src] = gout[dst].double() * torch.exp(rel[flat_src].double() - lse[dst].double())
     tol = dict(rtol=1e-2, atol=1e-2) if es == 2 else dict(rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(gb.double(), gb_expect, **tol)
+
+
+@pytest.mark.parametrize("extra_rows", [0, 100])
+def test_identity_message_index_plans(extra_rows):
+    """flat_src = arange (the usual message-row index) builds its plan without a
+    sort or segment scan; message rows past the edges get zero gradient."""
+
+    ops = torch.ops.relm_mp
+    g = torch.Generator(device="cuda").manual_seed(7)
+    e, n, d = 70000, 3000, 24
+    rel_rows = e + extra_rows
+    rel = torch.randn(rel_rows, d, device="cuda", generator=g)
+    flat_src = torch.arange(e, device="cuda")
+    dst = torch.randint(0, n, (e,), device="cuda", generator=g)
+    gout = torch.randn(n, d, device="cuda", generator=g)
+    mp.clear_plan_cache()
+    gs = ops.fanin_reduce_sum_backward(gout, flat_src, dst, rel_rows)
+    expect = torch.zeros(rel_rows, d, device="cuda")
+    expect[:e] = gout[dst]
+    assert torch.equal(gs, expect)
+    lse = ops.fanin_reduce(rel, flat_src, dst, n, 1)
+    gl = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel_rows)
+    expect_l = torch.zeros(rel_rows, d, device="cuda", dtype=torch.float64)
+    expect_l[:e] = gout[dst].double() * torch.exp(rel[:e].double() - lse[dst].double())
+    torch.testing.assert_close(gl.double(), expect_l, rtol=1e-5, atol=1e-6)
