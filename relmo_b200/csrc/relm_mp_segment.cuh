@@ -366,11 +366,15 @@ __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret
 
 // Row map with packed rows; same results as k_row_map.
 template < typename T, int MODE >
-__global__ void __launch_bounds__(kThreads, (MODE == kLseBwd || MODE == kLse) ? 3 : 4) k_row_map_packed(SegParams p)
+__global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) || MODE == kLse) ? 3 : 4)
+   k_row_map_packed(SegParams p)
 {
    using A = typename AccOf< T >::type;
    constexpr int VN = 16 / (int)sizeof(T);
-   constexpr int U = (MODE == kLseBwd) ? 2 : 4;  // row loads in flight per lane group (x3 for kLseBwd)
+   // Row loads in flight per lane group (x3 for kLseBwd). Occupancy pays more
+   // than deeper unrolling here (measured): 2-byte types hold 8 values per
+   // vector, so their logsumexp backward keeps one row set in flight.
+   constexpr int U = (MODE == kLseBwd && sizeof(T) == 2) ? 1 : 2;
    constexpr int UL = (MODE == kLseBwd) ? U : 1;
    if(MODE != kCopyLast && *p.has_dups) return;
    const int lane = threadIdx.x & 31;
@@ -895,6 +899,11 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem)
    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
 }
+// Same, with the destination as a shared-window address.
+__device__ __forceinline__ void cp_async16_s(unsigned s, const void* gmem)
+{
+   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template < int N >
 __device__ __forceinline__ void cp_async_wait()
@@ -969,7 +978,7 @@ __host__ __device__ constexpr int stream_warp_bytes(int tables)
 // that began in an earlier tile go out as head partials, the row still open at
 // the end as the tail partial (combined by k_fixup in tile order).
 template < typename T, int PB, int MODE >
-__global__ void __launch_bounds__(kStreamThreads) k_seg_stream(SegParams p)
+__global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
 {
    using A = typename AccOf< T >::type;
    constexpr int VN = PB / (int)sizeof(T);
@@ -1022,7 +1031,16 @@ __global__ void __launch_bounds__(kStreamThreads) k_seg_stream(SegParams p)
       };
       // Copies batch k (rows j_begin + k*B ...) into stage k % kStreamStages.
       // Lane l copies 16-byte chunk (l mod chunks) of rows l / chunks, + 32 / chunks, ...
-      // (chunks is a power of two; wider rows give a lane several chunks).
+      // (chunks is a power of two; wider rows give a lane several chunks). With
+      // chunks <= 32 a lane's copies of one batch are 512 bytes apart in shared
+      // memory, and its source offsets are 32-bit row ids times the row size.
+      const int cl = lane & (chunks - 1);
+      const int b_first = chunks <= 32 ? lane / chunks : 0;
+      const int rpi = chunks <= 32 ? 32 / chunks : 1;
+      const unsigned s_lane = (unsigned)__cvta_generic_to_shared(wbase) + (unsigned)(b_first * CBW + cl * 16);
+      const char* g_lane = table + cbyte + cl * 16;
+      const char* g2_lane = (NT == 2) ? table2 + cbyte + cl * 16 : nullptr;
+      const unsigned rbytes = (unsigned)row_bytes;
       auto issue = [&](int k) __attribute__((always_inline)) {
          if(k < nbatches) {
             const int j0 = j_begin + k * B;
@@ -1037,12 +1055,11 @@ __global__ void __launch_bounds__(kStreamThreads) k_seg_stream(SegParams p)
             unsigned char* st = wbase + (k % kStreamStages) * kStreamStageBytes;
             const int32_t* sgb = sg + (j0 - gbase);
             if(chunks <= 32) {
-               const int c = lane & (chunks - 1);
-               const int rpi = 32 / chunks;
-               for(int b = lane / chunks; b < nb; b += rpi) {
-                  const int64_t off = (int64_t)sgb[b] * row_bytes + cbyte + c * 16;
-                  cp_async16(st + b * CBW + c * 16, table + off);
-                  if(NT == 2) cp_async16(st + kStreamStages * kStreamStageBytes + b * CBW + c * 16, table2 + off);
+               unsigned sa = s_lane + (unsigned)((k % kStreamStages) * kStreamStageBytes);
+               for(int b = b_first; b < nb; b += rpi, sa += 512u) {
+                  const uint64_t off = (uint64_t)(unsigned)sgb[b] * rbytes;
+                  cp_async16_s(sa, g_lane + off);
+                  if(NT == 2) cp_async16_s(sa + (unsigned)(kStreamStages * kStreamStageBytes), g2_lane + off);
                }
             } else {
                for(int b = 0; b < nb; ++b) {
