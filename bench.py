@@ -487,7 +487,9 @@ def main() -> int:
     peaks = measured_peaks()
     dominant = max(per_op, key=lambda k: per_op[k]["ms"])
     achieved = per_op[dominant]["gbs"]
-    traffic = ncu_traffic().get(args.workload, {}).get(dominant)
+    # ncu traffic figures are per workload and storage type (fp32 under the bare workload name)
+    traffic_key = args.workload if dtype == torch.float32 else f"{args.workload}:{args.dtype}"
+    traffic = ncu_traffic().get(traffic_key, {}).get(dominant)
     roofline = {
         "bound": "hbm", "kernel": dominant, "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
         "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": traffic,

@@ -957,8 +957,8 @@ __device__ __forceinline__ void store_chunk(T* p, const typename AccOf< T >::typ
 
 constexpr int kStreamWarps = 4;
 constexpr int kStreamThreads = kStreamWarps * 32;
-constexpr int kStreamStages = 3;
-constexpr int kStreamStageBytes = 2048;  // per warp, stage and gathered table
+constexpr int kStreamStages = 2;
+constexpr int kStreamStageBytes = 4096;  // per warp, stage and gathered table
 constexpr int kStreamMeta = 96;         // staged gidx / row-end entries per warp
 
 __host__ __device__ constexpr int stream_warp_bytes(int tables)
