@@ -15,7 +15,12 @@ Activations are resolved by name ("mish", "relu", "gelu", "silu", "tanh"), the
 names relmo passes to torch_geometric's ``activation_resolver``.
 
 These blocks are dense contractions run by cuBLAS through torch; they are not
-part of the accelerated fan-out / fan-in path.
+part of the accelerated fan-out / fan-in path. ``Linear`` is ``nn.Linear``
+(same parameters, same results) whose backward, for bf16/fp16 gradients,
+takes the bias gradient as a matrix-vector product with a ones vector:
+torch's column-sum reduction of a tall [rows, out] bf16 gradient ran at well
+under a tenth of HBM bandwidth and was a third of the GPU time of a
+decentralized train step (cfg4: 2.14 -> 1.89 s per step).
 """
 
 from __future__ import annotations
@@ -24,6 +29,7 @@ import itertools
 from typing import Callable, Iterable
 
 import torch
+import torch.nn.functional as F
 from torch import nn
 
 _ACTIVATIONS: dict[str, Callable[[], nn.Module]] = {
@@ -35,6 +41,42 @@ _ACTIVATIONS: dict[str, Callable[[], nn.Module]] = {
     "tanh": nn.Tanh,
     "elu": nn.ELU,
 }
+
+
+class _LinearFn(torch.autograd.Function):
+    """y = x W^T + b with the bias gradient as ones^T @ grad (a GEMV)."""
+
+    @staticmethod
+    @torch.amp.custom_fwd(device_type="cuda")
+    def forward(ctx, x, weight, bias):
+        ctx.save_for_backward(x, weight)
+        ctx.has_bias = bias is not None
+        return F.linear(x, weight, bias)
+
+    @staticmethod
+    @torch.amp.custom_bwd(device_type="cuda")
+    def backward(ctx, grad):
+        x, weight = ctx.saved_tensors
+        g2 = grad.reshape(-1, grad.size(-1))
+        gx = gw = gb = None
+        if ctx.needs_input_grad[0]:
+            gx = torch.matmul(grad, weight.to(grad.dtype))
+        if ctx.needs_input_grad[1]:
+            gw = g2.t().mm(x.reshape(-1, x.size(-1)).to(g2.dtype))
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            gb = torch.mv(g2.t(), torch.ones(g2.size(0), device=g2.device, dtype=g2.dtype))
+        return gx, gw, gb
+
+
+class Linear(nn.Linear):
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        # Only 2-byte gradients take the GEMV bias path: fp32 column sums are
+        # fast in torch, and the Python autograd node costs launch time that
+        # small fp32 models (launch-bound) notice.
+        low = x.dtype in (torch.bfloat16, torch.float16) or torch.is_autocast_enabled(x.device.type)
+        if low and self.bias is not None:
+            return _LinearFn.apply(x, self.weight, self.bias)
+        return F.linear(x, self.weight, self.bias)
 
 
 def activation(name: str | nn.Module | Callable | None) -> nn.Module:
@@ -58,7 +100,7 @@ class MLP(nn.Module):
         layers: list[nn.Module] = []
         for idx, (din, dout) in enumerate(itertools.pairwise(dims)):
             last = idx == len(dims) - 2
-            layers.append(nn.Linear(din, dout, bias=bias_last_layer if last else True))
+            layers.append(Linear(din, dout, bias=bias_last_layer if last else True))
             if not last:
                 layers.append(activation(act))
         self.net = nn.Sequential(*layers)
@@ -71,10 +113,10 @@ class SimpleMLP(nn.Module):
     def __init__(self, in_size: int, embedding_size: int | Iterable[int], out_size: int, act: str = "mish"):
         super().__init__()
         sizes = tuple(embedding_size) if isinstance(embedding_size, Iterable) else (int(embedding_size),)
-        layers: list[nn.Module] = [nn.Linear(in_size, sizes[0]), activation(act)]
+        layers: list[nn.Module] = [Linear(in_size, sizes[0]), activation(act)]
         for a, b in itertools.pairwise(sizes):
-            layers += [nn.Linear(a, b), activation(act)]
-        layers.append(nn.Linear(sizes[-1], out_size))
+            layers += [Linear(a, b), activation(act)]
+        layers.append(Linear(sizes[-1], out_size))
         self.mlp = nn.Sequential(*layers)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
@@ -110,8 +152,8 @@ class FiLM(nn.Module):
 
     def __init__(self, cond_dim: int, feat_dim: int):
         super().__init__()
-        self.to_gamma = nn.Linear(cond_dim, feat_dim)
-        self.to_beta = nn.Linear(cond_dim, feat_dim)
+        self.to_gamma = Linear(cond_dim, feat_dim)
+        self.to_beta = Linear(cond_dim, feat_dim)
 
     def forward(self, h: torch.Tensor, c: torch.Tensor) -> torch.Tensor:
         return self.to_gamma(c) * h + self.to_beta(c)
@@ -122,7 +164,7 @@ class FiLMBlock(nn.Module):
 
     def __init__(self, in_dim: int, out_dim: int, cond_dim: int, act: str = "mish"):
         super().__init__()
-        self.lin = nn.Linear(in_dim, out_dim)
+        self.lin = Linear(in_dim, out_dim)
         self.film = FiLM(cond_dim, out_dim)
         self.act = activation(act)
 
@@ -138,7 +180,7 @@ class FiLMMLP(nn.Module):
         for h in hidden_dims:
             self.blocks.append(FiLMBlock(prev, h, cond_dim, act))
             prev = h
-        self.out = nn.Linear(prev, out_dim)
+        self.out = Linear(prev, out_dim)
 
     def forward(self, x: torch.Tensor, cond: torch.Tensor) -> torch.Tensor:
         h = x
