@@ -240,6 +240,17 @@ RELM_MP_API int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* ro
  * (plan rows = x rows, gather index = flat_dst): every x row is read once. */
 RELM_MP_API int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
                                           int64_t emb, const uint32_t* cover, void* out, void* stream);
+/* Logsumexp backward (mp_ops.cpp:3286-3325) through the FORWARD's plan (output
+ * rows = destination rows, gather index = flat_src), for a flat_src that uses
+ * each message row at most once (cover from relm_mp_plan_gather_cover, no
+ * repeats): grad_rel[m] = grad_out[d] * exp(rel[m] - lse_out[d]) for every edge
+ * (d, m), 0 for message rows no edge uses. Reads each destination row's
+ * grad_out / lse_out once instead of once per message; rows of 16..256 bytes
+ * (a power of two times 16) with 16-byte aligned tables, else UNSUPPORTED. */
+RELM_MP_API int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtype,
+                                                        const void* grad_out, const void* lse_out,
+                                                        const void* rel, int64_t emb, const uint32_t* cover,
+                                                        void* grad_rel, void* stream);
 /* out[r] = table[gidx[last edge of r]] or 0 for rows without edges (fanout forward). */
 RELM_MP_API int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
                              int64_t emb, void* out, void* stream);

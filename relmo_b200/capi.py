@@ -80,6 +80,7 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
     "relm_mp_plan_gather_cover": (_INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), _P]),
     "relm_mp_plan_nonempty_rows": (_INT, [_PLANP, ctypes.POINTER(_I64), _P]),
+    "relm_mp_plan_scatter_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_scatter_rows": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
     "relm_mp_plan_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _SZ, _P]),

@@ -574,6 +574,35 @@ int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, con
    return dispatch_scatter(dtype, p, s, cover, plan->gather_rows, st);
 }
 
+int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* grad_out,
+                                            const void* lse_out, const void* rel, int64_t emb, const uint32_t* cover,
+                                            void* grad_rel, void* stream)
+{
+   if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
+   if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
+   if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   if(plan->gather_rows == 0 || emb == 0) return RELM_MP_OK;
+   if(plan->num_edges == 0) return fill_rows(dtype, grad_rel, plan->gather_rows * emb, false, st);
+   const void* ptrs[4] = {grad_out, lse_out, rel, grad_rel};
+   const Shape s = choose_map_shape(emb, (int)dtype_size(dtype), ptrs, 4);
+   if(s.chmax != kPackedCh)
+      return fail(RELM_MP_ERR_UNSUPPORTED, "destination-ordered logsumexp backward needs rows of 16..256 bytes "
+                                           "(a power of two times 16) with 16-byte aligned tables.");
+   SegParams p = base_params(plan, emb, s);
+   p.table = grad_out;
+   p.table2 = lse_out;
+   p.own = rel;
+   p.out = grad_rel;
+   switch(dtype) {
+      case RELM_MP_FLOAT32: return launch_scatter_lse_bwd< float >(p, cover, plan->gather_rows, st);
+      case RELM_MP_FLOAT64: return launch_scatter_lse_bwd< double >(p, cover, plan->gather_rows, st);
+      case RELM_MP_BFLOAT16: return launch_scatter_lse_bwd< __nv_bfloat16 >(p, cover, plan->gather_rows, st);
+      case RELM_MP_FLOAT16: return launch_scatter_lse_bwd< __half >(p, cover, plan->gather_rows, st);
+   }
+   return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
 int relm_mp_plan_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int mode, const void* table, int64_t emb,
                         void* out, void* scratch, size_t scratch_bytes, void* stream)
 {

@@ -100,6 +100,21 @@ int launch_scatter_packed(const SegParams& p, const uint32_t* cover, int64_t out
    return check_launch("k_zero_uncovered");
 }
 
+template < typename T >
+int launch_scatter_lse_bwd(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream)
+{
+   const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
+   k_scatter_lse_bwd_packed< T ><<< grid, kThreads, 0, stream >>>(p);
+   int rc = check_launch("k_scatter_lse_bwd_packed");
+   if(rc) return rc;
+   int64_t blocks = (out_rows + kThreads - 1) / kThreads;
+   const int64_t cap = (int64_t)148 * 8;
+   if(blocks > cap) blocks = cap;
+   if(blocks < 1) blocks = 1;
+   k_zero_uncovered< T, 16, 1 ><<< (unsigned)blocks, kThreads, 0, stream >>>(p, cover, out_rows);
+   return check_launch("k_zero_uncovered");
+}
+
 // VB choices per storage type: the element size (scalar path) and 16 bytes are
 // available with 1 or 4 chunks per lane; intermediate widths with 1 chunk.
 #define RELM_MP_SHAPE_DISPATCH(T, FN, ...)                                        \
@@ -206,6 +221,7 @@ int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegPara
    namespace relm_mp {                                                                          \
    template int launch_row_map< T >(const SegParams&, int, int, int, cudaStream_t);             \
    template int launch_scatter_rows< T >(const SegParams&, const uint32_t*, int64_t, int, int, cudaStream_t); \
+   template int launch_scatter_lse_bwd< T >(const SegParams&, const uint32_t*, int64_t, cudaStream_t);        \
    template int launch_seg_reduce< T >(const SegParams&, int, int, const SegParams&, int, int, int, cudaStream_t); \
    template int launch_seg_stream< T >(const SegParams&, int, int, const SegParams&, int, int, cudaStream_t);     \
    }

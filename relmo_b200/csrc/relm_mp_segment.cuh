@@ -620,6 +620,116 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
    __syncwarp();
 }
 
+// Logsumexp backward in destination order, for message rows used at most
+// once (packed rows): walks the forward's plan (rows = destination rows,
+// gidx = message rows); each destination row's grad_out and lse rows are read
+// once, and every message row m of it gets
+// grad_rel[m] = grad_out[d] * exp(rel[m] - lse[d]) (the row-map expression,
+// bit for bit). Two store groups of 32 / L message rows are loaded per step.
+template < typename T >
+__global__ void __launch_bounds__(kThreads) k_scatter_lse_bwd_packed(SegParams p)
+{
+   using A = typename AccOf< T >::type;
+   constexpr int VN = 16 / (int)sizeof(T);
+   __shared__ int32_t s_gidx[kWarps][kStage];
+   __shared__ int32_t s_rend[kWarps][kStage];
+   const int wib = threadIdx.x >> 5;
+   const int64_t tile = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+   if(tile >= p.num_tiles) return;
+   const int lane = threadIdx.x & 31;
+   const int L = p.lanes;
+   const int RPI = 32 / L;
+   const int sub = lane / L;
+   const int64_t col = (int64_t)(lane - sub * L) * VN;
+   int32_t* sg = s_gidx[wib];
+   int32_t* sr = s_rend[wib];
+   const int r_begin = p.tile_row[tile];
+   const int j_begin = p.tile_edge[tile];
+   const int r_end = p.tile_row[tile + 1];
+   const int j_end = p.tile_edge[tile + 1];
+   if(j_begin == j_end) return;
+   const T* gout = static_cast< const T* >(p.table);   // grad_out, by destination row
+   const T* lse = static_cast< const T* >(p.table2);   // forward output, by destination row
+   const T* rel = static_cast< const T* >(p.own);      // messages, by message row
+   T* out = static_cast< T* >(p.out);                  // grad_rel, by message row
+   int gbase = j_begin, gcount = 0;
+   int rbase = r_begin, rcount = 0;
+   auto row_end = [&](int R) __attribute__((always_inline)) -> int {
+      if(R >= r_end) return j_end;
+      if(R - rbase >= rcount) {
+         __syncwarp();
+         rbase = R;
+         rcount = (r_end - R) < kStage ? (r_end - R) : kStage;
+         for(int i = lane; i < rcount; i += 32) sr[i] = p.row_ptr[R + 1 + i];
+         __syncwarp();
+      }
+      const int e = sr[R - rbase];
+      return e < j_end ? e : j_end;
+   };
+   int R = r_begin;
+   int j = j_begin;
+   int e_end = row_end(R);
+   while(e_end <= j) {
+      ++R;
+      e_end = row_end(R);
+   }
+   uint4 cg = ldg16(gout + (int64_t)R * p.emb + col);
+   uint4 co = ldg16(lse + (int64_t)R * p.emb + col);
+   while(j < j_end) {
+      int Rn = R + 1;
+      int e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
+      while(Rn <= r_end && e_next <= e_end) {
+         ++Rn;
+         e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
+      }
+      const bool has_next = e_end < j_end;
+      uint4 ng = cg, no = co;
+      if(has_next) {
+         ng = ldg16(gout + (int64_t)Rn * p.emb + col);
+         no = ldg16(lse + (int64_t)Rn * p.emb + col);
+      }
+      const T* eg = reinterpret_cast< const T* >(&cg);
+      const T* eo = reinterpret_cast< const T* >(&co);
+      for(; j < e_end; j += 2 * RPI) {
+         const int need = (j + 2 * RPI) < e_end ? (j + 2 * RPI) : e_end;
+         if(need > gbase + gcount) {
+            __syncwarp();
+            gbase = j;
+            gcount = (j_end - j) < kStage ? (j_end - j) : kStage;
+            for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j + i];
+            __syncwarp();
+         }
+         int64_t m[2];
+         uint4 v[2];
+#pragma unroll
+         for(int h = 0; h < 2; ++h) {
+            const int jj = j + h * RPI + sub;
+            m[h] = jj < e_end ? (int64_t)sg[jj - gbase] : -1;
+            v[h] = make_uint4(0u, 0u, 0u, 0u);
+            if(m[h] >= 0) v[h] = ldg16(rel + m[h] * p.emb + col);
+         }
+#pragma unroll
+         for(int h = 0; h < 2; ++h) {
+            if(m[h] < 0) continue;
+            const T* ev = reinterpret_cast< const T* >(&v[h]);
+            uint4 r;
+            T* er = reinterpret_cast< T* >(&r);
+#pragma unroll
+            for(int k = 0; k < VN; ++k)
+               er[k] = from_acc< T >(A(0) + to_acc(eg[k]) * exp_acc(to_acc(ev[k]) - to_acc(eo[k])));
+            *reinterpret_cast< uint4* >(out + m[h] * p.emb + col) = r;
+         }
+      }
+      j = e_end;
+      if(!has_next) break;
+      cg = ng;
+      co = no;
+      R = Rn;
+      e_end = e_next;
+   }
+   __syncwarp();
+}
+
 // Zero rows of `out` whose bit in the cover bitmap is clear.
 template < typename T, int VB, int CH >
 __global__ void __launch_bounds__(kThreads) k_zero_uncovered(SegParams p, const uint32_t* __restrict__ cover,
@@ -1354,6 +1464,8 @@ int launch_row_map(const SegParams& p, int mode, int vb, int chmax, cudaStream_t
 template < typename T >
 int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegParams& p, int vb, int chmax, int mode,
                       cudaStream_t stream);
+template < typename T >
+int launch_scatter_lse_bwd(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream);
 template < typename T >
 int launch_scatter_rows(const SegParams& p, const uint32_t* cover, int64_t out_rows, int vb, int chmax,
                         cudaStream_t stream);

@@ -478,6 +478,28 @@ Tensor fanin_reduce_logsumexp_backward_cuda(const Tensor& grad_out, const Tensor
    const Tensor o = contig(out);
    const Tensor src = contig(flat_src);
    const Tensor dst = contig(dst_idx);
+   // As in the sum backward: with flat_src repeating no row and the grad_out /
+   // out rows in use above the L2 working set, walk the forward's plan in
+   // destination order, reading each destination's grad_out and out rows once.
+   const int64_t row_bytes = emb * (int64_t)g.element_size();
+   if(g.size(0) * row_bytes > kScatterWorkingSet && rel.size(0) == rel_rows) {
+      PlanCache& cache = PlanCache::get();
+      if(const PlanPtr fp = cache.peek(dst, src, g.size(0), g.size(0), rel_rows)) {
+         if(cache.nonempty_rows(fp, g) * row_bytes > kScatterWorkingSet) {
+            cache.ensure_cover(fp, g);
+            if(fp->cover_dups == 0) {
+               const int rc = relm_mp_plan_scatter_logsumexp_backward(
+                  &fp->plan, dt, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb, cover_bits(fp), grad_rel.data_ptr(),
+                  stream_of(g)
+               );
+               if(rc != RELM_MP_ERR_UNSUPPORTED) {  // unsupported row shape: the per-message-row path below
+                  check_status(rc, "fanin_reduce_logsumexp_backward");
+                  return grad_rel;
+               }
+            }
+         }
+      }
+   }
    Tensor keep;
    const int64_t bound = std::min(rel_rows, rel.size(0));
    const relm_mp_plan plan = get_plan(src, dst, rel_rows, bound, g.size(0), "flat_src", "dst_idx", false, &keep);

@@ -124,3 +124,31 @@ def test_identity_message_index_plans(extra_rows):
     expect_l = torch.zeros(rel_rows, d, device="cuda", dtype=torch.float64)
     expect_l[:e] = gout[dst].double() * torch.exp(rel[:e].double() - lse[dst].double())
     torch.testing.assert_close(gl.double(), expect_l, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype,emb", [(torch.float32, 32), (torch.bfloat16, 64)])
+def test_lse_backward_destination_order_path(dtype, emb):
+    """Above the L2 working set, with the forward's plan cached and message rows
+    used once, the logsumexp backward walks the forward's plan in destination
+    order; it must equal the per-message-row path bit for bit."""
+
+    ops = torch.ops.relm_mp
+    g = torch.Generator(device="cuda").manual_seed(11)
+    rows, edges = 1 << 20, 1 << 22
+    dst = torch.randint(0, rows, (edges,), device="cuda", generator=g)
+    flat_src = torch.randperm(edges + 1000, device="cuda", generator=g)[:edges]  # some message rows unused
+    rel = torch.randn(edges + 1000, emb, device="cuda", generator=g).to(dtype)
+    gout = torch.randn(rows, emb, device="cuda", generator=g).to(dtype)
+    mp.clear_plan_cache()
+    lse = ops.fanin_reduce(rel, flat_src, dst, rows, 1)  # caches the destination-ordered plan
+    warm = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel.size(0))
+    mp.clear_plan_cache()
+    cold = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel.size(0))
+    assert torch.equal(warm, cold)
+    used = torch.zeros(rel.size(0), dtype=torch.bool, device="cuda")
+    used[flat_src] = True
+    assert bool((warm[~used] == 0).all())
+    e = torch.arange(0, edges, 9973, device="cuda")
+    expect = gout[dst[e]].double() * torch.exp(rel[flat_src[e]].double() - lse[dst[e]].double())
+    tol = dict(rtol=1e-2, atol=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(warm[flat_src[e]].double(), expect, **tol)
