@@ -219,7 +219,8 @@ def shard_workload(wl: workloads.FanWorkload, rank: int, world: int) -> workload
 
     from relmo_b200 import partition
 
-    sh = partition.shard_by_destination(wl.flat_src, wl.dst, wl.dim_size, rank, world)
+    ranges = partition.balanced_destination_ranges(wl.dst, wl.dim_size, world)
+    sh = partition.shard_by_destination(wl.flat_src, wl.dst, wl.dim_size, rank, world, ranges)
     none = torch.empty(0, dtype=torch.int64, device=wl.dst.device)
     return workloads.FanWorkload(
         wl.name, wl.x[:0], none, none, 0, wl.msgs.index_select(0, sh.rel_rows), sh.flat_src, sh.dst, sh.dim_size,
@@ -519,7 +520,7 @@ def main() -> int:
                 "dst": "zipf(1.3)" if args.workload.startswith("cfg2") else args.workload,
                 "per_rank_batches": 1, "l2": "inputs larger than L2 (no flush needed)",
                 "step": f"plan builds (cache cleared) + {len(op_list)} ops",
-                "parallelism": (f"destination-range partition x{world}, no collective" if partitioned
+                "parallelism": (f"work-balanced destination-range partition x{world}, no collective" if partitioned
                                 else f"independent batches x{world}"),
             },
             "roofline": roofline,

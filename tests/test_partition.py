@@ -32,6 +32,21 @@ def test_destination_ranges_cover_rows():
         partition.destination_ranges(4, 0)
 
 
+def test_balanced_ranges_split_work():
+    wl = _problem()
+    for world in (1, 2, 3, 8):
+        r = partition.balanced_destination_ranges(wl.dst, wl.dim_size, world)
+        assert len(r) == world and r[0][0] == 0 and r[-1][1] == wl.dim_size
+        assert all(a[1] == b[0] for a, b in zip(r, r[1:]))
+        deg = torch.bincount(wl.dst, minlength=wl.dim_size)
+        work = [int(hi - lo + deg[lo:hi].sum()) for lo, hi in r]
+        total = wl.dim_size + wl.dst.numel()
+        # a boundary can only miss its target by the work of one row
+        assert max(work) <= total / world + int(deg.max()) + 1
+    with pytest.raises(ValueError):
+        partition.shard_by_destination(wl.flat_src, wl.dst, wl.dim_size, 0, 2, [(0, 5), (6, wl.dim_size)])
+
+
 def test_shard_rejects_bad_arguments():
     i = torch.arange(4)
     with pytest.raises(ValueError):
@@ -52,11 +67,12 @@ def _full(wl, mode):
     return out.detach(), rel.grad
 
 
-def _sharded(wl, mode, world):
+def _sharded(wl, mode, world, balanced=False):
     outs = []
     grad = torch.zeros_like(wl.msgs)
+    ranges = partition.balanced_destination_ranges(wl.dst, wl.dim_size, world) if balanced else None
     for r in range(world):
-        sh = partition.shard_by_destination(wl.flat_src, wl.dst, wl.dim_size, r, world)
+        sh = partition.shard_by_destination(wl.flat_src, wl.dst, wl.dim_size, r, world, ranges)
         rel = wl.msgs.index_select(0, sh.rel_rows).requires_grad_(True)
         out = mp.fanin_reduce(rel, sh.flat_src, sh.dst, sh.dim_size, mode)
         (out * wl.grad_nodes[sh.row_lo : sh.row_hi]).sum().backward()
@@ -65,12 +81,13 @@ def _sharded(wl, mode, world):
     return partition.gather_output(outs), grad
 
 
+@pytest.mark.parametrize("balanced", [False, True])
 @pytest.mark.parametrize("mode", [0, 1])
 @pytest.mark.parametrize("world", [1, 3, 8])
-def test_partition_equals_full_cpu(mode, world):
+def test_partition_equals_full_cpu(mode, world, balanced):
     wl = _problem()
     out, grad = _full(wl, mode)
-    pout, pgrad = _sharded(wl, mode, world)
+    pout, pgrad = _sharded(wl, mode, world, balanced)
     torch.testing.assert_close(pout, out, rtol=1e-5, atol=1e-6, equal_nan=True)
     torch.testing.assert_close(pgrad, grad, rtol=1e-5, atol=1e-6)
 
@@ -116,7 +133,7 @@ def test_partition_equals_full_gpu(mode):
     assert mp.available()
     wl = _problem(device="cuda")
     out, grad = _full(wl, mode)
-    pout, pgrad = _sharded(wl, mode, 8)
+    pout, pgrad = _sharded(wl, mode, 8, balanced=True)
     if mode == 0:
         row_abs = torch.zeros_like(out).index_add_(0, wl.dst, wl.msgs.abs().index_select(0, wl.flat_src))
         assert bool(((pout - out).abs() <= 1e-6 + 1e-5 * out.abs() + 1e-5 * row_abs).all())
