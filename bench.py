@@ -282,6 +282,36 @@ def time_oracle_port(wl: workloads.FanWorkload, repeats: int = 1, op_list=OPS) -
     return best, sum(op_bytes(wl, op_list).values())
 
 
+MODEL_CPU_STATES = {"cfg3": 32, "cfg4": 8}
+
+
+def model_cpu_baseline(name: str, steps: int = 2, warmup: int = 1, states: int | None = None) -> dict:
+    """Train steps of the RGNN workload on the host cores with relmo's torch
+    formulas for the fan ops (the path relmo takes without its kernels; the
+    reference model itself needs torch_geometric, not installed here), fp32,
+    on a bounded sample of states. Returns states/s and the sample."""
+
+    from relmo_b200 import model_train
+
+    cfg = model_train.CONFIGS[name]
+    n = int(states or MODEL_CPU_STATES[name])
+    torch.manual_seed(0)
+    model = model_train.build_model(cfg.kind, cfg.embedding_size, cfg.num_layers, cfg.aggregation, cfg.arities,
+                                    use_kernels=False)
+    opt = torch.optim.AdamW(model.parameters(), lr=1e-3)
+    batch = cfg.batch(seed=0, device="cpu", states=n)
+    for _ in range(warmup):
+        model_train.train_step(model, opt, [batch])
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        model_train.train_step(model, opt, [batch])
+    dt = (time.perf_counter() - t0) / steps
+    return {"value": round(n / dt, 3), "unit": "states/s", "cores": torch.get_num_threads(), "kind": "port",
+            "states": n,
+            "sample": f"{name} model, {n} states per step (of {cfg.global_states}), fp32, relmo's torch formulas "
+                      f"for the fan ops (PyG-free restatement), {steps} steps after {warmup} warm-up"}
+
+
 def reference_arm(args) -> None:
     """--impl reference: the reference's CPU ops on the host cores."""
 
@@ -290,6 +320,18 @@ def reference_arm(args) -> None:
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
+    if args.workload in ("cfg3", "cfg4"):
+        base = model_cpu_baseline(args.workload, steps=max(args.steps, 1), warmup=args.warmup)
+        line = {
+            "impl": "reference", "metric": MODEL_METRIC, "value": base["value"], "unit": "states/s",
+            "n_gpus": args.gpus, "steps": max(args.steps, 1), "warmup": args.warmup,
+            "ms_per_step": round(base["states"] / base["value"] * 1e3, 3), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": args.workload}, "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "states/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return
     edges = args.cpu_edges
     wl = cpu_sample(args.workload, edges)
     kind = "port"
@@ -642,6 +684,9 @@ def model_main(args, device, rank, world, local_rank) -> int:
                     warmup=args.warmup, e2e=not args.no_e2e)
     clocks = sampler.stop()
     launches = capi.lib().relm_mp_kernel_launches() - launches0
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = model_cpu_baseline(args.workload)
     if rank == 0:
         line = {
             "metric": MODEL_METRIC, "value": r["states_per_s"], "unit": "states/s", "n_gpus": world,
@@ -651,7 +696,7 @@ def model_main(args, device, rank, world, local_rank) -> int:
             "config": {k: r[k] for k in ("workload", "model", "emb", "layers", "aggregation", "global_states",
                                          "per_rank_states", "micro_states", "micro_batches", "parallelism")}
             | {"l2": "activations far larger than L2 (no flush needed)"},
-            "roofline": None, "cpu_baseline": None, "e2e": r.get("e2e"),
+            "roofline": None, "cpu_baseline": cpu, "e2e": r.get("e2e"),
             "gpu_launches": int(r["relm_mp_launches_per_step"] * args.steps),
             "relm_mp_launches_all_phases": int(launches), "clocks": clocks, "loss": r["loss"],
             "loss_finite": r["loss_finite"],
