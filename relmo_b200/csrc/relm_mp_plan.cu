@@ -53,20 +53,45 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
                                                        int64_t key_bound, int64_t gat_bound,
                                                        uint32_t* __restrict__ key32,
                                                        int32_t* __restrict__ gat32,
-                                                       PlanStats* __restrict__ st)
+                                                       PlanStats* __restrict__ st, bool paired)
 {
-   const int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+   const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
    bool descent = false;
    bool moved = false;
-   if(e < n) {
-      const int64_t k = key[e];
-      const int64_t g = gat[e];
+   auto check = [&](int64_t e, int64_t k, int64_t g) __attribute__((always_inline)) {
       if(k < 0 || k >= key_bound) atomicMin(&st->out_bad, (unsigned long long)e);
       if(g < 0 || g >= gat_bound) atomicMin(&st->gather_bad, (unsigned long long)e);
-      key32[e] = (uint32_t)k;
-      gat32[e] = (int32_t)g;
-      if(e + 1 < n) descent = key[e + 1] < k;
-      moved = k != e;
+      moved |= k != e;
+   };
+   if(paired) {
+      // Two edges per thread with 16-byte loads (16-byte aligned indices): twice
+      // the bytes in flight of the one-edge form. Odd n: the last thread takes
+      // the final edge alone.
+      const int64_t pairs = n / 2;
+      if(t < pairs) {
+         const longlong2 kk = __ldg(reinterpret_cast< const longlong2* >(key) + t);
+         const longlong2 gg = __ldg(reinterpret_cast< const longlong2* >(gat) + t);
+         const int64_t e = 2 * t;
+         check(e, kk.x, gg.x);
+         check(e + 1, kk.y, gg.y);
+         reinterpret_cast< uint2* >(key32)[t] = make_uint2((uint32_t)kk.x, (uint32_t)kk.y);
+         reinterpret_cast< int2* >(gat32)[t] = make_int2((int32_t)gg.x, (int32_t)gg.y);
+         descent = kk.y < kk.x || (e + 2 < n && __ldg(key + e + 2) < kk.y);
+      } else if(t == pairs && (n & 1)) {
+         const int64_t e = n - 1;
+         const int64_t k = key[e];
+         const int64_t g = gat[e];
+         check(e, k, g);
+         key32[e] = (uint32_t)k;
+         gat32[e] = (int32_t)g;
+      }
+   } else if(t < n) {
+      const int64_t k = key[t];
+      const int64_t g = gat[t];
+      check(t, k, g);
+      key32[t] = (uint32_t)k;
+      gat32[t] = (int32_t)g;
+      if(t + 1 < n) descent = key[t + 1] < k;
    }
    // One flag write per block at most, and none once the flag is set: a single
    // counter hit by every warp of an unsorted index serialises at L2.
@@ -96,15 +121,36 @@ __global__ void __launch_bounds__(kThreads) k_mark_ends(const uint32_t* __restri
 {
    bool dup = false;
    int ends = 0;
-   for(int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
-      const uint32_t k = keys[e];
-      const bool last = e == n - 1 || keys[e + 1] != k;
+   auto visit = [&](int64_t e, uint32_t k, bool last) __attribute__((always_inline)) {
       if(last) {
          mark[(int64_t)k + 1] = (int32_t)(e + 1);
          ++ends;
       } else {
          dup = true;
       }
+   };
+   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+   int64_t scalar_from = 0;
+   if((reinterpret_cast< uintptr_t >(keys) & 15u) == 0) {
+      // Four keys per 16-byte load (the loop is latency-bound with one 4-byte
+      // load per thread in flight); the next group's first key comes from L1/L2.
+      const int64_t groups = n / 4;
+      for(int64_t g = t0; g < groups; g += stride) {
+         const uint4 q = __ldg(reinterpret_cast< const uint4* >(keys) + g);
+         const int64_t e = g * 4;
+         const bool tail = e + 4 >= n;
+         const uint32_t nx = tail ? 0u : __ldg(keys + e + 4);
+         visit(e, q.x, q.y != q.x);
+         visit(e + 1, q.y, q.z != q.y);
+         visit(e + 2, q.z, q.w != q.z);
+         visit(e + 3, q.w, tail || nx != q.w);
+      }
+      scalar_from = groups * 4;
+   }
+   for(int64_t e = scalar_from + t0; e < n; e += stride) {
+      const uint32_t k = keys[e];
+      visit(e, k, e == n - 1 || keys[e + 1] != k);
    }
    __shared__ int s_ends[kThreads / 32];
 #pragma unroll
@@ -296,8 +342,12 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
    if((rc = check_launch("k_init_stats"))) return rc;
    if(num_edges > 0) {
-      k_validate<<< grid_for(num_edges), kThreads, 0, stream >>>(
-         out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, pl.gidx, sl.stats
+      const bool paired = (reinterpret_cast< uintptr_t >(out_index) & 15u) == 0 &&
+                          (reinterpret_cast< uintptr_t >(gather_index) & 15u) == 0 &&
+                          (reinterpret_cast< uintptr_t >(sl.key_in) & 7u) == 0 &&
+                          (reinterpret_cast< uintptr_t >(pl.gidx) & 7u) == 0;
+      k_validate<<< grid_for(paired ? num_edges / 2 + 1 : num_edges), kThreads, 0, stream >>>(
+         out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, pl.gidx, sl.stats, paired
       );
       if((rc = check_launch("k_validate"))) return rc;
    }

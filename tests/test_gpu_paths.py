@@ -152,3 +152,28 @@ def test_lse_backward_destination_order_path(dtype, emb):
     expect = gout[dst[e]].double() * torch.exp(rel[flat_src[e]].double() - lse[dst[e]].double())
     tol = dict(rtol=1e-2, atol=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-5, atol=1e-6)
     torch.testing.assert_close(warm[flat_src[e]].double(), expect, **tol)
+
+
+@pytest.mark.parametrize("offset", [0, 1])
+@pytest.mark.parametrize("n", [9999, 10000])
+def test_validation_paths_aligned_and_offset_indices(offset, n):
+    """Index validation reads two edges per thread from 16-byte aligned index
+    tensors and one per thread otherwise (a view starting at an odd element);
+    both give the same plans, and the same first offending edge."""
+
+    ops = torch.ops.relm_mp
+    g = torch.Generator(device="cuda").manual_seed(n + offset)
+    base_dst = torch.randint(0, 500, (n + 1,), device="cuda", generator=g)
+    base_src = torch.randperm(n + 1, device="cuda", generator=g)
+    dst, src = base_dst[offset : offset + n], base_src[offset : offset + n] % n
+    rel = torch.randn(n, 8, device="cuda", generator=g)
+    mp.clear_plan_cache()
+    a = ops.fanin_reduce(rel, src, dst, 500, 0)
+    mp.clear_plan_cache()
+    b = ops.fanin_reduce(rel, src.clone(), dst.clone(), 500, 0)
+    assert torch.equal(a, b)
+    bad = dst.clone()
+    bad[n - 2] = 777  # odd or even position depending on n
+    bad[n - 1] = -3
+    with pytest.raises(RuntimeError, match="dst_idx index out of bounds: 777 not in"):
+        ops.fanin_reduce(rel, src, bad, 500, 0)
