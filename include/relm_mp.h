@@ -221,6 +221,21 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
 RELM_MP_API size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, int64_t emb,
                                          relm_mp_dtype dtype, int mode);
 
+/* Index packing of the pack ops (fanout_pack_multi, fanin_pack_multi,
+ * fanout_pack_from_edges, fanin_pack_from_edges; mp_ops.cpp:412-570,
+ * 2511-2773): out[start_k + i] = parts[k].src[i] * parts[k].mul + parts[k].add
+ * for every part k in order (start_k = sum of the earlier parts' len), i.e. the
+ * per-part offset / arity arithmetic and the concatenation of all parts, in
+ * one kernel launch per 64 parts. `parts` is a host array; src and out are
+ * device int64 arrays; parts with len 0 are skipped. */
+typedef struct relm_mp_index_part {
+   const int64_t* src;
+   int64_t len;
+   int64_t mul;
+   int64_t add;
+} relm_mp_index_part;
+RELM_MP_API int relm_mp_pack_index(const relm_mp_index_part* parts, int num_parts, int64_t* out, void* stream);
+
 /* 32-bit words of a cover bitmap over `rows` rows. */
 static inline size_t relm_mp_cover_words(int64_t rows) { return rows > 0 ? (size_t)((rows + 31) / 32) : 1u; }
 

@@ -80,6 +80,7 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
     "relm_mp_plan_gather_cover": (_INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), _P]),
     "relm_mp_plan_nonempty_rows": (_INT, [_PLANP, ctypes.POINTER(_I64), _P]),
+    "relm_mp_pack_index": (_INT, [_P, _INT, _P, _P]),
     "relm_mp_plan_scatter_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_scatter_rows": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
@@ -87,6 +88,29 @@ SIGNATURES: dict[str, tuple] = {
 }
 
 _LIB: ctypes.CDLL | None = None
+
+
+class IndexPart(ctypes.Structure):
+    """relm_mp_index_part: out[start + i] = src[i] * mul + add."""
+
+    _fields_ = [("src", ctypes.c_void_p), ("len", ctypes.c_int64), ("mul", ctypes.c_int64), ("add", ctypes.c_int64)]
+
+
+def pack_index(parts, muls, adds, out=None):
+    """Concatenate index tensors `parts` (int64, one CUDA device) as
+    part * mul + add, in one launch per 64 parts."""
+
+    torch = _torch()
+    parts = [p.contiguous() for p in parts]
+    total = sum(int(p.numel()) for p in parts)
+    device = parts[0].device
+    if out is None:
+        out = torch.empty(total, dtype=torch.int64, device=device)
+    arr = (IndexPart * max(len(parts), 1))()
+    for i, (p, m, a) in enumerate(zip(parts, muls, adds)):
+        arr[i] = IndexPart(_ptr(p), int(p.numel()), int(m), int(a))
+    check(lib().relm_mp_pack_index(ctypes.cast(arr, ctypes.c_void_p), len(parts), _ptr(out), _stream(device)))
+    return out
 
 
 class RelmMpError(RuntimeError):

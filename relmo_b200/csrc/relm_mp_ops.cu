@@ -56,6 +56,36 @@ __global__ void k_cover(const int32_t* __restrict__ gidx, int64_t n, uint32_t* _
    if(__syncthreads_or(dup) && threadIdx.x == 0 && *((volatile int32_t*)dups) == 0) *dups = 1;
 }
 
+// Up to kPackParts index parts per launch, passed by value.
+constexpr int kPackParts = 64;
+struct PackParts {
+   const int64_t* src[kPackParts];
+   int64_t mul[kPackParts];
+   int64_t add[kPackParts];
+   int64_t start[kPackParts + 1];  // output position of each part; start[count] = end
+   int count;
+};
+
+// out[o] = src_k[o - start_k] * mul_k + add_k for the part k holding o; a
+// grid-stride walk over the launch's output range, the part found by binary
+// search over the (<= 64) part starts.
+__global__ void __launch_bounds__(kThreads) k_pack_index(const PackParts pk, int64_t* __restrict__ out)
+{
+   const int64_t lo = pk.start[0];
+   const int64_t hi = pk.start[pk.count];
+   for(int64_t o = lo + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; o < hi; o += (int64_t)gridDim.x * blockDim.x) {
+      int a = 0, b = pk.count - 1;  // last part with start <= o
+      while(a < b) {
+         const int m = (a + b + 1) >> 1;
+         if(pk.start[m] <= o)
+            a = m;
+         else
+            b = m - 1;
+      }
+      out[o] = __ldg(pk.src[a] + (o - pk.start[a])) * pk.mul[a] + pk.add[a];
+   }
+}
+
 struct Shape {
    int vb;
    int chmax;
@@ -515,6 +545,40 @@ int relm_mp_plan_gather_last(const relm_mp_plan* plan, relm_mp_dtype dtype, cons
    p.table = table;
    p.out = out;
    return dispatch_gather(dtype, p, s, st);
+}
+
+int relm_mp_pack_index(const relm_mp_index_part* parts, int num_parts, int64_t* out, void* stream)
+{
+   if(num_parts < 0 || (num_parts > 0 && !parts)) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "parts must not be NULL.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   int64_t start = 0;
+   PackParts pk{};
+   auto flush = [&]() -> int {
+      if(pk.count == 0) return RELM_MP_OK;
+      const int64_t total = pk.start[pk.count];
+      int64_t blocks = (total - pk.start[0] + kThreads - 1) / kThreads;
+      if(blocks > 148 * 16) blocks = 148 * 16;
+      k_pack_index<<< (unsigned)blocks, kThreads, 0, st >>>(pk, out);
+      pk.count = 0;
+      return check_launch("k_pack_index");
+   };
+   for(int k = 0; k < num_parts; ++k) {
+      const relm_mp_index_part& q = parts[k];
+      if(q.len < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "part lengths must be >= 0.");
+      if(q.len == 0) continue;
+      if(!q.src || !out) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "index pointers must not be NULL.");
+      pk.src[pk.count] = q.src;
+      pk.mul[pk.count] = q.mul;
+      pk.add[pk.count] = q.add;
+      pk.start[pk.count] = start;
+      start += q.len;
+      pk.start[pk.count + 1] = start;
+      if(++pk.count == kPackParts) {
+         const int rc = flush();
+         if(rc) return rc;
+      }
+   }
+   return flush();
 }
 
 int relm_mp_plan_gather_cover(const relm_mp_plan* plan, uint32_t* cover, int* has_dups, void* stream)

@@ -545,6 +545,43 @@ Tensor cat_or_single(const std::vector< Tensor >& parts)
 
 Tensor empty_index_like(const Tensor& ref) { return at::empty({0}, ref.options().dtype(at::kLong)); }
 
+// The index arithmetic of a pack op, part k: idx_k * mul_k + add_k, concatenated.
+// CUDA index parts on one device: one relm_mp_pack_index launch (per 64
+// parts); otherwise the ATen formula (a kernel per part plus a cat).
+bool all_on_one_cuda_device(const std::vector< Tensor >& parts)
+{
+   if(parts.empty() || !parts[0].is_cuda()) return false;
+   for(const auto& t : parts)
+      if(!t.is_cuda() || t.device() != parts[0].device()) return false;
+   return true;
+}
+
+Tensor pack_index(const std::vector< Tensor >& parts, const std::vector< int64_t >& mul,
+                  const std::vector< int64_t >& add, const Tensor& like)
+{
+   if(parts.empty()) return empty_index_like(like);
+   if(parts.size() == 1 && mul[0] == 1 && add[0] == 0) return parts[0];
+   if(!all_on_one_cuda_device(parts)) {
+      std::vector< Tensor > terms;
+      for(size_t i = 0; i < parts.size(); ++i)
+         terms.push_back(mul[i] == 1 ? parts[i] + add[i] : parts[i] * mul[i] + add[i]);
+      return cat_or_single(terms);
+   }
+   c10::cuda::CUDAGuard guard(parts[0].device());
+   int64_t total = 0;
+   std::vector< Tensor > keep;
+   std::vector< relm_mp_index_part > ps;
+   for(size_t i = 0; i < parts.size(); ++i) {
+      keep.push_back(contig(parts[i]));
+      ps.push_back(relm_mp_index_part{keep.back().data_ptr< int64_t >(), keep.back().numel(), mul[i], add[i]});
+      total += keep.back().numel();
+   }
+   Tensor out = at::empty({total}, parts[0].options());
+   check_status(relm_mp_pack_index(ps.data(), (int)ps.size(), out.data_ptr< int64_t >(), stream_of(parts[0])),
+                "pack index");
+   return out;
+}
+
 std::tuple< Tensor, Tensor, Tensor > pack_multi(const std::vector< Tensor >& value_parts,
                                                 const std::vector< Tensor >& first_idx_parts,
                                                 const std::vector< Tensor >& second_idx_parts, const char* op,
@@ -555,7 +592,7 @@ std::tuple< Tensor, Tensor, Tensor > pack_multi(const std::vector< Tensor >& val
       value_parts.size() == first_idx_parts.size() && value_parts.size() == second_idx_parts.size(), op,
       " expects matching sequence lengths."
    );
-   std::vector< Tensor > firsts;
+   std::vector< int64_t > first_add;
    int64_t offset = 0;
    check_rank(value_parts[0], 2, what);
    for(size_t i = 0; i < value_parts.size(); ++i) {
@@ -571,10 +608,12 @@ std::tuple< Tensor, Tensor, Tensor > pack_multi(const std::vector< Tensor >& val
          first_idx_parts[i].numel() == second_idx_parts[i].numel(), op, " expects ", first_name, " and ",
          second_name, " lengths to match per part."
       );
-      firsts.push_back(first_idx_parts[i] + offset);
+      first_add.push_back(offset);
       offset += value_parts[i].size(0);
    }
-   return {cat_or_single(value_parts), cat_or_single(firsts), cat_or_single(second_idx_parts)};
+   const std::vector< int64_t > ones(value_parts.size(), 1), zeros(value_parts.size(), 0);
+   return {cat_or_single(value_parts), pack_index(first_idx_parts, ones, first_add, value_parts[0]),
+           pack_index(second_idx_parts, ones, zeros, value_parts[0])};
 }
 
 std::tuple< Tensor, Tensor, Tensor > fanout_pack_multi(at::TensorList x_parts, at::TensorList src_idx_parts,
@@ -612,6 +651,7 @@ std::tuple< Tensor, Tensor, Tensor > fanout_pack_from_edges(at::TensorList x_par
       offset += x.size(0);
    }
    std::vector< Tensor > srcs, dsts;
+   std::vector< int64_t > src_mul, src_add, dst_mul, dst_add;
    for(size_t i = 0; i < n; ++i) {
       check_int64_index(edge_src_parts[i], "edge_src");
       check_int64_index(edge_dst_parts[i], "edge_dst");
@@ -622,12 +662,16 @@ std::tuple< Tensor, Tensor, Tensor > fanout_pack_from_edges(at::TensorList x_par
       TORCH_CHECK(arity > 0, op, " expects arity > 0.");
       const int64_t pos = pos_parts[i];
       TORCH_CHECK(pos >= 0 && pos < arity, op, " expects pos in [0, arity), got pos=", pos, " arity=", arity, ".");
-      srcs.push_back(edge_src_parts[i] + offsets[part]);
-      dsts.push_back(edge_dst_parts[i] * arity + (slot_offset_parts[i] + pos));
+      srcs.push_back(edge_src_parts[i]);
+      src_mul.push_back(1);
+      src_add.push_back(offsets[part]);
+      dsts.push_back(edge_dst_parts[i]);
+      dst_mul.push_back(arity);
+      dst_add.push_back(slot_offset_parts[i] + pos);
    }
    const Tensor x_cat = cat_or_single(x_parts.vec());
    if(n == 0) return {x_cat, empty_index_like(x_parts[0]), empty_index_like(x_parts[0])};
-   return {x_cat, cat_or_single(srcs), cat_or_single(dsts)};
+   return {x_cat, pack_index(srcs, src_mul, src_add, x_parts[0]), pack_index(dsts, dst_mul, dst_add, x_parts[0])};
 }
 
 std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_parts, at::TensorList edge_src_parts,
@@ -651,26 +695,31 @@ std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_pa
       offset += r.size(0);
    }
    std::vector< Tensor > srcs, dsts;
+   std::vector< int64_t > src_mul, src_add;
    for(size_t i = 0; i < n; ++i) {
       check_int64_index(edge_src_parts[i], "edge_src");
       check_int64_index(edge_dst_parts[i], "edge_dst");
       TORCH_CHECK(edge_src_parts[i].numel() == edge_dst_parts[i].numel(), op, " expects edge src/dst lengths to match.");
       const int64_t part = rel_part_ids[i];
       TORCH_CHECK(part >= 0 && part < (int64_t)rel_parts.size(), op, " rel_part_ids out of range: ", part, ".");
-      Tensor local = edge_src_parts[i];
+      int64_t mul = 1, add = offsets[part];
       if(mode != 1) {
          const int64_t arity = arity_parts[i];
          TORCH_CHECK(arity > 0, op, " expects arity > 0.");
          const int64_t pos = pos_parts[i];
          TORCH_CHECK(pos >= 0 && pos < arity, op, " expects pos in [0, arity), got pos=", pos, " arity=", arity, ".");
-         local = local * arity + pos;
+         mul = arity;
+         add += pos;
       }
-      srcs.push_back(local + offsets[part]);
+      srcs.push_back(edge_src_parts[i]);
+      src_mul.push_back(mul);
+      src_add.push_back(add);
       dsts.push_back(edge_dst_parts[i]);
    }
    const Tensor rel_cat = cat_or_single(rel_parts.vec());
    if(n == 0) return {rel_cat, empty_index_like(rel_parts[0]), empty_index_like(rel_parts[0])};
-   return {rel_cat, cat_or_single(srcs), cat_or_single(dsts)};
+   const std::vector< int64_t > ones(n, 1), zeros(n, 0);
+   return {rel_cat, pack_index(srcs, src_mul, src_add, rel_parts[0]), pack_index(dsts, ones, zeros, rel_parts[0])};
 }
 
 // build_torch / build_cuda_tag describe the torch this layer was compiled
