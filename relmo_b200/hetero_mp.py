@@ -133,28 +133,47 @@ def build_fused_routing(batch: RelationalBatch, relation_arities: dict, conditio
         offsets[p] = total
         total += int(batch.relations[p].size(0))
     device = batch.object_state.device
-    objs, slots, conds, masks, meta = [], [], [], [], []
-    for p in order:
-        args = batch.relations[p]
-        n, k = int(args.size(0)), int(args.size(1))
-        rows = torch.arange(n, device=device, dtype=torch.int64) + offsets[p]
-        for pos in range(k):
-            objs.append(args[:, pos])
-            slots.append(rows * max_arity + pos)
-        conds.append(torch.full((n,), int(condition_index[p]), device=device, dtype=torch.int64))
-        mask_row = torch.zeros(max_arity, device=device, dtype=dtype)
-        mask_row[:k] = 1.0
-        masks.append(mask_row.expand(n, max_arity))
-        meta.append((p, offsets[p], n, k))
     empty_idx = torch.empty(0, dtype=torch.int64, device=device)
-    obj = torch.cat(objs) if objs else empty_idx
-    slot = torch.cat(slots) if slots else empty_idx
-    return FusedRouting(
-        order, offsets, total, obj, slot,
-        torch.cat(conds) if conds else empty_idx,
-        torch.cat(masks) if masks else torch.zeros((0, max_arity), device=device, dtype=dtype),
-        _empty_rows(obj, batch.num_objects), meta,
-    )
+    meta = [(p, offsets[p], int(batch.relations[p].size(0)), int(batch.relations[p].size(1))) for p in order]
+    if not order:
+        return FusedRouting(order, offsets, 0, empty_idx, empty_idx, empty_idx,
+                            torch.zeros((0, max_arity), device=device, dtype=dtype),
+                            _empty_rows(empty_idx, batch.num_objects), meta)
+    # (atom, pos) edges of every predicate through the fan-out pack op (one
+    # device pass for all parts): object = args[atom, pos], slot =
+    # (offset_p + atom) * max_arity + pos.
+    max_n = max(n for _, _, n, _ in meta)
+    atoms = torch.arange(max_n, device=device, dtype=torch.int64)
+    src_parts, dst_parts, pos_parts, slot_parts = [], [], [], []
+    for p, off, n, k in meta:
+        args = batch.relations[p]
+        for pos in range(k):
+            src_parts.append(args[:, pos])
+            dst_parts.append(atoms[:n])
+            pos_parts.append(pos)
+            slot_parts.append(off * max_arity)
+    nparts = len(src_parts)
+    _, obj, slot = _pack_from_edges([empty_idx.view(0, 1).float()], src_parts, dst_parts, [0] * nparts,
+                                    [max_arity] * nparts, pos_parts, slot_parts)
+    # per atom row: its predicate's condition row and slot mask
+    counts = torch.tensor([n for _, _, n, _ in meta], device=device)
+    pred_of_row = torch.repeat_interleave(torch.arange(len(meta), device=device), counts, output_size=total)
+    cond_table = torch.tensor([int(condition_index[p]) for p in order], device=device, dtype=torch.int64)
+    mask_table = (torch.arange(max_arity).view(1, -1) < torch.tensor([k for *_, k in meta]).view(-1, 1))
+    mask_table = mask_table.to(device=device, dtype=dtype)
+    return FusedRouting(order, offsets, total, obj, slot, cond_table[pred_of_row], mask_table[pred_of_row],
+                        _empty_rows(obj, batch.num_objects), meta)
+
+
+def _pack_from_edges(x_parts, edge_src, edge_dst, part_ids, arity, pos, slot_offsets):
+    """The fan-out pack op (relm_mp_pack_index on CUDA) or, without the library,
+    the reference's formula."""
+
+    if mp.available():
+        return torch.ops.relm_mp.fanout_pack_from_edges(x_parts, edge_src, edge_dst, part_ids, arity, pos, slot_offsets)
+    from .ops import mp_pack
+
+    return mp_pack.fanout_pack_from_edges_python(x_parts, edge_src, edge_dst, part_ids, arity, pos, slot_offsets)
 
 
 @dataclass
