@@ -1331,13 +1331,12 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
 }
 
 // Folds tail partials [t_first, t_last) of one row into (m, s) in tile order;
-// eight independent loads in flight.
-template < typename T, int MODE >
+// F independent loads in flight (8; kLongFold in the long-row fixup).
+template < typename T, int MODE, int F = 8 >
 __device__ __forceinline__ void fixup_combine(const SegParams& p, int64_t t_first, int64_t t_last, int64_t col,
                                               typename AccOf< T >::type& m, typename AccOf< T >::type& s)
 {
    using A = typename AccOf< T >::type;
-   constexpr int F = 8;
    const A* tail_val = static_cast< const A* >(p.tail_val);
    const A* tail_aux = static_cast< const A* >(p.tail_aux);
    int64_t u = t_first;
@@ -1412,6 +1411,7 @@ __global__ void __launch_bounds__(kThreads) k_fixup(SegParams p)
 }
 
 constexpr int kLongThreads = 1024;
+constexpr int kLongFold = 16;  // partials in flight per lane in the long-row fixup (latency-bound)
 
 // Block per long row: each of the 32 warps folds one contiguous slice of the
 // row's partials, then warp 0 folds the 32 slice results in order.
@@ -1439,7 +1439,7 @@ __global__ void __launch_bounds__(kLongThreads) k_fixup_long(SegParams p)
       const int64_t col = col0 + lane;
       A m = (MODE == kLse) ? -(A)INFINITY : A(0);
       A s = A(0);
-      if(col < p.emb && u0 < u1) fixup_combine< T, MODE >(p, u0, u1, col, m, s);
+      if(col < p.emb && u0 < u1) fixup_combine< T, MODE, kLongFold >(p, u0, u1, col, m, s);
       sm_m[warp][lane] = m;
       sm_s[warp][lane] = s;
       __syncthreads();
