@@ -43,6 +43,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from datetime import timedelta
 from pathlib import Path
@@ -113,7 +114,7 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.gpu_index = gpu_index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f"clocks_bench_{os.getpid()}.csv"
+        self.path = Path(tempfile.gettempdir()) / f"relm_mp_clocks_{os.getpid()}_{gpu_index}.csv"
 
     def start(self) -> None:
         try:
