@@ -177,3 +177,27 @@ def test_validation_paths_aligned_and_offset_indices(offset, n):
     bad[n - 1] = -3
     with pytest.raises(RuntimeError, match="dst_idx index out of bounds: 777 not in"):
         ops.fanin_reduce(rel, src, bad, 500, 0)
+
+
+def test_large_backwards_with_unpacked_rows():
+    """Above the working set with 192-byte rows (not a power of two times 16):
+    the sum backward scatters through the general scatter kernel and the
+    logsumexp backward falls back to the per-message-row path; both equal the
+    paths taken without a cached forward plan."""
+
+    ops = torch.ops.relm_mp
+    g = torch.Generator(device="cuda").manual_seed(21)
+    rows, edges, emb = 1 << 19, 1 << 21, 48
+    dst = torch.randint(0, rows, (edges,), device="cuda", generator=g)
+    flat_src = torch.randperm(edges, device="cuda", generator=g)
+    rel = torch.randn(edges, emb, device="cuda", generator=g)
+    gout = torch.randn(rows, emb, device="cuda", generator=g)
+    mp.clear_plan_cache()
+    lse = ops.fanin_reduce(rel, flat_src, dst, rows, 1)
+    warm_s = ops.fanin_reduce_sum_backward(gout, flat_src, dst, edges)
+    warm_l = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)
+    mp.clear_plan_cache()
+    cold_s = ops.fanin_reduce_sum_backward(gout, flat_src, dst, edges)
+    cold_l = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)
+    assert torch.equal(warm_s, cold_s)
+    assert torch.equal(warm_l, cold_l)
