@@ -199,7 +199,8 @@ RELM_MP_API size_t relm_mp_plan_bytes(int64_t num_edges, int64_t num_rows);
 RELM_MP_API size_t relm_mp_plan_scratch_bytes(int64_t num_edges, int64_t num_rows);
 /* Validates out_index in [0, num_rows) and gather_index in [0, gather_rows)
  * (names are used in error messages; NULL gives "out_index"/"gather_index"),
- * then builds the plan. Synchronizes `stream` once. */
+ * then builds the plan. Synchronizes `stream` once. A NULL gather_index is
+ * the identity (edge e gathers row e), e.g. the pooling of slot rows. */
 RELM_MP_API int relm_mp_plan_build(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
                        int64_t num_rows, int64_t gather_rows, const char* out_index_name,
                        const char* gather_index_name, void* plan_mem, size_t plan_bytes,
@@ -278,6 +279,99 @@ RELM_MP_API int relm_mp_plan_logsumexp_backward(const relm_mp_plan* plan, relm_m
                                     const void* grad_out, const void* lse_out, const void* rel,
                                     int64_t emb, void* grad_rel, void* scratch,
                                     size_t scratch_bytes, void* stream);
+
+/* Sum with a fused epilogue, the indexed sum / mean of the LGAN ops
+ * (relmo/ops/mp_common.py:88-118, mp_ops.cpp:3433-3454):
+ *   out[r] = base[r] + (sum over edges j of r of table[gidx[j]]) / max(d_r, 1)
+ * with d_r = row_div[r] when row_div != NULL (an int64 array over the plan's
+ * rows, converted to the value type before the clamp, as
+ * `arities.to(dtype).clamp_min(1)`), else the number of edges of r when
+ * divide_by_count != 0 (mean), else 1. base may be NULL (0) or equal to out.
+ * Scratch: relm_mp_plan_reduce_scratch_bytes(plan, emb, dtype, RELM_MP_MODE_SUM).
+ * No counterpart in the reference (its LGAN ops run atomics, then a separate
+ * divide pass, cu:938-1026). */
+RELM_MP_API int relm_mp_plan_reduce_ex(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
+                                       int64_t emb, const void* base, const int64_t* row_div,
+                                       int divide_by_count, void* out, void* scratch, size_t scratch_bytes,
+                                       void* stream);
+/* relm_mp_plan_scatter_rows with each plan row divided by max(row_div[r], 1)
+ * (row_div may be NULL). cover may be NULL when every out row is gathered by
+ * some edge (nothing is zeroed then): the slot gradient of the LGAN pool,
+ * out[s] = table[r] / max(arity[r], 1) through the pool's plan. */
+RELM_MP_API int relm_mp_plan_scatter_rows_div(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
+                                              int64_t emb, const int64_t* row_div, const uint32_t* cover,
+                                              void* out, void* stream);
+/* counts[g] = number of the plan's edges gathering row g, g < gather_rows
+ * (int32, deterministic integer atomics). */
+RELM_MP_API int relm_mp_plan_gather_counts(const relm_mp_plan* plan, int32_t* counts, void* stream);
+/* out[r] = in[r] / max(counts[r], 1) for r < rows (out may equal in): the
+ * `gathered / counts.clamp_min(1)` of the mean-mode reverse aggregation
+ * (mp_ops.cpp:3542-3553). */
+RELM_MP_API int relm_mp_divide_rows(relm_mp_dtype dtype, const void* in, int64_t rows, int64_t emb,
+                                    const int32_t* counts, void* out, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * LGAN ops (`sum` / `mean` modes):
+ *
+ *   relm_mp_lgan_pool_reduce                  <- lgan_pool_reduce                  (mp_ops.cpp:3350-3469, schema 3778)
+ *   relm_mp_lgan_pool_reduce_backward         <- lgan_pool_reduce_backward         (mp_ops.cpp:3471-3572, schema 3781)
+ *   relm_mp_lgan_relation_graph_step          <- lgan_relation_graph_step          (mp_ops.cpp:3574-3656, schema 3784)
+ *   relm_mp_lgan_relation_graph_step_backward <- lgan_relation_graph_step_backward (mp_ops.cpp:3658-3743, schema 3787)
+ *
+ * agg(x, src, dst, rows)[t] = sum of x[src[e]] over the edges e with dst[e] = t,
+ * divided by max(edges into t, 1) in mode RELM_MP_MODE_MEAN. The relation
+ * graph step computes x1 = x + agg(x, rr_src, rr_dst, R), tn = agg(x1, tn_rel,
+ * tn_ent, N), nn = agg(x1, nn_rel, nn_ent, N); the pool first forms
+ * x[r] = (sum of the slot rows s with slot_to_relation_instance[s] = r) /
+ * max(relation_instance_arities[r], 1). Backward ops return the gradient of
+ * the first input from the gradients of the three outputs. Each aggregation
+ * runs through a plan built in the workspace (one at a time), so every call
+ * synchronizes `stream` once per aggregation for index validation.
+ * ------------------------------------------------------------------------- */
+
+/* Mode of the LGAN ops, as relmo.ops.mp_constants MODE_MEAN (mode 0 is sum). */
+#define RELM_MP_MODE_MEAN 2
+
+typedef struct relm_mp_lgan_graph {
+   const int64_t* rr_src; /* relation -> relation edges */
+   const int64_t* rr_dst;
+   int64_t num_rr;
+   const int64_t* tn_rel; /* relation -> entity edges (TN) */
+   const int64_t* tn_ent;
+   int64_t num_tn;
+   const int64_t* nn_rel; /* relation -> entity edges (NN) */
+   const int64_t* nn_ent;
+   int64_t num_nn;
+   int64_t relation_count;  /* R: rows of relation_pair_x (length of relation_instance_arities) */
+   int64_t entity_dim_size; /* N: rows of tn_msgs / nn_msgs */
+} relm_mp_lgan_graph;
+
+/* One size for all four LGAN entry points (num_slots: rows of slot_messages,
+ * 0 for the relation graph step). */
+RELM_MP_API size_t relm_mp_lgan_workspace_bytes(const relm_mp_lgan_graph* graph, int64_t num_slots, int64_t emb,
+                                                relm_mp_dtype dtype);
+RELM_MP_API int relm_mp_lgan_relation_graph_step(relm_mp_dtype dtype, const relm_mp_lgan_graph* graph,
+                                                 const void* relation_pair_x, int64_t emb, int mode,
+                                                 void* relation_pair_x_out, void* tn_msgs, void* nn_msgs,
+                                                 void* workspace, size_t workspace_bytes, void* stream);
+RELM_MP_API int relm_mp_lgan_relation_graph_step_backward(relm_mp_dtype dtype, const relm_mp_lgan_graph* graph,
+                                                          const void* grad_relation_pair_x,
+                                                          const void* grad_tn_msgs, const void* grad_nn_msgs,
+                                                          int64_t emb, int mode, void* grad_relation_pair_x_in,
+                                                          void* workspace, size_t workspace_bytes, void* stream);
+RELM_MP_API int relm_mp_lgan_pool_reduce(relm_mp_dtype dtype, const relm_mp_lgan_graph* graph,
+                                         const void* slot_messages, int64_t num_slots, int64_t emb,
+                                         const int64_t* slot_to_relation_instance,
+                                         const int64_t* relation_instance_arities, int mode,
+                                         void* relation_pair_x, void* tn_msgs, void* nn_msgs, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+RELM_MP_API int relm_mp_lgan_pool_reduce_backward(relm_mp_dtype dtype, const relm_mp_lgan_graph* graph,
+                                                  const void* grad_relation_pair_x, const void* grad_tn_msgs,
+                                                  const void* grad_nn_msgs, int64_t emb, int64_t num_slots,
+                                                  const int64_t* slot_to_relation_instance,
+                                                  const int64_t* relation_instance_arities, int mode,
+                                                  void* grad_slot_messages, void* workspace,
+                                                  size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -179,3 +179,104 @@ def fanin_reduce_logsumexp_backward(grad_out, rel_flat, flat_src, dst_idx, out, 
         ctypes.c_int64(src.shape[0]), ctypes.c_int64(int(rel_rows)), _ptr(res),
     )
     return res
+
+
+LGAN_INDEX_NAMES = ("rr_src", "rr_dst", "tn_rel", "tn_ent", "nn_rel", "nn_ent", "slot_to_relation_instance")
+
+
+def _lgan_mode(mode: int, op: str) -> int:
+    if int(mode) not in (0, 2):
+        raise ValueError(f"{op} supports only mode 0=sum or 2=mean.")
+    return 1 if int(mode) == 2 else 0
+
+
+def _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent):
+    ix = [_idx(a) for a in (rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent)]
+    args = []
+    for k in range(0, 6, 2):
+        args += [_ptr(ix[k]), _ptr(ix[k + 1]), ctypes.c_int64(ix[k].shape[0])]
+    return ix, args
+
+
+def lgan_relation_graph_step(x, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, entity_dim_size: int, mode: int):
+    """mp_ops.cpp:3627-3656 (ATen formulas): (x + agg_rr(x), agg_tn(x1), agg_nn(x1))."""
+
+    mean = _lgan_mode(mode, "lgan_relation_graph_step")
+    x = _vals(x)
+    ix, graph = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent)
+    rows, emb = x.shape
+    x1 = np.empty_like(x)
+    tn = np.empty((int(entity_dim_size), emb), dtype=x.dtype)
+    nn = np.empty_like(tn)
+    _call(
+        f"relm_oracle_lgan_relation_graph_step_{_suffix(x.dtype)}", LGAN_INDEX_NAMES,
+        _ptr(x), ctypes.c_int64(rows), ctypes.c_int64(emb), *graph, ctypes.c_int64(int(entity_dim_size)),
+        ctypes.c_int(mean), _ptr(x1), _ptr(tn), _ptr(nn),
+    )
+    return x1, tn, nn
+
+
+def lgan_relation_graph_step_backward(grad_x, grad_tn, grad_nn, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent,
+                                      relation_count: int, mode: int):
+    """mp_ops.cpp:3715-3743 (ATen formulas)."""
+
+    mean = _lgan_mode(mode, "lgan_relation_graph_step_backward")
+    gx = _vals(grad_x)
+    gtn = _vals(grad_tn).astype(gx.dtype, copy=False)
+    gnn = _vals(grad_nn).astype(gx.dtype, copy=False)
+    ix, graph = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent)
+    emb = gx.shape[1]
+    out = np.empty((int(relation_count), emb), dtype=gx.dtype)
+    gtn = np.ascontiguousarray(gtn)
+    gnn = np.ascontiguousarray(gnn)
+    _call(
+        f"relm_oracle_lgan_relation_graph_step_backward_{_suffix(gx.dtype)}", LGAN_INDEX_NAMES,
+        _ptr(gx), _ptr(gtn), _ptr(gnn), ctypes.c_int64(gtn.shape[0]), ctypes.c_int64(emb), *graph,
+        ctypes.c_int64(int(relation_count)), ctypes.c_int(mean), _ptr(out),
+    )
+    return out
+
+
+def lgan_pool_reduce(slot_messages, slot_to_relation_instance, relation_instance_arities, rr_src, rr_dst, tn_rel,
+                     tn_ent, nn_rel, nn_ent, entity_dim_size: int, mode: int):
+    """mp_ops.cpp:3424-3469 (ATen formulas): pool the slots to relation instances
+    (sum / max(arity, 1)), then the relation graph step."""
+
+    mean = _lgan_mode(mode, "lgan_pool_reduce")
+    slots = _vals(slot_messages)
+    s2r = _idx(slot_to_relation_instance)
+    ar = _idx(relation_instance_arities)
+    ix, graph = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent)
+    emb = slots.shape[1]
+    x1 = np.empty((ar.shape[0], emb), dtype=slots.dtype)
+    tn = np.empty((int(entity_dim_size), emb), dtype=slots.dtype)
+    nn = np.empty_like(tn)
+    _call(
+        f"relm_oracle_lgan_pool_reduce_{_suffix(slots.dtype)}", LGAN_INDEX_NAMES,
+        _ptr(slots), ctypes.c_int64(slots.shape[0]), ctypes.c_int64(emb), _ptr(s2r), _ptr(ar),
+        ctypes.c_int64(ar.shape[0]), *graph, ctypes.c_int64(int(entity_dim_size)), ctypes.c_int(mean),
+        _ptr(x1), _ptr(tn), _ptr(nn),
+    )
+    return x1, tn, nn
+
+
+def lgan_pool_reduce_backward(grad_x, grad_tn, grad_nn, slot_to_relation_instance, relation_instance_arities,
+                              rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, relation_count: int, mode: int):
+    """mp_ops.cpp:3527-3572 (ATen formulas)."""
+
+    mean = _lgan_mode(mode, "lgan_pool_reduce_backward")
+    gx = _vals(grad_x)
+    gtn = np.ascontiguousarray(_vals(grad_tn).astype(gx.dtype, copy=False))
+    gnn = np.ascontiguousarray(_vals(grad_nn).astype(gx.dtype, copy=False))
+    s2r = _idx(slot_to_relation_instance)
+    ar = _idx(relation_instance_arities)
+    ix, graph = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent)
+    emb = gx.shape[1]
+    out = np.empty((s2r.shape[0], emb), dtype=gx.dtype)
+    _call(
+        f"relm_oracle_lgan_pool_reduce_backward_{_suffix(gx.dtype)}", LGAN_INDEX_NAMES,
+        _ptr(gx), _ptr(gtn), _ptr(gnn), ctypes.c_int64(gtn.shape[0]), ctypes.c_int64(emb), _ptr(s2r),
+        ctypes.c_int64(s2r.shape[0]), _ptr(ar), *graph, ctypes.c_int64(int(relation_count)), ctypes.c_int(mean),
+        _ptr(out),
+    )
+    return out

@@ -40,6 +40,7 @@ CUDA_SOURCES = [
     "relm_mp_seg_bf16.cu",
     "relm_mp_seg_f16.cu",
     "relm_mp_noalloc.cu",
+    "relm_mp_lgan.cu",
 ]
 TORCH_SOURCES = ["relm_mp_torch.cpp"]
 HEADERS = ["relm_mp_internal.cuh", "relm_mp_segment.cuh", "relm_mp_seg_impl.cuh"]

@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "librelm_mp_b200.so"
 
 FLOAT32, FLOAT64, BFLOAT16, FLOAT16 = 0, 1, 2, 3
 MODE_SUM, MODE_LOGSUMEXP, MODE_LOGSUMEXP_BACKWARD = 0, 1, 2
+MODE_MEAN = 2  # LGAN ops
 STATUS_NAMES = {
     0: "RELM_MP_OK",
     1: "RELM_MP_ERR_INVALID_ARGUMENT",
@@ -49,6 +50,27 @@ class Plan(ctypes.Structure):
 
 
 _PLANP = ctypes.POINTER(Plan)
+
+
+class LganGraph(ctypes.Structure):
+    """relm_mp_lgan_graph: the RR / TN / NN edge lists of the LGAN ops."""
+
+    _fields_ = [
+        ("rr_src", ctypes.c_void_p),
+        ("rr_dst", ctypes.c_void_p),
+        ("num_rr", ctypes.c_int64),
+        ("tn_rel", ctypes.c_void_p),
+        ("tn_ent", ctypes.c_void_p),
+        ("num_tn", ctypes.c_int64),
+        ("nn_rel", ctypes.c_void_p),
+        ("nn_ent", ctypes.c_void_p),
+        ("num_nn", ctypes.c_int64),
+        ("relation_count", ctypes.c_int64),
+        ("entity_dim_size", ctypes.c_int64),
+    ]
+
+
+_GRAPHP = ctypes.POINTER(LganGraph)
 
 SIGNATURES: dict[str, tuple] = {
     "relm_mp_status_string": (_STR, [_INT]),
@@ -85,6 +107,24 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_scatter_rows": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
     "relm_mp_plan_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_plan_reduce_ex": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _INT, _P, _P, _SZ, _P]),
+    "relm_mp_plan_scatter_rows_div": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P, _P]),
+    "relm_mp_plan_gather_counts": (_INT, [_PLANP, _P, _P]),
+    "relm_mp_divide_rows": (_INT, [_INT, _P, _I64, _I64, _P, _P, _P]),
+    "relm_mp_lgan_workspace_bytes": (_SZ, [_GRAPHP, _I64, _I64, _INT]),
+    "relm_mp_lgan_relation_graph_step": (_INT, [_INT, _GRAPHP, _P, _I64, _INT, _P, _P, _P, _P, _SZ, _P]),
+    "relm_mp_lgan_relation_graph_step_backward": (
+        _INT,
+        [_INT, _GRAPHP, _P, _P, _P, _I64, _INT, _P, _P, _SZ, _P],
+    ),
+    "relm_mp_lgan_pool_reduce": (
+        _INT,
+        [_INT, _GRAPHP, _P, _I64, _I64, _P, _P, _INT, _P, _P, _P, _P, _SZ, _P],
+    ),
+    "relm_mp_lgan_pool_reduce_backward": (
+        _INT,
+        [_INT, _GRAPHP, _P, _P, _P, _I64, _I64, _P, _P, _INT, _P, _P, _SZ, _P],
+    ),
 }
 
 _LIB: ctypes.CDLL | None = None
@@ -167,6 +207,17 @@ def _stream(device) -> int:
 
 def _workspace(nbytes: int, device):
     return _torch().empty(max(int(nbytes), 1), dtype=_torch().uint8, device=device)
+
+
+def divide_rows(x, counts, out=None):
+    """out[r] = x[r] / max(counts[r], 1) (relm_mp_divide_rows; out may be x)."""
+
+    x = x.contiguous()
+    if out is None:
+        out = _torch().empty_like(x)
+    check(lib().relm_mp_divide_rows(dtype_code(x), _ptr(x), x.size(0), x.size(1), _ptr(counts.contiguous()),
+                                    _ptr(out), _stream(x.device)))
+    return out
 
 
 def fanout_scatter(x, src, flat_dst, out_rows: int, out=None):
@@ -272,8 +323,11 @@ class PlanHandle:
     """A plan built through the C ABI, owning its device memory (torch)."""
 
     def __init__(self, out_index, gather_index, num_rows: int, gather_rows: int):
+        """gather_index None: the identity (edge e gathers row e)."""
+
         torch = _torch()
-        out_index, gather_index = out_index.contiguous(), gather_index.contiguous()
+        out_index = out_index.contiguous()
+        gather_index = gather_index.contiguous() if gather_index is not None else None
         e = out_index.numel()
         self.memory = _workspace(lib().relm_mp_plan_bytes(e, int(num_rows)), out_index.device)
         scratch = _workspace(lib().relm_mp_plan_scratch_bytes(e, int(num_rows)), out_index.device)
@@ -308,6 +362,45 @@ class PlanHandle:
         check(lib().relm_mp_plan_reduce(
             ctypes.byref(self.plan), dtype_code(table), int(mode), _ptr(table), emb, _ptr(out),
             scratch.data_ptr(), scratch.numel(), _stream(table.device),
+        ))
+        return out
+
+    def reduce_ex(self, table, base=None, row_div=None, divide_by_count: bool = False, out=None):
+        """out[r] = base[r] + sum / max(d_r, 1) (relm_mp_plan_reduce_ex); out may be base."""
+
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        if out is None:
+            out = torch.empty((self.plan.num_rows, emb), dtype=table.dtype, device=table.device)
+        scratch = _workspace(
+            lib().relm_mp_plan_reduce_scratch_bytes(ctypes.byref(self.plan), emb, dtype_code(table), MODE_SUM),
+            table.device,
+        )
+        check(lib().relm_mp_plan_reduce_ex(
+            ctypes.byref(self.plan), dtype_code(table), _ptr(table), emb, _ptr(base), _ptr(row_div),
+            int(bool(divide_by_count)), _ptr(out), scratch.data_ptr(), scratch.numel(), _stream(table.device),
+        ))
+        return out
+
+    def gather_counts(self):
+        """Edges per gathered row (int32 CUDA tensor)."""
+
+        torch = _torch()
+        counts = torch.empty(max(int(self.plan.gather_rows), 1), dtype=torch.int32, device=self.device)
+        check(lib().relm_mp_plan_gather_counts(ctypes.byref(self.plan), _ptr(counts), _stream(self.device)))
+        return counts[: int(self.plan.gather_rows)]
+
+    def scatter_rows_div(self, table, row_div, cover=None):
+        """out[gidx[e]] = table[row of e] / max(row_div[row], 1); cover None: every out row is an edge target."""
+
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        out = torch.empty((self.plan.gather_rows, emb), dtype=table.dtype, device=table.device)
+        check(lib().relm_mp_plan_scatter_rows_div(
+            ctypes.byref(self.plan), dtype_code(table), _ptr(table), emb, _ptr(row_div), _ptr(cover), _ptr(out),
+            _stream(table.device),
         ))
         return out
 
@@ -352,9 +445,91 @@ class PlanHandle:
         return out
 
 
+# ---- LGAN ops (op-level entry points) --------------------------------------------
+
+
+def _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, relation_count: int, entity_dim_size: int):
+    ix = [i.contiguous().long() for i in (rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent)]
+    g = LganGraph(
+        _ptr(ix[0]), _ptr(ix[1]), ix[0].numel(), _ptr(ix[2]), _ptr(ix[3]), ix[2].numel(),
+        _ptr(ix[4]), _ptr(ix[5]), ix[4].numel(), int(relation_count), int(entity_dim_size),
+    )
+    return g, ix
+
+
+def _lgan_ws(g, num_slots: int, like):
+    return _workspace(lib().relm_mp_lgan_workspace_bytes(ctypes.byref(g), int(num_slots), like.size(1),
+                                                         dtype_code(like)), like.device)
+
+
+def lgan_relation_graph_step(x, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, entity_dim_size: int, mode: int):
+    torch = _torch()
+    x = x.contiguous()
+    g, keep = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, x.size(0), entity_dim_size)
+    x1 = torch.empty_like(x)
+    tn = torch.empty((int(entity_dim_size), x.size(1)), dtype=x.dtype, device=x.device)
+    nn = torch.empty_like(tn)
+    ws = _lgan_ws(g, 0, x)
+    check(lib().relm_mp_lgan_relation_graph_step(
+        dtype_code(x), ctypes.byref(g), _ptr(x), x.size(1), int(mode), _ptr(x1), _ptr(tn), _ptr(nn),
+        ws.data_ptr(), ws.numel(), _stream(x.device),
+    ))
+    del keep
+    return x1, tn, nn
+
+
+def lgan_relation_graph_step_backward(gx, gtn, gnn, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent,
+                                      relation_count: int, mode: int):
+    torch = _torch()
+    gx, gtn, gnn = gx.contiguous(), gtn.contiguous(), gnn.contiguous()
+    g, keep = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, relation_count, gtn.size(0))
+    out = torch.empty((int(relation_count), gx.size(1)), dtype=gx.dtype, device=gx.device)
+    ws = _lgan_ws(g, 0, gx)
+    check(lib().relm_mp_lgan_relation_graph_step_backward(
+        dtype_code(gx), ctypes.byref(g), _ptr(gx), _ptr(gtn), _ptr(gnn), gx.size(1), int(mode), _ptr(out),
+        ws.data_ptr(), ws.numel(), _stream(gx.device),
+    ))
+    del keep
+    return out
+
+
+def lgan_pool_reduce(slots, slot_to_rel, arities, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent,
+                     entity_dim_size: int, mode: int):
+    torch = _torch()
+    slots, s2r, ar = slots.contiguous(), slot_to_rel.contiguous().long(), arities.contiguous()
+    R = ar.numel()
+    g, keep = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, R, entity_dim_size)
+    x1 = torch.empty((R, slots.size(1)), dtype=slots.dtype, device=slots.device)
+    tn = torch.empty((int(entity_dim_size), slots.size(1)), dtype=slots.dtype, device=slots.device)
+    nn = torch.empty_like(tn)
+    ws = _lgan_ws(g, slots.size(0), slots)
+    check(lib().relm_mp_lgan_pool_reduce(
+        dtype_code(slots), ctypes.byref(g), _ptr(slots), slots.size(0), slots.size(1), _ptr(s2r), _ptr(ar),
+        int(mode), _ptr(x1), _ptr(tn), _ptr(nn), ws.data_ptr(), ws.numel(), _stream(slots.device),
+    ))
+    del keep
+    return x1, tn, nn
+
+
+def lgan_pool_reduce_backward(gx, gtn, gnn, slot_to_rel, arities, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent,
+                              relation_count: int, mode: int):
+    torch = _torch()
+    gx, gtn, gnn = gx.contiguous(), gtn.contiguous(), gnn.contiguous()
+    s2r, ar = slot_to_rel.contiguous().long(), arities.contiguous()
+    g, keep = _lgan_graph(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, relation_count, gtn.size(0))
+    out = torch.empty((s2r.numel(), gx.size(1)), dtype=gx.dtype, device=gx.device)
+    ws = _lgan_ws(g, s2r.numel(), gx)
+    check(lib().relm_mp_lgan_pool_reduce_backward(
+        dtype_code(gx), ctypes.byref(g), _ptr(gx), _ptr(gtn), _ptr(gnn), gx.size(1), s2r.numel(), _ptr(s2r),
+        _ptr(ar), int(mode), _ptr(out), ws.data_ptr(), ws.numel(), _stream(gx.device),
+    ))
+    del keep
+    return out
+
+
 class _DeviceArray:
     def __init__(self, ptr: int, n: int, typestr: str):
-        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": typestr, "data": (int(ptr), True), "version": 3}
+        self.__cuda_array_interface__ = {"shape": (int(n),), "typestr": typestr, "data": (int(ptr), False), "version": 3}
 
 
 def _device_int32(ptr: int, n: int, device):

@@ -347,10 +347,18 @@ int dispatch_stream(relm_mp_dtype dtype, const SegParams& pm, const Shape& sm, c
    return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
 }
 
+// Epilogue of a planned sum (relm_mp_plan_reduce_ex): out = base + sum / divisor.
+struct SumEpilogue {
+   const void* base = nullptr;
+   const int64_t* row_div = nullptr;
+   int divide_by_count = 0;
+   bool on() const { return base || row_div || divide_by_count; }
+};
+
 // Planned reduction shared by relm_mp_plan_reduce / relm_mp_plan_logsumexp_backward.
 int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, const void* table,
                    const void* table2, const void* own, int64_t emb, void* out, void* scratch,
-                   size_t scratch_bytes, cudaStream_t stream)
+                   size_t scratch_bytes, cudaStream_t stream, const SumEpilogue& epi = SumEpilogue())
 {
    if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
    if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
@@ -362,6 +370,13 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    if(!scratch || scratch_bytes < rs.bytes)
       return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "reduce scratch is smaller than relm_mp_plan_reduce_scratch_bytes().");
    if(plan->num_edges == 0) {
+      if(epi.base) {  // base + 0 / d = base
+         if(epi.base == out) return RELM_MP_OK;
+         return check_cuda(
+            cudaMemcpyAsync(out, epi.base, (size_t)(plan->num_rows * emb * es), cudaMemcpyDeviceToDevice, stream),
+            "epilogue base copy"
+         );
+      }
       return fill_rows(dtype, out, plan->num_rows * emb, seg_mode == kLse, stream);
    }
    const void* ptrs[4] = {table, table2, own, out};
@@ -381,6 +396,12 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    p.long_count = rs.long_count;
    p.long_list = rs.long_list;
    p.max_long = rs.max_long;
+   if(seg_mode == kSum && epi.on()) {
+      seg_mode = kSumEpi;
+      p.epi_base = epi.base;
+      p.epi_div = epi.row_div;
+      p.epi_count = epi.divide_by_count ? 1 : 0;
+   }
    int rc = check_cuda(cudaMemsetAsync(rs.long_count, 0, sizeof(int32_t), stream), "long_count memset");
    if(rc) return rc;
    const StreamShape ss = choose_stream_shape(emb, (int)es, ptrs, 4);
@@ -621,13 +642,13 @@ int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* rows, void* st
    return RELM_MP_OK;
 }
 
-int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
-                              const uint32_t* cover, void* out, void* stream)
+namespace {
+
+int scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
+                 const int64_t* row_div, const uint32_t* cover, void* out, cudaStream_t st)
 {
-   if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
    if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
    if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
-   cudaStream_t st = static_cast< cudaStream_t >(stream);
    if(plan->gather_rows == 0 || emb == 0) return RELM_MP_OK;
    if(plan->num_edges == 0) return fill_rows(dtype, out, plan->gather_rows * emb, false, st);
    const void* ptrs[2] = {table, out};
@@ -635,7 +656,24 @@ int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, con
    SegParams p = base_params(plan, emb, s);
    p.table = table;
    p.out = out;
+   p.epi_div = row_div;
    return dispatch_scatter(dtype, p, s, cover, plan->gather_rows, st);
+}
+
+}  // namespace
+
+int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
+                              const uint32_t* cover, void* out, void* stream)
+{
+   if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
+   return scatter_rows(plan, dtype, table, emb, nullptr, cover, out, static_cast< cudaStream_t >(stream));
+}
+
+int relm_mp_plan_scatter_rows_div(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
+                                  const int64_t* row_div, const uint32_t* cover, void* out, void* stream)
+{
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   return scatter_rows(plan, dtype, table, emb, row_div, cover, out, static_cast< cudaStream_t >(stream));
 }
 
 int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* grad_out,
@@ -675,6 +713,20 @@ int relm_mp_plan_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int mode,
    return planned_reduce(
       plan, dtype, mode == RELM_MP_MODE_SUM ? kSum : kLse, table, nullptr, nullptr, emb, out, scratch,
       scratch_bytes, static_cast< cudaStream_t >(stream)
+   );
+}
+
+int relm_mp_plan_reduce_ex(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
+                           const void* base, const int64_t* row_div, int divide_by_count, void* out,
+                           void* scratch, size_t scratch_bytes, void* stream)
+{
+   SumEpilogue e;
+   e.base = base;
+   e.row_div = row_div;
+   e.divide_by_count = divide_by_count;
+   return planned_reduce(
+      plan, dtype, kSum, table, nullptr, nullptr, emb, out, scratch, scratch_bytes,
+      static_cast< cudaStream_t >(stream), e
    );
 }
 

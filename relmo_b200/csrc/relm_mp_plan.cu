@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       const int64_t pairs = n / 2;
       if(t < pairs) {
          const longlong2 kk = __ldg(reinterpret_cast< const longlong2* >(key) + t);
-         const longlong2 gg = __ldg(reinterpret_cast< const longlong2* >(gat) + t);
+         const longlong2 gg =
+            gat ? __ldg(reinterpret_cast< const longlong2* >(gat) + t) : make_longlong2(2 * t, 2 * t + 1);
          const int64_t e = 2 * t;
          check(e, kk.x, gg.x);
          check(e + 1, kk.y, gg.y);
@@ -80,14 +81,14 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       } else if(t == pairs && (n & 1)) {
          const int64_t e = n - 1;
          const int64_t k = key[e];
-         const int64_t g = gat[e];
+         const int64_t g = gat ? gat[e] : e;
          check(e, k, g);
          key32[e] = (uint32_t)k;
          gat32[e] = (int32_t)g;
       }
    } else if(t < n) {
       const int64_t k = key[t];
-      const int64_t g = gat[t];
+      const int64_t g = gat ? gat[t] : t;
       check(t, k, g);
       key32[t] = (uint32_t)k;
       gat32[t] = (int32_t)g;
@@ -312,8 +313,7 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
       return fail(
          RELM_MP_ERR_UNSUPPORTED, "relm_mp supports num_edges + num_rows < 2^31 and < 2^31 gathered rows."
       );
-   if(num_edges > 0 && (!out_index || !gather_index))
-      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "index pointers must not be NULL.");
+   if(num_edges > 0 && !out_index) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_index must not be NULL.");
    const PlanLayout pl = plan_layout(plan_mem, num_edges, num_rows);
    const ScratchLayout sl = scratch_layout(scratch, num_edges, num_rows);
    if(!plan_mem || plan_bytes < pl.bytes)
@@ -367,10 +367,10 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
          use_gather = host.gather_bad < host.out_bad;
       const unsigned long long pos = use_gather ? host.gather_bad : host.out_bad;
       const int64_t* arr = use_gather ? gather_index : out_index;
-      int64_t value = 0;
-      if((rc = check_cuda(
-             cudaMemcpy(&value, arr + pos, sizeof(int64_t), cudaMemcpyDeviceToHost), "bad index copy"
-          )))
+      int64_t value = (int64_t)pos;  // a NULL (identity) gather index gathers row e at edge e
+      if(arr && (rc = check_cuda(
+                    cudaMemcpy(&value, arr + pos, sizeof(int64_t), cudaMemcpyDeviceToHost), "bad index copy"
+                 )))
          return rc;
       char msg[256];
       snprintf(

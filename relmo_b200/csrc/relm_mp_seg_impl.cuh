@@ -11,6 +11,8 @@ int launch_reduce_shape(const SegParams& p, int mode, cudaStream_t stream)
    const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
    if(mode == kSum)
       k_seg_reduce< T, VB, CH, kSum ><<< grid, kThreads, 0, stream >>>(p);
+   else if(mode == kSumEpi)
+      k_seg_reduce< T, VB, CH, kSumEpi ><<< grid, kThreads, 0, stream >>>(p);
    else if(mode == kLse)
       k_seg_reduce< T, VB, CH, kLse ><<< grid, kThreads, 0, stream >>>(p);
    else
@@ -44,6 +46,8 @@ int launch_map_shape(const SegParams& p, int mode, cudaStream_t stream)
       k_row_map< T, VB, CH, kCopyLast ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    else if(mode == kSum)
       k_row_map< T, VB, CH, kSum ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kSumEpi)
+      k_row_map< T, VB, CH, kSumEpi ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    else if(mode == kLse)
       k_row_map< T, VB, CH, kLse ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    else
@@ -55,9 +59,12 @@ template < typename T, int VB, int CH >
 int launch_scatter_shape(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream)
 {
    const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
-   k_scatter_rows< T, VB, CH ><<< grid, kThreads, 0, stream >>>(p);
+   if(p.epi_div)
+      k_scatter_rows< T, VB, CH, true ><<< grid, kThreads, 0, stream >>>(p);
+   else
+      k_scatter_rows< T, VB, CH, false ><<< grid, kThreads, 0, stream >>>(p);
    int rc = check_launch("k_scatter_rows");
-   if(rc) return rc;
+   if(rc || !cover) return rc;  // no bitmap: every out row is the target of an edge
    int64_t blocks = (out_rows + kThreads - 1) / kThreads;
    const int64_t cap = (int64_t)148 * 8;
    if(blocks > cap) blocks = cap;
@@ -78,6 +85,8 @@ int launch_map_packed(const SegParams& p, int mode, cudaStream_t stream)
       k_row_map_packed< T, kCopyLast ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    else if(mode == kSum)
       k_row_map_packed< T, kSum ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kSumEpi)
+      k_row_map_packed< T, kSumEpi ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    else if(mode == kLse)
       k_row_map_packed< T, kLse ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
    else
@@ -89,9 +98,12 @@ template < typename T >
 int launch_scatter_packed(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream)
 {
    const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
-   k_scatter_rows_packed< T ><<< grid, kThreads, 0, stream >>>(p);
+   if(p.epi_div)
+      k_scatter_rows_packed< T, true ><<< grid, kThreads, 0, stream >>>(p);
+   else
+      k_scatter_rows_packed< T, false ><<< grid, kThreads, 0, stream >>>(p);
    int rc = check_launch("k_scatter_rows_packed");
-   if(rc) return rc;
+   if(rc || !cover) return rc;  // no bitmap: every out row is the target of an edge
    int64_t blocks = (out_rows + kThreads - 1) / kThreads;
    const int64_t cap = (int64_t)148 * 8;
    if(blocks > cap) blocks = cap;
@@ -160,6 +172,7 @@ int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegPara
    auto run = [&]() -> int { RELM_MP_SHAPE_DISPATCH(T, launch_reduce_shape, p, mode, stream); };
    if((rc = run())) return rc;
    if(mode == kSum) return launch_fixups< T, kSum >(p, stream);
+   if(mode == kSumEpi) return launch_fixups< T, kSumEpi >(p, stream);
    if(mode == kLse) return launch_fixups< T, kLse >(p, stream);
    return launch_fixups< T, kLseBwd >(p, stream);
 }
@@ -187,6 +200,7 @@ template < typename T, int PB >
 int launch_stream_mode(const SegParams& p, int mode, cudaStream_t stream)
 {
    if(mode == kSum) return launch_stream_shape< T, PB, kSum >(p, stream);
+   if(mode == kSumEpi) return launch_stream_shape< T, PB, kSumEpi >(p, stream);
    if(mode == kLse) return launch_stream_shape< T, PB, kLse >(p, stream);
    return launch_stream_shape< T, PB, kLseBwd >(p, stream);
 }
@@ -211,6 +225,7 @@ int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegPara
    }
    if(rc) return rc;
    if(mode == kSum) return launch_fixups< T, kSum >(p, stream);
+   if(mode == kSumEpi) return launch_fixups< T, kSumEpi >(p, stream);
    if(mode == kLse) return launch_fixups< T, kLse >(p, stream);
    return launch_fixups< T, kLseBwd >(p, stream);
 }

@@ -23,7 +23,10 @@
 
 namespace relm_mp {
 
-enum SegMode : int { kSum = 0, kLse = 1, kLseBwd = 2, kCopyLast = 3 };
+enum SegMode : int { kSum = 0, kLse = 1, kLseBwd = 2, kCopyLast = 3, kSumEpi = 4 };
+// kSumEpi: kSum with the epilogue of SegParams::epi_* applied where a row's
+// final value is written (a separate instantiation, so kSum keeps its code).
+__host__ __device__ constexpr bool sum_mode(int m) { return m == kSum || m == kSumEpi; }
 
 template < typename T >
 struct AccOf {
@@ -212,7 +215,47 @@ struct SegParams {
    int32_t* long_list;
    int64_t max_long;
    const int32_t* has_dups;  // device flag of the plan: some row holds more than one edge
+   // kSumEpi epilogue (indexed sum / mean of the LGAN ops): the final value
+   // of row R is epi_base[R] + sum / max(d, 1) with d = epi_div[R] when
+   // epi_div is set, else the row's edge count when epi_count, else 1. The
+   // dividing scatter (k_scatter_rows*<DIV>) divides plan row R by
+   // max(epi_div[R], 1).
+   const void* epi_base;
+   const int64_t* epi_div;
+   int epi_count;
 };
+
+// Divisor of output row R in the SUM epilogue (at least 1; integers convert
+// to the accumulator type before the clamp, as `counts.to(dtype).clamp_min(1)`).
+template < typename T >
+__device__ __forceinline__ typename AccOf< T >::type epi_divisor(const SegParams& p, int64_t R)
+{
+   using A = typename AccOf< T >::type;
+   int64_t d = 1;
+   if(p.epi_div)
+      d = p.epi_div[R];
+   else if(p.epi_count)
+      d = (int64_t)p.row_ptr[R + 1] - (int64_t)p.row_ptr[R];
+   const A a = (A)d;
+   return a > A(1) ? a : A(1);
+}
+
+// v[k] <- base[R, col + k] + v[k] / divisor(R), k < N (an IEEE division, like
+// the reference's `out / counts`; exact for a divisor of 1).
+template < typename T, int N >
+__device__ __forceinline__ void epi_apply(const SegParams& p, int64_t R, int64_t col,
+                                          typename AccOf< T >::type (&v)[N])
+{
+   using A = typename AccOf< T >::type;
+   const A d = epi_divisor< T >(p, R);
+   const T* base = static_cast< const T* >(p.epi_base);
+#pragma unroll
+   for(int k = 0; k < N; ++k) {
+      A r = v[k] / d;
+      if(base) r += to_acc(base[R * p.emb + col + k]);
+      v[k] = r;
+   }
+}
 
 // Entries of gidx / row ends a warp stages in shared memory at a time.
 constexpr int kStage = 256;
@@ -334,7 +377,7 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
                         res[k] = (MODE == kLse) ? ninf : A(0);
                      } else if(MODE == kCopyLast) {
                         res[k] = v[u][c][k];
-                     } else if(MODE == kSum) {
+                     } else if(sum_mode(MODE)) {
                         res[k] = A(0) + v[u][c][k];
                      } else if(MODE == kLse) {
                         A m = ninf, sacc = A(0);
@@ -345,6 +388,7 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
                         res[k] = A(0) + v[u][c][k] * exp_acc(o[ui][c][k] - w[ui][c][k]);
                      }
                   }
+                  if(MODE == kSumEpi) epi_apply< T, VN >(p, r0 + base + u, cols.col[c], res);
                   store_vec< T, VB >(out + (r0 + base + u) * p.emb + cols.col[c], res);
                }
             }
@@ -363,6 +407,19 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
 constexpr int kPackedCh = 0;
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast< const uint4* >(p)); }
+
+// The elements of a 16-byte vector divided by d (rounded back to T).
+template < typename T >
+__device__ __forceinline__ uint4 div_raw16(uint4 v, typename AccOf< T >::type d)
+{
+   constexpr int VN = 16 / (int)sizeof(T);
+   const T* e = reinterpret_cast< const T* >(&v);
+   uint4 r;
+   T* o = reinterpret_cast< T* >(&r);
+#pragma unroll
+   for(int k = 0; k < VN; ++k) o[k] = from_acc< T >(to_acc(e[k]) / d);
+   return r;
+}
 
 // Row map with packed rows; same results as k_row_map.
 template < typename T, int MODE >
@@ -426,24 +483,26 @@ __global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) 
             const T* eo = reinterpret_cast< const T* >(&o[u % UL]);
             uint4 r;
             T* er = reinterpret_cast< T* >(&r);
+            A res[VN];
 #pragma unroll
             for(int k = 0; k < VN; ++k) {
-               A res;
                if(src[u] < 0) {
-                  res = (MODE == kLse) ? ninf : A(0);
+                  res[k] = (MODE == kLse) ? ninf : A(0);
                } else if(MODE == kCopyLast) {
-                  res = to_acc(ev[k]);
-               } else if(MODE == kSum) {
-                  res = A(0) + to_acc(ev[k]);
+                  res[k] = to_acc(ev[k]);
+               } else if(sum_mode(MODE)) {
+                  res[k] = A(0) + to_acc(ev[k]);
                } else if(MODE == kLse) {
                   A m = ninf, sacc = A(0);
                   lse_push(m, sacc, to_acc(ev[k]));
-                  res = lse_value(m, sacc);
+                  res[k] = lse_value(m, sacc);
                } else {
-                  res = A(0) + to_acc(ev[k]) * exp_acc(to_acc(eo[k]) - to_acc(ew[k]));
+                  res[k] = A(0) + to_acc(ev[k]) * exp_acc(to_acc(eo[k]) - to_acc(ew[k]));
                }
-               er[k] = from_acc< T >(res);
             }
+            if(MODE == kSumEpi) epi_apply< T, VN >(p, r0 + row, col, res);
+#pragma unroll
+            for(int k = 0; k < VN; ++k) er[k] = from_acc< T >(res[k]);
             *reinterpret_cast< uint4* >(out + (r0 + row) * p.emb + col) = r;
          }
       }
@@ -456,7 +515,7 @@ __global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) 
 // next row's load is issued before the current row's stores) and stores it to
 // out[gidx[j]] for every edge j of the row in the tile. No reduction, so rows
 // that span tiles need no partials: each tile reloads the row it starts with.
-template < typename T, int VB, int CH >
+template < typename T, int VB, int CH, bool DIV >
 __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
 {
    using A = typename AccOf< T >::type;
@@ -496,6 +555,13 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
 #pragma unroll
          for(int c = 0; c < CH; ++c)
             if(cols.ok[c]) load_vec< T, VB >(table + (int64_t)R * p.emb + cols.col[c], v[c]);
+         if(DIV) {
+            const A d = epi_divisor< T >(p, R);
+#pragma unroll
+            for(int c = 0; c < CH; ++c)
+#pragma unroll
+               for(int k = 0; k < VN; ++k) v[c][k] = v[c][k] / d;
+         }
       };
       int R = r_begin;
       int j = j_begin;
@@ -544,7 +610,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
 
 // k_scatter_rows with packed rows: the lane groups store the current row to
 // 32 / L destinations per instruction.
-template < typename T >
+template < typename T, bool DIV >
 __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
 {
    constexpr int VN = 16 / (int)sizeof(T);
@@ -588,7 +654,11 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
       ++R;
       e_end = row_end(R);
    }
-   uint4 cur = ldg16(table + (int64_t)R * p.emb + col);
+   auto load_row = [&](int Rr) __attribute__((always_inline)) -> uint4 {
+      const uint4 v = ldg16(table + (int64_t)Rr * p.emb + col);
+      return DIV ? div_raw16< T >(v, epi_divisor< T >(p, Rr)) : v;
+   };
+   uint4 cur = load_row(R);
    while(j < j_end) {
       int Rn = R + 1;
       int e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
@@ -598,7 +668,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
       }
       const bool has_next = e_end < j_end;
       uint4 nxt = cur;
-      if(has_next) nxt = ldg16(table + (int64_t)Rn * p.emb + col);
+      if(has_next) nxt = load_row(Rn);
       for(; j < e_end; j += RPI) {
          const int need = (j + RPI) < e_end ? (j + RPI) : e_end;
          if(need > gbase + gcount) {
@@ -877,6 +947,7 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
 #pragma unroll
                   for(int k = 0; k < VN; ++k)
                      fin[k] = (MODE == kLse) ? lse_value(acc[c][k], aux[c][k]) : acc[c][k];
+                  if(MODE == kSumEpi) epi_apply< T, VN >(p, R, col[c], fin);
                   store_vec< T, VB >(out + (int64_t)R * p.emb + col[c], fin);
                }
             }
@@ -890,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
             if(!ok[c]) continue;
 #pragma unroll
             for(int k = 0; k < VN; ++k) {
-               if(MODE == kSum)
+               if(sum_mode(MODE))
                   acc[c][k] += val[c][k];
                else if(MODE == kLse)
                   lse_push(acc[c][k], aux[c][k], val[c][k]);
@@ -1211,6 +1282,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
             A fin_[VN];                                                                         \
             _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_) fin_[k_] =                         \
                (MODE == kLse) ? lse_value(acc[k_], aux[k_]) : acc[k_];                          \
+            if(MODE == kSumEpi) epi_apply< T, VN >(p, (R_), col, fin_);                    \
             store_chunk< T, PB >(out + (int64_t)(R_)*p.emb + col, fin_);                         \
          }                                                                                      \
       }                                                                                         \
@@ -1266,7 +1338,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
                         load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q + i) * CBW), v[i]);
 #pragma unroll
                      for(int x = 0; x < VN; ++x) {
-                        if(MODE == kSum) {
+                        if(sum_mode(MODE)) {
                            acc[x] += v[0][x] + v[1][x] + v[2][x] + v[3][x];
                         } else {
                            const A vx[4] = {v[0][x], v[1][x], v[2][x], v[3][x]};
@@ -1283,12 +1355,12 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
                            load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q + i) * CBW), v[i]);
                         } else {
 #pragma unroll
-                           for(int x = 0; x < VN; ++x) v[i][x] = (MODE == kSum) ? A(0) : ninf;
+                           for(int x = 0; x < VN; ++x) v[i][x] = (sum_mode(MODE)) ? A(0) : ninf;
                         }
                      }
 #pragma unroll
                      for(int x = 0; x < VN; ++x) {
-                        if(MODE == kSum) {
+                        if(sum_mode(MODE)) {
                            acc[x] += v[0][x] + v[1][x] + v[2][x];
                         } else {
                            const A vx[3] = {v[0][x], v[1][x], v[2][x]};
@@ -1378,6 +1450,11 @@ __device__ __forceinline__ void fixup_finish(const SegParams& p, int64_t R, int6
       res = lse_value(m, s);
    } else {
       res = m + head_val[off];
+      if(MODE == kSumEpi) {
+         A one[1] = {res};
+         epi_apply< T, 1 >(p, R, col, one);
+         res = one[0];
+      }
    }
    static_cast< T* >(p.out)[R * p.emb + col] = from_acc< T >(res);
 }

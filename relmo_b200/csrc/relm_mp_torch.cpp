@@ -4,9 +4,11 @@
 // src/_ops/mp/mp_ops.cpp:3754-3838) for the hot path and the pack ops its call
 // sites use, with:
 //   - CUDA kernels for fanout_scatter, fanout_scatter_backward, fanin_reduce,
-//     fanin_reduce_sum_backward, fanin_reduce_logsumexp_backward, all running
-//     through librelm_mp_b200.so (include/relm_mp.h). There is no CPU or ATen
-//     fallback for CUDA tensors: an unsupported dtype raises.
+//     fanin_reduce_sum_backward, fanin_reduce_logsumexp_backward and the four
+//     LGAN ops (lgan_pool_reduce, lgan_relation_graph_step and their
+//     backwards, sum / mean modes), all running through librelm_mp_b200.so
+//     (include/relm_mp.h). There is no CPU or ATen fallback for CUDA tensors:
+//     an unsupported dtype raises.
 //   - Meta kernels (shapes only) so the ops trace under torch.compile / fake
 //     tensors.
 //   - CompositeImplicitAutograd pack ops (index arithmetic + cat, as
@@ -143,6 +145,7 @@ struct PlanEntry {
    Tensor cover;         // gather-index coverage bitmap (int32 words), computed on first use
    int cover_dups = -1;  // -1 unknown, 0 each gather row at most once, 1 repeats
    int64_t nonempty_rows = -1;  // output rows holding edges, read on first use
+   Tensor gather_counts;        // int32 edges per gathered row, computed on first use
 };
 using PlanPtr = std::shared_ptr< PlanEntry >;
 
@@ -190,7 +193,8 @@ class PlanCache {
       );
       check_status(rc, "plan build");
       auto entry = std::make_shared< PlanEntry >(
-         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1, -1}
+         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1, -1,
+                   Tensor()}
       );
       std::lock_guard< std::mutex > lock(mu_);
       ++builds_;
@@ -239,6 +243,19 @@ class PlanCache {
       e->cover_dups = dups;
    }
 
+   // Edges per gathered row of the entry's plan (computed once per plan).
+   const int32_t* gather_counts(const PlanPtr& e, const Tensor& like)
+   {
+      std::lock_guard< std::mutex > lock(cover_mu_);
+      if(!e->gather_counts.defined()) {
+         Tensor counts = at::empty({std::max< int64_t >(e->gather_rows, 1)}, like.options().dtype(at::kInt));
+         check_status(relm_mp_plan_gather_counts(&e->plan, counts.data_ptr< int32_t >(), stream_of(like)),
+                      "gather counts");
+         e->gather_counts = counts;
+      }
+      return e->gather_counts.data_ptr< int32_t >();
+   }
+
    void clear()
    {
       std::lock_guard< std::mutex > lock(mu_);
@@ -250,7 +267,9 @@ class PlanCache {
       std::lock_guard< std::mutex > lock(mu_);
       evict_dead_locked();
       int64_t bytes = 0;
-      for(const auto& e : entries_) bytes += e->memory.numel() + (e->cover.defined() ? e->cover.numel() * 4 : 0);
+      for(const auto& e : entries_)
+         bytes += e->memory.numel() + (e->cover.defined() ? e->cover.numel() * 4 : 0) +
+                  (e->gather_counts.defined() ? e->gather_counts.numel() * 4 : 0);
       return {(int64_t)entries_.size(), hits_, builds_, bytes, (int64_t)capacity_};
    }
 
@@ -725,6 +744,321 @@ std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_pa
 // build_torch / build_cuda_tag describe the torch this layer was compiled
 // against (what the reference loader checks, mp_runtime.py:175-228); the
 // kernel library's own metadata follows.
+
+// ---- LGAN ops, sum / mean modes (mp_ops.cpp:3350-3743) ------------------------
+//
+// Each indexed reduction (mp_common.py:88-118) is a planned sum with its fused
+// epilogue: out = base + sum / max(count, 1) (mean) or / max(arity, 1) (pool).
+// Plans come from the cache, so the layers of one LGAN forward and backward
+// sort each index pair once. int32 indices are accepted as the reference does
+// and widened to int64 (a new tensor per call, so their plans are not reused).
+
+constexpr int64_t kModeMean = 2;
+
+void check_int32_or_int64_index(const Tensor& t, const char* name)
+{
+   check_rank(t, 1, name);
+   TORCH_CHECK(t.scalar_type() == at::kLong || t.scalar_type() == at::kInt, name,
+               " must have dtype torch.int64 or torch.int32.");
+}
+
+Tensor index64(const Tensor& t) { return t.scalar_type() == at::kLong ? contig(t) : t.to(at::kLong).contiguous(); }
+
+// [0, n) on the tensor's device: the gather index of the slot pooling. One
+// cached arange per device, grown when needed, so pooling plans stay cached.
+Tensor identity_index(int64_t n, const Tensor& like)
+{
+   static std::mutex mu;
+   static std::vector< Tensor > per_device;
+   std::lock_guard< std::mutex > lock(mu);
+   const int dev = like.device().index();
+   if((int)per_device.size() <= dev) per_device.resize(dev + 1);
+   Tensor& a = per_device[dev];
+   if(!a.defined() || a.numel() < n)
+      a = at::arange(std::max< int64_t >(n, 1024), like.options().dtype(at::kLong));
+   return a.narrow(0, 0, n);
+}
+
+struct LganIndices {
+   Tensor rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent;
+};
+
+LganIndices lgan_indices(const Tensor& rr_src, const Tensor& rr_dst, const Tensor& tn_rel, const Tensor& tn_ent,
+                         const Tensor& nn_rel, const Tensor& nn_ent)
+{
+   check_int32_or_int64_index(rr_src, "rr_src");
+   check_int32_or_int64_index(rr_dst, "rr_dst");
+   check_int32_or_int64_index(tn_rel, "tn_rel");
+   check_int32_or_int64_index(tn_ent, "tn_ent");
+   check_int32_or_int64_index(nn_rel, "nn_rel");
+   check_int32_or_int64_index(nn_ent, "nn_ent");
+   TORCH_CHECK(rr_src.size(0) == rr_dst.size(0), "rr_src and rr_dst must have equal length.");
+   TORCH_CHECK(tn_rel.size(0) == tn_ent.size(0), "tn_rel and tn_ent must have equal length.");
+   TORCH_CHECK(nn_rel.size(0) == nn_ent.size(0), "nn_rel and nn_ent must have equal length.");
+   return {index64(rr_src), index64(rr_dst), index64(tn_rel), index64(tn_ent), index64(nn_rel), index64(nn_ent)};
+}
+
+void check_lgan_mode(int64_t mode, const char* op)
+{
+   TORCH_CHECK(mode == kModeSum || mode == kModeMean, op, " supports only mode 0=sum or 2=mean.");
+}
+
+void check_all_on(const Tensor& ref, std::initializer_list< const Tensor* > ts, const char* op)
+{
+   for(const Tensor* t : ts)
+      TORCH_CHECK(t->device() == ref.device(), op, " expects all tensors on the same device.");
+}
+
+// Planned sum with epilogue: out = base + sum / divisor over the plan of (out_index, gather_index).
+void planned_sum_ex(const PlanPtr& e, relm_mp_dtype dt, const Tensor& table, const Tensor* base,
+                    const int64_t* row_div, bool by_count, Tensor& out, const char* op)
+{
+   const int64_t emb = table.size(1);
+   Tensor scratch = byte_buffer(relm_mp_plan_reduce_scratch_bytes(&e->plan, emb, dt, RELM_MP_MODE_SUM), table);
+   check_status(relm_mp_plan_reduce_ex(&e->plan, dt, table.data_ptr(), emb, base ? base->data_ptr() : nullptr,
+                                       row_div, by_count ? 1 : 0, out.data_ptr(), scratch.data_ptr(),
+                                       (size_t)scratch.numel(), stream_of(table)),
+                op);
+}
+
+// out[t] = base[t] + (sum of table[src[e]] over dst[e] = t) (/ max(count, 1) in mean mode).
+void lgan_forward_agg(relm_mp_dtype dt, const Tensor& table, const Tensor& src, const Tensor& dst, int64_t rows,
+                      const char* src_name, const char* dst_name, const Tensor* base, bool mean, Tensor& out,
+                      const char* op)
+{
+   if(src.numel() == 0 || rows == 0 || table.size(1) == 0) {  // mp_ops.cpp:3433-3437
+      if(base)
+         out.copy_(*base);
+      else
+         out.zero_();
+      return;
+   }
+   const PlanPtr e = PlanCache::get().lookup(dst, src, rows, rows, table.size(0), dst_name, src_name, false);
+   planned_sum_ex(e, dt, table, base, nullptr, mean, out, op);
+}
+
+// The reverse (mp_ops.cpp:3527-3555): out[s] = base[s] + sum over src[e] = s of
+// grad[dst[e]] (/ max(count of dst[e], 1) in mean mode).
+void lgan_reverse_agg(relm_mp_dtype dt, const Tensor& grad, const Tensor& src, const Tensor& dst, int64_t rows,
+                      const char* src_name, const char* dst_name, const Tensor* base, bool mean, Tensor& out,
+                      const char* op)
+{
+   if(src.numel() == 0 || rows == 0 || grad.size(1) == 0) {
+      if(base)
+         out.copy_(*base);
+      else
+         out.zero_();
+      return;
+   }
+   const PlanPtr e = PlanCache::get().lookup(src, dst, rows, rows, grad.size(0), src_name, dst_name, false);
+   Tensor table = grad;
+   if(mean) {
+      table = at::empty_like(grad);
+      const int32_t* counts = PlanCache::get().gather_counts(e, grad);
+      check_status(relm_mp_divide_rows(dt, grad.data_ptr(), grad.size(0), grad.size(1), counts, table.data_ptr(),
+                                       stream_of(grad)),
+                   op);
+   }
+   planned_sum_ex(e, dt, table, base, nullptr, false, out, op);
+}
+
+// x1 = x + agg_rr(x); tn = agg_tn(x1); nn = agg_nn(x1)
+std::tuple< Tensor, Tensor, Tensor > lgan_graph_forward(relm_mp_dtype dt, const Tensor& x, const LganIndices& ix,
+                                                        int64_t entity_dim_size, bool mean, const char* op)
+{
+   const int64_t R = x.size(0), emb = x.size(1);
+   Tensor x1 = at::empty({R, emb}, x.options());
+   Tensor tn = at::empty({entity_dim_size, emb}, x.options());
+   Tensor nn = at::empty({entity_dim_size, emb}, x.options());
+   lgan_forward_agg(dt, x, ix.rr_src, ix.rr_dst, R, "rr_src", "rr_dst", &x, mean, x1, op);
+   lgan_forward_agg(dt, x1, ix.tn_rel, ix.tn_ent, entity_dim_size, "tn_rel", "tn_ent", nullptr, mean, tn, op);
+   lgan_forward_agg(dt, x1, ix.nn_rel, ix.nn_ent, entity_dim_size, "nn_rel", "nn_ent", nullptr, mean, nn, op);
+   return {x1, tn, nn};
+}
+
+// Gradient of the graph step's input from the gradients of (x1, tn, nn).
+Tensor lgan_graph_backward(relm_mp_dtype dt, const Tensor& gx, const Tensor& gtn, const Tensor& gnn,
+                           const LganIndices& ix, int64_t relation_count, bool mean, const char* op)
+{
+   const int64_t emb = gx.size(1);
+   Tensor g1 = at::empty({relation_count, emb}, gx.options());
+   lgan_reverse_agg(dt, gtn, ix.tn_rel, ix.tn_ent, relation_count, "tn_rel", "tn_ent", &gx, mean, g1, op);
+   lgan_reverse_agg(dt, gnn, ix.nn_rel, ix.nn_ent, relation_count, "nn_rel", "nn_ent", &g1, mean, g1, op);
+   Tensor g0 = at::empty({relation_count, emb}, gx.options());
+   lgan_reverse_agg(dt, g1, ix.rr_src, ix.rr_dst, relation_count, "rr_src", "rr_dst", &g1, mean, g0, op);
+   return g0;
+}
+
+void check_lgan_grads(const Tensor& gx, const Tensor& gtn, const Tensor& gnn, int64_t relation_count, const char* op)
+{
+   check_rank(gx, 2, "grad_relation_pair_x");
+   check_rank(gtn, 2, "grad_tn_msgs");
+   check_rank(gnn, 2, "grad_nn_msgs");
+   TORCH_CHECK(relation_count >= 0, "relation_count must be >= 0.");
+   TORCH_CHECK(gx.size(0) == relation_count, op, ": grad_relation_pair_x must have relation_count rows.");
+   TORCH_CHECK(gtn.size(1) == gx.size(1) && gnn.size(1) == gx.size(1) && gtn.size(0) == gnn.size(0), op,
+               ": grad_tn_msgs and grad_nn_msgs must be [entity_dim_size, emb] like each other.");
+   TORCH_CHECK(gtn.scalar_type() == gx.scalar_type() && gnn.scalar_type() == gx.scalar_type(), op,
+               ": the three gradients must share dtype.");
+}
+
+// mp_ops.cpp:3574-3656
+std::tuple< Tensor, Tensor, Tensor > lgan_relation_graph_step_cuda(const Tensor& relation_pair_x, const Tensor& rr_src,
+                                                                   const Tensor& rr_dst, const Tensor& tn_rel,
+                                                                   const Tensor& tn_ent, const Tensor& nn_rel,
+                                                                   const Tensor& nn_ent, int64_t entity_dim_size,
+                                                                   int64_t mode)
+{
+   const char* op = "lgan_relation_graph_step";
+   check_rank(relation_pair_x, 2, "relation_pair_x");
+   check_all_on(relation_pair_x, {&rr_src, &rr_dst, &tn_rel, &tn_ent, &nn_rel, &nn_ent},
+                "lgan_relation_graph_step");
+   TORCH_CHECK(entity_dim_size >= 0, "entity_dim_size must be >= 0.");
+   const LganIndices ix = lgan_indices(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent);
+   check_lgan_mode(mode, op);
+   c10::cuda::CUDAGuard guard(relation_pair_x.device());
+   const relm_mp_dtype dt = to_dtype(relation_pair_x, op);
+   return lgan_graph_forward(dt, contig(relation_pair_x), ix, entity_dim_size, mode == kModeMean, op);
+}
+
+// mp_ops.cpp:3658-3743
+Tensor lgan_relation_graph_step_backward_cuda(const Tensor& grad_relation_pair_x, const Tensor& grad_tn_msgs,
+                                              const Tensor& grad_nn_msgs, const Tensor& rr_src, const Tensor& rr_dst,
+                                              const Tensor& tn_rel, const Tensor& tn_ent, const Tensor& nn_rel,
+                                              const Tensor& nn_ent, int64_t relation_count, int64_t mode)
+{
+   const char* op = "lgan_relation_graph_step_backward";
+   check_all_on(grad_relation_pair_x, {&grad_tn_msgs, &grad_nn_msgs, &rr_src, &rr_dst, &tn_rel, &tn_ent, &nn_rel,
+                                       &nn_ent},
+                op);
+   const LganIndices ix = lgan_indices(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent);
+   check_lgan_grads(grad_relation_pair_x, grad_tn_msgs, grad_nn_msgs, relation_count, op);
+   check_lgan_mode(mode, op);
+   c10::cuda::CUDAGuard guard(grad_relation_pair_x.device());
+   const relm_mp_dtype dt = to_dtype(grad_relation_pair_x, op);
+   return lgan_graph_backward(dt, contig(grad_relation_pair_x), contig(grad_tn_msgs), contig(grad_nn_msgs), ix,
+                              relation_count, mode == kModeMean, op);
+}
+
+// The slot-pooling plan: output rows = relation instances, gather = slot ids.
+PlanPtr pool_plan(const Tensor& slot_to_rel, int64_t relation_count, const Tensor& like)
+{
+   const int64_t S = slot_to_rel.numel();
+   return PlanCache::get().lookup(slot_to_rel, identity_index(S, like), relation_count, relation_count, S,
+                                  "slot_to_relation_instance", "slot", false);
+}
+
+// mp_ops.cpp:3350-3469
+std::tuple< Tensor, Tensor, Tensor > lgan_pool_reduce_cuda(const Tensor& slot_messages,
+                                                           const Tensor& slot_to_relation_instance,
+                                                           const Tensor& relation_instance_arities,
+                                                           const Tensor& rr_src, const Tensor& rr_dst,
+                                                           const Tensor& tn_rel, const Tensor& tn_ent,
+                                                           const Tensor& nn_rel, const Tensor& nn_ent,
+                                                           int64_t entity_dim_size, int64_t mode)
+{
+   const char* op = "lgan_pool_reduce";
+   check_rank(slot_messages, 2, "slot_messages");
+   check_int32_or_int64_index(slot_to_relation_instance, "slot_to_relation_instance");
+   check_int64_index(relation_instance_arities, "relation_instance_arities");
+   check_all_on(slot_messages, {&slot_to_relation_instance, &relation_instance_arities, &rr_src, &rr_dst, &tn_rel,
+                                &tn_ent, &nn_rel, &nn_ent},
+                op);
+   TORCH_CHECK(entity_dim_size >= 0, "entity_dim_size must be >= 0.");
+   TORCH_CHECK(slot_to_relation_instance.size(0) == slot_messages.size(0),
+               "slot_to_relation_instance length must match slot_messages rows.");
+   const LganIndices ix = lgan_indices(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent);
+   check_lgan_mode(mode, op);
+   c10::cuda::CUDAGuard guard(slot_messages.device());
+   const relm_mp_dtype dt = to_dtype(slot_messages, op);
+   const Tensor slots = contig(slot_messages);
+   const Tensor s2r = index64(slot_to_relation_instance);
+   const Tensor arities = contig(relation_instance_arities);
+   const int64_t R = arities.size(0), emb = slots.size(1);
+   // x[r] = (sum of the slot rows of r) / max(arity[r], 1)  (mp_ops.cpp:3424-3432)
+   Tensor x0 = at::empty({R, emb}, slots.options());
+   if(slots.size(0) == 0 || R == 0 || emb == 0) {
+      x0.zero_();
+   } else {
+      const PlanPtr e = pool_plan(s2r, R, slots);
+      planned_sum_ex(e, dt, slots, nullptr, arities.data_ptr< int64_t >(), false, x0, op);
+   }
+   return lgan_graph_forward(dt, x0, ix, entity_dim_size, mode == kModeMean, op);
+}
+
+// mp_ops.cpp:3471-3572
+Tensor lgan_pool_reduce_backward_cuda(const Tensor& grad_relation_pair_x, const Tensor& grad_tn_msgs,
+                                      const Tensor& grad_nn_msgs, const Tensor& slot_to_relation_instance,
+                                      const Tensor& relation_instance_arities, const Tensor& rr_src,
+                                      const Tensor& rr_dst, const Tensor& tn_rel, const Tensor& tn_ent,
+                                      const Tensor& nn_rel, const Tensor& nn_ent, int64_t relation_count,
+                                      int64_t mode)
+{
+   const char* op = "lgan_pool_reduce_backward";
+   check_int32_or_int64_index(slot_to_relation_instance, "slot_to_relation_instance");
+   check_int64_index(relation_instance_arities, "relation_instance_arities");
+   check_all_on(grad_relation_pair_x, {&grad_tn_msgs, &grad_nn_msgs, &slot_to_relation_instance,
+                                       &relation_instance_arities, &rr_src, &rr_dst, &tn_rel, &tn_ent, &nn_rel,
+                                       &nn_ent},
+                op);
+   const LganIndices ix = lgan_indices(rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent);
+   check_lgan_grads(grad_relation_pair_x, grad_tn_msgs, grad_nn_msgs, relation_count, op);
+   check_lgan_mode(mode, op);
+   TORCH_CHECK(relation_instance_arities.size(0) >= relation_count,
+               "relation_instance_arities must have at least relation_count entries.");
+   c10::cuda::CUDAGuard guard(grad_relation_pair_x.device());
+   const relm_mp_dtype dt = to_dtype(grad_relation_pair_x, op);
+   const Tensor gx = contig(grad_relation_pair_x);
+   const Tensor g0 = lgan_graph_backward(dt, gx, contig(grad_tn_msgs), contig(grad_nn_msgs), ix, relation_count,
+                                         mode == kModeMean, op);
+   const Tensor s2r = index64(slot_to_relation_instance);
+   const Tensor arities = contig(relation_instance_arities);
+   const int64_t S = s2r.size(0), emb = gx.size(1);
+   Tensor grad_slots = at::empty({S, emb}, gx.options());
+   if(S == 0 || emb == 0) return grad_slots;
+   // grad_slot[s] = g0[r] / max(arity[r], 1) through the pooling plan (every slot is one edge)
+   const PlanPtr e = pool_plan(s2r, relation_count, gx);
+   check_status(relm_mp_plan_scatter_rows_div(&e->plan, dt, g0.data_ptr(), emb, arities.data_ptr< int64_t >(),
+                                              nullptr, grad_slots.data_ptr(), stream_of(gx)),
+                op);
+   return grad_slots;
+}
+
+std::tuple< Tensor, Tensor, Tensor > lgan_pool_reduce_meta(const Tensor& slot_messages, const Tensor&,
+                                                           const Tensor& arities, const Tensor&, const Tensor&,
+                                                           const Tensor&, const Tensor&, const Tensor&, const Tensor&,
+                                                           int64_t entity_dim_size, int64_t)
+{
+   const int64_t emb = slot_messages.size(1);
+   return {at::empty({arities.size(0), emb}, slot_messages.options()),
+           at::empty({entity_dim_size, emb}, slot_messages.options()),
+           at::empty({entity_dim_size, emb}, slot_messages.options())};
+}
+
+Tensor lgan_pool_reduce_backward_meta(const Tensor& grad_relation_pair_x, const Tensor&, const Tensor&,
+                                      const Tensor& slot_to_relation_instance, const Tensor&, const Tensor&,
+                                      const Tensor&, const Tensor&, const Tensor&, const Tensor&, const Tensor&,
+                                      int64_t, int64_t)
+{
+   return at::empty({slot_to_relation_instance.size(0), grad_relation_pair_x.size(1)},
+                    grad_relation_pair_x.options());
+}
+
+std::tuple< Tensor, Tensor, Tensor > lgan_relation_graph_step_meta(const Tensor& x, const Tensor&, const Tensor&,
+                                                                   const Tensor&, const Tensor&, const Tensor&,
+                                                                   const Tensor&, int64_t entity_dim_size, int64_t)
+{
+   return {at::empty_like(x), at::empty({entity_dim_size, x.size(1)}, x.options()),
+           at::empty({entity_dim_size, x.size(1)}, x.options())};
+}
+
+Tensor lgan_relation_graph_step_backward_meta(const Tensor& grad_relation_pair_x, const Tensor&, const Tensor&,
+                                              const Tensor&, const Tensor&, const Tensor&, const Tensor&,
+                                              const Tensor&, const Tensor&, int64_t relation_count, int64_t)
+{
+   return at::empty({relation_count, grad_relation_pair_x.size(1)}, grad_relation_pair_x.options());
+}
+
 std::string build_info()
 {
    return std::string("build_torch=") + RELM_MP_BUILD_TORCH_VERSION + ";build_cuda_tag=" + RELM_MP_BUILD_CUDA_TAG
@@ -761,6 +1095,25 @@ TORCH_LIBRARY(relm_mp, m)
       "fanin_pack_from_edges(Tensor[] rel_parts, Tensor[] edge_src_parts, Tensor[] edge_dst_parts, int[] rel_part_ids, "
       "int[] arity_parts, int[] pos_parts, int mode) -> (Tensor, Tensor, Tensor)"
    );
+   m.def(
+      "lgan_pool_reduce(Tensor slot_messages, Tensor slot_to_relation_instance, Tensor relation_instance_arities, "
+      "Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int entity_dim_size, "
+      "int mode) -> (Tensor, Tensor, Tensor)"
+   );
+   m.def(
+      "lgan_pool_reduce_backward(Tensor grad_relation_pair_x, Tensor grad_tn_msgs, Tensor grad_nn_msgs, "
+      "Tensor slot_to_relation_instance, Tensor relation_instance_arities, Tensor rr_src, Tensor rr_dst, "
+      "Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int relation_count, int mode) -> Tensor"
+   );
+   m.def(
+      "lgan_relation_graph_step(Tensor relation_pair_x, Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, "
+      "Tensor nn_rel, Tensor nn_ent, int entity_dim_size, int mode) -> (Tensor, Tensor, Tensor)"
+   );
+   m.def(
+      "lgan_relation_graph_step_backward(Tensor grad_relation_pair_x, Tensor grad_tn_msgs, Tensor grad_nn_msgs, "
+      "Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int relation_count, "
+      "int mode) -> Tensor"
+   );
    m.def("build_info() -> str");
 }
 
@@ -771,6 +1124,10 @@ TORCH_LIBRARY_IMPL(relm_mp, CUDA, m)
    m.impl("fanin_reduce", relm_b200::fanin_reduce_cuda);
    m.impl("fanin_reduce_sum_backward", relm_b200::fanin_reduce_sum_backward_cuda);
    m.impl("fanin_reduce_logsumexp_backward", relm_b200::fanin_reduce_logsumexp_backward_cuda);
+   m.impl("lgan_pool_reduce", relm_b200::lgan_pool_reduce_cuda);
+   m.impl("lgan_pool_reduce_backward", relm_b200::lgan_pool_reduce_backward_cuda);
+   m.impl("lgan_relation_graph_step", relm_b200::lgan_relation_graph_step_cuda);
+   m.impl("lgan_relation_graph_step_backward", relm_b200::lgan_relation_graph_step_backward_cuda);
 }
 
 TORCH_LIBRARY_IMPL(relm_mp, Meta, m)
@@ -780,6 +1137,10 @@ TORCH_LIBRARY_IMPL(relm_mp, Meta, m)
    m.impl("fanin_reduce", relm_b200::fanin_reduce_meta);
    m.impl("fanin_reduce_sum_backward", relm_b200::fanin_reduce_sum_backward_meta);
    m.impl("fanin_reduce_logsumexp_backward", relm_b200::fanin_reduce_logsumexp_backward_meta);
+   m.impl("lgan_pool_reduce", relm_b200::lgan_pool_reduce_meta);
+   m.impl("lgan_pool_reduce_backward", relm_b200::lgan_pool_reduce_backward_meta);
+   m.impl("lgan_relation_graph_step", relm_b200::lgan_relation_graph_step_meta);
+   m.impl("lgan_relation_graph_step_backward", relm_b200::lgan_relation_graph_step_backward_meta);
 }
 
 TORCH_LIBRARY_IMPL(relm_mp, CompositeImplicitAutograd, m)

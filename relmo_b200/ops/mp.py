@@ -11,8 +11,12 @@ the four pack helpers, ``available``, ``assert_runtime_compat``, ``__all__``
 - CPU tensors, and fanin modes other than sum/logsumexp, use the reference's
   ATen formulas (``mp_pack``), as relmo's Python fallback does.
 
-The fused block/program and LGAN ops of relmo are a different model family and
-are not part of this package.
+The LGAN indexed reductions (``_lgan_pool_reduce``, ``_lgan_relation_graph_step``,
+mp.py:468-525, modes ``"sum"`` / ``"mean"``) follow the same policy: CUDA
+tensors run ``torch.ops.relm_mp.lgan_*`` through the reference's autograd
+wrappers, CPU tensors the reference's Python formulas. The fused block /
+program ops of relmo (``block_*``, ``program_*``, ``_lgan_build_pointwise_step``)
+are a different model family and are not part of this package.
 """
 
 from __future__ import annotations
@@ -20,6 +24,13 @@ from __future__ import annotations
 from .mp_autograd import _FaninReduceLogSumExpFunction, _FaninReduceSumFunction, _FanoutScatterFunction
 from .mp_constants import MODE_LOGSUMEXP, MODE_MEAN, MODE_SUM
 from .mp_dispatch import dispatch_namespace_op, is_cuda, require_gpu_custom
+from .mp_lgan import (
+    _LGANPoolReduceFunction,
+    _LGANRelationGraphStepFunction,
+    lgan_pool_reduce_python,
+    lgan_relation_graph_step_python,
+    resolve_lgan_mode,
+)
 from .mp_pack import (
     fanin_pack_from_edges_python,
     fanin_pack_multi_python,
@@ -99,6 +110,36 @@ def fanin_pack_from_edges(rel_parts, edge_src_parts, edge_dst_parts, rel_part_id
         int(mode),
         fallback=fanin_pack_from_edges_python,
     )
+
+
+def _lgan_pool_reduce(slot_messages, slot_to_relation_instance, relation_instance_arities, rr_src, rr_dst, tn_rel,
+                      tn_ent, nn_rel, nn_ent, *, entity_dim_size: int, mode: str):
+    """Pool slot messages to relation instances (mean over each instance's
+    arity), then run the RR / TN / NN indexed reductions; returns
+    ``(relation_pair_x, tn_msgs, nn_msgs)``."""
+
+    require_torch("_lgan_pool_reduce")
+    mode_int = resolve_lgan_mode("_lgan_pool_reduce", mode)
+    args = (slot_messages, slot_to_relation_instance, relation_instance_arities, rr_src, rr_dst, tn_rel, tn_ent,
+            nn_rel, nn_ent, int(entity_dim_size), int(mode_int))
+    if is_cuda(slot_messages):
+        require_gpu_custom("lgan_pool_reduce")
+        return _LGANPoolReduceFunction.apply(*args)
+    return lgan_pool_reduce_python(*args)
+
+
+def _lgan_relation_graph_step(relation_pair_x, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, *,
+                              entity_dim_size: int, mode: str):
+    """RR / TN / NN propagation on pooled relation-instance embeddings; returns
+    ``(relation_pair_x + rr_msgs, tn_msgs, nn_msgs)``."""
+
+    require_torch("_lgan_relation_graph_step")
+    mode_int = resolve_lgan_mode("_lgan_relation_graph_step", mode)
+    args = (relation_pair_x, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, int(entity_dim_size), int(mode_int))
+    if is_cuda(relation_pair_x):
+        require_gpu_custom("lgan_relation_graph_step")
+        return _LGANRelationGraphStepFunction.apply(*args)
+    return lgan_relation_graph_step_python(*args)
 
 
 def clear_plan_cache() -> None:

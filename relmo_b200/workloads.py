@@ -10,6 +10,10 @@ configurations:
   destinations, sorted or unsorted.
 * ``cfg5`` - skewed stress test: N=2**22, E=2**26, D=32, 64 hub destinations
   with 100k messages each, the rest uniform.
+* ``lgan`` - LGAN pool + graph step (sum / mean indexed reductions): 2**17
+  entities, 2**20 relation instances of arity 1..3, 4 RR edges per instance,
+  D=64 (no reference benchmark exists for these ops; shapes of a planning
+  batch).
 
 Everything is drawn from one ``torch.Generator`` per call in a fixed order, so a
 seed fully determines a workload on a given device type.
@@ -192,6 +196,115 @@ def algorithmic_bytes(op: str, wl: FanWorkload, elem_bytes: int | None = None) -
     if op == "fanin_lse_bwd":
         return 2 * e * d * s + 2 * ud * d * s + 16 * e
     raise ValueError(op)
+
+
+# ---- LGAN batches (lgan_pool_reduce / lgan_relation_graph_step) ----------------------
+
+
+@dataclass
+class LganWorkload:
+    """Inputs of one LGAN pool + graph step and its backward.
+
+    ``R`` relation instances of arity 1..max_arity own ``S`` slots
+    (``slot_to_relation_instance`` = each instance repeated arity times, in
+    order); every slot names a uniform random entity of ``N``. TN edges join
+    each instance to the entity of its first slot, NN edges to the entities of
+    its other slots, RR edges are ``rr_per_relation * R`` uniform instance
+    pairs. Upstream gradients ``grad_x [R, D]``, ``grad_tn / grad_nn [N, D]``.
+    """
+
+    name: str
+    slots: torch.Tensor
+    slot_to_rel: torch.Tensor
+    arities: torch.Tensor
+    rr_src: torch.Tensor
+    rr_dst: torch.Tensor
+    tn_rel: torch.Tensor
+    tn_ent: torch.Tensor
+    nn_rel: torch.Tensor
+    nn_ent: torch.Tensor
+    entity_dim_size: int
+    grad_x: torch.Tensor
+    grad_tn: torch.Tensor
+    grad_nn: torch.Tensor
+
+    @property
+    def emb(self) -> int:
+        return int(self.slots.size(1))
+
+    @property
+    def relation_count(self) -> int:
+        return int(self.arities.numel())
+
+    @property
+    def num_slots(self) -> int:
+        return int(self.slots.size(0))
+
+    def graph(self) -> tuple:
+        return (self.rr_src, self.rr_dst, self.tn_rel, self.tn_ent, self.nn_rel, self.nn_ent)
+
+    def to(self, device, dtype: torch.dtype | None = None) -> "LganWorkload":
+        def v(t):
+            return t.to(device=device, dtype=dtype) if dtype is not None else t.to(device)
+
+        return LganWorkload(
+            self.name, v(self.slots), self.slot_to_rel.to(device), self.arities.to(device), self.rr_src.to(device),
+            self.rr_dst.to(device), self.tn_rel.to(device), self.tn_ent.to(device), self.nn_rel.to(device),
+            self.nn_ent.to(device), self.entity_dim_size, v(self.grad_x), v(self.grad_tn), v(self.grad_nn),
+        )
+
+
+def lgan(seed: int = 0, device="cpu", entities: int = 1 << 17, relations: int = 1 << 20, max_arity: int = 3,
+         rr_per_relation: int = 4, emb: int = 64, dtype: torch.dtype = torch.float32) -> LganWorkload:
+    """Synthetic LGAN batch (shapes of a planning-domain batch: ~2 slots per
+    relation instance, 8x more instances than entities). Draw order: arities,
+    slot entities, RR pairs, slot values, the three upstream gradients."""
+
+    g = _gen(device, seed)
+    kw = dict(device=device, generator=g)
+    R, N = int(relations), int(entities)
+    arities = torch.randint(1, int(max_arity) + 1, (R,), dtype=torch.int64, **kw)
+    slot_to_rel = torch.repeat_interleave(torch.arange(R, dtype=torch.int64, device=device), arities)
+    S = int(slot_to_rel.numel())
+    slot_ent = torch.randint(0, N, (S,), dtype=torch.int64, **kw)
+    first = torch.ones(S, dtype=torch.bool, device=device)
+    first[1:] = slot_to_rel[1:] != slot_to_rel[:-1]
+    rr_src = torch.randint(0, R, (int(rr_per_relation) * R,), dtype=torch.int64, **kw)
+    rr_dst = torch.randint(0, R, (int(rr_per_relation) * R,), dtype=torch.int64, **kw)
+    slots = torch.randn(S, int(emb), dtype=torch.float32, **kw)
+    grad_x = torch.randn(R, int(emb), dtype=torch.float32, **kw)
+    grad_tn = torch.randn(N, int(emb), dtype=torch.float32, **kw)
+    grad_nn = torch.randn(N, int(emb), dtype=torch.float32, **kw)
+    wl = LganWorkload(
+        "lgan", slots, slot_to_rel, arities, rr_src, rr_dst, slot_to_rel[first], slot_ent[first],
+        slot_to_rel[~first], slot_ent[~first], N, grad_x, grad_tn, grad_nn,
+    )
+    return wl.to(device, dtype) if dtype != torch.float32 else wl
+
+
+def lgan_algorithmic_bytes(wl: LganWorkload, elem_bytes: int | None = None) -> dict[str, int]:
+    """Compulsory HBM traffic of lgan_pool_reduce and its backward (the
+    reference's composition: every intermediate row written and read once,
+    every distinct gathered row read once, every int64 index read once; the
+    pool's slot rows and the arities read once)."""
+
+    s = elem_bytes if elem_bytes is not None else wl.slots.element_size()
+    rb = wl.emb * s
+    R, N, S = wl.relation_count, wl.entity_dim_size, wl.num_slots
+    e_rr, e_tn, e_nn = int(wl.rr_src.numel()), int(wl.tn_rel.numel()), int(wl.nn_rel.numel())
+
+    def uniq(t) -> int:
+        return int(torch.unique(t).numel()) if t.numel() else 0
+
+    fwd = (S * rb + 8 * S + 8 * R + R * rb                      # pool: slots, index, arities -> x0
+           + uniq(wl.rr_src) * rb + 16 * e_rr + R * rb + R * rb  # x1 = x0 + agg_rr(x0)
+           + uniq(wl.tn_rel) * rb + 16 * e_tn + N * rb          # tn = agg(x1)
+           + uniq(wl.nn_rel) * rb + 16 * e_nn + N * rb)         # nn = agg(x1)
+    bwd = (R * rb + uniq(wl.tn_ent) * rb + 16 * e_tn + R * rb   # g1 = gx + rev_tn(gtn)
+           + uniq(wl.nn_ent) * rb + 16 * e_nn + R * rb + R * rb  # g1 += rev_nn(gnn)
+           + uniq(wl.rr_dst) * rb + 16 * e_rr + R * rb + R * rb  # g0 = g1 + rev_rr(g1)
+           + R * rb + 8 * R + 8 * S + S * rb)                   # grad_slots = g0[s2r] / arity
+    return {"lgan_fwd": fwd, "lgan_bwd": bwd}
 
 
 # ---- relational batches (RelationalGNN workloads) ------------------------------------

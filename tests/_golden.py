@@ -34,6 +34,28 @@ def load_cases() -> list[Case]:
     return cases
 
 
+@dataclass
+class LganCase:
+    name: str
+    op: str
+    args: list  # numpy arrays or ints
+    outs: list[np.ndarray]
+    raises: str | None
+    message: str | None
+
+
+def load_lgan_cases() -> list[LganCase]:
+    z = np.load(GOLDEN / "ref_lgan.npz")
+    meta = json.loads(bytes(z["__meta__"]).decode())
+    cases = []
+    for name in sorted(meta):
+        entry = meta[name]
+        args = [z[a["tensor"]] if "tensor" in a else a["int"] for a in entry["args"]]
+        outs = [z[f"{name}__out{k}"] for k in range(entry.get("outputs") or 0)]
+        cases.append(LganCase(name, entry["op"], args, outs, entry["raises"], entry.get("message")))
+    return cases
+
+
 def load_cfg1() -> tuple[dict, dict[str, np.ndarray]]:
     z = np.load(GOLDEN / "ref_cfg1.npz")
     meta = json.loads(bytes(z["__meta__"]).decode())

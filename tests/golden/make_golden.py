@@ -5,6 +5,7 @@ torch namespace, the same one ``relmo_b200`` registers):
 
     python oracle/build_ref.py          # builds oracle/_ref/relm_mp_ref.so
     python tests/golden/make_golden.py  # writes tests/golden/*.npz
+    python tests/golden/make_golden.py --only-lgan   # ref_lgan.npz alone
 
 Inputs come from the reference's own test fixtures
 (``tests/python/test_mp_ops.py:171-347`` of maichmueller/relmo: the literal index
@@ -15,6 +16,12 @@ indices) and the cfg1 parity workload. Outputs are what
 
 Files:
 * ``ref_cases.npz`` - small cases, inputs and outputs stored in full.
+* ``ref_lgan.npz`` - the LGAN ops (``lgan_pool_reduce``, ``lgan_relation_graph_step``
+  and their backwards, sum and mean modes): the literal fixtures of
+  ``tests/python/test_flat_lgan_relational_gnn.py:270-626`` of maichmueller/relmo
+  (seeded values where the test draws unseeded ``randn``), edge cases and a
+  seeded random case; inputs and outputs stored in full. Tuple outputs are
+  stored as ``<case>__out0``, ``__out1``, ...
 * ``ref_cfg1.npz`` - cfg1 (N=2000, D=32, E=20000, seed 0). Inputs are regenerated
   from the seed and pinned by SHA-256; outputs stored in full when they are
   [N, D], by SHA-256 when bit-exact [E, D], and by a row sample plus float64
@@ -158,6 +165,118 @@ def run_small(ops) -> dict[str, np.ndarray]:
     return arrays
 
 
+def lgan_cases():
+    """(name, op, args) for the LGAN ops; "@case:k" refers to output k of an earlier case."""
+
+    g = torch.Generator().manual_seed(4321)
+
+    def randn(*shape, dtype=torch.float32):
+        return torch.randn(*shape, generator=g, dtype=torch.float64).to(dtype)
+
+    def idx(*v, dtype=torch.int64):
+        return torch.tensor(v, dtype=dtype)
+
+    def graph(rr, tn, nn, dtype=torch.int64):
+        return [idx(*rr[0], dtype=dtype), idx(*rr[1], dtype=dtype), idx(*tn[0], dtype=dtype),
+                idx(*tn[1], dtype=dtype), idx(*nn[0], dtype=dtype), idx(*nn[1], dtype=dtype)]
+
+    cases = []
+    # test_flat_lgan_relational_gnn.py:270-311 (pool, literal values)
+    slots = torch.tensor([[1.0, 0.0], [0.0, 1.0], [1.0, 1.0], [2.0, 0.0], [0.0, 2.0]])
+    g1 = graph(((0, 1), (1, 2)), ((0, 1, 2), (0, 1, 2)), ((1, 2), (2, 4)))
+    for mode, tag in ((0, "sum"), (2, "mean")):
+        cases.append((f"pool_lit_{tag}", "lgan_pool_reduce", [slots, idx(0, 0, 1, 1, 2), idx(2, 2, 1), *g1, 5, mode]))
+        cases.append((f"pool_lit_{tag}_bwd", "lgan_pool_reduce_backward",
+                      [torch.ones(3, 2), torch.ones(5, 2), torch.ones(5, 2), idx(0, 0, 1, 1, 2), idx(2, 2, 1), *g1,
+                       3, mode]))
+    # test_flat_lgan_relational_gnn.py:534-585 (indices of the CUDA backward test, seeded values)
+    s2r = idx(0, 0, 1, 1, 1, 2, 3, 3, 4)
+    ar = idx(2, 3, 1, 2, 1)
+    g2 = graph(((0, 1, 2, 3), (1, 2, 3, 4)), ((0, 2, 4), (0, 3, 5)), ((1, 3, 4), (2, 4, 6)))
+    for mode, tag in ((0, "sum"), (2, "mean")):
+        cases.append((f"pool_bwdfix_{tag}", "lgan_pool_reduce", [randn(9, 4), s2r, ar, *g2, 7, mode]))
+        cases.append((f"pool_bwdfix_{tag}_bwd", "lgan_pool_reduce_backward",
+                      [randn(5, 4), randn(7, 4), randn(7, 4), s2r, ar, *g2, 5, mode]))
+    # test_flat_lgan_relational_gnn.py:587-626 (graph step, literal values)
+    x = torch.tensor([[0.5, 0.5], [1.0, 0.5], [0.0, 2.0]])
+    for mode, tag in ((0, "sum"), (2, "mean")):
+        cases.append((f"step_lit_{tag}", "lgan_relation_graph_step", [x, *g1, 5, mode]))
+        cases.append((f"step_lit_{tag}_bwd", "lgan_relation_graph_step_backward",
+                      [randn(3, 2), randn(5, 2), randn(5, 2), *g1, 3, mode]))
+    # repeated targets (mean counts > 1), a relation without slots, arity 0 (clamped to 1)
+    g3 = graph(((0, 1, 2, 3, 3, 0), (1, 1, 1, 0, 2, 2)), ((0, 1, 2, 3, 1), (0, 0, 0, 2, 2)),
+               ((3, 2, 2), (1, 1, 3)))
+    for mode, tag in ((0, "sum"), (2, "mean")):
+        cases.append((f"dups_{tag}", "lgan_pool_reduce",
+                      [randn(6, 5), idx(0, 1, 1, 3, 3, 3), idx(1, 2, 0, 3), *g3, 4, mode]))
+        cases.append((f"dups_{tag}_bwd", "lgan_pool_reduce_backward",
+                      [randn(4, 5), randn(4, 5), randn(4, 5), idx(0, 1, 1, 3, 3, 3), idx(1, 2, 0, 3), *g3, 4,
+                       mode]))
+        cases.append((f"dups_step_{tag}", "lgan_relation_graph_step", [randn(4, 5), *g3, 4, mode]))
+        cases.append((f"dups_step_{tag}_bwd", "lgan_relation_graph_step_backward",
+                      [randn(4, 5), randn(4, 5), randn(4, 5), *g3, 4, mode]))
+    # empty edge sets, zero entities, float64, int32 indices
+    e0 = ((), ())
+    g4 = graph(e0, ((0, 1), (1, 0)), e0)
+    cases.append(("empty_rr_nn", "lgan_relation_graph_step", [randn(3, 4), *g4, 2, 2]))
+    cases.append(("empty_rr_nn_bwd", "lgan_relation_graph_step_backward",
+                  [randn(3, 4), randn(2, 4), randn(2, 4), *g4, 3, 2]))
+    g5 = graph(((0,), (1,)), e0, e0)
+    cases.append(("zero_entities", "lgan_pool_reduce", [randn(3, 4), idx(0, 1, 1), idx(1, 2), *g5, 0, 0]))
+    cases.append(("no_slots", "lgan_pool_reduce", [torch.zeros(0, 4), idx(), idx(1, 2), *g5, 2, 2]))
+    cases.append(("f64_pool_mean", "lgan_pool_reduce",
+                  [randn(9, 3, dtype=torch.float64), s2r, ar, *g2, 7, 2]))
+    cases.append(("f64_pool_mean_bwd", "lgan_pool_reduce_backward",
+                  [randn(5, 3, dtype=torch.float64), randn(7, 3, dtype=torch.float64),
+                   randn(7, 3, dtype=torch.float64), s2r, ar, *g2, 5, 2]))
+    g2i = graph(((0, 1, 2, 3), (1, 2, 3, 4)), ((0, 2, 4), (0, 3, 5)), ((1, 3, 4), (2, 4, 6)), dtype=torch.int32)
+    cases.append(("int32_step_mean", "lgan_relation_graph_step", [randn(5, 4), *g2i, 7, 2]))
+    # seeded random graph
+    R, N, S, D = 50, 20, 120, 16
+    rnd = [torch.randint(0, R, (200,), generator=g), torch.randint(0, R, (200,), generator=g),
+           torch.randint(0, R, (100,), generator=g), torch.randint(0, N, (100,), generator=g),
+           torch.randint(0, R, (80,), generator=g), torch.randint(0, N, (80,), generator=g)]
+    s2r_r = torch.randint(0, R, (S,), generator=g)
+    ar_r = torch.randint(0, 4, (R,), generator=g)
+    for mode, tag in ((0, "sum"), (2, "mean")):
+        cases.append((f"random_{tag}", "lgan_pool_reduce", [randn(S, D), s2r_r, ar_r, *rnd, N, mode]))
+        cases.append((f"random_{tag}_bwd", "lgan_pool_reduce_backward",
+                      [randn(R, D), randn(N, D), randn(N, D), s2r_r, ar_r, *rnd, R, mode]))
+    # out-of-range indices: the reference raises
+    cases.append(("oob_tn_ent", "lgan_relation_graph_step", [randn(3, 2), *graph(e0, ((0,), (5,)), e0), 5, 0]))
+    cases.append(("oob_rr_src", "lgan_relation_graph_step", [randn(3, 2), *graph(((-1,), (0,)), e0, e0), 5, 0]))
+    cases.append(("oob_slot", "lgan_pool_reduce", [randn(2, 2), idx(0, 3), idx(1, 1), *graph(e0, e0, e0), 2, 0]))
+    cases.append(("bad_mode", "lgan_relation_graph_step", [randn(3, 2), *g1, 5, 1]))
+    return cases
+
+
+def run_lgan(ops) -> dict[str, np.ndarray]:
+    arrays: dict[str, np.ndarray] = {}
+    meta: dict[str, dict] = {}
+    for name, op, args in lgan_cases():
+        entry = {"op": op, "args": []}
+        for i, a in enumerate(args):
+            if isinstance(a, torch.Tensor):
+                key = f"{name}__arg{i}"
+                arrays[key] = a.numpy()
+                entry["args"].append({"tensor": key})
+            else:
+                entry["args"].append({"int": int(a)})
+        try:
+            out = getattr(ops, op)(*args)
+            outs = out if isinstance(out, (tuple, list)) else (out,)
+            for k, o in enumerate(outs):
+                arrays[f"{name}__out{k}"] = o.numpy()
+            entry["outputs"] = len(outs)
+            entry["raises"] = None
+        except Exception as exc:  # the reference raises for out-of-range indices and bad modes
+            entry["raises"] = type(exc).__name__
+            entry["message"] = str(exc).splitlines()[0]
+        meta[name] = entry
+    arrays["__meta__"] = np.frombuffer(json.dumps(meta, sort_keys=True).encode(), dtype=np.uint8)
+    return arrays
+
+
 def run_cfg1(ops) -> dict[str, np.ndarray]:
     wl = workloads.cfg1(seed=0)
     arrays: dict[str, np.ndarray] = {}
@@ -191,6 +310,12 @@ def main() -> int:
     torch.set_num_threads(1)
     ops = load_reference()
     info = ops.build_info()
+    lgan = run_lgan(ops)
+    lgan["__build_info__"] = np.frombuffer(info.encode(), dtype=np.uint8)
+    np.savez_compressed(HERE / "ref_lgan.npz", **lgan)
+    print("wrote", HERE / "ref_lgan.npz")
+    if "--only-lgan" in sys.argv:
+        return 0
     small = run_small(ops)
     small["__build_info__"] = np.frombuffer(info.encode(), dtype=np.uint8)
     np.savez_compressed(HERE / "ref_cases.npz", **small)
