@@ -29,6 +29,13 @@ accumulation, DDP gradient all-reduce over NCCL. One step = forward, loss,
 backward and AdamW over the whole global batch; states/s = global states per
 step / max-over-ranks step time.
 
+LGAN step (``lgan_step`` in the line; ``--workload lgan`` prints it as the
+headline): one lgan_pool_reduce and its backward (mean mode; sum alongside) on a
+synthetic LGAN batch - 2^17 entities, 2^20 relation instances of arity 1..3
+(~2^21 slots), 4 RR edges per instance, D=64 fp32; GB/s of compulsory traffic
+(workloads.lgan_algorithmic_bytes) per step, plans built inside the step, and
+per-op times with cached plans (the per-layer cost inside a model).
+
 --impl reference: the reference's own CPU relm_mp library
 (``oracle/_ref/relm_mp_ref.so``, built from the reference sources) on the
 host cores, on a bounded edge sample of the same workload; rank 0 only.
@@ -56,6 +63,7 @@ sys.path.insert(0, str(ROOT))
 from relmo_b200 import workloads  # noqa: E402
 
 METRIC = "fanin/fanout GB/s vs HBM peak"
+LGAN_METRIC = "lgan pool+graph step GB/s vs HBM peak"
 MODEL_METRIC = "RGNN train states/s"
 UNIT = "GB/s"
 OPS = ("fanout_fwd", "fanout_bwd", "fanin_sum_fwd", "fanin_sum_bwd", "fanin_lse_fwd", "fanin_lse_bwd")
@@ -333,6 +341,9 @@ def reference_arm(args) -> None:
         }
         print(json.dumps(line), flush=True)
         return
+    if args.workload == "lgan":
+        print(json.dumps(lgan_reference_line(args, threads)), flush=True)
+        return
     edges = args.cpu_edges
     wl = cpu_sample(args.workload, edges)
     kind = "port"
@@ -378,7 +389,7 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["b200", "reference"], default="b200")
     parser.add_argument("--workload", default="cfg2-unsorted",
-                        choices=["cfg2-unsorted", "cfg2-sorted", "cfg5", "cfg1", "cfg3", "cfg4"])
+                        choices=["cfg2-unsorted", "cfg2-sorted", "cfg5", "cfg1", "cfg3", "cfg4", "lgan"])
     parser.add_argument("--dtype", default="float32", choices=["float32", "bfloat16"])
     parser.add_argument("--cpu-edges", type=int, default=1 << 22, help="edge sample of the reference arm")
     parser.add_argument("--port-edges", type=int, default=1 << 20, help="edge sample of the cpu_baseline leg")
@@ -396,6 +407,10 @@ def main() -> int:
     parser.add_argument("--model-warmup", type=int, default=3)
     parser.add_argument("--model-states", type=int, default=None, help="override the global batch (states)")
     parser.add_argument("--micro-states", type=int, default=None, help="states per micro-batch (cfg4 default 512)")
+    parser.add_argument("--lgan", type=int, default=1, help="add the LGAN step to the cfg2 line (0: no)")
+    parser.add_argument("--lgan-relations", type=int, default=1 << 20, help="LGAN relation instances")
+    parser.add_argument("--lgan-entities", type=int, default=1 << 17, help="LGAN entities")
+    parser.add_argument("--lgan-steps", type=int, default=5, help="timed LGAN steps in the cfg2 line")
     args = parser.parse_args()
 
     if args.impl == "reference":
@@ -420,6 +435,8 @@ def main() -> int:
     assert mp.available(), "relm_mp library not loadable"
     if args.workload in ("cfg3", "cfg4"):
         return model_main(args, device, rank, world, local_rank)
+    if args.workload == "lgan":
+        return lgan_main(args, device, rank, world, local_rank)
     ops = torch.ops.relm_mp
     dtype = torch.float32 if args.dtype == "float32" else torch.bfloat16
     op_list = ops_of(args.workload)
@@ -545,6 +562,10 @@ def main() -> int:
             continue  # single-GPU configuration
         rgnn[name] = model_bench(name, args, device, rank, world, max_over_ranks, barrier,
                                  steps=args.model_steps, warmup=args.model_warmup)
+    lgan = None
+    if args.lgan:
+        lgan = lgan_bench(args, device, rank, world, max_over_ranks, sum_over_ranks, barrier,
+                          steps=args.lgan_steps, warmup=3)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = cpu_sample(args.workload, args.port_edges)
@@ -573,6 +594,7 @@ def main() -> int:
             "clocks": clocks,
             "per_op": per_op,
             "rgnn_train": rgnn or None,
+            "lgan_step": lgan,
             "plan_and_first_call_ms": round(first_calls_ms, 3),
             "ops_only_ms": round(ops_ms, 3),
             "ops_only_gbs": round(step_bytes / ops_ms / 1e6, 1),
@@ -707,6 +729,250 @@ def model_main(args, device, rank, world, local_rank) -> int:
     if world > 1:
         import torch.distributed as dist
 
+        dist.destroy_process_group()
+    return 0
+
+
+# ---- LGAN step (lgan_pool_reduce + backward) ---------------------------------------------
+
+
+def lgan_workload(args, seed: int, device, relations=None, entities=None) -> workloads.LganWorkload:
+    return workloads.lgan(seed=seed, device=device, relations=int(relations or args.lgan_relations),
+                          entities=int(entities or args.lgan_entities))
+
+
+def lgan_ops(ops, wl: workloads.LganWorkload, mode: int):
+    outs = ops.lgan_pool_reduce(wl.slots, wl.slot_to_rel, wl.arities, *wl.graph(), wl.entity_dim_size, mode)
+    grad = ops.lgan_pool_reduce_backward(wl.grad_x, wl.grad_tn, wl.grad_nn, wl.slot_to_rel, wl.arities, *wl.graph(),
+                                         wl.relation_count, mode)
+    return outs, grad
+
+
+def lgan_bench(args, device, rank, world, max_over_ranks, sum_over_ranks, barrier, *, steps: int, warmup: int,
+               e2e: bool = False) -> dict:
+    """LGAN forward + backward per rank on its own batch (seed = rank): the full
+    step with plan builds (mean and sum modes), and forward / backward alone
+    with cached plans."""
+
+    from relmo_b200.ops import mp
+
+    ops = torch.ops.relm_mp
+    wl = lgan_workload(args, rank, device)
+    nbytes = workloads.lgan_algorithmic_bytes(wl)
+    step_bytes = nbytes["lgan_fwd"] + nbytes["lgan_bwd"]
+    stream = torch.cuda.current_stream()
+    out = {
+        "workload": "lgan", "entities": wl.entity_dim_size, "relations": wl.relation_count, "slots": wl.num_slots,
+        "rr_edges": int(wl.rr_src.numel()), "tn_edges": int(wl.tn_rel.numel()), "nn_edges": int(wl.nn_rel.numel()),
+        "emb": wl.emb, "dtype": "f32", "bytes_per_step": step_bytes,
+    }
+    for mode, tag in ((2, "mean"), (0, "sum")):
+        # cached plans: forward and backward alone
+        for _ in range(max(warmup, 3)):
+            lgan_ops(ops, wl, mode)
+        per_op = {}
+        for name in ("lgan_fwd", "lgan_bwd"):
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            ev0.record(stream)
+            for _ in range(args.reps):
+                if name == "lgan_fwd":
+                    ops.lgan_pool_reduce(wl.slots, wl.slot_to_rel, wl.arities, *wl.graph(), wl.entity_dim_size, mode)
+                else:
+                    ops.lgan_pool_reduce_backward(wl.grad_x, wl.grad_tn, wl.grad_nn, wl.slot_to_rel, wl.arities,
+                                                  *wl.graph(), wl.relation_count, mode)
+            ev1.record(stream)
+            torch.cuda.synchronize()
+            ms = ev0.elapsed_time(ev1) / args.reps
+            per_op[name] = {"ms": round(ms, 4), "gbs": round(nbytes[name] / ms / 1e6, 1)}
+
+        def step():
+            mp.clear_plan_cache()
+            return lgan_ops(ops, wl, mode)
+
+        for _ in range(max(warmup, 3)):
+            step()
+        barrier()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record(stream)
+        for _ in range(steps):
+            step()
+        ev1.record(stream)
+        barrier()
+        elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+        job_bytes = sum_over_ranks(step_bytes)
+        ops_ms = per_op["lgan_fwd"]["ms"] + per_op["lgan_bwd"]["ms"]
+        out[tag] = {
+            "value": round(job_bytes * steps / elapsed / 1e9, 2), "unit": UNIT,
+            "ms_per_step": round(elapsed / steps * 1e3, 4), "steps": steps,
+            "ops_only_ms": round(ops_ms, 4), "ops_only_gbs": round(step_bytes / ops_ms / 1e6, 1), "per_op": per_op,
+        }
+    if e2e:
+        out["e2e"] = lgan_end_to_end(ops, wl, args, device, max_over_ranks, sum_over_ranks, barrier, step_bytes)
+    return out
+
+
+def lgan_end_to_end(ops, wl, args, device, max_over_ranks, sum_over_ranks, barrier, step_bytes) -> dict:
+    """Mean-mode forward + backward through torch.ops.relm_mp with every input
+    copied in from pinned host memory and every output copied back inside the
+    timed region (the index copies change the indices' versions, so every step
+    also rebuilds its plans, as a new batch would)."""
+
+    names = ("slots", "slot_to_rel", "arities", "rr_src", "rr_dst", "tn_rel", "tn_ent", "nn_rel", "nn_ent",
+             "grad_x", "grad_tn", "grad_nn")
+    host = {n: getattr(wl, n).cpu().pin_memory() for n in names}
+    dev = {n: torch.empty_like(getattr(wl, n)) for n in names}
+    dwl = workloads.LganWorkload("lgan", *(dev[n] for n in names[:9]), wl.entity_dim_size,
+                                 *(dev[n] for n in names[9:]))
+    compute = torch.cuda.current_stream()
+    outs_host = []
+
+    def one():
+        for n in names:
+            dev[n].copy_(host[n], non_blocking=True)
+        outs, grad = lgan_ops(ops, dwl, 2)
+        res = list(outs) + [grad]
+        if not outs_host:
+            outs_host.extend(torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in res)
+        for h, t in zip(outs_host, res):
+            h.copy_(t, non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = sum(t.numel() * t.element_size() for t in outs_host)
+    barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(compute)
+    for _ in range(args.e2e_steps):
+        one()
+    ev1.record(compute)
+    barrier()
+    elapsed = max_over_ranks(ev0.elapsed_time(ev1) / 1e3)
+    return {
+        "value": round(sum_over_ranks(step_bytes) * args.e2e_steps / elapsed / 1e9, 3), "unit": UNIT,
+        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+        "ms_per_step": round(elapsed / args.e2e_steps * 1e3, 2), "steps": args.e2e_steps,
+        "copies": "pinned host buffers, copies and ops in order on the current stream",
+    }
+
+
+def lgan_cpu_port(relations: int = 1 << 18, entities: int = 1 << 15) -> dict:
+    """The C oracle (one thread) on a bounded LGAN sample: forward + backward, mean."""
+
+    from oracle import oracle
+
+    wl = workloads.lgan(seed=0, device="cpu", relations=relations, entities=entities)
+    nb = workloads.lgan_algorithmic_bytes(wl)
+    graph = [t for t in wl.graph()]
+    t0 = time.perf_counter()
+    oracle.lgan_pool_reduce(wl.slots.numpy(), wl.slot_to_rel, wl.arities, *graph, wl.entity_dim_size, 2)
+    oracle.lgan_pool_reduce_backward(wl.grad_x.numpy(), wl.grad_tn.numpy(), wl.grad_nn.numpy(), wl.slot_to_rel,
+                                     wl.arities, *graph, wl.relation_count, 2)
+    secs = time.perf_counter() - t0
+    return {"value": round((nb["lgan_fwd"] + nb["lgan_bwd"]) / secs / 1e9, 4), "unit": UNIT, "cores": 1,
+            "kind": "port", "sample": f"lgan with {relations} relation instances, {entities} entities (same arity, "
+                                      f"RR density and D), mean forward + backward once, C oracle, 1 thread"}
+
+
+def lgan_reference_line(args, threads: int) -> dict:
+    """--impl reference --workload lgan: the reference's CPU library (ATen
+    formulas) on a bounded sample, all host threads."""
+
+    relations, entities = 1 << 19, 1 << 16
+    wl = workloads.lgan(seed=0, device="cpu", relations=relations, entities=entities)
+    nb = workloads.lgan_algorithmic_bytes(wl)
+    step_bytes = nb["lgan_fwd"] + nb["lgan_bwd"]
+    if REF_LIB.is_file():
+        torch.ops.load_library(str(REF_LIB))
+        ops, kind, cores = torch.ops.relm_mp, "reference", threads
+        run = lambda: lgan_ops(ops, wl, 2)  # noqa: E731
+    else:
+        from oracle import oracle
+
+        kind, cores = "port", 1
+
+        def run():
+            graph = list(wl.graph())
+            oracle.lgan_pool_reduce(wl.slots.numpy(), wl.slot_to_rel, wl.arities, *graph, wl.entity_dim_size, 2)
+            oracle.lgan_pool_reduce_backward(wl.grad_x.numpy(), wl.grad_tn.numpy(), wl.grad_nn.numpy(),
+                                             wl.slot_to_rel, wl.arities, *graph, wl.relation_count, 2)
+    times = []
+    for i in range(args.warmup + max(args.steps, 1)):
+        t0 = time.perf_counter()
+        run()
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t0)
+    step = sum(times) / len(times)
+    value = step_bytes / step / 1e9
+    sample = f"lgan with {relations} relation instances, {entities} entities, mean forward + backward per step"
+    return {
+        "impl": "reference", "metric": LGAN_METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": max(args.steps, 1), "warmup": args.warmup, "ms_per_step": round(step * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "lgan", "relations_sample": relations, "entities_sample": entities, "emb": wl.emb},
+        "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cores, "kind": kind, "sample": sample},
+        "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def lgan_main(args, device, rank, world, local_rank) -> int:
+    """--workload lgan: the LGAN step (mean) as the headline line."""
+
+    def barrier():
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def reduce(v: float, op) -> float:
+        if world == 1:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    import torch.distributed as dist
+
+    from relmo_b200 import capi
+    from relmo_b200.ops import mp_runtime
+
+    max_over_ranks = lambda v: reduce(v, dist.ReduceOp.MAX)  # noqa: E731
+    sum_over_ranks = lambda v: reduce(v, dist.ReduceOp.SUM)  # noqa: E731
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    launches0 = capi.lib().relm_mp_kernel_launches()
+    r = lgan_bench(args, device, rank, world, max_over_ranks, sum_over_ranks, barrier, steps=args.steps,
+                   warmup=args.warmup, e2e=not args.no_e2e)
+    launches = capi.lib().relm_mp_kernel_launches() - launches0
+    clocks = sampler.stop()
+    peaks = measured_peaks()
+    mean = r["mean"]
+    achieved = mean["ops_only_gbs"]
+    cpu = lgan_cpu_port() if rank == 0 and world == 1 and not args.no_cpu_baseline else None
+    if rank == 0:
+        line = {
+            "metric": LGAN_METRIC, "value": mean["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": mean["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {k: r[k] for k in ("workload", "entities", "relations", "slots", "rr_edges", "tn_edges",
+                                         "nn_edges", "emb")}
+            | {"mode": "mean", "step": "plan builds (cache cleared) + lgan_pool_reduce + backward",
+               "l2": "inputs larger than L2 (no flush needed)", "parallelism": f"independent batches x{world}"},
+            "roofline": {
+                "bound": "hbm", "kernel": "lgan_pool_reduce + backward, plans cached", "achieved": achieved,
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": ncu_traffic().get("lgan", {}).get("lgan_step"), "algorithmic_bytes": r["bytes_per_step"],
+                "peak_source": peaks["source"],
+            },
+            "cpu_baseline": cpu, "e2e": r.get("e2e"), "gpu_launches": int(launches), "clocks": clocks,
+            "lgan_step": r, "libs": mp_runtime.loaded_library_paths(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
         dist.destroy_process_group()
     return 0
 

@@ -301,6 +301,14 @@ RELM_MP_API int relm_mp_plan_reduce_ex(const relm_mp_plan* plan, relm_mp_dtype d
 RELM_MP_API int relm_mp_plan_scatter_rows_div(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
                                               int64_t emb, const int64_t* row_div, const uint32_t* cover,
                                               void* out, void* stream);
+/* The gather form of the same: out[s] = table[out_index[s]] / max(row_div[out_index[s]], 1)
+ * for s < plan->num_edges, where out_index is the array the plan was built from
+ * (validated by that build) and the plan gathers the identity (a NULL
+ * gather_index: gather_rows == num_edges). Reads the original index order, so
+ * slots come out in order with one 16-byte load and store per chunk. */
+RELM_MP_API int relm_mp_plan_gather_rows_div(const relm_mp_plan* plan, const int64_t* out_index, relm_mp_dtype dtype,
+                                             const void* table, int64_t emb, const int64_t* row_div, void* out,
+                                             void* stream);
 /* counts[g] = number of the plan's edges gathering row g, g < gather_rows
  * (int32, deterministic integer atomics). */
 RELM_MP_API int relm_mp_plan_gather_counts(const relm_mp_plan* plan, int32_t* counts, void* stream);

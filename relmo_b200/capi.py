@@ -110,6 +110,7 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_reduce_ex": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _INT, _P, _P, _SZ, _P]),
     "relm_mp_plan_scatter_rows_div": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P, _P]),
     "relm_mp_plan_gather_counts": (_INT, [_PLANP, _P, _P]),
+    "relm_mp_plan_gather_rows_div": (_INT, [_PLANP, _P, _INT, _P, _I64, _P, _P, _P]),
     "relm_mp_divide_rows": (_INT, [_INT, _P, _I64, _I64, _P, _P, _P]),
     "relm_mp_lgan_workspace_bytes": (_SZ, [_GRAPHP, _I64, _I64, _INT]),
     "relm_mp_lgan_relation_graph_step": (_INT, [_INT, _GRAPHP, _P, _I64, _INT, _P, _P, _P, _P, _SZ, _P]),
@@ -401,6 +402,19 @@ class PlanHandle:
         check(lib().relm_mp_plan_scatter_rows_div(
             ctypes.byref(self.plan), dtype_code(table), _ptr(table), emb, _ptr(row_div), _ptr(cover), _ptr(out),
             _stream(table.device),
+        ))
+        return out
+
+    def gather_rows_div(self, out_index, table, row_div):
+        """out[s] = table[out_index[s]] / max(row_div[out_index[s]], 1) (identity-gather plan of out_index)."""
+
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        out = torch.empty((self.plan.num_edges, emb), dtype=table.dtype, device=table.device)
+        check(lib().relm_mp_plan_gather_rows_div(
+            ctypes.byref(self.plan), _ptr(out_index.contiguous()), dtype_code(table), _ptr(table), emb,
+            _ptr(row_div), _ptr(out), _stream(table.device),
         ))
         return out
 

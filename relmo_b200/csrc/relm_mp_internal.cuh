@@ -23,6 +23,10 @@ int plan_tile_items(int64_t num_edges, int64_t num_rows);
 // Tiles with a head partial whose row spans more than this many tiles are
 // combined by the block-wide long-row fixup instead of a single warp.
 constexpr int kLongRowTiles = 64;
+// Plans whose rows all hold at most this many edges are reduced a lane group
+// per row (k_seg_rows_packed) when the row size allows it; the plan build sets
+// device flag [1] when some row is longer (merge-path kernels then).
+constexpr int kShortRowEdges = 32;
 constexpr int kThreads = 256;
 
 // Alignment of every sub-buffer carved out of a workspace.

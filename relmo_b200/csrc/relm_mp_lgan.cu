@@ -49,6 +49,76 @@ __global__ void __launch_bounds__(kThreads) k_divide_rows(const T* in, int64_t r
    }
 }
 
+// 16-byte chunks (rows a multiple of 16 bytes, 16-byte aligned): thread per
+// chunk, grid-stride; the divisor of a chunk's row comes from L1/L2.
+template < typename T, typename A >
+__global__ void __launch_bounds__(kThreads) k_divide_rows16(const T* in, int64_t chunks, int chunks_per_row,
+                                                            const int32_t* __restrict__ counts, T* out)
+{
+   constexpr int VN = 16 / (int)sizeof(T);
+   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+   for(int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += stride) {
+      const int32_t n = counts[c / chunks_per_row];
+      const A d = n > 1 ? (A)n : A(1);
+      uint4 v = *reinterpret_cast< const uint4* >(in + c * VN);
+      T* e = reinterpret_cast< T* >(&v);
+#pragma unroll
+      for(int k = 0; k < VN; ++k) store_acc(e + k, load_acc(e + k) / d);
+      *reinterpret_cast< uint4* >(out + c * VN) = v;
+   }
+}
+
+// out[s] = table[index[s]] / max(div[index[s]], 1) (div may be null): thread
+// per 16-byte chunk of an output row, grid-stride. The slots of one relation
+// instance are adjacent, so a table row and its divisor are read from L1/L2
+// after the first of them.
+template < typename T, typename A >
+__global__ void __launch_bounds__(kThreads) k_gather_div16(const T* __restrict__ table,
+                                                           const int64_t* __restrict__ index, int64_t chunks,
+                                                           int chunks_per_row, const int64_t* __restrict__ div,
+                                                           T* __restrict__ out)
+{
+   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+   for(int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < chunks; c += stride) {
+      const int64_t s = c / chunks_per_row;
+      const int64_t k = c - s * chunks_per_row;
+      const int64_t g = __ldg(index + s);
+      uint4 v = __ldg(reinterpret_cast< const uint4* >(table) + g * chunks_per_row + k);
+      if(div) {
+         const A dv = (A)__ldg(div + g);
+         const A d = dv > A(1) ? dv : A(1);
+         T* e = reinterpret_cast< T* >(&v);
+#pragma unroll
+         for(int i = 0; i < 16 / (int)sizeof(T); ++i) store_acc(e + i, load_acc(e + i) / d);
+      }
+      reinterpret_cast< uint4* >(out)[c] = v;
+   }
+}
+
+// Element-wise form for rows that are not 16-byte multiples.
+template < typename T, typename A >
+__global__ void __launch_bounds__(kThreads) k_gather_div(const T* __restrict__ table, const int64_t* __restrict__ index,
+                                                         int64_t n, int64_t emb, const int64_t* __restrict__ div,
+                                                         T* __restrict__ out)
+{
+   const int64_t total = n * emb;
+   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+   for(int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += stride) {
+      const int64_t s = i / emb;
+      const int64_t g = __ldg(index + s);
+      A v = load_acc(table + g * emb + (i - s * emb));
+      if(div) {
+         const A dv = (A)__ldg(div + g);
+         v = v / (dv > A(1) ? dv : A(1));
+      }
+      store_acc(out + i, v);
+   }
+}
+
+template < typename T, typename A >
+void launch_gather_div(const void* table, const int64_t* index, int64_t n, int64_t emb, const int64_t* div, void* out,
+                       bool vec, cudaStream_t st);
+
 unsigned grid_for(int64_t items, int64_t per_block, int64_t cap)
 {
    int64_t b = (items + per_block - 1) / per_block;
@@ -232,6 +302,33 @@ int relm_mp_divide_rows(relm_mp_dtype dtype, const void* in, int64_t rows, int64
    if(rows < 0 || emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "rows and emb must be >= 0.");
    if(rows == 0 || emb == 0) return RELM_MP_OK;
    cudaStream_t st = static_cast< cudaStream_t >(stream);
+   const int64_t row_bytes = emb * (int64_t)dtype_size(dtype);
+   if(row_bytes % 16 == 0 && (reinterpret_cast< uintptr_t >(in) & 15u) == 0 &&
+      (reinterpret_cast< uintptr_t >(out) & 15u) == 0) {
+      const int cpr = (int)(row_bytes / 16);
+      const int64_t chunks = rows * cpr;
+      const unsigned g16 = grid_for(chunks, kThreads, 148 * 32);
+      switch(dtype) {
+         case RELM_MP_FLOAT32:
+            k_divide_rows16< float, float ><<< g16, kThreads, 0, st >>>((const float*)in, chunks, cpr, counts,
+                                                                         (float*)out);
+            break;
+         case RELM_MP_FLOAT64:
+            k_divide_rows16< double, double ><<< g16, kThreads, 0, st >>>((const double*)in, chunks, cpr, counts,
+                                                                           (double*)out);
+            break;
+         case RELM_MP_BFLOAT16:
+            k_divide_rows16< __nv_bfloat16, float ><<< g16, kThreads, 0, st >>>(
+               (const __nv_bfloat16*)in, chunks, cpr, counts, (__nv_bfloat16*)out
+            );
+            break;
+         case RELM_MP_FLOAT16:
+            k_divide_rows16< __half, float ><<< g16, kThreads, 0, st >>>((const __half*)in, chunks, cpr, counts,
+                                                                          (__half*)out);
+            break;
+      }
+      return check_launch("k_divide_rows16");
+   }
    const unsigned grid = grid_for(rows, kRowWarps, 148 * 16);
    switch(dtype) {
       case RELM_MP_FLOAT32:
@@ -254,6 +351,53 @@ int relm_mp_divide_rows(relm_mp_dtype dtype, const void* in, int64_t rows, int64
          break;
    }
    return check_launch("k_divide_rows");
+}
+
+namespace {
+
+template < typename T, typename A >
+void launch_gather_div(const void* table, const int64_t* index, int64_t n, int64_t emb, const int64_t* div, void* out,
+                       bool vec, cudaStream_t st)
+{
+   if(vec) {
+      const int cpr = (int)(emb * (int64_t)sizeof(T) / 16);
+      const int64_t chunks = n * cpr;
+      k_gather_div16< T, A ><<< grid_for(chunks, kThreads, 148 * 32), kThreads, 0, st >>>(
+         static_cast< const T* >(table), index, chunks, cpr, div, static_cast< T* >(out)
+      );
+   } else {
+      k_gather_div< T, A ><<< grid_for(n * emb, kThreads, 148 * 32), kThreads, 0, st >>>(
+         static_cast< const T* >(table), index, n, emb, div, static_cast< T* >(out)
+      );
+   }
+}
+
+}  // namespace
+
+int relm_mp_plan_gather_rows_div(const relm_mp_plan* plan, const int64_t* out_index, relm_mp_dtype dtype,
+                                 const void* table, int64_t emb, const int64_t* row_div, void* out, void* stream)
+{
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   if(!lgan_dtype_ok(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
+   if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
+   if(plan->gather_rows != plan->num_edges)
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "the plan must gather the identity (one slot per edge).");
+   const int64_t n = plan->num_edges;
+   if(n == 0 || emb == 0) return RELM_MP_OK;
+   if(!out_index || !table || !out) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "pointers must not be NULL.");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   const size_t es = dtype_size(dtype);
+   const bool vec = (emb * (int64_t)es) % 16 == 0 && (reinterpret_cast< uintptr_t >(table) & 15u) == 0 &&
+                    (reinterpret_cast< uintptr_t >(out) & 15u) == 0;
+   switch(dtype) {
+      case RELM_MP_FLOAT32: launch_gather_div< float, float >(table, out_index, n, emb, row_div, out, vec, st); break;
+      case RELM_MP_FLOAT64: launch_gather_div< double, double >(table, out_index, n, emb, row_div, out, vec, st); break;
+      case RELM_MP_BFLOAT16:
+         launch_gather_div< __nv_bfloat16, float >(table, out_index, n, emb, row_div, out, vec, st);
+         break;
+      case RELM_MP_FLOAT16: launch_gather_div< __half, float >(table, out_index, n, emb, row_div, out, vec, st); break;
+   }
+   return check_launch("k_gather_div");
 }
 
 size_t relm_mp_lgan_workspace_bytes(const relm_mp_lgan_graph* graph, int64_t num_slots, int64_t emb,
@@ -340,6 +484,6 @@ int relm_mp_lgan_pool_reduce_backward(relm_mp_dtype dtype, const relm_mp_lgan_gr
    if((rc = op.plan(slot_to_relation_instance, nullptr, num_slots, graph->relation_count, num_slots,
                     "slot_to_relation_instance", "slot", &p, &m)))
       return rc;
-   return relm_mp_plan_scatter_rows_div(&p, dtype, grad_x, emb, relation_instance_arities, nullptr,
-                                        grad_slot_messages, op.st);
+   return relm_mp_plan_gather_rows_div(&p, slot_to_relation_instance, dtype, grad_x, emb, relation_instance_arities,
+                                       grad_slot_messages, op.st);
 }

@@ -379,9 +379,9 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
       }
       return fill_rows(dtype, out, plan->num_rows * emb, seg_mode == kLse, stream);
    }
-   const void* ptrs[4] = {table, table2, own, out};
-   const Shape s = choose_map_shape(emb, (int)es, ptrs, 4);
-   const Shape sr = choose_reduce_shape(emb, (int)es, ptrs, 4);
+   const void* ptrs[5] = {table, table2, own, out, epi.base};
+   const Shape s = choose_map_shape(emb, (int)es, ptrs, 5);
+   const Shape sr = choose_reduce_shape(emb, (int)es, ptrs, 5);
    SegParams p = base_params(plan, emb, s);
    p.table = table;
    p.table2 = table2;
@@ -396,6 +396,8 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    p.long_count = rs.long_count;
    p.long_list = rs.long_list;
    p.max_long = rs.max_long;
+   // rows of 16..256 bytes (packed): plans without long rows go to the short-row kernel
+   p.short_rows = s.chmax == kPackedCh ? 1 : 0;
    if(seg_mode == kSum && epi.on()) {
       seg_mode = kSumEpi;
       p.epi_base = epi.base;
@@ -404,7 +406,7 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    }
    int rc = check_cuda(cudaMemsetAsync(rs.long_count, 0, sizeof(int32_t), stream), "long_count memset");
    if(rc) return rc;
-   const StreamShape ss = choose_stream_shape(emb, (int)es, ptrs, 4);
+   const StreamShape ss = choose_stream_shape(emb, (int)es, ptrs, 5);
    if(ss.pb > 0) {
       SegParams pst = p;
       pst.lanes = ss.lanes;

@@ -113,6 +113,17 @@ __global__ void __launch_bounds__(kThreads) k_identity_rows(int32_t* __restrict_
    if(blockIdx.x == 0 && threadIdx.x == 0) flags[2] = (int32_t)num_edges;
 }
 
+// flags[1] = 1 when some row holds more than kShortRowEdges edges.
+__global__ void __launch_bounds__(kThreads) k_long_rows(const int32_t* __restrict__ row_ptr, int64_t num_rows,
+                                                        int32_t* __restrict__ flags)
+{
+   bool long_row = false;
+   for(int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; r < num_rows;
+       r += (int64_t)gridDim.x * blockDim.x)
+      long_row |= __ldg(row_ptr + r + 1) - __ldg(row_ptr + r) > kShortRowEdges;
+   if(__syncthreads_or(long_row) && threadIdx.x == 0 && *((volatile int32_t*)&flags[1]) == 0) flags[1] = 1;
+}
+
 // mark[k + 1] = e + 1 where edge e ends the segment of row k (sorted keys);
 // flags[0] (has_dups) becomes nonzero if some row holds more than one edge;
 // flags[2] counts the rows that hold edges.
@@ -447,6 +458,12 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
       pl.row_ptr, num_rows, num_edges, tiles, plan->tile_items, pl.tile_row, pl.tile_edge
    );
    if((rc = check_launch("k_partition"))) return rc;
+   if(num_edges > 0) {
+      unsigned grid = grid_for(num_rows);
+      if(grid > 148u * 4u) grid = 148u * 4u;
+      k_long_rows<<< grid, kThreads, 0, stream >>>(pl.row_ptr, num_rows, pl.flags);
+      if((rc = check_launch("k_long_rows"))) return rc;
+   }
    return RELM_MP_OK;
 }
 

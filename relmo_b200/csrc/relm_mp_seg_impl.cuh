@@ -94,6 +94,28 @@ int launch_map_packed(const SegParams& p, int mode, cudaStream_t stream)
    return check_launch("k_row_map_packed");
 }
 
+// The short-row kernel (returns at once unless the plan has repeated rows and
+// no row above kShortRowEdges edges).
+template < typename T >
+int launch_rows_packed(const SegParams& p, int mode, cudaStream_t stream)
+{
+   const int rpi = 32 / (p.lanes > 0 ? p.lanes : 1);
+   const int64_t warps = (p.num_rows + rpi - 1) / rpi;
+   int64_t blocks = (warps * 32 + kThreads - 1) / kThreads;
+   const int64_t cap = (int64_t)148 * 16;
+   if(blocks > cap) blocks = cap;
+   if(blocks < 1) blocks = 1;
+   if(mode == kSum)
+      k_seg_rows_packed< T, kSum ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kSumEpi)
+      k_seg_rows_packed< T, kSumEpi ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else if(mode == kLse)
+      k_seg_rows_packed< T, kLse ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   else
+      k_seg_rows_packed< T, kLseBwd ><<< (unsigned)blocks, kThreads, 0, stream >>>(p);
+   return check_launch("k_seg_rows_packed");
+}
+
 template < typename T >
 int launch_scatter_packed(const SegParams& p, const uint32_t* cover, int64_t out_rows, cudaStream_t stream)
 {
@@ -169,6 +191,7 @@ int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegPara
    // the device from the plan's has_dups flag.
    int rc;
    if((rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
+   if(pm.short_rows && (rc = launch_rows_packed< T >(pm, mode, stream))) return rc;
    auto run = [&]() -> int { RELM_MP_SHAPE_DISPATCH(T, launch_reduce_shape, p, mode, stream); };
    if((rc = run())) return rc;
    if(mode == kSum) return launch_fixups< T, kSum >(p, stream);
@@ -181,11 +204,12 @@ template < typename T, int PB, int MODE >
 int launch_stream_shape(const SegParams& p, cudaStream_t stream)
 {
    constexpr int NT = (MODE == kLseBwd) ? 2 : 1;
-   const size_t smem = (size_t)kStreamWarps * stream_warp_bytes(NT);
+   const size_t smem = (size_t)kStreamWarps * stream_warp_bytes(NT, MODE == kSumEpi && p.epi_div);
    static bool configured = false;  // one attribute call per instantiation (per process)
    if(!configured) {
+      const size_t most = (size_t)kStreamWarps * stream_warp_bytes(NT, MODE == kSumEpi);
       const int rc = check_cuda(
-         cudaFuncSetAttribute(k_seg_stream< T, PB, MODE >, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+         cudaFuncSetAttribute(k_seg_stream< T, PB, MODE >, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most),
          "k_seg_stream smem attribute"
       );
       if(rc) return rc;
@@ -211,6 +235,7 @@ int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegPara
 {
    int rc;
    if((rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
+   if(pm.short_rows && (rc = launch_rows_packed< T >(pm, mode, stream))) return rc;
    constexpr int ES = (int)sizeof(T);
    if(pb == 4 && ES <= 4) {
       rc = launch_stream_mode< T, (ES <= 4 ? 4 : 8) >(p, mode, stream);

@@ -214,7 +214,10 @@ struct SegParams {
    int32_t* long_count;
    int32_t* long_list;
    int64_t max_long;
-   const int32_t* has_dups;  // device flag of the plan: some row holds more than one edge
+   const int32_t* has_dups;  // device flags of the plan: [0] some row holds more than one edge,
+                             // [1] some row holds more than kShortRowEdges edges
+   int short_rows;           // k_seg_rows_packed was launched too: the merge-path kernels and
+                             // fixups leave plans without long rows to it
    // kSumEpi epilogue (indexed sum / mean of the LGAN ops): the final value
    // of row R is epi_base[R] + sum / max(d, 1) with d = epi_div[R] when
    // epi_div is set, else the row's edge count when epi_count, else 1. The
@@ -224,6 +227,13 @@ struct SegParams {
    const int64_t* epi_div;
    int epi_count;
 };
+
+// The merge-path kernels (and their fixups) serve the plan: some row holds
+// more than one edge, and some row is long or k_seg_rows_packed was not launched.
+__device__ __forceinline__ bool merge_path_runs(const SegParams& p)
+{
+   return p.has_dups[0] != 0 && (!p.short_rows || p.has_dups[1] != 0);
+}
 
 // Divisor of output row R in the SUM epilogue (at least 1; integers convert
 // to the accumulator type before the clamp, as `counts.to(dtype).clamp_min(1)`).
@@ -456,11 +466,27 @@ __global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) 
       const int nrows = (int)((p.num_rows - r0) < 32 ? (p.num_rows - r0) : 32);
       for(int base = 0; base < nrows; base += RPI * U) {
          uint4 v[U], w[UL], o[UL];
+         // kSumEpi: base rows and divisors, loaded with the table rows (rows of
+         // this kernel hold at most one edge, so a count divisor is 1)
+         constexpr int UE = (MODE == kSumEpi) ? U : 1;
+         uint4 eb[UE];
+         A ed[UE];
          int32_t src[U];
 #pragma unroll
          for(int u = 0; u < U; ++u) {
             const int row = base + u * RPI + sub;
             src[u] = __shfl_sync(0xffffffffu, src_cur, row & 31);
+            if(MODE == kSumEpi) {
+               eb[u % UE] = make_uint4(0u, 0u, 0u, 0u);
+               ed[u % UE] = A(1);
+               if(row < nrows) {
+                  if(p.epi_base) eb[u % UE] = ldg16(static_cast< const T* >(p.epi_base) + (r0 + row) * p.emb + col);
+                  if(p.epi_div) {
+                     const A dv = (A)p.epi_div[r0 + row];
+                     ed[u % UE] = dv > A(1) ? dv : A(1);
+                  }
+               }
+            }
             v[u] = make_uint4(0u, 0u, 0u, 0u);
             if(MODE == kLseBwd) {
                w[u % UL] = make_uint4(0u, 0u, 0u, 0u);
@@ -500,13 +526,117 @@ __global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) 
                   res[k] = A(0) + to_acc(ev[k]) * exp_acc(to_acc(eo[k]) - to_acc(ew[k]));
                }
             }
-            if(MODE == kSumEpi) epi_apply< T, VN >(p, r0 + row, col, res);
+            if(MODE == kSumEpi) {
+               const T* ebk = reinterpret_cast< const T* >(&eb[u % UE]);
+#pragma unroll
+               for(int k = 0; k < VN; ++k) {
+                  const A q = res[k] / ed[u % UE];
+                  res[k] = p.epi_base ? q + to_acc(ebk[k]) : q;
+               }
+            }
 #pragma unroll
             for(int k = 0; k < VN; ++k) er[k] = from_acc< T >(res[k]);
             *reinterpret_cast< uint4* >(out + (r0 + row) * p.emb + col) = r;
          }
       }
       src_cur = src_next;
+   }
+}
+
+// Segment reduction for plans whose rows hold at most kShortRowEdges edges
+// (some more than one), packed rows: the L = row bytes / 16 lanes of a lane
+// group own one output row at a time and fold its edges kSrU at a time, all
+// their loads in flight together (and, for kSumEpi / kLseBwd, the row's base /
+// own row with them). No partials: a row never spans lane groups. Same
+// results as the merge-path kernels up to the order of the additions.
+constexpr int kSrU = 4;
+
+template < typename T, int MODE >
+__global__ void __launch_bounds__(kThreads) k_seg_rows_packed(SegParams p)
+{
+   using A = typename AccOf< T >::type;
+   constexpr int VN = 16 / (int)sizeof(T);
+   constexpr int NT = (MODE == kLseBwd) ? 2 : 1;
+   if(!p.has_dups[0] || p.has_dups[1]) return;
+   const int lane = threadIdx.x & 31;
+   const int L = p.lanes;
+   const int RPI = 32 / L;
+   const int sub = lane / L;
+   const int64_t col = (int64_t)(lane - sub * L) * VN;
+   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+   const T* table = static_cast< const T* >(p.table);
+   const T* table2 = static_cast< const T* >(p.table2);
+   const T* own = static_cast< const T* >(p.own);
+   T* out = static_cast< T* >(p.out);
+   const A ninf = -(A)INFINITY;
+   for(int64_t r = warp * RPI + sub; r < p.num_rows; r += nwarps * RPI) {
+      const int e0 = __ldg(p.row_ptr + r);
+      const int e1 = __ldg(p.row_ptr + r + 1);
+      uint4 side = make_uint4(0u, 0u, 0u, 0u);  // kSumEpi: base row; kLseBwd: own row
+      A dv = A(1);
+      if(MODE == kSumEpi) {
+         if(p.epi_base) side = ldg16(static_cast< const T* >(p.epi_base) + r * p.emb + col);
+         if(p.epi_div) {
+            const A d = (A)__ldg(p.epi_div + r);
+            dv = d > A(1) ? d : A(1);
+         } else if(p.epi_count && e1 - e0 > 1) {
+            dv = (A)(e1 - e0);
+         }
+      } else if(MODE == kLseBwd) {
+         side = ldg16(own + r * p.emb + col);
+      }
+      A acc[VN], aux[VN];
+#pragma unroll
+      for(int k = 0; k < VN; ++k) {
+         acc[k] = (MODE == kLse) ? ninf : A(0);
+         aux[k] = A(0);
+      }
+      for(int j = e0; j < e1; j += kSrU) {
+         const int n = (e1 - j) < kSrU ? (e1 - j) : kSrU;
+         uint4 v[kSrU], w[NT == 2 ? kSrU : 1];
+#pragma unroll
+         for(int i = 0; i < kSrU; ++i) {
+            v[i] = make_uint4(0u, 0u, 0u, 0u);
+            if(NT == 2) w[i % (NT == 2 ? kSrU : 1)] = make_uint4(0u, 0u, 0u, 0u);
+            if(i < n) {
+               const int64_t g = __ldg(p.gidx + j + i);
+               v[i] = ldg16(table + g * p.emb + col);
+               if(NT == 2) w[i % (NT == 2 ? kSrU : 1)] = ldg16(table2 + g * p.emb + col);
+            }
+         }
+#pragma unroll
+         for(int k = 0; k < VN; ++k) {
+            A x[kSrU];
+#pragma unroll
+            for(int i = 0; i < kSrU; ++i) x[i] = to_acc(reinterpret_cast< const T* >(&v[i])[k]);
+            if(sum_mode(MODE)) {
+#pragma unroll
+               for(int i = 0; i < kSrU; ++i)
+                  if(i < n) acc[k] += x[i];
+            } else if(MODE == kLse) {
+               lse_fold< A, kSrU >(acc[k], aux[k], x, n);
+            } else {
+               const A o = to_acc(reinterpret_cast< const T* >(&side)[k]);
+#pragma unroll
+               for(int i = 0; i < kSrU; ++i)
+                  if(i < n)
+                     acc[k] += x[i] * exp_acc(o - to_acc(reinterpret_cast< const T* >(&w[i % (NT == 2 ? kSrU : 1)])[k]));
+            }
+         }
+      }
+      uint4 res;
+      T* er = reinterpret_cast< T* >(&res);
+#pragma unroll
+      for(int k = 0; k < VN; ++k) {
+         A f = (MODE == kLse) ? lse_value(acc[k], aux[k]) : acc[k];
+         if(MODE == kSumEpi) {
+            if(dv != A(1)) f = f / dv;
+            if(p.epi_base) f += to_acc(reinterpret_cast< const T* >(&side)[k]);
+         }
+         er[k] = from_acc< T >(f);
+      }
+      *reinterpret_cast< uint4* >(out + r * p.emb + col) = res;
    }
 }
 
@@ -555,6 +685,10 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
 #pragma unroll
          for(int c = 0; c < CH; ++c)
             if(cols.ok[c]) load_vec< T, VB >(table + (int64_t)R * p.emb + cols.col[c], v[c]);
+      };
+      // DIV: rows are divided when they become current (after their loads
+      // overlapped the previous row's stores).
+      auto divide_row = [&](int R, A (&v)[CH][VN]) __attribute__((always_inline)) {
          if(DIV) {
             const A d = epi_divisor< T >(p, R);
 #pragma unroll
@@ -572,6 +706,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
       }
       A cur[CH][VN];
       load_row(R, cur);
+      divide_row(R, cur);
       while(j < j_end) {
          // next row with edges in this tile, and its data, before storing this one
          int Rn = R + 1;
@@ -601,6 +736,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows(SegParams p)
          for(int c = 0; c < CH; ++c)
 #pragma unroll
             for(int k = 0; k < VN; ++k) cur[c][k] = nxt[c][k];
+         divide_row(Rn, cur);
          R = Rn;
          e_end = e_next;
       }
@@ -654,11 +790,11 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
       ++R;
       e_end = row_end(R);
    }
-   auto load_row = [&](int Rr) __attribute__((always_inline)) -> uint4 {
-      const uint4 v = ldg16(table + (int64_t)Rr * p.emb + col);
-      return DIV ? div_raw16< T >(v, epi_divisor< T >(p, Rr)) : v;
-   };
-   uint4 cur = load_row(R);
+   // DIV: the next row and its divisor are loaded ahead and divided when the
+   // row becomes current, so the loads overlap the current row's stores.
+   using A = typename AccOf< T >::type;
+   uint4 cur = ldg16(table + (int64_t)R * p.emb + col);
+   if(DIV) cur = div_raw16< T >(cur, epi_divisor< T >(p, R));
    while(j < j_end) {
       int Rn = R + 1;
       int e_next = (Rn <= r_end) ? row_end(Rn) : j_end;
@@ -668,7 +804,11 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
       }
       const bool has_next = e_end < j_end;
       uint4 nxt = cur;
-      if(has_next) nxt = load_row(Rn);
+      A dn = A(1);
+      if(has_next) {
+         nxt = ldg16(table + (int64_t)Rn * p.emb + col);
+         if(DIV) dn = epi_divisor< T >(p, Rn);
+      }
       for(; j < e_end; j += RPI) {
          const int need = (j + RPI) < e_end ? (j + RPI) : e_end;
          if(need > gbase + gcount) {
@@ -683,7 +823,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_rows_packed(SegParams p)
       }
       j = e_end;
       if(!has_next) break;
-      cur = nxt;
+      cur = DIV ? div_raw16< T >(nxt, dn) : nxt;
       R = Rn;
       e_end = e_next;
    }
@@ -852,7 +992,7 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
    __shared__ int32_t s_rend[kWarps][kStage];
    const int wib = threadIdx.x >> 5;
    const int64_t tile = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-   if(tile >= p.num_tiles || !*p.has_dups) return;
+   if(tile >= p.num_tiles || !merge_path_runs(p)) return;
    const int lane = threadIdx.x & 31;
    const int L = p.lanes;
    const int G = 32 / L;
@@ -1142,9 +1282,17 @@ constexpr int kStreamStages = 2;
 constexpr int kStreamStageBytes = 4096;  // per warp, stage and gathered table
 constexpr int kStreamMeta = 96;         // staged gidx / row-end entries per warp
 
-__host__ __device__ constexpr int stream_warp_bytes(int tables)
+// Per-warp shared memory: the stages, staged gidx and row ends, and for the
+// SUM epilogue the staged divisors (8 bytes each).
+__host__ __device__ constexpr int stream_warp_bytes(int tables, bool epi = false)
 {
-   return tables * kStreamStages * kStreamStageBytes + 2 * kStreamMeta * 4;
+   return tables * kStreamStages * kStreamStageBytes + 2 * kStreamMeta * 4 + (epi ? kStreamMeta * 8 : 0);
+}
+
+// Prefetch of a contiguous range to L2 (16-byte aligned, a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes)
+{
+   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // Segment reduction over one merge-path tile per warp, with the gathered rows
@@ -1168,10 +1316,17 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
    const int wib = threadIdx.x >> 5;
    const int lane = threadIdx.x & 31;
    const int64_t tile = (int64_t)blockIdx.x * kStreamWarps + wib;
-   if(tile >= p.num_tiles || !*p.has_dups) return;
-   unsigned char* wbase = smem + (size_t)wib * stream_warp_bytes(NT);
+   if(tile >= p.num_tiles || !merge_path_runs(p)) return;
+   // kSumEpi with 8..16-byte lane chunks: divisors staged beside the row ends,
+   // base rows prefetched to L2 per tile and into registers two rows ahead
+   // (rows of 32-byte lane chunks keep the plain epilogue: their two extra
+   // register rows would spill)
+   constexpr bool PF = MODE == kSumEpi && PB <= 16;
+   // (the divisor staging takes shared memory only when there is a divisor array)
+   unsigned char* wbase = smem + (size_t)wib * stream_warp_bytes(NT, MODE == kSumEpi && p.epi_div);
    int32_t* sg = reinterpret_cast< int32_t* >(wbase + NT * kStreamStages * kStreamStageBytes);
    int32_t* sr = sg + kStreamMeta;
+   A* sdv = reinterpret_cast< A* >(sr + kStreamMeta);  // kSumEpi: divisor of row rbase + i
    const int CBW = (int)p.block_cols * (int)sizeof(T);  // bytes of a column block
    const int B = p.ch;                                   // rows per stage
    const bool lane_ok = lane < p.lanes;
@@ -1205,7 +1360,13 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
             __syncwarp();
             rbase = R;
             rcount = (r_end - R) < kStreamMeta ? (r_end - R) : kStreamMeta;
-            for(int i = lane; i < rcount; i += 32) sr[i] = p.row_ptr[R + 1 + i];
+            for(int i = lane; i < rcount; i += 32) {
+               sr[i] = p.row_ptr[R + 1 + i];
+               if(PF && p.epi_div) {
+                  const A dv = (A)p.epi_div[R + i];
+                  sdv[i] = dv > A(1) ? dv : A(1);
+               }
+            }
             __syncwarp();
          }
          return sr[R - rbase];
@@ -1258,6 +1419,36 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
       A acc[VN];
       A aux[VN];
       A ownv[VN];
+      // kSumEpi: the divisor is the staged row's edge count (row ends already
+      // walked) or its staged divisor, and the base row is read at the flush
+      // from L2 (the tile's base rows are prefetched there at its start). The
+      // kernel is issue-bound on short rows, so the epilogue is kept to a few
+      // instructions: no division when the divisor is 1.
+      int e_rstart = 0;
+      auto epi_finish = [&](int Rr, int cnt, A (&fin)[VN]) __attribute__((always_inline)) {
+         if constexpr(PF) {
+            const A d = p.epi_div ? sdv[Rr - rbase] : ((p.epi_count && cnt > 1) ? (A)cnt : A(1));
+            if(d != A(1)) {
+#pragma unroll
+               for(int k_ = 0; k_ < VN; ++k_) fin[k_] = fin[k_] / d;
+            }
+            if(p.epi_base) {
+               A b[VN];
+               load_chunk_global< T, PB >(static_cast< const T* >(p.epi_base) + (int64_t)Rr * p.emb + col, b);
+#pragma unroll
+               for(int k_ = 0; k_ < VN; ++k_) fin[k_] += b[k_];
+            }
+         }
+      };
+      if(PF) {
+         if(cb == 0 && lane == 0 && p.epi_base) {  // this tile's base rows, to L2
+            const int r_last = r_end < (int)p.num_rows ? r_end : (int)p.num_rows - 1;
+            const char* b0 = static_cast< const char* >(p.epi_base) + (int64_t)r_begin * row_bytes;
+            int64_t left = (int64_t)(r_last - r_begin + 1) * row_bytes;
+            for(; left > 0; b0 += 32768, left -= 32768) prefetch_l2(b0, (unsigned)(left < 32768 ? left : 32768));
+         }
+         if(p.epi_count) e_rstart = p.row_ptr[r_begin];
+      }
 #define RELM_MP_STREAM_RESET()                                  \
    do {                                                         \
       _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_)          \
@@ -1267,9 +1458,15 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
       }                                                         \
    } while(0)
       // Finishes row R_: final output, or the head partial when it began earlier.
-#define RELM_MP_STREAM_FLUSH(R_)                                                                 \
+#define RELM_MP_STREAM_FLUSH(R_, RE_)                                                            \
    do {                                                                                         \
       const bool head_ = ((R_) == r_begin) && began_before;                                     \
+      int cnt_ = 0;                                                                             \
+      if(PF) { /* RE_: row_end(R_), which also holds R_'s divisor in the staged window */       \
+         const int re_ = (RE_);                                                                 \
+         cnt_ = re_ - e_rstart;                                                                 \
+         e_rstart = re_;                                                                        \
+      }                                                                                         \
       if(lane_ok) {                                                                             \
          if(head_) {                                                                            \
             const int64_t off_ = tile * p.emb + col;                                            \
@@ -1282,7 +1479,11 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
             A fin_[VN];                                                                         \
             _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_) fin_[k_] =                         \
                (MODE == kLse) ? lse_value(acc[k_], aux[k_]) : acc[k_];                          \
-            if(MODE == kSumEpi) epi_apply< T, VN >(p, (R_), col, fin_);                    \
+            if(PF) {                                                                            \
+               epi_finish((R_), cnt_, fin_);                                                    \
+            } else if(MODE == kSumEpi) {                                                        \
+               epi_apply< T, VN >(p, (R_), col, fin_);                                           \
+            }                                                                                   \
             store_chunk< T, PB >(out + (int64_t)(R_)*p.emb + col, fin_);                         \
          }                                                                                      \
       }                                                                                         \
@@ -1307,7 +1508,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
          int b = 0;
          while(b < nb) {
             while(rend <= j0 + b) {
-               RELM_MP_STREAM_FLUSH(R);
+               RELM_MP_STREAM_FLUSH(R, rend);
                ++R;
                rend = (R < r_end) ? row_end(R) : INT_MAX;
             }
@@ -1378,7 +1579,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
       cp_async_wait< 0 >();
       if(R < r_end) pending = false;
       while(R < r_end) {
-         RELM_MP_STREAM_FLUSH(R);
+         RELM_MP_STREAM_FLUSH(R, row_end(R));
          ++R;
       }
 #undef RELM_MP_STREAM_FLUSH
@@ -1467,7 +1668,7 @@ __global__ void __launch_bounds__(kThreads) k_fixup(SegParams p)
 {
    using A = typename AccOf< T >::type;
    const int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-   if(t >= p.num_tiles || !*p.has_dups) return;
+   if(t >= p.num_tiles || !merge_path_runs(p)) return;
    const int lane = threadIdx.x & 31;
    const int R = p.head_row[t];
    if(R < 0) return;
@@ -1500,7 +1701,7 @@ __global__ void __launch_bounds__(kLongThreads) k_fixup_long(SegParams p)
    __shared__ A sm_m[W][32];
    __shared__ A sm_s[W][32];
    const int64_t b = blockIdx.x;
-   if(!*p.has_dups) return;
+   if(!merge_path_runs(p)) return;
    const int count = *p.long_count;
    if(b >= count || b >= p.max_long) return;
    const int64_t t = p.long_list[b];

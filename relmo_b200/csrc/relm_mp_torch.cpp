@@ -1016,10 +1016,10 @@ Tensor lgan_pool_reduce_backward_cuda(const Tensor& grad_relation_pair_x, const 
    const int64_t S = s2r.size(0), emb = gx.size(1);
    Tensor grad_slots = at::empty({S, emb}, gx.options());
    if(S == 0 || emb == 0) return grad_slots;
-   // grad_slot[s] = g0[r] / max(arity[r], 1) through the pooling plan (every slot is one edge)
+   // grad_slot[s] = g0[r] / max(arity[r], 1) for the relation r of slot s (s2r validated by the pooling plan)
    const PlanPtr e = pool_plan(s2r, relation_count, gx);
-   check_status(relm_mp_plan_scatter_rows_div(&e->plan, dt, g0.data_ptr(), emb, arities.data_ptr< int64_t >(),
-                                              nullptr, grad_slots.data_ptr(), stream_of(gx)),
+   check_status(relm_mp_plan_gather_rows_div(&e->plan, s2r.data_ptr< int64_t >(), dt, g0.data_ptr(), emb,
+                                             arities.data_ptr< int64_t >(), grad_slots.data_ptr(), stream_of(gx)),
                 op);
    return grad_slots;
 }

@@ -38,3 +38,34 @@ def test_partition_splits_bytes_exactly(world):
     assert sum(sh.flat_src.numel() for sh in shards) == wl.flat_src.numel()
     assert sum(sh.dim_size for sh in shards) == wl.dim_size
     assert sum(sum(bench.op_bytes(sh, bench.FANIN_OPS).values()) for sh in shards) == total
+
+
+def test_lgan_workload_and_bytes():
+    """The synthetic LGAN batch has the documented structure, and its byte count
+    adds the parts of lgan_pool_reduce and its backward."""
+
+    wl = workloads.lgan(seed=2, entities=300, relations=2000, emb=8)
+    R, N, S = wl.relation_count, wl.entity_dim_size, wl.num_slots
+    assert torch.equal(torch.bincount(wl.slot_to_rel, minlength=R), wl.arities)
+    assert bool((wl.arities >= 1).all()) and bool((wl.arities <= 3).all())
+    assert wl.tn_rel.numel() == R and torch.equal(wl.tn_rel, torch.arange(R))
+    assert wl.nn_rel.numel() == S - R
+    assert wl.rr_src.numel() == 4 * R
+    assert int(wl.tn_ent.max()) < N and int(wl.nn_ent.max()) < N
+    b = workloads.lgan_algorithmic_bytes(wl)
+    rb = 8 * 4
+    assert b["lgan_fwd"] > S * rb + 4 * R * rb and b["lgan_bwd"] > S * rb + 6 * R * rb
+    assert workloads.lgan_algorithmic_bytes(wl, elem_bytes=2)["lgan_fwd"] < b["lgan_fwd"]
+
+
+def test_lgan_reference_line_keys(monkeypatch):
+    """--impl reference --workload lgan prints the contract's keys (run on a tiny sample)."""
+
+    monkeypatch.setattr(bench, "REF_LIB", bench.ROOT / "oracle" / "_ref" / "missing.so")  # the port: no library load
+    orig = workloads.lgan
+    monkeypatch.setattr(workloads, "lgan", lambda **kw: orig(**{**kw, "relations": 256, "entities": 64}))
+    args = type("A", (), {"gpus": 1, "steps": 1, "warmup": 0})()
+    line = bench.lgan_reference_line(args, threads=1)
+    for key in ("impl", "metric", "value", "unit", "cpu_baseline", "e2e", "config"):
+        assert key in line
+    assert line["impl"] == "reference" and line["cpu_baseline"]["kind"] == "port" and line["value"] > 0

@@ -239,6 +239,8 @@ def test_dividing_scatter_and_counts(dtype, emb) -> None:
     acc = torch.float64 if dtype == torch.float64 else torch.float32  # the kernels divide in the accumulator type
     expect = (table.to(acc)[s2r] / arities.to(acc).clamp_min(1.0)[s2r, None]).to(dtype)
     torch.testing.assert_close(got, expect, rtol=0, atol=0)
+    torch.testing.assert_close(plan.gather_rows_div(s2r, table, arities), expect, rtol=0, atol=0)
+    torch.testing.assert_close(plan.gather_rows_div(s2r, table, None), table[s2r], rtol=0, atol=0)
     counts = plan.gather_counts()
     assert torch.equal(counts, torch.ones(S, dtype=torch.int32, device="cuda"))
     pr = capi.PlanHandle(torch.randint(0, 50, (999,), device="cuda", generator=g),

@@ -201,3 +201,54 @@ def test_large_backwards_with_unpacked_rows():
     cold_l = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)
     assert torch.equal(warm_s, cold_s)
     assert torch.equal(warm_l, cold_l)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
+@pytest.mark.parametrize("row_bytes", [16, 64, 256])
+@pytest.mark.parametrize("longest", [32, 33])
+def test_short_and_long_row_plans(dtype, row_bytes, longest):
+    """Plans whose rows hold at most 32 edges are reduced a lane group per row
+    (k_seg_rows_packed); one longer row switches the plan to the merge-path
+    kernels (device flag [1] of the plan). Both give the reference sums,
+    logsumexp, both backwards and the fused sum epilogue."""
+
+    from relmo_b200 import capi
+
+    ops = torch.ops.relm_mp
+    es = torch.empty((), dtype=dtype).element_size()
+    emb = row_bytes // es
+    g = torch.Generator(device="cuda").manual_seed(longest * 1000 + row_bytes)
+    rows = 3000
+    deg = torch.randint(0, 9, (rows,), device="cuda", generator=g)
+    deg[17] = longest
+    dst = torch.repeat_interleave(torch.arange(rows, device="cuda"), deg)
+    dst = dst[torch.randperm(dst.numel(), device="cuda", generator=g)]
+    e = dst.numel()
+    flat_src = torch.randperm(e, device="cuda", generator=g)
+    rel = torch.randn(e, emb, device="cuda", generator=g).to(dtype)
+    plan = capi.PlanHandle(dst, flat_src, rows, e)
+    flags = capi._device_int32(plan.plan.device_flags, 4, torch.device("cuda")).cpu()
+    assert int(flags[0]) == 1 and int(flags[1]) == int(longest > 32)
+    tol = dict(rtol=1e-2, atol=1e-2) if es == 2 else dict(rtol=1e-5, atol=1e-5)
+    r64 = rel.double()
+    s = ops.fanin_reduce(rel, flat_src, dst, rows, 0)
+    expect = torch.zeros(rows, emb, dtype=torch.float64, device="cuda").index_add_(0, dst, r64[flat_src])
+    torch.testing.assert_close(s.double(), expect, **tol)
+    lse = ops.fanin_reduce(rel, flat_src, dst, rows, 1)
+    m = torch.full((rows, emb), float("-inf"), dtype=torch.float64, device="cuda")
+    m = m.scatter_reduce(0, dst[:, None].expand(-1, emb), r64[flat_src], "amax")
+    ex = torch.zeros(rows, emb, dtype=torch.float64, device="cuda").index_add_(0, dst, (r64[flat_src] - m[dst]).exp())
+    expect_lse = ex.log() + m
+    torch.testing.assert_close(lse.double(), expect_lse, equal_nan=True, **tol)
+    gout = torch.randn(rows, emb, device="cuda", generator=g).to(dtype)
+    gl = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, e)
+    expect_gl = torch.zeros(e, emb, dtype=torch.float64, device="cuda")
+    expect_gl[flat_src] = gout.double()[dst] * (r64[flat_src] - lse.double()[dst]).exp()
+    torch.testing.assert_close(gl.double(), expect_gl, **tol)
+    # the source-side plan of a fan-out backward has the same row lengths
+    gs = ops.fanout_scatter_backward(rel, dst, flat_src, rows)
+    torch.testing.assert_close(gs.double(), expect, **tol)
+    base = torch.randn(rows, emb, device="cuda", generator=g).to(dtype)
+    got = plan.reduce_ex(rel, base=base, divide_by_count=True)
+    cnt = torch.bincount(dst, minlength=rows).double().clamp_min(1.0)[:, None]
+    torch.testing.assert_close(got.double(), expect / cnt + base.double(), **tol)
