@@ -307,3 +307,32 @@ def test_train_step_cfg3_runs_and_loss_finite(_lib):
     opt = model_train.make_optimizer(m)
     losses = [float(model_train.train_step(m, opt, [batch])) for _ in range(3)]
     assert all(math.isfinite(v) for v in losses)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("position", ["pre", "post"])
+@pytest.mark.parametrize("cond", ["film", "concat"])
+@pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
+def test_fused_input_assembly_matches_concatenation(_lib, position, cond, dtype):
+    """The fan-out stored straight into the central module's input buffer
+    (CentralFusedLayer._fused_inputs) gives the values and gradients of the
+    fan-out + concatenation path."""
+
+    batch = workloads.cfg3_batch(states=16).to("cuda")
+    torch.manual_seed(0)
+    m = CentralizedRelationalGNN(32, 3, "logsumexp", workloads.CFG3_ARITIES, condition_position=position,
+                                 central_conditioning=cond).to(device="cuda", dtype=dtype)
+    assert not m.central_layer.fuse_inputs  # off by default (one more plan per forward)
+    out = []
+    for fuse in (True, False):
+        m.central_layer.fuse_inputs = fuse
+        m.zero_grad()
+        x = m(batch)[0]
+        train_loss(x).backward()
+        out.append((x.detach().clone(), {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}))
+    (xa, ga), (xb, gb) = out
+    tol = dict(rtol=1e-12, atol=1e-12) if dtype == torch.float64 else dict(rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(xa, xb, **tol)
+    assert ga.keys() == gb.keys() and len(ga) > 0
+    for n in ga:
+        torch.testing.assert_close(ga[n], gb[n], **tol)
