@@ -179,6 +179,13 @@ RELM_MP_API int relm_mp_fanin_reduce_noalloc(relm_mp_dtype dtype, const void* re
  * ------------------------------------------------------------------------- */
 
 #define RELM_MP_PLAN_SORTED_INPUT 1u /* out_index was already non-decreasing */
+/* Host copies of the plan's device flags (set by relm_mp_plan_read_flags, or
+ * by a caller that copied device_flags[0..1] itself): when KNOWN is set, the
+ * planned reductions launch only the kernel family the plan needs instead of
+ * all of them (the others would return at once on the device). */
+#define RELM_MP_PLAN_FLAGS_KNOWN 2u
+#define RELM_MP_PLAN_REPEATS 4u   /* device_flags[0]: some row holds more than one edge */
+#define RELM_MP_PLAN_LONG_ROWS 8u /* device_flags[1]: some row holds more than 32 edges */
 
 typedef struct relm_mp_plan {
    int64_t num_edges;
@@ -191,8 +198,9 @@ typedef struct relm_mp_plan {
    const int32_t* gidx;     /* device [num_edges]: gathered row of the j-th edge in row order */
    const int32_t* tile_row; /* device [num_tiles + 1]: first row of each tile */
    const int32_t* tile_edge;/* device [num_tiles + 1]: first edge of each tile */
-   const int32_t* device_flags; /* device [1]: nonzero when some row has more than one
-                                   edge; kernels read it on the device (no host copy) */
+   const int32_t* device_flags; /* device [4]: [0] nonzero when some row has more than one
+                                   edge, [1] when some row has more than 32; kernels read
+                                   them on the device (no host copy needed) */
 } relm_mp_plan;
 
 RELM_MP_API size_t relm_mp_plan_bytes(int64_t num_edges, int64_t num_rows);
@@ -217,6 +225,10 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
                                       const char* gather_index_name, int gather_checked_first,
                                       void* plan_mem, size_t plan_bytes, void* scratch,
                                       size_t scratch_bytes, void* stream, relm_mp_plan* plan);
+
+/* Copies device_flags[0..1] into plan->flags (RELM_MP_PLAN_FLAGS_KNOWN,
+ * RELM_MP_PLAN_REPEATS, RELM_MP_PLAN_LONG_ROWS). Synchronizes `stream`. */
+RELM_MP_API int relm_mp_plan_read_flags(relm_mp_plan* plan, void* stream);
 
 /* Scratch for the planned reductions (partials of rows that span tiles). */
 RELM_MP_API size_t relm_mp_plan_reduce_scratch_bytes(const relm_mp_plan* plan, int64_t emb,

@@ -99,6 +99,7 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _P, _I64, _I64, _I64, _I64, _STR, _STR, _INT, _P, _SZ, _P, _SZ, _P, _PLANP],
     ),
     "relm_mp_plan_reduce_scratch_bytes": (_SZ, [_PLANP, _I64, _INT, _INT]),
+    "relm_mp_plan_read_flags": (_INT, [_PLANP, _P]),
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
     "relm_mp_plan_gather_cover": (_INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), _P]),
     "relm_mp_plan_nonempty_rows": (_INT, [_PLANP, ctypes.POINTER(_I64), _P]),
@@ -340,6 +341,13 @@ class PlanHandle:
             _stream(out_index.device), ctypes.byref(self.plan),
         ))
         del torch
+
+    def read_flags(self) -> int:
+        """Copies the plan's device flags into plan.flags (later planned calls
+        launch only the kernels the plan needs); returns plan.flags."""
+
+        check(lib().relm_mp_plan_read_flags(ctypes.byref(self.plan), _stream(self.device)))
+        return int(self.plan.flags)
 
     def row_ptr(self):
         """row_ptr of the plan as a CPU int64 tensor."""

@@ -398,13 +398,24 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
    p.max_long = rs.max_long;
    // rows of 16..256 bytes (packed): plans without long rows go to the short-row kernel
    p.short_rows = s.chmax == kPackedCh ? 1 : 0;
+   p.launch = kLaunchAll;
+   if(plan->flags & RELM_MP_PLAN_FLAGS_KNOWN) {  // launch only the family the plan needs
+      if(!(plan->flags & RELM_MP_PLAN_REPEATS))
+         p.launch = kLaunchRowMap;
+      else if(p.short_rows && !(plan->flags & RELM_MP_PLAN_LONG_ROWS))
+         p.launch = kLaunchShort;
+      else
+         p.launch = kLaunchMerge;
+   }
    if(seg_mode == kSum && epi.on()) {
       seg_mode = kSumEpi;
       p.epi_base = epi.base;
       p.epi_div = epi.row_div;
       p.epi_count = epi.divide_by_count ? 1 : 0;
    }
-   int rc = check_cuda(cudaMemsetAsync(rs.long_count, 0, sizeof(int32_t), stream), "long_count memset");
+   int rc = (p.launch & kLaunchMerge)
+               ? check_cuda(cudaMemsetAsync(rs.long_count, 0, sizeof(int32_t), stream), "long_count memset")
+               : RELM_MP_OK;
    if(rc) return rc;
    const StreamShape ss = choose_stream_shape(emb, (int)es, ptrs, 5);
    if(ss.pb > 0) {
@@ -705,6 +716,17 @@ int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dt
       case RELM_MP_FLOAT16: return launch_scatter_lse_bwd< __half >(p, cover, plan->gather_rows, st);
    }
    return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype");
+}
+
+int relm_mp_plan_read_flags(relm_mp_plan* plan, void* stream)
+{
+   if(!plan || !plan->device_flags) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   int32_t f[2] = {0, 0};
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   int rc = check_cuda(cudaMemcpyAsync(f, plan->device_flags, sizeof f, cudaMemcpyDeviceToHost, st), "flags copy");
+   if(rc || (rc = check_cuda(cudaStreamSynchronize(st), "flags sync"))) return rc;
+   plan->flags |= RELM_MP_PLAN_FLAGS_KNOWN | (f[0] ? RELM_MP_PLAN_REPEATS : 0u) | (f[1] ? RELM_MP_PLAN_LONG_ROWS : 0u);
+   return RELM_MP_OK;
 }
 
 int relm_mp_plan_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int mode, const void* table, int64_t emb,

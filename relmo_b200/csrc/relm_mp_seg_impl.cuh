@@ -190,8 +190,9 @@ int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegPara
    // merge-path kernels return at once for them (and vice versa), decided on
    // the device from the plan's has_dups flag.
    int rc;
-   if((rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
-   if(pm.short_rows && (rc = launch_rows_packed< T >(pm, mode, stream))) return rc;
+   if((pm.launch & kLaunchRowMap) && (rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
+   if(pm.short_rows && (pm.launch & kLaunchShort) && (rc = launch_rows_packed< T >(pm, mode, stream))) return rc;
+   if(!(p.launch & kLaunchMerge)) return RELM_MP_OK;
    auto run = [&]() -> int { RELM_MP_SHAPE_DISPATCH(T, launch_reduce_shape, p, mode, stream); };
    if((rc = run())) return rc;
    if(mode == kSum) return launch_fixups< T, kSum >(p, stream);
@@ -234,8 +235,9 @@ int launch_seg_stream(const SegParams& pm, int vb_map, int ch_map, const SegPara
                       cudaStream_t stream)
 {
    int rc;
-   if((rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
-   if(pm.short_rows && (rc = launch_rows_packed< T >(pm, mode, stream))) return rc;
+   if((pm.launch & kLaunchRowMap) && (rc = launch_row_map< T >(pm, mode, vb_map, ch_map, stream))) return rc;
+   if(pm.short_rows && (pm.launch & kLaunchShort) && (rc = launch_rows_packed< T >(pm, mode, stream))) return rc;
+   if(!(p.launch & kLaunchMerge)) return RELM_MP_OK;
    constexpr int ES = (int)sizeof(T);
    if(pb == 4 && ES <= 4) {
       rc = launch_stream_mode< T, (ES <= 4 ? 4 : 8) >(p, mode, stream);

@@ -24,6 +24,9 @@
 namespace relm_mp {
 
 enum SegMode : int { kSum = 0, kLse = 1, kLseBwd = 2, kCopyLast = 3, kSumEpi = 4 };
+// Kernel families a planned reduction launches (SegParams::launch).
+enum LaunchFamily : int { kLaunchRowMap = 1, kLaunchShort = 2, kLaunchMerge = 4, kLaunchAll = 7 };
+
 // kSumEpi: kSum with the epilogue of SegParams::epi_* applied where a row's
 // final value is written (a separate instantiation, so kSum keeps its code).
 __host__ __device__ constexpr bool sum_mode(int m) { return m == kSum || m == kSumEpi; }
@@ -218,6 +221,8 @@ struct SegParams {
                              // [1] some row holds more than kShortRowEdges edges
    int short_rows;           // k_seg_rows_packed was launched too: the merge-path kernels and
                              // fixups leave plans without long rows to it
+   int launch;               // host only: kernel families to launch (kLaunch*), all of them
+                             // unless the host knows the plan's flags
    // kSumEpi epilogue (indexed sum / mean of the LGAN ops): the final value
    // of row R is epi_base[R] + sum / max(d, 1) with d = epi_div[R] when
    // epi_div is set, else the row's edge count when epi_count, else 1. The

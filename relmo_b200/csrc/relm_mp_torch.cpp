@@ -24,6 +24,7 @@
 // distinct index pair pays the sort once.
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CUDAEvent.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/util/intrusive_ptr.h>
 #include <torch/library.h>
@@ -146,6 +147,8 @@ struct PlanEntry {
    int cover_dups = -1;  // -1 unknown, 0 each gather row at most once, 1 repeats
    int64_t nonempty_rows = -1;  // output rows holding edges, read on first use
    Tensor gather_counts;        // int32 edges per gathered row, computed on first use
+   Tensor host_flags;           // pinned copy of the plan's device flags, filled after the build
+   std::shared_ptr< at::cuda::CUDAEvent > flags_copied;
 };
 using PlanPtr = std::shared_ptr< PlanEntry >;
 
@@ -178,6 +181,7 @@ class PlanCache {
                && e.gather_rows == gather_rows && e.memory.device() == out_index.device()) {
                entries_.splice(entries_.begin(), entries_, it);
                ++hits_;
+               learn_flags(*entries_.front());
                return entries_.front();
             }
          }
@@ -194,8 +198,17 @@ class PlanCache {
       check_status(rc, "plan build");
       auto entry = std::make_shared< PlanEntry >(
          PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1, -1,
-                   Tensor()}
+                   Tensor(), Tensor(), nullptr}
       );
+      // The row facts of the plan, to the host without a sync: once the copy
+      // has landed, later calls launch only the kernels the plan needs.
+      entry->host_flags = at::empty({4}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
+      const c10::cuda::CUDAStream cs = at::cuda::getCurrentCUDAStream(out_index.device().index());
+      const cudaError_t err = cudaMemcpyAsync(entry->host_flags.data_ptr(), plan.device_flags, 4 * sizeof(int32_t),
+                                              cudaMemcpyDeviceToHost, cs.stream());
+      TORCH_CHECK(err == cudaSuccess, "plan flags copy: ", cudaGetErrorString(err));
+      entry->flags_copied = std::make_shared< at::cuda::CUDAEvent >();
+      entry->flags_copied->record(cs);
       std::lock_guard< std::mutex > lock(mu_);
       ++builds_;
       entries_.push_front(entry);
@@ -281,6 +294,15 @@ class PlanCache {
    }
 
  private:
+   // Sets the plan's host flag bits once the copy of its device flags landed.
+   static void learn_flags(PlanEntry& e)
+   {
+      if((e.plan.flags & RELM_MP_PLAN_FLAGS_KNOWN) || !e.flags_copied || !e.flags_copied->query()) return;
+      const int32_t* f = e.host_flags.data_ptr< int32_t >();
+      e.plan.flags |= RELM_MP_PLAN_FLAGS_KNOWN | (f[0] ? RELM_MP_PLAN_REPEATS : 0u) | (f[1] ? RELM_MP_PLAN_LONG_ROWS : 0u);
+      e.flags_copied.reset();
+   }
+
    void evict_dead_locked()
    {
       for(auto it = entries_.begin(); it != entries_.end();) {

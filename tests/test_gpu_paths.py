@@ -252,3 +252,46 @@ def test_short_and_long_row_plans(dtype, row_bytes, longest):
     got = plan.reduce_ex(rel, base=base, divide_by_count=True)
     cnt = torch.bincount(dst, minlength=rows).double().clamp_min(1.0)[:, None]
     torch.testing.assert_close(got.double(), expect / cnt + base.double(), **tol)
+
+
+@pytest.mark.parametrize("kind", ["one_edge", "short", "long"])
+@pytest.mark.parametrize("emb", [64, 3])
+def test_known_plan_flags_launch_one_family(kind, emb):
+    """With the plan's flags copied to the host (relm_mp_plan_read_flags; the
+    torch layer does it without a sync once the copy after the build landed),
+    a planned reduction launches only the kernel family the plan needs - with
+    bit-identical results."""
+
+    from relmo_b200 import capi
+
+    g = torch.Generator(device="cuda").manual_seed(len(kind) * 10 + emb)
+    rows = 4000
+    if kind == "one_edge":
+        out_idx = torch.randperm(rows, device="cuda", generator=g)[:3000]
+    else:
+        deg = torch.randint(0, 6, (rows,), device="cuda", generator=g)
+        deg[5] = 40 if kind == "long" else 6
+        out_idx = torch.repeat_interleave(torch.arange(rows, device="cuda"), deg)
+        out_idx = out_idx[torch.randperm(out_idx.numel(), device="cuda", generator=g)]
+    e = out_idx.numel()
+    gather = torch.randint(0, 5000, (e,), device="cuda", generator=g)
+    table = torch.randn(5000, emb, device="cuda", generator=g)
+    plan = capi.PlanHandle(out_idx, gather, rows, 5000)
+    launches = capi.lib().relm_mp_kernel_launches
+    results = []
+    counts = []
+    for known in (False, True):
+        if known:
+            flags = plan.read_flags()
+            assert flags & 2
+            assert bool(flags & 4) == (kind != "one_edge")
+            assert bool(flags & 8) == (kind == "long")
+        n0 = launches()
+        res = [plan.reduce(table, 0), plan.reduce(table, 1), plan.reduce_ex(table, base=table[:rows].contiguous(),
+                                                                         divide_by_count=True)]
+        torch.cuda.synchronize()
+        counts.append(launches() - n0)
+        results.append(res)
+    for a, b in zip(*results):
+        assert torch.equal(a.isnan(), b.isnan()) and torch.equal(torch.nan_to_num(a), torch.nan_to_num(b))
+    assert counts[1] < counts[0]
