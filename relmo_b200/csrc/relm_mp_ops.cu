@@ -621,8 +621,9 @@ int relm_mp_plan_gather_cover(const relm_mp_plan* plan, uint32_t* cover, int* ha
    cudaStream_t st = static_cast< cudaStream_t >(stream);
    int rc;
    // The last int of the cover buffer's allocation is not ours: keep the flag
-   // in the plan's own device flags word (index 1), cleared first.
-   int32_t* flag = const_cast< int32_t* >(plan->device_flags) + 1;
+   // in the plan's own spare device flags word (index 3; words 0-2 hold the
+   // plan's row facts, which later reductions read), cleared first.
+   int32_t* flag = const_cast< int32_t* >(plan->device_flags) + 3;
    if((rc = check_cuda(cudaMemsetAsync(cover, 0, relm_mp_cover_words(plan->gather_rows) * sizeof(uint32_t), st),
                        "cover memset")))
       return rc;

@@ -295,3 +295,33 @@ def test_known_plan_flags_launch_one_family(kind, emb):
     for a, b in zip(*results):
         assert torch.equal(a.isnan(), b.isnan()) and torch.equal(torch.nan_to_num(a), torch.nan_to_num(b))
     assert counts[1] < counts[0]
+
+
+def test_coverage_pass_keeps_plan_row_flags():
+    """The fan-out's coverage pass works in a spare device flag word: the plan's
+    row facts (repeats, long rows) survive it, so a fan-out backward over the
+    same (shared, cached) plan with long source rows runs the merge-path
+    kernels and gives the reference sums - on the first call and on later
+    calls, when the host knows the plan's flags."""
+
+    from relmo_b200 import capi
+
+    ops = torch.ops.relm_mp
+    g = torch.Generator(device="cuda").manual_seed(77)
+    n, e, emb = 2000, 30000, 64
+    src = torch.randint(0, n, (e,), device="cuda", generator=g)
+    src[:50] = 3  # one source row with 50+ slots: a long row
+    flat_dst = torch.randperm(e, device="cuda", generator=g)
+    x = torch.randn(n, emb, device="cuda", generator=g)
+    grad = torch.randn(e, emb, device="cuda", generator=g)
+    expect = torch.zeros(n, emb, dtype=torch.float64, device="cuda").index_add_(0, src, grad.double()[flat_dst])
+    for _ in range(3):
+        out = ops.fanout_scatter(x, src, flat_dst, e)  # coverage of the source plan
+        assert torch.equal(out[flat_dst], x[src])
+        gx = ops.fanout_scatter_backward(grad, src, flat_dst, n)
+        torch.testing.assert_close(gx.double(), expect, rtol=1e-5, atol=1e-4)
+    plan = capi.PlanHandle(src, flat_dst, n, e)
+    before = capi._device_int32(plan.plan.device_flags, 3, torch.device("cuda")).cpu().tolist()
+    cover, dups = plan.gather_cover()
+    after = capi._device_int32(plan.plan.device_flags, 3, torch.device("cuda")).cpu().tolist()
+    assert not dups and before == after and before[0] == 1 and before[1] == 1
