@@ -28,7 +28,8 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 OUT_DIR = HERE / "_ref"
 OUT_LIB = OUT_DIR / "relm_mp_ref.so"
-DEFAULT_REFERENCE_ROOT = Path(os.environ.get("RELMO_REFERENCE_ROOT", "/root/reference"))
+# the reference checkout: $RELMO_REFERENCE_ROOT, else a `reference` directory beside this repository
+DEFAULT_REFERENCE_ROOT = Path(os.environ.get("RELMO_REFERENCE_ROOT", str(HERE.parents[1] / "reference")))
 REFERENCE_SOURCE = Path("src/_ops/mp/mp_ops.cpp")
 
 
