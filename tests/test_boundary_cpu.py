@@ -24,7 +24,7 @@ from relmo_b200.ops import mp, mp_runtime
 ROOT = Path(__file__).resolve().parents[1]
 HEADER = ROOT / "include" / "relm_mp.h"
 
-# Verbatim from maichmueller/relmo src/_ops/mp/mp_ops.cpp:3756-3786.
+# Verbatim from maichmueller/relmo src/_ops/mp/mp_ops.cpp:3756-3788.
 REFERENCE_SCHEMAS = {
     "fanout_scatter": "relm_mp::fanout_scatter(Tensor x_cat, Tensor src_global_idx, Tensor flat_dst, int out_rows) -> Tensor",
     "fanout_scatter_backward": "relm_mp::fanout_scatter_backward(Tensor grad_out, Tensor src_global_idx, Tensor flat_dst, int x_rows) -> Tensor",
@@ -36,6 +36,11 @@ REFERENCE_SCHEMAS = {
     "fanout_pack_from_edges": "relm_mp::fanout_pack_from_edges(Tensor[] x_parts, Tensor[] edge_src_parts, Tensor[] edge_dst_parts, int[] src_part_ids, int[] arity_parts, int[] pos_parts, int[] slot_offset_parts) -> (Tensor, Tensor, Tensor)",
     "fanin_pack_from_edges": "relm_mp::fanin_pack_from_edges(Tensor[] rel_parts, Tensor[] edge_src_parts, Tensor[] edge_dst_parts, int[] rel_part_ids, int[] arity_parts, int[] pos_parts, int mode) -> (Tensor, Tensor, Tensor)",
     "build_info": "relm_mp::build_info() -> str",
+    # mp_ops.cpp:3777-3788
+    "lgan_pool_reduce": "relm_mp::lgan_pool_reduce(Tensor slot_messages, Tensor slot_to_relation_instance, Tensor relation_instance_arities, Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int entity_dim_size, int mode) -> (Tensor, Tensor, Tensor)",
+    "lgan_pool_reduce_backward": "relm_mp::lgan_pool_reduce_backward(Tensor grad_relation_pair_x, Tensor grad_tn_msgs, Tensor grad_nn_msgs, Tensor slot_to_relation_instance, Tensor relation_instance_arities, Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int relation_count, int mode) -> Tensor",
+    "lgan_relation_graph_step": "relm_mp::lgan_relation_graph_step(Tensor relation_pair_x, Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int entity_dim_size, int mode) -> (Tensor, Tensor, Tensor)",
+    "lgan_relation_graph_step_backward": "relm_mp::lgan_relation_graph_step_backward(Tensor grad_relation_pair_x, Tensor grad_tn_msgs, Tensor grad_nn_msgs, Tensor rr_src, Tensor rr_dst, Tensor tn_rel, Tensor tn_ent, Tensor nn_rel, Tensor nn_ent, int relation_count, int mode) -> Tensor",
 }
 
 
@@ -95,6 +100,17 @@ def test_meta_kernels_give_shapes() -> None:
     assert torch.ops.relm_mp.fanin_reduce_sum_backward(x, i, i, 12).shape == (12, 7)
     assert torch.ops.relm_mp.fanin_reduce_logsumexp_backward(x, x, i, i, x, 9).shape == (9, 7)
     assert torch.ops.relm_mp.fanout_scatter_backward(x, i, i, 3).shape == (3, 7)
+    # LGAN ops: (relation rows, entity rows, entity rows) and the input gradients
+    slots = torch.empty(12, 7, device="meta")
+    ar = torch.empty(5, dtype=torch.int64, device="meta")
+    e = torch.empty(8, dtype=torch.int64, device="meta")
+    x1, tn, nn = torch.ops.relm_mp.lgan_pool_reduce(slots, i[:12], ar, e, e, e, e, e, e, 6, 2)
+    assert x1.shape == (5, 7) and tn.shape == (6, 7) and nn.shape == (6, 7)
+    g = torch.ops.relm_mp.lgan_pool_reduce_backward(x1, tn, nn, i[:12], ar, e, e, e, e, e, e, 5, 0)
+    assert g.shape == (12, 7)
+    y, tn2, _ = torch.ops.relm_mp.lgan_relation_graph_step(x1, e, e, e, e, e, e, 4, 0)
+    assert y.shape == (5, 7) and tn2.shape == (4, 7)
+    assert torch.ops.relm_mp.lgan_relation_graph_step_backward(y, tn2, tn2, e, e, e, e, e, e, 5, 2).shape == (5, 7)
 
 
 def test_cpu_facade_follows_reference_formulas() -> None:
