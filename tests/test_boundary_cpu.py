@@ -79,6 +79,12 @@ def test_workspace_queries_without_gpu() -> None:
     ws = lib.relm_mp_fanin_reduce_workspace_bytes(e, n, d, capi.FLOAT32, 1)
     assert ws > plan
     assert lib.relm_mp_fanout_scatter_workspace_bytes(-1, n, n, d, capi.FLOAT32) == 0
+    # LGAN: one workspace for the four entry points; grows with the edge lists and the slots
+    g = capi.LganGraph(None, None, 4 << 20, None, None, 1 << 20, None, None, 1 << 20, 1 << 20, 1 << 17)
+    small = lib.relm_mp_lgan_workspace_bytes(capi.ctypes.byref(g), 0, d, capi.FLOAT32)
+    pooled = lib.relm_mp_lgan_workspace_bytes(capi.ctypes.byref(g), 1 << 24, d, capi.FLOAT32)
+    assert small >= 2 * (1 << 20) * d * 4 and pooled > small
+    assert lib.relm_mp_lgan_workspace_bytes(None, 0, d, capi.FLOAT32) == 0
 
 
 def test_torch_library_registers_reference_schemas() -> None:
