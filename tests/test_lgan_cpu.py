@@ -98,3 +98,43 @@ def test_mode_strings() -> None:
         mp._lgan_relation_graph_step(x, e, e, e, e, e, e, entity_dim_size=1, mode="logsumexp")
     out = mp._lgan_relation_graph_step(x, e, e, e, e, e, e, entity_dim_size=1, mode=" MEAN ")
     assert out[1].shape == (1, 3)
+
+
+def _random_graph(rng, R, N, S):
+    def pairs(n, a, b):
+        return rng.integers(0, a, n), rng.integers(0, b, n)
+
+    rr = pairs(int(rng.integers(0, 3 * R + 1)), R, R)
+    tn = pairs(int(rng.integers(0, 2 * R + 1)), R, max(N, 1)) if N > 0 else (np.zeros(0, int), np.zeros(0, int))
+    nn = pairs(int(rng.integers(0, 2 * R + 1)), R, max(N, 1)) if N > 0 else (np.zeros(0, int), np.zeros(0, int))
+    s2r = rng.integers(0, R, S) if R > 0 else np.zeros(0, int)
+    arities = rng.integers(-1, 4, R)  # zero and negative arities clamp to 1
+    return [np.asarray(a, dtype=np.int64) for a in (*rr, *tn, *nn)], s2r.astype(np.int64), arities.astype(np.int64)
+
+
+@pytest.mark.parametrize("seed", range(12))
+@pytest.mark.parametrize("mode", [0, 2])
+def test_oracle_matches_python_formulas_on_random_graphs(seed, mode):
+    """The C oracle and the Python ATen formulas (relmo's mp_fallbacks) agree on
+    random small LGAN graphs - empty edge sets, repeated targets, relations
+    without slots, zero arities - forward and backward, in float64."""
+
+    rng = np.random.default_rng(seed)
+    R, N, S, D = int(rng.integers(1, 30)), int(rng.integers(0, 12)), int(rng.integers(0, 60)), int(rng.integers(1, 6))
+    graph, s2r, ar = _random_graph(rng, R, N, S)
+    slots = rng.standard_normal((S, D))
+    x1, tn, nn = oracle.lgan_pool_reduce(slots, s2r, ar, *graph, N, mode)
+    tg = [torch.from_numpy(a) for a in graph]
+    ts = torch.from_numpy(slots).requires_grad_(True)
+    px1, ptn, pnn = lgan_pool_reduce_python(ts, torch.from_numpy(s2r), torch.from_numpy(ar), *tg, N, mode)
+    for a, b in ((x1, px1), (tn, ptn), (nn, pnn)):
+        np.testing.assert_allclose(a, b.detach().numpy(), rtol=1e-12, atol=1e-12)
+    gx, gtn, gnn = rng.standard_normal((R, D)), rng.standard_normal((N, D)), rng.standard_normal((N, D))
+    g_or = oracle.lgan_pool_reduce_backward(gx, gtn, gnn, s2r, ar, *graph, R, mode)
+    torch.autograd.backward((px1, ptn, pnn), (torch.from_numpy(gx), torch.from_numpy(gtn), torch.from_numpy(gnn)))
+    np.testing.assert_allclose(g_or, ts.grad.numpy(), rtol=1e-12, atol=1e-12)
+    x = rng.standard_normal((R, D))
+    y = oracle.lgan_relation_graph_step(x, *graph, N, mode)
+    py = lgan_relation_graph_step_python(torch.from_numpy(x), *tg, N, mode)
+    for a, b in zip(y, py):
+        np.testing.assert_allclose(a, b.numpy(), rtol=1e-12, atol=1e-12)
