@@ -153,12 +153,20 @@ RELM_MP_API int relm_mp_fanin_reduce_logsumexp_backward(relm_mp_dtype dtype, con
  * cudaMalloc's implicit device synchronization while other work is in
  * flight). No counterpart in the reference library: it is relm_mp_fanin_reduce
  * with its workspace taken from a static device array of
- * RELM_MP_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
- * exit. The call allocates nothing. Problems whose workspace
- * (relm_mp_fanin_reduce_workspace_bytes) exceeds that size are rejected with
- * RELM_MP_ERR_WORKSPACE_TOO_SMALL. The first call on a device looks up the
- * array's device address; make that first call before any stream capture.
- * All calls on a device share the array: calls that overlap on the GPU race. */
+ * RELM_MP_NOALLOC_SCRATCH_BYTES inside the library. The call allocates
+ * nothing. Problems whose workspace (relm_mp_fanin_reduce_workspace_bytes)
+ * exceeds that size are rejected with RELM_MP_ERR_WORKSPACE_TOO_SMALL.
+ *  - The first call on a device loads the library's module that holds the
+ *    array (CUDA loads modules lazily by default), which commits the array on
+ *    that device and may synchronize the device, and looks up the array's
+ *    device address. Make one warm-up call per device at set-up, before any
+ *    stream capture (or run with CUDA_MODULE_LOADING=EAGER). From then on the
+ *    device holds the array until exit. A cudaDeviceReset after that first
+ *    call is not supported (the kept address would be stale).
+ *  - Like relm_mp_fanin_reduce, every call reads its index validation result
+ *    back to the host: it blocks the calling thread until `stream` drains.
+ *  - All calls on a device share the array: calls that overlap on the GPU
+ *    (other streams, other threads) race. */
 #define RELM_MP_NOALLOC_SCRATCH_BYTES (16u << 20)
 RELM_MP_API int relm_mp_fanin_reduce_noalloc(relm_mp_dtype dtype, const void* rel_flat, int64_t rel_rows,
                                              int64_t emb, const int64_t* flat_src, const int64_t* dst_idx,

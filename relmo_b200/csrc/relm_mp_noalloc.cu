@@ -9,13 +9,18 @@
 // file-scope static device array, so a call allocates nothing; the caller
 // still passes the inputs and the output.
 //
-// Every GPU that loads the library holds the array (RELM_MP_NOALLOC_SCRATCH_BYTES)
-// until the process exits. All calls on a device share it: calls whose work
-// overlaps on the GPU (different streams, different host threads) race on it.
+// This file holds no kernel, so its module is loaded on the first call on a
+// device (CUDA loads modules lazily by default): that call commits the
+// RELM_MP_NOALLOC_SCRATCH_BYTES array on the device, and the load may
+// synchronize the device. From then on the device holds the array until the
+// process exits. Callers make one warm-up call per device at set-up (or run
+// with CUDA_MODULE_LOADING=EAGER, which loads it with the library). All calls
+// on a device share the array: calls whose work overlaps on the GPU (different
+// streams, different host threads) race on it.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdio>
-#include <mutex>
 
 #include "relm_mp_internal.cuh"
 
@@ -24,26 +29,28 @@ namespace {
 static __device__ __align__(256) unsigned char g_noalloc_scratch[RELM_MP_NOALLOC_SCRATCH_BYTES];
 
 constexpr int kMaxDevices = 64;
-std::mutex g_setup_mu;
-void* g_scratch_ptr[kMaxDevices] = {};
+std::atomic< void* > g_scratch_ptr[kMaxDevices];
 
 // Device address of the static scratch on the current device. Host code sees
 // g_noalloc_scratch only as a host-side stand-in symbol, so the address comes
-// from cudaGetSymbolAddress, once per device, with that device current.
+// from cudaGetSymbolAddress, looked up once per device with that device
+// current and kept for the later calls (no lock: two threads racing on the
+// first call store the same address). A cudaDeviceReset after the first call
+// is not supported: the module may reload elsewhere and the kept address
+// would be stale.
 int scratch_address(void** out)
 {
    int dev = -1;
    int rc = relm_mp::check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
    if(rc) return rc;
    if(dev < 0 || dev >= kMaxDevices) return relm_mp::fail(RELM_MP_ERR_UNSUPPORTED, "device index out of range.");
-   std::lock_guard< std::mutex > lock(g_setup_mu);
-   if(!g_scratch_ptr[dev]) {
-      void* ptr = nullptr;
+   void* ptr = g_scratch_ptr[dev].load(std::memory_order_acquire);
+   if(!ptr) {
       rc = relm_mp::check_cuda(cudaGetSymbolAddress(&ptr, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)");
       if(rc) return rc;
-      g_scratch_ptr[dev] = ptr;
+      g_scratch_ptr[dev].store(ptr, std::memory_order_release);
    }
-   *out = g_scratch_ptr[dev];
+   *out = ptr;
    return RELM_MP_OK;
 }
 

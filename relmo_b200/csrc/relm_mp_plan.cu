@@ -379,10 +379,14 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
       const unsigned long long pos = use_gather ? host.gather_bad : host.out_bad;
       const int64_t* arr = use_gather ? gather_index : out_index;
       int64_t value = (int64_t)pos;  // a NULL (identity) gather index gathers row e at edge e
-      if(arr && (rc = check_cuda(
-                    cudaMemcpy(&value, arr + pos, sizeof(int64_t), cudaMemcpyDeviceToHost), "bad index copy"
-                 )))
-         return rc;
+      if(arr) {
+         if((rc = check_cuda(
+                cudaMemcpyAsync(&value, arr + pos, sizeof(int64_t), cudaMemcpyDeviceToHost, stream),
+                "bad index copy"
+             )))
+            return rc;
+         if((rc = check_cuda(cudaStreamSynchronize(stream), "bad index sync"))) return rc;
+      }
       char msg[256];
       snprintf(
          msg,
