@@ -1,0 +1,243 @@
+"""Parity at the benchmarked sizes, against the C oracle run in float64.
+
+The bench measures cfg2 (N=2^20 destination rows, E=2^24 messages, D=64,
+truncated Zipf(1.3) destinations: one row holds ~4.3 M messages and ~770 k
+rows are empty) and cfg5 (N=2^22, E=2^26, D=32, 64 hubs x 100 k messages).
+These shapes reach the kernels the small tests reach only in part: the
+long-row fixup over thousands of tiles, the destination-ordered scatter
+backwards above the L2 working set, runs of empty rows. Each test runs the ops
+through ``torch.ops.relm_mp`` exactly as the bench does (plan cache cleared,
+forwards first, so the backwards find the forward's plan), then once more for
+the backwards with the cache cleared (the per-message-row paths), and compares
+every output element with the oracle (``oracle/relm_mp_oracle.c``, the
+reference CPU loops of mp_ops.cpp:2815-2911 and the ATen formulas of
+mp_ops.cpp:2981-3036) evaluated in float64 on the same inputs.
+
+Tolerances:
+* fan-out forward and the injective sum backward (copies): bit-exact;
+* fp32 sums: |got - ref| <= 1e-6 + 1e-5 * max(|ref|, sum of |terms| of the
+  row) (the kernel adds a row's terms in another order than the sequential
+  reference loop);
+* fp32 logsumexp and its backward: 1e-5 relative / 1e-6 absolute;
+* bf16 storage with fp32 accumulation: 1e-2 relative against the float64
+  oracle on the upcast inputs (1e-3 absolute, sums on the |terms| scale).
+
+The oracle is evaluated per column block on a thread pool: every column is
+independent and each block runs the unchanged sequential oracle, so the result
+is identical to one whole-array call.
+"""
+
+from __future__ import annotations
+
+import os
+from concurrent.futures import ThreadPoolExecutor
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from relmo_b200 import workloads
+from relmo_b200.ops import mp
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _host(t: torch.Tensor) -> np.ndarray:
+    if t.dtype in (torch.bfloat16, torch.float16):
+        t = t.float()
+    return t.cpu().numpy()
+
+
+def _threads(bytes_per_block: int, blocks: int) -> int:
+    try:
+        import psutil
+
+        avail = psutil.virtual_memory().available
+    except Exception:  # pragma: no cover - psutil is in the image
+        avail = 32 << 30
+    by_mem = max(1, int(avail * 0.6) // max(1, bytes_per_block))
+    return max(1, min(os.cpu_count() or 1, blocks, by_mem))
+
+
+def _col_blocks(emb: int, width: int) -> list[tuple[int, int]]:
+    return [(c, min(emb, c + width)) for c in range(0, emb, width)]
+
+
+def _run_blocks(work, emb: int, width: int, rows: int) -> None:
+    blocks = _col_blocks(emb, width)
+    # per block in flight: ~4 float64 arrays of rows x width
+    nthreads = _threads(4 * rows * width * 8, len(blocks))
+    with ThreadPoolExecutor(nthreads) as ex:
+        fails = [f for f in ex.map(lambda b: work(*b), blocks) if f]
+    assert not fails, "; ".join(fails[:4])
+
+
+def _col64(a: np.ndarray, c0: int, c1: int) -> np.ndarray:
+    return np.ascontiguousarray(a[:, c0:c1], dtype=np.float64)
+
+
+def _sum_violations(got: np.ndarray, ref: np.ndarray, scale: np.ndarray, rtol: float, atol: float) -> str | None:
+    got = got.astype(np.float64)
+    err = np.abs(got - ref)
+    bound = atol + rtol * np.maximum(np.abs(ref), scale)
+    bad = ~(err <= bound)
+    if bad.any():
+        return f"{int(bad.sum())} elements out of tolerance, worst excess {float((err - bound)[bad].max()):.3g}"
+    return None
+
+
+def _close_violations(got: np.ndarray, ref: np.ndarray, rtol: float, atol: float) -> str | None:
+    got = got.astype(np.float64)
+    same_inf = np.isinf(ref) & (got == ref)
+    both_nan = np.isnan(ref) & np.isnan(got)
+    with np.errstate(invalid="ignore"):  # inf - inf at the matching infinities
+        err = np.abs(got - ref)
+        ok = same_inf | both_nan | (err <= atol + rtol * np.abs(ref))
+    if not ok.all():
+        return f"{int((~ok).sum())} elements out of tolerance"
+    return None
+
+
+def _fan_ops(wl: workloads.FanWorkload, fanout: bool) -> dict[str, torch.Tensor]:
+    """The bench's op sequence through torch.ops.relm_mp, then the backwards
+    again without cached plans. Results on the host."""
+
+    ops = torch.ops.relm_mp
+    res: dict[str, torch.Tensor] = {}
+    mp.clear_plan_cache()
+    if fanout:
+        res["fanout_fwd"] = ops.fanout_scatter(wl.x, wl.src, wl.flat_dst, wl.out_rows).cpu()
+        res["fanout_bwd"] = ops.fanout_scatter_backward(wl.grad_slots, wl.src, wl.flat_dst, wl.x.size(0)).cpu()
+    res["sum"] = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 0).cpu()
+    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+    rows = wl.msgs.size(0)
+    res["lse"] = lse.cpu()
+    res["sum_bwd"] = ops.fanin_reduce_sum_backward(wl.grad_nodes, wl.flat_src, wl.dst, rows).cpu()
+    res["lse_bwd"] = ops.fanin_reduce_logsumexp_backward(wl.grad_nodes, wl.msgs, wl.flat_src, wl.dst, lse, rows).cpu()
+    mp.clear_plan_cache()
+    res["sum_bwd_cold"] = ops.fanin_reduce_sum_backward(wl.grad_nodes, wl.flat_src, wl.dst, rows).cpu()
+    res["lse_bwd_cold"] = ops.fanin_reduce_logsumexp_backward(
+        wl.grad_nodes, wl.msgs, wl.flat_src, wl.dst, lse, rows
+    ).cpu()
+    torch.cuda.synchronize()
+    mp.clear_plan_cache()
+    return res
+
+
+def _check_against_oracle(wl: workloads.FanWorkload, fanout: bool, half: bool) -> None:
+    got = _fan_ops(wl, fanout)
+    emb = wl.emb
+    n = wl.dim_size
+    e = wl.num_edges
+    src, flat_dst = wl.src.cpu().numpy(), wl.flat_dst.cpu().numpy()
+    flat_src, dst = wl.flat_src.cpu().numpy(), wl.dst.cpu().numpy()
+    msgs = _host(wl.msgs)
+    gnodes = _host(wl.grad_nodes)
+    if half:
+        s_rtol, s_atol, l_rtol, l_atol = 1e-2, 1e-3, 1e-2, 1e-3
+    else:
+        s_rtol, s_atol, l_rtol, l_atol = 1e-5, 1e-6, 1e-5, 1e-6
+    width = 4 if emb <= 32 else 8
+
+    # --- the destination rows: hub and empty rows explicitly ---------------------------------
+    deg = np.bincount(dst, minlength=n)
+    hub = int(deg.argmax())
+    empty = deg == 0
+    got_sum, got_lse = _host(got["sum"]), _host(got["lse"])
+    assert empty.any() and deg[hub] > 50_000
+    assert bool((got_sum[empty] == 0).all()), "rows without messages must sum to 0"
+    assert bool(np.isneginf(got_lse[empty]).all()), "rows without messages must give -inf"
+    assert bool(np.isfinite(got_lse[~empty]).all())
+
+    # --- fan-in forward, sum and logsumexp ---------------------------------------------------
+    def fanin_fwd(c0: int, c1: int) -> str | None:
+        v = _col64(msgs, c0, c1)
+        ref_s = oracle.fanin_reduce(v, flat_src, dst, n, 0)
+        scale = oracle.fanin_reduce(np.abs(v), flat_src, dst, n, 0)
+        f = _sum_violations(got_sum[:, c0:c1], ref_s, scale, s_rtol, s_atol)
+        if f:
+            return f"fanin sum cols {c0}:{c1}: {f}"
+        ref_l = oracle.fanin_reduce(v, flat_src, dst, n, 1)
+        f = _close_violations(got_lse[:, c0:c1], ref_l, l_rtol, l_atol)
+        if f:
+            return f"fanin lse cols {c0}:{c1}: {f}"
+        hub_err = np.abs(got_lse[hub, c0:c1] - ref_l[hub])
+        if not (hub_err <= l_atol + l_rtol * np.abs(ref_l[hub])).all():
+            return f"hub row lse cols {c0}:{c1}"
+        return None
+
+    _run_blocks(fanin_fwd, emb, width, e)
+    del got_sum
+
+    # --- fan-in backwards (message rows), warm (forward's plan) and cold ---------------------
+    lse64 = got_lse.astype(np.float64)  # the op's input `out`: the same values the GPU call got
+    gs = _host(got["sum_bwd"])
+    gs_cold = _host(got["sum_bwd_cold"])
+    gl = _host(got["lse_bwd"])
+    gl_cold = _host(got["lse_bwd_cold"])
+
+    def fanin_bwd(c0: int, c1: int) -> str | None:
+        g = _col64(gnodes, c0, c1)
+        ref = oracle.fanin_reduce_sum_backward(g, flat_src, dst, e)
+        for name, a in (("sum_bwd", gs), ("sum_bwd_cold", gs_cold)):
+            if not np.array_equal(a[:, c0:c1].astype(np.float64), ref):  # one term per message row: a copy
+                return f"{name} cols {c0}:{c1} not bit-exact"
+        del ref
+        v = _col64(msgs, c0, c1)
+        ref = oracle.fanin_reduce_logsumexp_backward(g, v, flat_src, dst, np.ascontiguousarray(lse64[:, c0:c1]), e)
+        for name, a in (("lse_bwd", gl), ("lse_bwd_cold", gl_cold)):
+            f = _close_violations(a[:, c0:c1], ref, l_rtol, l_atol)
+            if f:
+                return f"{name} cols {c0}:{c1}: {f}"
+        return None
+
+    _run_blocks(fanin_bwd, emb, width, e)
+    del gs, gs_cold, gl, gl_cold
+
+    if not fanout:
+        return
+    # --- fan-out forward (bit-exact copy) and backward ---------------------------------------
+    x = _host(wl.x)
+    gslots = _host(wl.grad_slots)
+    fo = _host(got["fanout_fwd"])
+    fb = _host(got["fanout_bwd"])
+    x_rows = x.shape[0]
+
+    def fan_out(c0: int, c1: int) -> str | None:
+        ref = oracle.fanout_scatter(np.ascontiguousarray(x[:, c0:c1]), src, flat_dst, wl.out_rows)
+        if not np.array_equal(fo[:, c0:c1], ref):
+            return f"fanout forward cols {c0}:{c1} not bit-exact"
+        del ref
+        g = _col64(gslots, c0, c1)
+        ref = oracle.fanout_scatter_backward(g, src, flat_dst, x_rows)
+        scale = oracle.fanout_scatter_backward(np.abs(g), src, flat_dst, x_rows)
+        f = _sum_violations(fb[:, c0:c1], ref, scale, s_rtol, s_atol)
+        return f"fanout backward cols {c0}:{c1}: {f}" if f else None
+
+    _run_blocks(fan_out, emb, width, e)
+
+
+@pytest.mark.parametrize(
+    "sorted_dst,dtype",
+    [(False, torch.float32), (True, torch.float32), (False, torch.bfloat16)],
+    ids=["fp32-unsorted", "fp32-sorted", "bf16-unsorted"],
+)
+def test_cfg2_full_size_against_oracle(sorted_dst: bool, dtype) -> None:
+    wl = workloads.cfg2(seed=0, device=DEV, sorted_dst=sorted_dst, dtype=dtype)
+    _check_against_oracle(wl, fanout=True, half=dtype != torch.float32)
+    del wl
+    torch.cuda.empty_cache()
+
+
+def test_cfg5_full_size_against_oracle() -> None:
+    # cfg5 is the fan-in ops (sum and logsumexp, forward and backward).
+    wl = workloads.cfg5(seed=0, device=DEV)
+    wl.x = wl.x[:1].clone()  # fan-out inputs unused: free their memory
+    wl.grad_slots = wl.grad_slots[:1].clone()
+    torch.cuda.empty_cache()
+    _check_against_oracle(wl, fanout=False, half=False)
+    del wl
+    torch.cuda.empty_cache()
