@@ -42,7 +42,7 @@ CUDA_SOURCES = [
     "relm_mp_noalloc.cu",
     "relm_mp_lgan.cu",
 ]
-TORCH_SOURCES = ["relm_mp_torch.cpp"]
+TORCH_SOURCES = ["relm_mp_torch.cpp", "relm_mp_cpu.cpp"]
 HEADERS = ["relm_mp_internal.cuh", "relm_mp_segment.cuh", "relm_mp_seg_impl.cuh"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
@@ -115,7 +115,7 @@ def build_torch(force: bool = False) -> Path:
     from torch.utils import cpp_extension
 
     sources = [CSRC / s for s in TORCH_SOURCES]
-    deps = sources + [INCLUDE / "relm_mp.h", CUDA_LIB, Path(__file__)]
+    deps = sources + [CSRC / "relm_mp_torch.h", INCLUDE / "relm_mp.h", CUDA_LIB, Path(__file__)]
     if not force and _newer(TORCH_LIB, deps):
         return TORCH_LIB
     version = str(torch.__version__).split("+")[0]

@@ -13,8 +13,8 @@
 //     tensors.
 //   - CompositeImplicitAutograd pack ops (index arithmetic + cat, as
 //     mp_ops.cpp:412-570 and 2511-2773) and build_info.
-// CPU tensors are not handled by this library (the Python facade keeps the
-// reference's ATen formulas for them).
+// CPU tensors go to the CPU kernels of relm_mp_cpu.cpp (the reference
+// library's loops and ATen formulas, same results and errors).
 //
 // Plans (relm_mp_plan) are cached per (output index, gather index) pair. The
 // key holds weak references to both index storages plus their version
@@ -40,6 +40,7 @@
 #include <vector>
 
 #include "relm_mp.h"
+#include "relm_mp_torch.h"
 
 #ifndef RELM_MP_BUILD_TORCH_VERSION
 #define RELM_MP_BUILD_TORCH_VERSION "unknown"

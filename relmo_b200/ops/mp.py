@@ -3,27 +3,30 @@
 Same functions, arguments and return values as relmo's ``src/relmo/ops/mp.py``
 for the fan-out / fan-in path (``fanout_scatter`` 43-52, ``fanin_reduce`` 55-70,
 the four pack helpers, ``available``, ``assert_runtime_compat``, ``__all__``
-528-544):
+528-544). Each call runs where ``mp_dispatch.route`` sends it:
 
-- CUDA tensors run the B200 kernels through ``torch.ops.relm_mp`` with the
+- CUDA tensors: the B200 kernels through ``torch.ops.relm_mp`` with the
   reference's autograd wrappers. There is no GPU fallback: if the library is
   missing or disabled the call raises.
-- CPU tensors, and fanin modes other than sum/logsumexp, use the reference's
-  ATen formulas (``mp_pack``), as relmo's Python fallback does.
+- CPU tensors: the library's CPU kernels (the reference CPU library's loops and
+  ATen formulas) when it loads, as relmo sends CPU tensors to its library;
+  otherwise the reference's Python formulas (``mp_pack``), or an error under
+  ``RELM_MP_FALLBACK=error``.
+- fanin modes other than sum / logsumexp (mean) use the Python formulas on every
+  device, as relmo's facade does (mp.py:64-65).
 
 The LGAN indexed reductions (``_lgan_pool_reduce``, ``_lgan_relation_graph_step``,
-mp.py:468-525, modes ``"sum"`` / ``"mean"``) follow the same policy: CUDA
-tensors run ``torch.ops.relm_mp.lgan_*`` through the reference's autograd
-wrappers, CPU tensors the reference's Python formulas. The fused block /
-program ops of relmo (``block_*``, ``program_*``, ``_lgan_build_pointwise_step``)
-are a different model family and are not part of this package.
+mp.py:468-525, modes ``"sum"`` / ``"mean"``) follow the same routing through the
+reference's autograd wrappers. The fused block / program ops of relmo
+(``block_*``, ``program_*``, ``_lgan_build_pointwise_step``) are a different
+model family and are not part of this package.
 """
 
 from __future__ import annotations
 
 from .mp_autograd import _FaninReduceLogSumExpFunction, _FaninReduceSumFunction, _FanoutScatterFunction
 from .mp_constants import MODE_LOGSUMEXP, MODE_MEAN, MODE_SUM
-from .mp_dispatch import dispatch_namespace_op, is_cuda, require_gpu_custom
+from .mp_dispatch import CUSTOM, call, route
 from .mp_lgan import (
     _LGANPoolReduceFunction,
     _LGANRelationGraphStepFunction,
@@ -42,12 +45,17 @@ from .mp_pack import (
 from .mp_runtime import TORCH_IMPORT_ERROR, assert_runtime_compat, available, ops_namespace, require_torch, torch
 
 
+def _first(parts):
+    """The tensor whose device decides where a pack op runs (None for no parts)."""
+
+    return parts[0] if len(parts) else None
+
+
 def fanout_scatter(x_cat, src_global_idx, flat_dst, out_rows: int):
     """``out = zeros(out_rows, D); out[flat_dst[e]] = x_cat[src_global_idx[e]]``."""
 
     require_torch("fanout_scatter")
-    if is_cuda(x_cat):
-        require_gpu_custom("fanout_scatter")
+    if route("fanout_scatter", x_cat) == CUSTOM:
         return _FanoutScatterFunction.apply(x_cat, src_global_idx, flat_dst, int(out_rows))
     return fanout_scatter_python(x_cat, src_global_idx, flat_dst, int(out_rows))
 
@@ -60,8 +68,7 @@ def fanin_reduce(rel_flat, flat_src, dst_idx, dim_size: int, mode: int):
     mode_int = int(mode)
     if mode_int not in (MODE_SUM, MODE_LOGSUMEXP):
         return fanin_reduce_python(rel_flat, flat_src, dst_idx, int(dim_size), mode_int)
-    if is_cuda(rel_flat):
-        require_gpu_custom("fanin_reduce")
+    if route("fanin_reduce", rel_flat) == CUSTOM:
         if mode_int == MODE_SUM:
             return _FaninReduceSumFunction.apply(rel_flat, flat_src, dst_idx, int(dim_size))
         return _FaninReduceLogSumExpFunction.apply(rel_flat, flat_src, dst_idx, int(dim_size))
@@ -70,21 +77,23 @@ def fanin_reduce(rel_flat, flat_src, dst_idx, dim_size: int, mode: int):
 
 def fanout_pack_multi(x_parts, src_idx_parts, flat_dst_parts):
     require_torch("fanout_pack_multi")
-    return dispatch_namespace_op(
-        "fanout_pack_multi", x_parts, src_idx_parts, flat_dst_parts, fallback=fanout_pack_multi_python
+    return call(
+        "fanout_pack_multi", x_parts, src_idx_parts, flat_dst_parts, tensor=_first(x_parts),
+        python=fanout_pack_multi_python,
     )
 
 
 def fanin_pack_multi(rel_parts, flat_src_parts, dst_idx_parts):
     require_torch("fanin_pack_multi")
-    return dispatch_namespace_op(
-        "fanin_pack_multi", rel_parts, flat_src_parts, dst_idx_parts, fallback=fanin_pack_multi_python
+    return call(
+        "fanin_pack_multi", rel_parts, flat_src_parts, dst_idx_parts, tensor=_first(rel_parts),
+        python=fanin_pack_multi_python,
     )
 
 
 def fanout_pack_from_edges(x_parts, edge_src_parts, edge_dst_parts, src_part_ids, arity_parts, pos_parts, slot_offset_parts):
     require_torch("fanout_pack_from_edges")
-    return dispatch_namespace_op(
+    return call(
         "fanout_pack_from_edges",
         x_parts,
         edge_src_parts,
@@ -93,13 +102,14 @@ def fanout_pack_from_edges(x_parts, edge_src_parts, edge_dst_parts, src_part_ids
         [int(v) for v in arity_parts],
         [int(v) for v in pos_parts],
         [int(v) for v in slot_offset_parts],
-        fallback=fanout_pack_from_edges_python,
+        tensor=_first(x_parts),
+        python=fanout_pack_from_edges_python,
     )
 
 
 def fanin_pack_from_edges(rel_parts, edge_src_parts, edge_dst_parts, rel_part_ids, arity_parts, pos_parts, mode: int):
     require_torch("fanin_pack_from_edges")
-    return dispatch_namespace_op(
+    return call(
         "fanin_pack_from_edges",
         rel_parts,
         edge_src_parts,
@@ -108,7 +118,8 @@ def fanin_pack_from_edges(rel_parts, edge_src_parts, edge_dst_parts, rel_part_id
         [int(v) for v in arity_parts],
         [int(v) for v in pos_parts],
         int(mode),
-        fallback=fanin_pack_from_edges_python,
+        tensor=_first(rel_parts),
+        python=fanin_pack_from_edges_python,
     )
 
 
@@ -122,8 +133,7 @@ def _lgan_pool_reduce(slot_messages, slot_to_relation_instance, relation_instanc
     mode_int = resolve_lgan_mode("_lgan_pool_reduce", mode)
     args = (slot_messages, slot_to_relation_instance, relation_instance_arities, rr_src, rr_dst, tn_rel, tn_ent,
             nn_rel, nn_ent, int(entity_dim_size), int(mode_int))
-    if is_cuda(slot_messages):
-        require_gpu_custom("lgan_pool_reduce")
+    if route("lgan_pool_reduce", slot_messages) == CUSTOM:
         return _LGANPoolReduceFunction.apply(*args)
     return lgan_pool_reduce_python(*args)
 
@@ -136,8 +146,7 @@ def _lgan_relation_graph_step(relation_pair_x, rr_src, rr_dst, tn_rel, tn_ent, n
     require_torch("_lgan_relation_graph_step")
     mode_int = resolve_lgan_mode("_lgan_relation_graph_step", mode)
     args = (relation_pair_x, rr_src, rr_dst, tn_rel, tn_ent, nn_rel, nn_ent, int(entity_dim_size), int(mode_int))
-    if is_cuda(relation_pair_x):
-        require_gpu_custom("lgan_relation_graph_step")
+    if route("lgan_relation_graph_step", relation_pair_x) == CUSTOM:
         return _LGANRelationGraphStepFunction.apply(*args)
     return lgan_relation_graph_step_python(*args)
 
@@ -145,20 +154,20 @@ def _lgan_relation_graph_step(relation_pair_x, rr_src, rr_dst, tn_rel, tn_ent, n
 def clear_plan_cache() -> None:
     """Drop every cached index plan (they are rebuilt on the next call)."""
 
-    require_gpu_custom("clear_plan_cache")
+    ops_namespace()  # loads the library (raises when it is unusable)
     torch.ops.relm_mp_b200.clear_plan_cache()
 
 
 def plan_cache_stats() -> dict[str, int]:
     """Entries, hits, builds, bytes and capacity of the index-plan cache."""
 
-    require_gpu_custom("plan_cache_stats")
+    ops_namespace()  # loads the library (raises when it is unusable)
     entries, hits, builds, nbytes, capacity = torch.ops.relm_mp_b200.plan_cache_stats()
     return {"entries": entries, "hits": hits, "builds": builds, "bytes": nbytes, "capacity": capacity}
 
 
 def set_plan_cache_capacity(capacity: int) -> None:
-    require_gpu_custom("set_plan_cache_capacity")
+    ops_namespace()  # loads the library (raises when it is unusable)
     torch.ops.relm_mp_b200.set_plan_cache_capacity(int(capacity))
 
 

@@ -154,8 +154,3 @@ def test_pack_ops_through_the_library() -> None:
     )
     assert torch.equal(s3, torch.tensor([1, 5, 7]))
     assert torch.equal(d3, torch.tensor([1, 0, 2]))
-
-
-def test_cpu_tensors_are_rejected_by_the_cuda_library() -> None:
-    with pytest.raises(NotImplementedError):
-        torch.ops.relm_mp.fanout_scatter(torch.randn(3, 2), torch.tensor([0]), torch.tensor([0]), 2)
