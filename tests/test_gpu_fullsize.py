@@ -29,9 +29,6 @@ is identical to one whole-array call.
 
 from __future__ import annotations
 
-import os
-from concurrent.futures import ThreadPoolExecutor
-
 import numpy as np
 import pytest
 import torch
@@ -39,6 +36,7 @@ import torch
 from oracle import oracle
 from relmo_b200 import workloads
 from relmo_b200.ops import mp
+from tests._oracle_blocks import close_violations, col64, run_blocks, sum_violations
 
 pytestmark = pytest.mark.gpu
 
@@ -49,56 +47,6 @@ def _host(t: torch.Tensor) -> np.ndarray:
     if t.dtype in (torch.bfloat16, torch.float16):
         t = t.float()
     return t.cpu().numpy()
-
-
-def _threads(bytes_per_block: int, blocks: int) -> int:
-    try:
-        import psutil
-
-        avail = psutil.virtual_memory().available
-    except Exception:  # pragma: no cover - psutil is in the image
-        avail = 32 << 30
-    by_mem = max(1, int(avail * 0.6) // max(1, bytes_per_block))
-    return max(1, min(os.cpu_count() or 1, blocks, by_mem))
-
-
-def _col_blocks(emb: int, width: int) -> list[tuple[int, int]]:
-    return [(c, min(emb, c + width)) for c in range(0, emb, width)]
-
-
-def _run_blocks(work, emb: int, width: int, rows: int) -> None:
-    blocks = _col_blocks(emb, width)
-    # per block in flight: ~4 float64 arrays of rows x width
-    nthreads = _threads(4 * rows * width * 8, len(blocks))
-    with ThreadPoolExecutor(nthreads) as ex:
-        fails = [f for f in ex.map(lambda b: work(*b), blocks) if f]
-    assert not fails, "; ".join(fails[:4])
-
-
-def _col64(a: np.ndarray, c0: int, c1: int) -> np.ndarray:
-    return np.ascontiguousarray(a[:, c0:c1], dtype=np.float64)
-
-
-def _sum_violations(got: np.ndarray, ref: np.ndarray, scale: np.ndarray, rtol: float, atol: float) -> str | None:
-    got = got.astype(np.float64)
-    err = np.abs(got - ref)
-    bound = atol + rtol * np.maximum(np.abs(ref), scale)
-    bad = ~(err <= bound)
-    if bad.any():
-        return f"{int(bad.sum())} elements out of tolerance, worst excess {float((err - bound)[bad].max()):.3g}"
-    return None
-
-
-def _close_violations(got: np.ndarray, ref: np.ndarray, rtol: float, atol: float) -> str | None:
-    got = got.astype(np.float64)
-    same_inf = np.isinf(ref) & (got == ref)
-    both_nan = np.isnan(ref) & np.isnan(got)
-    with np.errstate(invalid="ignore"):  # inf - inf at the matching infinities
-        err = np.abs(got - ref)
-        ok = same_inf | both_nan | (err <= atol + rtol * np.abs(ref))
-    if not ok.all():
-        return f"{int((~ok).sum())} elements out of tolerance"
-    return None
 
 
 def _fan_ops(wl: workloads.FanWorkload, fanout: bool) -> dict[str, torch.Tensor]:
@@ -154,14 +102,14 @@ def _check_against_oracle(wl: workloads.FanWorkload, fanout: bool, half: bool) -
 
     # --- fan-in forward, sum and logsumexp ---------------------------------------------------
     def fanin_fwd(c0: int, c1: int) -> str | None:
-        v = _col64(msgs, c0, c1)
+        v = col64(msgs, c0, c1)
         ref_s = oracle.fanin_reduce(v, flat_src, dst, n, 0)
         scale = oracle.fanin_reduce(np.abs(v), flat_src, dst, n, 0)
-        f = _sum_violations(got_sum[:, c0:c1], ref_s, scale, s_rtol, s_atol)
+        f = sum_violations(got_sum[:, c0:c1], ref_s, scale, s_rtol, s_atol)
         if f:
             return f"fanin sum cols {c0}:{c1}: {f}"
         ref_l = oracle.fanin_reduce(v, flat_src, dst, n, 1)
-        f = _close_violations(got_lse[:, c0:c1], ref_l, l_rtol, l_atol)
+        f = close_violations(got_lse[:, c0:c1], ref_l, l_rtol, l_atol)
         if f:
             return f"fanin lse cols {c0}:{c1}: {f}"
         hub_err = np.abs(got_lse[hub, c0:c1] - ref_l[hub])
@@ -169,7 +117,7 @@ def _check_against_oracle(wl: workloads.FanWorkload, fanout: bool, half: bool) -
             return f"hub row lse cols {c0}:{c1}"
         return None
 
-    _run_blocks(fanin_fwd, emb, width, e)
+    run_blocks(fanin_fwd, emb, width, e)
     del got_sum
 
     # --- fan-in backwards (message rows), warm (forward's plan) and cold ---------------------
@@ -180,21 +128,21 @@ def _check_against_oracle(wl: workloads.FanWorkload, fanout: bool, half: bool) -
     gl_cold = _host(got["lse_bwd_cold"])
 
     def fanin_bwd(c0: int, c1: int) -> str | None:
-        g = _col64(gnodes, c0, c1)
+        g = col64(gnodes, c0, c1)
         ref = oracle.fanin_reduce_sum_backward(g, flat_src, dst, e)
         for name, a in (("sum_bwd", gs), ("sum_bwd_cold", gs_cold)):
             if not np.array_equal(a[:, c0:c1].astype(np.float64), ref):  # one term per message row: a copy
                 return f"{name} cols {c0}:{c1} not bit-exact"
         del ref
-        v = _col64(msgs, c0, c1)
+        v = col64(msgs, c0, c1)
         ref = oracle.fanin_reduce_logsumexp_backward(g, v, flat_src, dst, np.ascontiguousarray(lse64[:, c0:c1]), e)
         for name, a in (("lse_bwd", gl), ("lse_bwd_cold", gl_cold)):
-            f = _close_violations(a[:, c0:c1], ref, l_rtol, l_atol)
+            f = close_violations(a[:, c0:c1], ref, l_rtol, l_atol)
             if f:
                 return f"{name} cols {c0}:{c1}: {f}"
         return None
 
-    _run_blocks(fanin_bwd, emb, width, e)
+    run_blocks(fanin_bwd, emb, width, e)
     del gs, gs_cold, gl, gl_cold
 
     if not fanout:
@@ -211,13 +159,13 @@ def _check_against_oracle(wl: workloads.FanWorkload, fanout: bool, half: bool) -
         if not np.array_equal(fo[:, c0:c1], ref):
             return f"fanout forward cols {c0}:{c1} not bit-exact"
         del ref
-        g = _col64(gslots, c0, c1)
+        g = col64(gslots, c0, c1)
         ref = oracle.fanout_scatter_backward(g, src, flat_dst, x_rows)
         scale = oracle.fanout_scatter_backward(np.abs(g), src, flat_dst, x_rows)
-        f = _sum_violations(fb[:, c0:c1], ref, scale, s_rtol, s_atol)
+        f = sum_violations(fb[:, c0:c1], ref, scale, s_rtol, s_atol)
         return f"fanout backward cols {c0}:{c1}: {f}" if f else None
 
-    _run_blocks(fan_out, emb, width, e)
+    run_blocks(fan_out, emb, width, e)
 
 
 @pytest.mark.parametrize(

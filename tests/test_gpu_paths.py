@@ -13,10 +13,13 @@ reference's result.
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 import torch
 
+from oracle import oracle
 from relmo_b200.ops import mp
+from tests._oracle_blocks import close_violations, col64, run_blocks
 
 pytestmark = pytest.mark.gpu
 
@@ -126,11 +129,31 @@ def test_identity_message_index_plans(extra_rows):
     torch.testing.assert_close(gl.double(), expect_l, rtol=1e-5, atol=1e-6)
 
 
+def _oracle_lse_backward(gout, rel, flat_src, dst, lse, rel_rows, emb):
+    """float64 oracle of the logsumexp backward on the op's own inputs."""
+
+    g64 = gout.float().cpu().numpy()
+    r64 = rel.float().cpu().numpy()
+    o64 = lse.float().cpu().numpy()
+    fs, d = flat_src.cpu().numpy(), dst.cpu().numpy()
+    blocks: dict[tuple[int, int], np.ndarray] = {}
+
+    def work(c0: int, c1: int):
+        blocks[(c0, c1)] = oracle.fanin_reduce_logsumexp_backward(
+            col64(g64, c0, c1), col64(r64, c0, c1), fs, d, col64(o64, c0, c1), rel_rows
+        )
+        return None
+
+    run_blocks(work, emb, 8, rel_rows)
+    return blocks
+
+
 @pytest.mark.parametrize("dtype,emb", [(torch.float32, 32), (torch.bfloat16, 64)])
 def test_lse_backward_destination_order_path(dtype, emb):
     """Above the L2 working set, with the forward's plan cached and message rows
     used once, the logsumexp backward walks the forward's plan in destination
-    order; it must equal the per-message-row path bit for bit."""
+    order; without the cached plan it runs per message row. Both against the
+    float64 oracle on the same inputs (message rows no edge uses get 0)."""
 
     ops = torch.ops.relm_mp
     g = torch.Generator(device="cuda").manual_seed(11)
@@ -141,17 +164,15 @@ def test_lse_backward_destination_order_path(dtype, emb):
     gout = torch.randn(rows, emb, device="cuda", generator=g).to(dtype)
     mp.clear_plan_cache()
     lse = ops.fanin_reduce(rel, flat_src, dst, rows, 1)  # caches the destination-ordered plan
-    warm = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel.size(0))
+    warm = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel.size(0)).float().cpu().numpy()
     mp.clear_plan_cache()
-    cold = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel.size(0))
-    assert torch.equal(warm, cold)
-    used = torch.zeros(rel.size(0), dtype=torch.bool, device="cuda")
-    used[flat_src] = True
-    assert bool((warm[~used] == 0).all())
-    e = torch.arange(0, edges, 9973, device="cuda")
-    expect = gout[dst[e]].double() * torch.exp(rel[flat_src[e]].double() - lse[dst[e]].double())
-    tol = dict(rtol=1e-2, atol=1e-2) if dtype == torch.bfloat16 else dict(rtol=1e-5, atol=1e-6)
-    torch.testing.assert_close(warm[flat_src[e]].double(), expect, **tol)
+    cold = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, rel.size(0)).float().cpu().numpy()
+    ref = _oracle_lse_backward(gout, rel, flat_src, dst, lse, rel.size(0), emb)
+    rtol, atol = (1e-2, 1e-3) if dtype == torch.bfloat16 else (1e-5, 1e-6)
+    for (c0, c1), want in ref.items():
+        for name, got in (("warm", warm), ("cold", cold)):
+            f = close_violations(got[:, c0:c1], want, rtol, atol)
+            assert f is None, f"{name} cols {c0}:{c1}: {f}"
 
 
 @pytest.mark.parametrize("offset", [0, 1])
@@ -182,8 +203,8 @@ def test_validation_paths_aligned_and_offset_indices(offset, n):
 def test_large_backwards_with_unpacked_rows():
     """Above the working set with 192-byte rows (not a power of two times 16):
     the sum backward scatters through the general scatter kernel and the
-    logsumexp backward falls back to the per-message-row path; both equal the
-    paths taken without a cached forward plan."""
+    logsumexp backward falls back to the per-message-row path; both, with and
+    without a cached forward plan, against the float64 oracle."""
 
     ops = torch.ops.relm_mp
     g = torch.Generator(device="cuda").manual_seed(21)
@@ -194,13 +215,20 @@ def test_large_backwards_with_unpacked_rows():
     gout = torch.randn(rows, emb, device="cuda", generator=g)
     mp.clear_plan_cache()
     lse = ops.fanin_reduce(rel, flat_src, dst, rows, 1)
-    warm_s = ops.fanin_reduce_sum_backward(gout, flat_src, dst, edges)
-    warm_l = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)
+    got = {"warm_s": ops.fanin_reduce_sum_backward(gout, flat_src, dst, edges),
+           "warm_l": ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)}
     mp.clear_plan_cache()
-    cold_s = ops.fanin_reduce_sum_backward(gout, flat_src, dst, edges)
-    cold_l = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)
-    assert torch.equal(warm_s, cold_s)
-    assert torch.equal(warm_l, cold_l)
+    got["cold_s"] = ops.fanin_reduce_sum_backward(gout, flat_src, dst, edges)
+    got["cold_l"] = ops.fanin_reduce_logsumexp_backward(gout, rel, flat_src, dst, lse, edges)
+    got = {k: v.cpu().numpy() for k, v in got.items()}
+    # flat_src is a permutation: the sum backward copies one grad row per message row
+    ref_s = oracle.fanin_reduce_sum_backward(gout.cpu().numpy(), flat_src.cpu().numpy(), dst.cpu().numpy(), edges)
+    assert np.array_equal(got["warm_s"], ref_s) and np.array_equal(got["cold_s"], ref_s)
+    ref_l = _oracle_lse_backward(gout, rel, flat_src, dst, lse, edges, emb)
+    for (c0, c1), want in ref_l.items():
+        for name in ("warm_l", "cold_l"):
+            f = close_violations(got[name][:, c0:c1], want, 1e-5, 1e-6)
+            assert f is None, f"{name} cols {c0}:{c1}: {f}"
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float64])
