@@ -36,6 +36,14 @@ synthetic LGAN batch - 2^17 entities, 2^20 relation instances of arity 1..3
 (workloads.lgan_algorithmic_bytes) per step, plans built inside the step, and
 per-op times with cached plans (the per-layer cost inside a model).
 
+Also in the default line: every op's time, GB/s, fraction of the measured copy
+peak and messages/s with its plans cached (``per_op``); at N=1 the same table
+for cfg2 with bf16 storage (``per_op_bf16``) and for destination-sorted cfg2
+(``per_op_sorted``); and, at every N, cfg5 (2^22 rows, 2^26 messages, D=32,
+64 hubs x 100k) split over the ranks by work-balanced destination ranges with
+no collective (``cfg5_partitioned``: step time = max over ranks, the per-rank
+step times and edge counts).
+
 --impl reference: the reference's own CPU relm_mp library
 (``oracle/_ref/relm_mp_ref.so``, built from the reference sources) on the
 host cores, on a bounded edge sample of the same workload; rank 0 only.
@@ -237,6 +245,98 @@ def shard_workload(wl: workloads.FanWorkload, rank: int, world: int) -> workload
     )
 
 
+def time_per_op(ops, wl: workloads.FanWorkload, op_list, reps: int, nbytes: dict) -> dict:
+    """Each op on its own with its plans cached: CUDA-event time per call on the
+    current stream (2 untimed calls first), GB/s of its algorithmic bytes, the
+    fraction of the measured copy peak, and messages per second."""
+
+    peak = measured_peaks()["hbm_gbs"]
+    stream = torch.cuda.current_stream()
+    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
+    out = {}
+    for op in op_list:
+        for _ in range(2):
+            run_one_op(ops, wl, op, lse)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(reps):
+            run_one_op(ops, wl, op, lse)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        ms = ev0.elapsed_time(ev1) / reps
+        gbs = nbytes[op] / ms / 1e6
+        out[op] = {"ms": round(ms, 4), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                   "msgs_per_s": round(wl.num_edges / ms * 1e3, 1), "bytes": nbytes[op]}
+    return out
+
+
+def extra_per_op(ops, mp, name: str, dtype: torch.dtype, seed: int, device, reps: int) -> dict:
+    """Per-op table of another cfg2 variant (bf16 storage, or destination-sorted)."""
+
+    wl = make_workload(name, seed=seed, device=device, dtype=dtype)
+    nbytes = op_bytes(wl, OPS)
+    mp.clear_plan_cache()
+    table = time_per_op(ops, wl, OPS, reps, nbytes)
+    mp.clear_plan_cache()
+    del wl
+    torch.cuda.empty_cache()
+    return {"workload": name, "dtype": "f32" if dtype == torch.float32 else "bf16", "per_op": table}
+
+
+def cfg5_partitioned(ops, mp, device, rank: int, world: int, barrier, max_over_ranks, sum_over_ranks,
+                     steps: int, warmup: int) -> dict:
+    """cfg5 (2^22 rows, 2^26 messages, D=32, 64 hubs x 100k) split over the ranks
+    by work-balanced destination ranges (relmo_b200.partition): each rank runs
+    the four fan-in ops on its own edges, message rows and output rows, with no
+    collective; one step = plan cache cleared + the four ops. Strong scaling:
+    the whole job is the same at every N."""
+
+    wl = make_workload("cfg5", seed=0, device=device, dtype=torch.float32)
+    if world > 1:
+        wl = shard_workload(wl, rank, world)
+    wl.x = wl.x[:1].clone()  # fan-out inputs unused by the fan-in ops
+    wl.grad_slots = wl.grad_slots[:1].clone()
+    torch.cuda.empty_cache()
+    step_bytes = sum(op_bytes(wl, FANIN_OPS).values())
+
+    def step():
+        mp.clear_plan_cache()
+        run_ops(ops, wl, FANIN_OPS)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    barrier()
+    stream = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        step()
+    ev1.record(stream)
+    barrier()
+    mine = ev0.elapsed_time(ev1) / steps
+    elapsed_ms = max_over_ranks(mine)
+    job_bytes = sum_over_ranks(step_bytes)
+    per_rank = [[float(mine), float(wl.num_edges), float(wl.dim_size)]]
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor(per_rank[0], device=device, dtype=torch.float64)
+        allv = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(allv, t)
+        per_rank = [v.tolist() for v in allv]
+    mp.clear_plan_cache()
+    del wl
+    torch.cuda.empty_cache()
+    return {
+        "workload": "cfg5", "ops": list(FANIN_OPS), "ranks": world, "steps": steps,
+        "step": "plan builds (cache cleared) + 4 fan-in ops",
+        "ms_per_step": round(elapsed_ms, 4), "value": round(job_bytes / elapsed_ms / 1e6, 1), "unit": UNIT,
+        "scaling": "strong", "parallelism": f"work-balanced destination-range partition x{world}, no collective",
+        "per_rank": [{"ms": round(v[0], 4), "edges": int(v[1]), "rows": int(v[2])} for v in per_rank],
+    }
+
+
 def run_one_op(ops, wl, op: str, lse=None):
     if op == "fanout_fwd":
         return ops.fanout_scatter(wl.x, wl.src, wl.flat_dst, wl.out_rows)
@@ -376,7 +476,28 @@ def reference_arm(args) -> None:
                          "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if args.workload.startswith("cfg2") and args.reference_gpu:
+        line["reference_gpu"] = reference_gpu_ops(args.workload)
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_ops(workload: str) -> dict:
+    """The reference's own SIMT kernels (mp_cuda_kernels.cu built for sm_100a by
+    oracle/build_ref.py --cuda) timed per op on the full cfg2 workload on this
+    box's GPU, in a process of their own (oracle/ref_gpu_ops.py): the same-box
+    GPU baseline beside the CPU one. Not part of this arm's value."""
+
+    if not torch.cuda.is_available():
+        return {"unavailable": "no GPU in this process"}
+    try:
+        proc = subprocess.run([sys.executable, str(ROOT / "oracle" / "ref_gpu_ops.py"), "--workload", workload],
+                              capture_output=True, text=True, timeout=900)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "reference GPU ops did not finish in 900 s"}
+    for line in reversed(proc.stdout.splitlines()):
+        if line.startswith("{"):
+            return json.loads(line)
+    return {"unavailable": f"reference GPU ops exited {proc.returncode}: {proc.stderr.strip()[-300:]}"}
 
 
 # ---- B200 arm -------------------------------------------------------------------------------
@@ -408,6 +529,12 @@ def main() -> int:
     parser.add_argument("--model-states", type=int, default=None, help="override the global batch (states)")
     parser.add_argument("--micro-states", type=int, default=None, help="states per micro-batch (cfg4 default 512)")
     parser.add_argument("--lgan", type=int, default=1, help="add the LGAN step to the cfg2 line (0: no)")
+    parser.add_argument("--extra-tables", type=int, default=1,
+                        help="cfg2 line at N=1: add per-op tables of cfg2 bf16 and cfg2 sorted (0: no)")
+    parser.add_argument("--reference-gpu", type=int, default=1,
+                        help="--impl reference on cfg2: also time the reference's own GPU kernels (0: no)")
+    parser.add_argument("--cfg5-part", type=int, default=1,
+                        help="cfg2 line: add the cfg5 destination-range partition at every N (0: no)")
     parser.add_argument("--lgan-relations", type=int, default=1 << 20, help="LGAN relation instances")
     parser.add_argument("--lgan-entities", type=int, default=1 << 17, help="LGAN entities")
     parser.add_argument("--lgan-steps", type=int, default=5, help="timed LGAN steps in the cfg2 line")
@@ -482,23 +609,9 @@ def main() -> int:
         return run_ops(ops, wl, op_list)
 
     # ---- per-op kernel timing (plans cached): roofline of each op -------------------------
-    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
-    per_op = {}
     stream = torch.cuda.current_stream()
     timed_ops = op_list if not (args.ops_only and args.ops) else tuple(o for o in args.ops.split(",") if o)
-    for op in timed_ops:
-        for _ in range(2):
-            run_one_op(ops, wl, op, lse)
-        reps = args.reps
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        ev0.record(stream)
-        for _ in range(reps):
-            run_one_op(ops, wl, op, lse)
-        ev1.record(stream)
-        torch.cuda.synchronize()
-        ms = ev0.elapsed_time(ev1) / reps
-        per_op[op] = {"ms": round(ms, 4), "gbs": round(nbytes[op] / ms / 1e6, 1), "bytes": nbytes[op]}
+    per_op = time_per_op(ops, wl, timed_ops, args.reps, nbytes)
     if args.ops_only:
         if rank == 0:
             print(json.dumps({"per_op": per_op}), flush=True)
@@ -528,6 +641,7 @@ def main() -> int:
     value = job_bytes * args.steps / elapsed / 1e9
 
     # ---- plan build cost (separately) -----------------------------------------------------------
+    lse = ops.fanin_reduce(wl.msgs, wl.flat_src, wl.dst, wl.dim_size, 1)
     mp.clear_plan_cache()
     torch.cuda.synchronize()
     t0 = torch.cuda.Event(enable_timing=True)
@@ -566,6 +680,13 @@ def main() -> int:
     if args.lgan:
         lgan = lgan_bench(args, device, rank, world, max_over_ranks, sum_over_ranks, barrier,
                           steps=args.lgan_steps, warmup=3)
+    extra = {}
+    if world == 1 and args.workload == "cfg2-unsorted" and args.extra_tables:
+        extra["per_op_bf16"] = extra_per_op(ops, mp, "cfg2-unsorted", torch.bfloat16, 0, device, args.reps)
+        extra["per_op_sorted"] = extra_per_op(ops, mp, "cfg2-sorted", torch.float32, 0, device, args.reps)
+    if args.workload.startswith("cfg2") and args.cfg5_part:
+        extra["cfg5_partitioned"] = cfg5_partitioned(ops, mp, device, rank, world, barrier, max_over_ranks,
+                                                     sum_over_ranks, steps=args.steps, warmup=3)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         sample = cpu_sample(args.workload, args.port_edges)
@@ -600,6 +721,7 @@ def main() -> int:
             "ops_only_gbs": round(step_bytes / ops_ms / 1e6, 1),
             "libs": mp_runtime.loaded_library_paths(),
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

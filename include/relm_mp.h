@@ -300,6 +300,37 @@ RELM_MP_API int relm_mp_plan_logsumexp_backward(const relm_mp_plan* plan, relm_m
                                     int64_t emb, void* grad_rel, void* scratch,
                                     size_t scratch_bytes, void* stream);
 
+/* Logsumexp forms. NULL (or beta = 1, eps = 0) is fanin_reduce mode 1. The
+ * smoothed form is relmo's LogSumExpAggregation (relmo/models/aggr.py:96-123),
+ * the aggregation its models use for "logsumexp":
+ *   out[r] = m_r + (1/beta) log(eps + sum over edges j of r of e^(beta (x_j - m_r))),
+ *   m_r = max_j x_j (no gradient through it), rows without edges (1/beta) log(eps);
+ * its gradient is e^(beta (x_j - out[r])) per edge (the softmax of beta x with
+ * the eps term). relmo evaluates it with four ATen passes around a
+ * index_reduce_ amax; here it is one planned pass like the plain form. No
+ * counterpart in the reference's op library. */
+typedef struct relm_mp_lse_form {
+   double beta; /* > 0; relmo's default maximum_smoothness is 12 */
+   double eps;  /* >= 0; relmo adds 1e-16 */
+} relm_mp_lse_form;
+
+/* relm_mp_plan_reduce mode 1 with a logsumexp form (form NULL: plain). */
+RELM_MP_API int relm_mp_plan_reduce_lse(const relm_mp_plan* plan, relm_mp_dtype dtype, const relm_mp_lse_form* form,
+                                        const void* table, int64_t emb, void* out, void* scratch,
+                                        size_t scratch_bytes, void* stream);
+/* relm_mp_plan_logsumexp_backward for a form: grad_rel[r] = sum over edges j of
+ * r of grad_out[gidx[j]] * e^(beta (rel[r] - lse_out[gidx[j]])). */
+RELM_MP_API int relm_mp_plan_logsumexp_backward_ex(const relm_mp_plan* plan, relm_mp_dtype dtype,
+                                                   const relm_mp_lse_form* form, const void* grad_out,
+                                                   const void* lse_out, const void* rel, int64_t emb,
+                                                   void* grad_rel, void* scratch, size_t scratch_bytes,
+                                                   void* stream);
+/* relm_mp_plan_scatter_logsumexp_backward for a form. */
+RELM_MP_API int relm_mp_plan_scatter_logsumexp_backward_ex(const relm_mp_plan* plan, relm_mp_dtype dtype,
+                                                           const relm_mp_lse_form* form, const void* grad_out,
+                                                           const void* lse_out, const void* rel, int64_t emb,
+                                                           const uint32_t* cover, void* grad_rel, void* stream);
+
 /* Sum with a fused epilogue, the indexed sum / mean of the LGAN ops
  * (relmo/ops/mp_common.py:88-118, mp_ops.cpp:3433-3454):
  *   out[r] = base[r] + (sum over edges j of r of table[gidx[j]]) / max(d_r, 1)

@@ -72,6 +72,15 @@ class LganGraph(ctypes.Structure):
 
 _GRAPHP = ctypes.POINTER(LganGraph)
 
+
+class LseForm(ctypes.Structure):
+    """relm_mp_lse_form: the smoothed logsumexp's beta and eps."""
+
+    _fields_ = [("beta", ctypes.c_double), ("eps", ctypes.c_double)]
+
+
+_FORMP = ctypes.POINTER(LseForm)
+
 SIGNATURES: dict[str, tuple] = {
     "relm_mp_status_string": (_STR, [_INT]),
     "relm_mp_build_info": (_STR, []),
@@ -109,6 +118,9 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_reduce": (_INT, [_PLANP, _INT, _INT, _P, _I64, _P, _P, _SZ, _P]),
     "relm_mp_plan_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
     "relm_mp_plan_reduce_ex": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _INT, _P, _P, _SZ, _P]),
+    "relm_mp_plan_reduce_lse": (_INT, [_PLANP, _INT, _FORMP, _P, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_plan_logsumexp_backward_ex": (_INT, [_PLANP, _INT, _FORMP, _P, _P, _P, _I64, _P, _P, _SZ, _P]),
+    "relm_mp_plan_scatter_logsumexp_backward_ex": (_INT, [_PLANP, _INT, _FORMP, _P, _P, _P, _I64, _P, _P, _P]),
     "relm_mp_plan_scatter_rows_div": (_INT, [_PLANP, _INT, _P, _I64, _P, _P, _P, _P]),
     "relm_mp_plan_gather_counts": (_INT, [_PLANP, _P, _P]),
     "relm_mp_plan_gather_rows_div": (_INT, [_PLANP, _P, _INT, _P, _I64, _P, _P, _P]),
@@ -371,6 +383,44 @@ class PlanHandle:
         check(lib().relm_mp_plan_reduce(
             ctypes.byref(self.plan), dtype_code(table), int(mode), _ptr(table), emb, _ptr(out),
             scratch.data_ptr(), scratch.numel(), _stream(table.device),
+        ))
+        return out
+
+    def reduce_lse(self, table, beta: float | None = None, eps: float = 0.0):
+        """Logsumexp over each row's gathered rows: plain (beta None) or the
+        smoothed form (relm_mp_plan_reduce_lse)."""
+
+        torch = _torch()
+        table = table.contiguous()
+        emb = table.size(1)
+        out = torch.empty((self.plan.num_rows, emb), dtype=table.dtype, device=table.device)
+        form = ctypes.byref(LseForm(float(beta), float(eps))) if beta is not None else None
+        scratch = _workspace(
+            lib().relm_mp_plan_reduce_scratch_bytes(ctypes.byref(self.plan), emb, dtype_code(table), MODE_LOGSUMEXP),
+            table.device,
+        )
+        check(lib().relm_mp_plan_reduce_lse(
+            ctypes.byref(self.plan), dtype_code(table), form, _ptr(table), emb, _ptr(out),
+            scratch.data_ptr(), scratch.numel(), _stream(table.device),
+        ))
+        return out
+
+    def logsumexp_backward(self, grad_out, lse_out, rel, beta: float | None = None):
+        """grad_rel[r] = sum over r's edges of grad_out[g] * exp(beta (rel[r] - lse_out[g]))
+        (relm_mp_plan_logsumexp_backward_ex; beta None: 1)."""
+
+        torch = _torch()
+        grad_out, lse_out, rel = grad_out.contiguous(), lse_out.contiguous(), rel.contiguous()
+        emb = grad_out.size(1)
+        out = torch.empty((self.plan.num_rows, emb), dtype=grad_out.dtype, device=grad_out.device)
+        form = ctypes.byref(LseForm(float(beta), 0.0)) if beta is not None else None
+        scratch = _workspace(
+            lib().relm_mp_plan_reduce_scratch_bytes(ctypes.byref(self.plan), emb, dtype_code(grad_out), 2),
+            grad_out.device,
+        )
+        check(lib().relm_mp_plan_logsumexp_backward_ex(
+            ctypes.byref(self.plan), dtype_code(grad_out), form, _ptr(grad_out), _ptr(lse_out), _ptr(rel), emb,
+            _ptr(out), scratch.data_ptr(), scratch.numel(), _stream(grad_out.device),
         ))
         return out
 

@@ -18,6 +18,7 @@
 #include <ATen/ATen.h>
 #include <torch/library.h>
 
+#include <cmath>
 #include <cstdint>
 #include <cstring>
 #include <limits>
@@ -233,6 +234,54 @@ Tensor fanin_reduce_logsumexp_backward_cpu(const Tensor& grad_out, const Tensor&
    return grad_rel;
 }
 
+// ---- smoothed logsumexp (relmo's LogSumExpAggregation, models/aggr.py:96-123) -------------
+//
+// The formula relmo's models evaluate for "logsumexp" aggregation: per column,
+// m = row max over the messages (kept at 0 for rows without messages, no
+// gradient), out = (1/beta) log(eps + sum e^(beta (x - m))) + m. Its backward
+// weight is e^(beta (x - out)).
+
+void check_smoothed(double beta, double eps)
+{
+   TORCH_CHECK(beta > 0.0 && std::isfinite(beta), "smoothed logsumexp needs a finite beta > 0.");
+   TORCH_CHECK(eps >= 0.0, "smoothed logsumexp needs eps >= 0.");
+}
+
+Tensor smoothed_logsumexp_cpu(const Tensor& rel_flat, const Tensor& flat_src, const Tensor& dst_idx, int64_t dim_size,
+                              double beta, double eps)
+{
+   check_rank(rel_flat, 2, "rel_flat");
+   check_int64_index(flat_src, "flat_src");
+   check_int64_index(dst_idx, "dst_idx");
+   TORCH_CHECK(flat_src.size(0) == dst_idx.size(0), "flat_src and dst_idx must have equal length.");
+   TORCH_CHECK(dim_size >= 0, "dim_size must be >= 0.");
+   check_smoothed(beta, eps);
+   const Tensor msgs = rel_flat.index_select(0, flat_src);
+   Tensor row_max = at::zeros({dim_size, rel_flat.size(1)}, rel_flat.options());
+   row_max.index_reduce_(0, dst_idx, msgs, "amax", /*include_self=*/false);
+   Tensor sums = at::full_like(row_max, eps);
+   sums.index_add_(0, dst_idx, (beta * (msgs - row_max.index_select(0, dst_idx))).exp());
+   return (1.0 / beta) * sums.log() + row_max;
+}
+
+Tensor smoothed_logsumexp_backward_cpu(const Tensor& grad_out, const Tensor& rel_flat, const Tensor& flat_src,
+                                       const Tensor& dst_idx, const Tensor& out, int64_t rel_rows, double beta)
+{
+   check_rank(grad_out, 2, "grad_out");
+   check_rank(rel_flat, 2, "rel_flat");
+   check_int64_index(flat_src, "flat_src");
+   check_int64_index(dst_idx, "dst_idx");
+   check_rank(out, 2, "out");
+   TORCH_CHECK(flat_src.size(0) == dst_idx.size(0), "flat_src and dst_idx must have equal length.");
+   TORCH_CHECK(rel_rows >= 0, "rel_rows must be >= 0.");
+   check_smoothed(beta, 0.0);
+   Tensor grad_rel = at::zeros({rel_rows, grad_out.size(1)}, rel_flat.options());
+   if(flat_src.numel() == 0 || rel_rows == 0) return grad_rel;
+   const Tensor weight = (beta * (rel_flat.index_select(0, flat_src) - out.index_select(0, dst_idx))).exp();
+   grad_rel.index_add_(0, flat_src, grad_out.index_select(0, dst_idx) * weight);
+   return grad_rel;
+}
+
 // ---- LGAN ops (sum / mean) --------------------------------------------------------
 
 // One indexed aggregation (relmo/ops/mp_common.py:88-118, mp_ops.cpp:3433-3454):
@@ -414,4 +463,10 @@ TORCH_LIBRARY_IMPL(relm_mp, CPU, m)
    m.impl("lgan_pool_reduce_backward", relm_b200::lgan_pool_reduce_backward_cpu);
    m.impl("lgan_relation_graph_step", relm_b200::lgan_relation_graph_step_cpu);
    m.impl("lgan_relation_graph_step_backward", relm_b200::lgan_relation_graph_step_backward_cpu);
+}
+
+TORCH_LIBRARY_IMPL(relm_mp_b200, CPU, m)
+{
+   m.impl("fanin_reduce_smoothed_logsumexp", relm_b200::smoothed_logsumexp_cpu);
+   m.impl("fanin_reduce_smoothed_logsumexp_backward", relm_b200::smoothed_logsumexp_backward_cpu);
 }

@@ -65,6 +65,8 @@ int64_t plan_num_tiles(int64_t num_edges, int64_t num_rows);
 
 // Element-wise fill of `count` elements of dtype with 0 or -inf.
 int fill_rows(relm_mp_dtype dtype, void* out, int64_t count, bool neg_inf, cudaStream_t stream);
+// out[0..count) = value (converted to the storage type).
+int fill_value(relm_mp_dtype dtype, void* out, int64_t count, double value, cudaStream_t stream);
 
 size_t dtype_size(relm_mp_dtype dtype);
 

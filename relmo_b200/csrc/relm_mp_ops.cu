@@ -279,6 +279,40 @@ bool valid_dtype(relm_mp_dtype d)
    return d == RELM_MP_FLOAT32 || d == RELM_MP_FLOAT64 || d == RELM_MP_BFLOAT16 || d == RELM_MP_FLOAT16;
 }
 
+// The plain logsumexp of fanin_reduce mode 1.
+void set_plain_lse(SegParams& p)
+{
+   p.lse_k = kLog2E;
+   p.lse_eps = 0.0;
+   p.lse_inv_beta = 1.0;
+   p.lse_empty = -INFINITY;
+}
+
+// Value of a row without messages in the smoothed form, (1/beta) log(eps),
+// evaluated in the accumulator type as the reference does it in the tensor's
+// (fp32 for fp32 / bf16 / fp16 tables).
+double smoothed_empty(relm_mp_dtype dtype, const relm_mp_lse_form& f)
+{
+   if(dtype == RELM_MP_FLOAT64) return (1.0 / f.beta) * log(f.eps);
+   const float inv = 1.0f / (float)f.beta;
+   return (double)(inv * logf((float)f.eps));
+}
+
+// The smoothed logsumexp (relmo's LogSumExpAggregation), or the plain one
+// for a NULL form.
+int set_lse_form(SegParams& p, relm_mp_dtype dtype, const relm_mp_lse_form* f)
+{
+   set_plain_lse(p);
+   if(!f) return RELM_MP_OK;
+   if(!(f->beta > 0.0) || !(f->eps >= 0.0) || !isfinite(f->beta))
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "logsumexp form needs beta > 0 and eps >= 0.");
+   p.lse_k = f->beta * kLog2E;
+   p.lse_eps = f->eps;
+   p.lse_inv_beta = dtype == RELM_MP_FLOAT64 ? 1.0 / f->beta : (double)(1.0f / (float)f->beta);
+   p.lse_empty = smoothed_empty(dtype, *f);
+   return RELM_MP_OK;
+}
+
 SegParams base_params(const relm_mp_plan* plan, int64_t emb, const Shape& s)
 {
    SegParams p{};
@@ -296,6 +330,7 @@ SegParams base_params(const relm_mp_plan* plan, int64_t emb, const Shape& s)
    p.ch = s.ch;
    p.col_blocks = s.col_blocks;
    p.block_cols = s.block_cols;
+   set_plain_lse(p);
    return p;
 }
 
@@ -358,7 +393,8 @@ struct SumEpilogue {
 // Planned reduction shared by relm_mp_plan_reduce / relm_mp_plan_logsumexp_backward.
 int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, const void* table,
                    const void* table2, const void* own, int64_t emb, void* out, void* scratch,
-                   size_t scratch_bytes, cudaStream_t stream, const SumEpilogue& epi = SumEpilogue())
+                   size_t scratch_bytes, cudaStream_t stream, const SumEpilogue& epi = SumEpilogue(),
+                   const relm_mp_lse_form* form = nullptr)
 {
    if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
    if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
@@ -377,12 +413,16 @@ int planned_reduce(const relm_mp_plan* plan, relm_mp_dtype dtype, int seg_mode, 
             "epilogue base copy"
          );
       }
-      return fill_rows(dtype, out, plan->num_rows * emb, seg_mode == kLse, stream);
+      if(seg_mode != kLse) return fill_rows(dtype, out, plan->num_rows * emb, false, stream);
+      SegParams f{};
+      if(const int rc = set_lse_form(f, dtype, form)) return rc;
+      return fill_value(dtype, out, plan->num_rows * emb, f.lse_empty, stream);
    }
    const void* ptrs[5] = {table, table2, own, out, epi.base};
    const Shape s = choose_map_shape(emb, (int)es, ptrs, 5);
    const Shape sr = choose_reduce_shape(emb, (int)es, ptrs, 5);
    SegParams p = base_params(plan, emb, s);
+   if(const int rc = set_lse_form(p, dtype, form)) return rc;
    p.table = table;
    p.table2 = table2;
    p.own = own;
@@ -469,14 +509,29 @@ int fill_rows(relm_mp_dtype dtype, void* out, int64_t count, bool neg_inf, cudaS
 {
    if(count <= 0) return RELM_MP_OK;
    if(!neg_inf) return check_cuda(cudaMemsetAsync(out, 0, (size_t)count * dtype_size(dtype), stream), "zero fill");
+   return fill_value(dtype, out, count, -INFINITY, stream);
+}
+
+int fill_value(relm_mp_dtype dtype, void* out, int64_t count, double value, cudaStream_t stream)
+{
+   if(count <= 0) return RELM_MP_OK;
    int64_t blocks = (count + kThreads - 1) / kThreads;
    if(blocks > 148 * 32) blocks = 148 * 32;
    switch(dtype) {
-      case RELM_MP_FLOAT32: k_fill_f32<<< (unsigned)blocks, kThreads, 0, stream >>>((float*)out, count, -INFINITY); break;
-      case RELM_MP_FLOAT64: k_fill_f64<<< (unsigned)blocks, kThreads, 0, stream >>>((double*)out, count, -INFINITY); break;
-      // -inf bit patterns: bf16 0xff80, fp16 0xfc00
-      case RELM_MP_BFLOAT16: k_fill_u16<<< (unsigned)blocks, kThreads, 0, stream >>>((unsigned short*)out, count, 0xff80); break;
-      case RELM_MP_FLOAT16: k_fill_u16<<< (unsigned)blocks, kThreads, 0, stream >>>((unsigned short*)out, count, 0xfc00); break;
+      case RELM_MP_FLOAT32: k_fill_f32<<< (unsigned)blocks, kThreads, 0, stream >>>((float*)out, count, (float)value); break;
+      case RELM_MP_FLOAT64: k_fill_f64<<< (unsigned)blocks, kThreads, 0, stream >>>((double*)out, count, value); break;
+      case RELM_MP_BFLOAT16: {
+         const __nv_bfloat16 h = __float2bfloat16_rn((float)value);
+         k_fill_u16<<< (unsigned)blocks, kThreads, 0, stream >>>((unsigned short*)out, count,
+                                                                   *reinterpret_cast< const unsigned short* >(&h));
+         break;
+      }
+      case RELM_MP_FLOAT16: {
+         const __half h = __float2half_rn((float)value);
+         k_fill_u16<<< (unsigned)blocks, kThreads, 0, stream >>>((unsigned short*)out, count,
+                                                                   *reinterpret_cast< const unsigned short* >(&h));
+         break;
+      }
    }
    return check_launch("fill");
 }
@@ -694,6 +749,15 @@ int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dt
                                             const void* lse_out, const void* rel, int64_t emb, const uint32_t* cover,
                                             void* grad_rel, void* stream)
 {
+   return relm_mp_plan_scatter_logsumexp_backward_ex(plan, dtype, nullptr, grad_out, lse_out, rel, emb, cover,
+                                                     grad_rel, stream);
+}
+
+int relm_mp_plan_scatter_logsumexp_backward_ex(const relm_mp_plan* plan, relm_mp_dtype dtype,
+                                               const relm_mp_lse_form* form, const void* grad_out,
+                                               const void* lse_out, const void* rel, int64_t emb,
+                                               const uint32_t* cover, void* grad_rel, void* stream)
+{
    if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
    if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
    if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
@@ -706,6 +770,7 @@ int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dt
       return fail(RELM_MP_ERR_UNSUPPORTED, "destination-ordered logsumexp backward needs rows of 16..256 bytes "
                                            "(a power of two times 16) with 16-byte aligned tables.");
    SegParams p = base_params(plan, emb, s);
+   if(const int rc = set_lse_form(p, dtype, form)) return rc;
    p.table = grad_out;
    p.table2 = lse_out;
    p.own = rel;
@@ -762,6 +827,26 @@ int relm_mp_plan_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtyp
    return planned_reduce(
       plan, dtype, kLseBwd, grad_out, lse_out, rel, emb, grad_rel, scratch, scratch_bytes,
       static_cast< cudaStream_t >(stream)
+   );
+}
+
+int relm_mp_plan_reduce_lse(const relm_mp_plan* plan, relm_mp_dtype dtype, const relm_mp_lse_form* form,
+                            const void* table, int64_t emb, void* out, void* scratch, size_t scratch_bytes,
+                            void* stream)
+{
+   return planned_reduce(
+      plan, dtype, kLse, table, nullptr, nullptr, emb, out, scratch, scratch_bytes,
+      static_cast< cudaStream_t >(stream), SumEpilogue(), form
+   );
+}
+
+int relm_mp_plan_logsumexp_backward_ex(const relm_mp_plan* plan, relm_mp_dtype dtype, const relm_mp_lse_form* form,
+                                       const void* grad_out, const void* lse_out, const void* rel, int64_t emb,
+                                       void* grad_rel, void* scratch, size_t scratch_bytes, void* stream)
+{
+   return planned_reduce(
+      plan, dtype, kLseBwd, grad_out, lse_out, rel, emb, grad_rel, scratch, scratch_bytes,
+      static_cast< cudaStream_t >(stream), SumEpilogue(), form
    );
 }
 

@@ -126,10 +126,27 @@ __device__ __forceinline__ float exp2_fast(float x)
    return r;
 }
 __device__ __forceinline__ double exp2_fast(double x) { return exp2(x); }
-__device__ __forceinline__ float exp_acc(float v) { return exp2_fast(v * (float)kLog2E); }
-__device__ __forceinline__ double exp_acc(double v) { return exp2_fast(v * kLog2E); }
+// e^(beta * v) = 2^(v * k) with k = beta * log2(e) (LseForm::k).
+__device__ __forceinline__ float exp_k(float v, float k) { return exp2_fast(v * k); }
+__device__ __forceinline__ double exp_k(double v, double k) { return exp2_fast(v * k); }
 __device__ __forceinline__ float log_acc(float v) { return logf(v); }
 __device__ __forceinline__ double log_acc(double v) { return log(v); }
+
+// The two logsumexp forms the kernels compute, as runtime constants:
+//   plain    (fanin_reduce mode 1): m + log(sum e^(x - m)); k = log2(e),
+//            eps = 0, inv_beta = 1, rows without values -inf;
+//   smoothed (relmo's LogSumExpAggregation, models/aggr.py:103-123):
+//            m + (1/beta) log(eps + sum e^(beta (x - m))); k = beta log2(e),
+//            rows without values (1/beta) log(eps).
+// The running maximum m stays in the units of x, so the smoothed form costs
+// no instruction more than the plain one in the folds.
+template < typename A >
+struct LseForm {
+   A k;
+   A eps;
+   A inv_beta;
+   A empty;
+};
 
 // Running log-sum-exp (m, s), value = m + log(s):
 //   m  running maximum, NaN as soon as a NaN was seen
@@ -140,14 +157,14 @@ __device__ __forceinline__ double log_acc(double v) { return log(v); }
 // reference's exp(-inf - (-inf))). A block of -inf values inside a row with
 // finite values therefore merges as the zero contribution it is.
 template < typename A >
-__device__ __forceinline__ A lse_value(A m, A s)
+__device__ __forceinline__ A lse_value(A m, A s, const LseForm< A >& f)
 {
-   if(m == -(A)INFINITY && s == A(0)) return signbit(s) ? (A)NAN : -(A)INFINITY;
-   return log_acc(s) + m;
+   if(m == -(A)INFINITY && s == A(0)) return signbit(s) ? (A)NAN : f.empty;
+   return log_acc(s + f.eps) * f.inv_beta + m;  // plain: log(s) + m exactly
 }
 
 template < typename A >
-__device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2)
+__device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2, A k)
 {
    if(m2 == -(A)INFINITY && s2 == A(0)) {
       if(signbit(s2) && m == -(A)INFINITY && s == A(0)) s = -A(0);
@@ -159,14 +176,14 @@ __device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2)
       return;
    }
    const A mn = nanmax(m, m2);
-   s = s * exp_acc(m - mn) + s2 * exp_acc(m2 - mn);
+   s = s * exp_k(m - mn, k) + s2 * exp_k(m2 - mn, k);
    m = mn;
 }
 
 // Folds n <= N values into (m, s): one max pass, one rescale of s and one
 // exponential per value, all as selects (no divergence between lanes).
 template < typename A, int N >
-__device__ __forceinline__ void lse_fold(A& m, A& s, const A (&v)[N], int n)
+__device__ __forceinline__ void lse_fold(A& m, A& s, const A (&v)[N], int n, A k)
 {
    A mr = m;
 #pragma unroll
@@ -174,20 +191,20 @@ __device__ __forceinline__ void lse_fold(A& m, A& s, const A (&v)[N], int n)
       if(i < n) mr = nanmax(mr, v[i]);
    // (x - mr) is exact for the maximum itself, so a row's largest value
    // contributes exactly 1 and a single-value row returns that value.
-   A t = s * exp_acc(m - mr);
+   A t = s * exp_k(m - mr, k);
 #pragma unroll
    for(int i = 0; i < N; ++i)
-      if(i < n) t += exp_acc(v[i] - mr);
+      if(i < n) t += exp_k(v[i] - mr, k);
    const bool only_ninf = mr == -(A)INFINITY;  // every value so far is -inf
    s = only_ninf ? ((n > 0) ? -fabs(s) : s) : t;
    m = mr;
 }
 
 template < typename A >
-__device__ __forceinline__ void lse_push(A& m, A& s, A v)
+__device__ __forceinline__ void lse_push(A& m, A& s, A v, A k)
 {
    const A one[1] = {v};
-   lse_fold< A, 1 >(m, s, one, 1);
+   lse_fold< A, 1 >(m, s, one, 1, k);
 }
 
 struct SegParams {
@@ -231,7 +248,19 @@ struct SegParams {
    const void* epi_base;
    const int64_t* epi_div;
    int epi_count;
+   // logsumexp form (LseForm; the host sets the plain one unless asked for the
+   // smoothed one): exponent scale, epsilon, 1 / beta, value of empty rows
+   double lse_k;
+   double lse_eps;
+   double lse_inv_beta;
+   double lse_empty;
 };
+
+template < typename A >
+__device__ __forceinline__ LseForm< A > lse_form(const SegParams& p)
+{
+   return LseForm< A >{(A)p.lse_k, (A)p.lse_eps, (A)p.lse_inv_beta, (A)p.lse_empty};
+}
 
 // The merge-path kernels (and their fixups) serve the plan: some row holds
 // more than one edge, and some row is long or k_seg_rows_packed was not launched.
@@ -350,6 +379,7 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
    T* out = static_cast< T* >(p.out);
    const int64_t groups = (p.num_rows + 31) / 32;
    const A ninf = -(A)INFINITY;
+   const LseForm< A > LF = lse_form< A >(p);
 
    int64_t g = warp;
    int32_t src_cur = row_source< MODE == kCopyLast >(p, g, groups, lane);
@@ -389,18 +419,18 @@ __global__ void __launch_bounds__(kThreads) k_row_map(SegParams p)
 #pragma unroll
                   for(int k = 0; k < VN; ++k) {
                      if(src[u] < 0) {
-                        res[k] = (MODE == kLse) ? ninf : A(0);
+                        res[k] = (MODE == kLse) ? LF.empty : A(0);
                      } else if(MODE == kCopyLast) {
                         res[k] = v[u][c][k];
                      } else if(sum_mode(MODE)) {
                         res[k] = A(0) + v[u][c][k];
                      } else if(MODE == kLse) {
                         A m = ninf, sacc = A(0);
-                        lse_push(m, sacc, v[u][c][k]);
-                        res[k] = lse_value(m, sacc);
+                        lse_push(m, sacc, v[u][c][k], LF.k);
+                        res[k] = lse_value(m, sacc, LF);
                      } else {
                         const int ui = (MODE == kLseBwd) ? u : 0;
-                        res[k] = A(0) + v[u][c][k] * exp_acc(o[ui][c][k] - w[ui][c][k]);
+                        res[k] = A(0) + v[u][c][k] * exp_k(o[ui][c][k] - w[ui][c][k], LF.k);
                      }
                   }
                   if(MODE == kSumEpi) epi_apply< T, VN >(p, r0 + base + u, cols.col[c], res);
@@ -462,6 +492,7 @@ __global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) 
    T* out = static_cast< T* >(p.out);
    const int64_t groups = (p.num_rows + 31) / 32;
    const A ninf = -(A)INFINITY;
+   const LseForm< A > LF = lse_form< A >(p);
 
    int64_t g = warp;
    int32_t src_cur = row_source< MODE == kCopyLast >(p, g, groups, lane);
@@ -518,17 +549,17 @@ __global__ void __launch_bounds__(kThreads, ((MODE == kLseBwd && sizeof(T) > 2) 
 #pragma unroll
             for(int k = 0; k < VN; ++k) {
                if(src[u] < 0) {
-                  res[k] = (MODE == kLse) ? ninf : A(0);
+                  res[k] = (MODE == kLse) ? LF.empty : A(0);
                } else if(MODE == kCopyLast) {
                   res[k] = to_acc(ev[k]);
                } else if(sum_mode(MODE)) {
                   res[k] = A(0) + to_acc(ev[k]);
                } else if(MODE == kLse) {
                   A m = ninf, sacc = A(0);
-                  lse_push(m, sacc, to_acc(ev[k]));
-                  res[k] = lse_value(m, sacc);
+                  lse_push(m, sacc, to_acc(ev[k]), LF.k);
+                  res[k] = lse_value(m, sacc, LF);
                } else {
-                  res[k] = A(0) + to_acc(ev[k]) * exp_acc(to_acc(eo[k]) - to_acc(ew[k]));
+                  res[k] = A(0) + to_acc(ev[k]) * exp_k(to_acc(eo[k]) - to_acc(ew[k]), LF.k);
                }
             }
             if(MODE == kSumEpi) {
@@ -575,6 +606,7 @@ __global__ void __launch_bounds__(kThreads) k_seg_rows_packed(SegParams p)
    const T* own = static_cast< const T* >(p.own);
    T* out = static_cast< T* >(p.out);
    const A ninf = -(A)INFINITY;
+   const LseForm< A > LF = lse_form< A >(p);
    for(int64_t r = warp * RPI + sub; r < p.num_rows; r += nwarps * RPI) {
       const int e0 = __ldg(p.row_ptr + r);
       const int e1 = __ldg(p.row_ptr + r + 1);
@@ -620,13 +652,13 @@ __global__ void __launch_bounds__(kThreads) k_seg_rows_packed(SegParams p)
                for(int i = 0; i < kSrU; ++i)
                   if(i < n) acc[k] += x[i];
             } else if(MODE == kLse) {
-               lse_fold< A, kSrU >(acc[k], aux[k], x, n);
+               lse_fold< A, kSrU >(acc[k], aux[k], x, n, LF.k);
             } else {
                const A o = to_acc(reinterpret_cast< const T* >(&side)[k]);
 #pragma unroll
                for(int i = 0; i < kSrU; ++i)
                   if(i < n)
-                     acc[k] += x[i] * exp_acc(o - to_acc(reinterpret_cast< const T* >(&w[i % (NT == 2 ? kSrU : 1)])[k]));
+                     acc[k] += x[i] * exp_k(o - to_acc(reinterpret_cast< const T* >(&w[i % (NT == 2 ? kSrU : 1)])[k]), LF.k);
             }
          }
       }
@@ -634,7 +666,7 @@ __global__ void __launch_bounds__(kThreads) k_seg_rows_packed(SegParams p)
       T* er = reinterpret_cast< T* >(&res);
 #pragma unroll
       for(int k = 0; k < VN; ++k) {
-         A f = (MODE == kLse) ? lse_value(acc[k], aux[k]) : acc[k];
+         A f = (MODE == kLse) ? lse_value(acc[k], aux[k], LF) : acc[k];
          if(MODE == kSumEpi) {
             if(dv != A(1)) f = f / dv;
             if(p.epi_base) f += to_acc(reinterpret_cast< const T* >(&side)[k]);
@@ -867,6 +899,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_lse_bwd_packed(SegParams p
    const T* lse = static_cast< const T* >(p.table2);   // forward output, by destination row
    const T* rel = static_cast< const T* >(p.own);      // messages, by message row
    T* out = static_cast< T* >(p.out);                  // grad_rel, by message row
+   const A lse_k = (A)p.lse_k;
    int gbase = j_begin, gcount = 0;
    int rbase = r_begin, rcount = 0;
    auto row_end = [&](int R) __attribute__((always_inline)) -> int {
@@ -931,7 +964,7 @@ __global__ void __launch_bounds__(kThreads) k_scatter_lse_bwd_packed(SegParams p
             T* er = reinterpret_cast< T* >(&r);
 #pragma unroll
             for(int k = 0; k < VN; ++k)
-               er[k] = from_acc< T >(A(0) + to_acc(eg[k]) * exp_acc(to_acc(ev[k]) - to_acc(eo[k])));
+               er[k] = from_acc< T >(A(0) + to_acc(eg[k]) * exp_k(to_acc(ev[k]) - to_acc(eo[k]), lse_k));
             *reinterpret_cast< uint4* >(out + m[h] * p.emb + col) = r;
          }
       }
@@ -1003,6 +1036,7 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
    const int G = 32 / L;
    const int grp = lane / L;
    const int sub = lane % L;
+   const LseForm< A > LF = lse_form< A >(p);
    int32_t* sg = s_gidx[wib];
    int32_t* sr = s_rend[wib];
    const int r_begin = p.tile_row[tile];
@@ -1065,7 +1099,7 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
                   const A om = __shfl_xor_sync(0xffffffffu, acc[c][k], off);
                   if(MODE == kLse) {
                      const A os = __shfl_xor_sync(0xffffffffu, aux[c][k], off);
-                     lse_merge(acc[c][k], aux[c][k], om, os);
+                     lse_merge(acc[c][k], aux[c][k], om, os, LF.k);
                   } else {
                      acc[c][k] += om;
                   }
@@ -1091,7 +1125,7 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
                   A fin[VN];
 #pragma unroll
                   for(int k = 0; k < VN; ++k)
-                     fin[k] = (MODE == kLse) ? lse_value(acc[c][k], aux[c][k]) : acc[c][k];
+                     fin[k] = (MODE == kLse) ? lse_value(acc[c][k], aux[c][k], LF) : acc[c][k];
                   if(MODE == kSumEpi) epi_apply< T, VN >(p, R, col[c], fin);
                   store_vec< T, VB >(out + (int64_t)R * p.emb + col[c], fin);
                }
@@ -1109,9 +1143,9 @@ __global__ void __launch_bounds__(kThreads, (value_regs< T, VB, CH >() <= 4) ? 3
                if(sum_mode(MODE))
                   acc[c][k] += val[c][k];
                else if(MODE == kLse)
-                  lse_push(acc[c][k], aux[c][k], val[c][k]);
+                  lse_push(acc[c][k], aux[c][k], val[c][k], LF.k);
                else
-                  acc[c][k] += val[c][k] * exp_acc(o2[c][k] - w2[c][k]);
+                  acc[c][k] += val[c][k] * exp_k(o2[c][k] - w2[c][k], LF.k);
             }
          }
       };
@@ -1350,6 +1384,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
    A* head_aux = static_cast< A* >(p.head_aux);
    A* tail_aux = static_cast< A* >(p.tail_aux);
    const A ninf = -(A)INFINITY;
+   const LseForm< A > LF = lse_form< A >(p);
    const int nbatches = (j_end - j_begin + B - 1) / B;
    const int chunks = CBW / 16;
    int head_row = -1;
@@ -1483,7 +1518,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
          } else {                                                                               \
             A fin_[VN];                                                                         \
             _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_) fin_[k_] =                         \
-               (MODE == kLse) ? lse_value(acc[k_], aux[k_]) : acc[k_];                          \
+               (MODE == kLse) ? lse_value(acc[k_], aux[k_], LF) : acc[k_];                      \
             if(PF) {                                                                            \
                epi_finish((R_), cnt_, fin_);                                                    \
             } else if(MODE == kSumEpi) {                                                        \
@@ -1533,7 +1568,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
                         reinterpret_cast< const T* >(src + kStreamStages * kStreamStageBytes + q * CBW), w
                      );
 #pragma unroll
-                     for(int x = 0; x < VN; ++x) acc[x] += v[x] * exp_acc(ownv[x] - w[x]);
+                     for(int x = 0; x < VN; ++x) acc[x] += v[x] * exp_k(ownv[x] - w[x], LF.k);
                   }
                } else {
                   int q = 0;
@@ -1548,7 +1583,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
                            acc[x] += v[0][x] + v[1][x] + v[2][x] + v[3][x];
                         } else {
                            const A vx[4] = {v[0][x], v[1][x], v[2][x], v[3][x]};
-                           lse_fold< A, 4 >(acc[x], aux[x], vx, 4);
+                           lse_fold< A, 4 >(acc[x], aux[x], vx, 4, LF.k);
                         }
                      }
                   }
@@ -1570,7 +1605,7 @@ __global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
                            acc[x] += v[0][x] + v[1][x] + v[2][x];
                         } else {
                            const A vx[3] = {v[0][x], v[1][x], v[2][x]};
-                           lse_fold< A, 3 >(acc[x], aux[x], vx, rem);
+                           lse_fold< A, 3 >(acc[x], aux[x], vx, rem, LF.k);
                         }
                      }
                   }
@@ -1617,6 +1652,7 @@ __device__ __forceinline__ void fixup_combine(const SegParams& p, int64_t t_firs
    using A = typename AccOf< T >::type;
    const A* tail_val = static_cast< const A* >(p.tail_val);
    const A* tail_aux = static_cast< const A* >(p.tail_aux);
+   const A k = (A)p.lse_k;
    int64_t u = t_first;
    for(; u + F <= t_last; u += F) {
       A a[F], b[F];
@@ -1628,7 +1664,7 @@ __device__ __forceinline__ void fixup_combine(const SegParams& p, int64_t t_firs
 #pragma unroll
       for(int i = 0; i < F; ++i) {
          if(MODE == kLse)
-            lse_merge(m, s, a[i], b[i]);
+            lse_merge(m, s, a[i], b[i], k);
          else
             m += a[i];
       }
@@ -1636,7 +1672,7 @@ __device__ __forceinline__ void fixup_combine(const SegParams& p, int64_t t_firs
    for(; u < t_last; ++u) {
       const int64_t off = u * p.emb + col;
       if(MODE == kLse)
-         lse_merge(m, s, tail_val[off], tail_aux[off]);
+         lse_merge(m, s, tail_val[off], tail_aux[off], k);
       else
          m += tail_val[off];
    }
@@ -1652,8 +1688,9 @@ __device__ __forceinline__ void fixup_finish(const SegParams& p, int64_t R, int6
    const int64_t off = t * p.emb + col;
    A res;
    if(MODE == kLse) {
-      lse_merge(m, s, head_val[off], head_aux[off]);
-      res = lse_value(m, s);
+      const LseForm< A > LF = lse_form< A >(p);
+      lse_merge(m, s, head_val[off], head_aux[off], LF.k);
+      res = lse_value(m, s, LF);
    } else {
       res = m + head_val[off];
       if(MODE == kSumEpi) {
@@ -1731,7 +1768,7 @@ __global__ void __launch_bounds__(kLongThreads) k_fixup_long(SegParams p)
          A ss = sm_s[0][lane];
          for(int w = 1; w < W; ++w) {
             if(MODE == kLse)
-               lse_merge(mm, ss, sm_m[w][lane], sm_s[w][lane]);
+               lse_merge(mm, ss, sm_m[w][lane], sm_s[w][lane], (A)p.lse_k);
             else
                mm += sm_m[w][lane];
          }

@@ -29,6 +29,7 @@
 #include <c10/util/intrusive_ptr.h>
 #include <torch/library.h>
 
+#include <cmath>
 #include <cstdint>
 #include <limits>
 #include <list>
@@ -380,14 +381,14 @@ Tensor fanout_scatter_cuda(const Tensor& x_cat, const Tensor& src_global_idx, co
 }
 
 Tensor planned_sum(const relm_mp_plan& plan, relm_mp_dtype dt, const Tensor& table, int64_t emb, Tensor& out,
-                   int mode, const char* op)
+                   int mode, const char* op, const relm_mp_lse_form* form = nullptr)
 {
    Tensor scratch = byte_buffer(relm_mp_plan_reduce_scratch_bytes(&plan, emb, dt, mode), table);
-   check_status(
-      relm_mp_plan_reduce(&plan, dt, mode, table.data_ptr(), emb, out.data_ptr(), scratch.data_ptr(),
-                          (size_t)scratch.numel(), stream_of(table)),
-      op
-   );
+   const int rc = form ? relm_mp_plan_reduce_lse(&plan, dt, form, table.data_ptr(), emb, out.data_ptr(),
+                                                 scratch.data_ptr(), (size_t)scratch.numel(), stream_of(table))
+                       : relm_mp_plan_reduce(&plan, dt, mode, table.data_ptr(), emb, out.data_ptr(),
+                                             scratch.data_ptr(), (size_t)scratch.numel(), stream_of(table));
+   check_status(rc, op);
    return out;
 }
 
@@ -415,9 +416,28 @@ Tensor fanout_scatter_backward_cuda(const Tensor& grad_out, const Tensor& src_gl
    return planned_sum(plan, dt, g, emb, grad_x, RELM_MP_MODE_SUM, "fanout_scatter_backward");
 }
 
+// Value of rows without messages: 0 (sum), -inf (plain logsumexp) or
+// (1/beta) log(eps) (smoothed; computed in the accumulator type).
+double empty_row_value(int64_t mode, const relm_mp_lse_form* form, const Tensor& like)
+{
+   if(mode == kModeSum) return 0.0;
+   if(!form) return -std::numeric_limits< double >::infinity();
+   if(like.scalar_type() == at::kDouble) return (1.0 / form->beta) * std::log(form->eps);
+   return (double)((1.0f / (float)form->beta) * std::log((float)form->eps));
+}
+
+Tensor fanin_reduce_cuda_impl(const Tensor& rel_flat, const Tensor& flat_src, const Tensor& dst_idx, int64_t dim_size,
+                              int64_t mode, const relm_mp_lse_form* form);
+
 // mp_ops.cpp:3327-3348 with 3168-3222 (sum) and 3005-3036 (logsumexp)
 Tensor fanin_reduce_cuda(const Tensor& rel_flat, const Tensor& flat_src, const Tensor& dst_idx, int64_t dim_size,
                          int64_t mode)
+{
+   return fanin_reduce_cuda_impl(rel_flat, flat_src, dst_idx, dim_size, mode, nullptr);
+}
+
+Tensor fanin_reduce_cuda_impl(const Tensor& rel_flat, const Tensor& flat_src, const Tensor& dst_idx, int64_t dim_size,
+                              int64_t mode, const relm_mp_lse_form* form)
 {
    check_rank(rel_flat, 2, "rel_flat");
    check_int64_index(flat_src, "flat_src");
@@ -433,7 +453,7 @@ Tensor fanin_reduce_cuda(const Tensor& rel_flat, const Tensor& flat_src, const T
    const int64_t emb = rel_flat.size(1);
    if(flat_src.numel() == 0 || dim_size == 0) {
       if(mode == kModeSum) return at::zeros({dim_size, emb}, rel_flat.options());
-      return at::full({dim_size, emb}, -std::numeric_limits< double >::infinity(), rel_flat.options());
+      return at::full({dim_size, emb}, empty_row_value(mode, form, rel_flat), rel_flat.options());
    }
    Tensor out = at::empty({dim_size, emb}, rel_flat.options());
    const Tensor rel = contig(rel_flat);
@@ -441,7 +461,7 @@ Tensor fanin_reduce_cuda(const Tensor& rel_flat, const Tensor& flat_src, const T
    const Tensor dst = contig(dst_idx);
    Tensor keep;
    const relm_mp_plan plan = get_plan(dst, src, dim_size, dim_size, rel.size(0), "dst_idx", "flat_src", true, &keep);
-   return planned_sum(plan, dt, rel, emb, out, (int)mode, "fanin_reduce");
+   return planned_sum(plan, dt, rel, emb, out, (int)mode, "fanin_reduce", mode == kModeLogSumExp ? form : nullptr);
 }
 
 // mp_ops.cpp:3224-3284
@@ -488,9 +508,20 @@ Tensor fanin_reduce_sum_backward_cuda(const Tensor& grad_out, const Tensor& flat
    return planned_sum(plan, dt, g, emb, grad_rel, RELM_MP_MODE_SUM, "fanin_reduce_sum_backward");
 }
 
+Tensor lse_backward_cuda_impl(const Tensor& grad_out, const Tensor& rel_flat, const Tensor& flat_src,
+                              const Tensor& dst_idx, const Tensor& out, int64_t rel_rows,
+                              const relm_mp_lse_form* form);
+
 // mp_ops.cpp:3286-3325
 Tensor fanin_reduce_logsumexp_backward_cuda(const Tensor& grad_out, const Tensor& rel_flat, const Tensor& flat_src,
                                             const Tensor& dst_idx, const Tensor& out, int64_t rel_rows)
+{
+   return lse_backward_cuda_impl(grad_out, rel_flat, flat_src, dst_idx, out, rel_rows, nullptr);
+}
+
+Tensor lse_backward_cuda_impl(const Tensor& grad_out, const Tensor& rel_flat, const Tensor& flat_src,
+                              const Tensor& dst_idx, const Tensor& out, int64_t rel_rows,
+                              const relm_mp_lse_form* form)
 {
    check_rank(grad_out, 2, "grad_out");
    check_rank(rel_flat, 2, "rel_flat");
@@ -530,9 +561,9 @@ Tensor fanin_reduce_logsumexp_backward_cuda(const Tensor& grad_out, const Tensor
          if(cache.nonempty_rows(fp, g) * row_bytes > kScatterWorkingSet) {
             cache.ensure_cover(fp, g);
             if(fp->cover_dups == 0) {
-               const int rc = relm_mp_plan_scatter_logsumexp_backward(
-                  &fp->plan, dt, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb, cover_bits(fp), grad_rel.data_ptr(),
-                  stream_of(g)
+               const int rc = relm_mp_plan_scatter_logsumexp_backward_ex(
+                  &fp->plan, dt, form, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb, cover_bits(fp),
+                  grad_rel.data_ptr(), stream_of(g)
                );
                if(rc != RELM_MP_ERR_UNSUPPORTED) {  // unsupported row shape: the per-message-row path below
                   check_status(rc, "fanin_reduce_logsumexp_backward");
@@ -547,11 +578,53 @@ Tensor fanin_reduce_logsumexp_backward_cuda(const Tensor& grad_out, const Tensor
    const relm_mp_plan plan = get_plan(src, dst, rel_rows, bound, g.size(0), "flat_src", "dst_idx", false, &keep);
    Tensor scratch = byte_buffer(relm_mp_plan_reduce_scratch_bytes(&plan, emb, dt, RELM_MP_MODE_LOGSUMEXP_BACKWARD), g);
    check_status(
-      relm_mp_plan_logsumexp_backward(&plan, dt, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb,
-                                      grad_rel.data_ptr(), scratch.data_ptr(), (size_t)scratch.numel(), stream_of(g)),
+      relm_mp_plan_logsumexp_backward_ex(&plan, dt, form, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb,
+                                         grad_rel.data_ptr(), scratch.data_ptr(), (size_t)scratch.numel(),
+                                         stream_of(g)),
       "fanin_reduce_logsumexp_backward"
    );
    return grad_rel;
+}
+
+// ---- smoothed logsumexp (relmo's LogSumExpAggregation, models/aggr.py:96-123) ------------
+//
+// The aggregation relmo's models use for "logsumexp": per column,
+// m + (1/beta) log(eps + sum e^(beta (x - m))) with m the row max (no gradient
+// through it), (1/beta) log(eps) for rows without messages. Same arguments
+// and checks as fanin_reduce / fanin_reduce_logsumexp_backward, plus beta and
+// eps; the backward weight is e^(beta (x - out)). Not part of the reference's
+// op library (relmo computes it with ATen around index_reduce_).
+
+relm_mp_lse_form smoothed_form(double beta, double eps)
+{
+   TORCH_CHECK(beta > 0.0 && std::isfinite(beta), "smoothed logsumexp needs a finite beta > 0.");
+   TORCH_CHECK(eps >= 0.0, "smoothed logsumexp needs eps >= 0.");
+   return relm_mp_lse_form{beta, eps};
+}
+
+Tensor smoothed_logsumexp_cuda(const Tensor& rel_flat, const Tensor& flat_src, const Tensor& dst_idx, int64_t dim_size,
+                               double beta, double eps)
+{
+   const relm_mp_lse_form f = smoothed_form(beta, eps);
+   return fanin_reduce_cuda_impl(rel_flat, flat_src, dst_idx, dim_size, kModeLogSumExp, &f);
+}
+
+Tensor smoothed_logsumexp_backward_cuda(const Tensor& grad_out, const Tensor& rel_flat, const Tensor& flat_src,
+                                        const Tensor& dst_idx, const Tensor& out, int64_t rel_rows, double beta)
+{
+   const relm_mp_lse_form f = smoothed_form(beta, 0.0);
+   return lse_backward_cuda_impl(grad_out, rel_flat, flat_src, dst_idx, out, rel_rows, &f);
+}
+
+Tensor smoothed_logsumexp_meta(const Tensor& rel_flat, const Tensor&, const Tensor&, int64_t dim_size, double, double)
+{
+   return at::empty({dim_size, rel_flat.size(1)}, rel_flat.options());
+}
+
+Tensor smoothed_logsumexp_backward_meta(const Tensor&, const Tensor& rel_flat, const Tensor&, const Tensor&,
+                                        const Tensor&, int64_t rel_rows, double)
+{
+   return at::empty({rel_rows, rel_flat.size(1)}, rel_flat.options());
 }
 
 // ---- Meta (shape) kernels ------------------------------------------------------
@@ -624,34 +697,65 @@ Tensor pack_index(const std::vector< Tensor >& parts, const std::vector< int64_t
    return out;
 }
 
+// The argument checks of the pack ops follow the reference's order and
+// messages (mp_ops.cpp:412-570, 2511-2773): callers match on them.
+
+// Rank, device, dtype and embedding dim of every value part (`vname` is
+// "x_parts" or "rel_parts").
+void check_value_parts(const std::vector< Tensor >& parts, const char* op, const char* vname)
+{
+   const std::string first = std::string(vname) + "[0]";
+   const std::string each = std::string(vname) + "[i]";
+   check_rank(parts[0], 2, first.c_str());
+   for(size_t i = 0; i < parts.size(); ++i) {
+      const Tensor& v = parts[i];
+      check_rank(v, 2, each.c_str());
+      TORCH_CHECK(v.device() == parts[0].device(), op, " expects all ", vname, " on the same device. Mismatch at part ",
+                  i, ".");
+      TORCH_CHECK(v.scalar_type() == parts[0].scalar_type(), op, " expects all ", vname,
+                  " with the same dtype. Mismatch at part ", i, ".");
+      TORCH_CHECK(v.size(1) == parts[0].size(1), op, " expects matching embedding dim across ", vname, ". Part ", i,
+                  " has emb=", v.size(1), ", expected ", parts[0].size(1), ".");
+   }
+}
+
+// fanout_pack_multi / fanin_pack_multi (mp_ops.cpp:412-570): the value parts
+// concatenated, the first index of part k offset by the rows of parts < k,
+// the second index concatenated.
 std::tuple< Tensor, Tensor, Tensor > pack_multi(const std::vector< Tensor >& value_parts,
                                                 const std::vector< Tensor >& first_idx_parts,
                                                 const std::vector< Tensor >& second_idx_parts, const char* op,
-                                                const char* what, const char* first_name, const char* second_name)
+                                                const char* what, const char* vname, const char* first_name,
+                                                const char* second_name)
 {
    TORCH_CHECK(!value_parts.empty(), op, " requires at least one ", what, ".");
-   TORCH_CHECK(
-      value_parts.size() == first_idx_parts.size() && value_parts.size() == second_idx_parts.size(), op,
-      " expects matching sequence lengths."
-   );
+   TORCH_CHECK(value_parts.size() == first_idx_parts.size() && value_parts.size() == second_idx_parts.size(), op,
+               " expects ", vname, ", ", first_name, "_parts, and ", second_name, "_parts with equal lengths.");
+   const std::string first_each = std::string(first_name) + "_parts[i]";
+   const std::string second_each = std::string(second_name) + "_parts[i]";
+   const std::string vfirst = std::string(vname) + "[0]";
+   const std::string veach = std::string(vname) + "[i]";
+   check_rank(value_parts[0], 2, vfirst.c_str());
    std::vector< int64_t > first_add;
    int64_t offset = 0;
-   check_rank(value_parts[0], 2, what);
    for(size_t i = 0; i < value_parts.size(); ++i) {
-      check_rank(value_parts[i], 2, what);
-      TORCH_CHECK(
-         value_parts[i].device() == value_parts[0].device() && value_parts[i].scalar_type() == value_parts[0].scalar_type()
-            && value_parts[i].size(1) == value_parts[0].size(1),
-         op, " expects every ", what, " on one device with one dtype and embedding dim. Mismatch at part ", i, "."
-      );
-      check_int64_index(first_idx_parts[i], first_name);
-      check_int64_index(second_idx_parts[i], second_name);
-      TORCH_CHECK(
-         first_idx_parts[i].numel() == second_idx_parts[i].numel(), op, " expects ", first_name, " and ",
-         second_name, " lengths to match per part."
-      );
+      const Tensor& v = value_parts[i];
+      check_rank(v, 2, veach.c_str());
+      check_int64_index(first_idx_parts[i], first_each.c_str());
+      check_int64_index(second_idx_parts[i], second_each.c_str());
+      TORCH_CHECK(v.device() == value_parts[0].device(), op, " expects all ", vname,
+                  " on the same device. Mismatch at part ", i, ".");
+      TORCH_CHECK(v.scalar_type() == value_parts[0].scalar_type(), op, " expects all ", vname,
+                  " with the same dtype. Mismatch at part ", i, ".");
+      TORCH_CHECK(v.size(1) == value_parts[0].size(1), op, " expects matching embedding dim across ", vname, ". Part ",
+                  i, " has emb=", v.size(1), ", expected ", value_parts[0].size(1), ".");
+      TORCH_CHECK(first_idx_parts[i].device() == value_parts[0].device() &&
+                     second_idx_parts[i].device() == value_parts[0].device(),
+                  op, " expects all index tensors on the same device as ", vname, ".");
+      TORCH_CHECK(first_idx_parts[i].size(0) == second_idx_parts[i].size(0), op, " expects ", first_name, " and ",
+                  second_name, " lengths to match for part ", i, ".");
       first_add.push_back(offset);
-      offset += value_parts[i].size(0);
+      offset += v.size(0);
    }
    const std::vector< int64_t > ones(value_parts.size(), 1), zeros(value_parts.size(), 0);
    return {cat_or_single(value_parts), pack_index(first_idx_parts, ones, first_add, value_parts[0]),
@@ -662,16 +766,32 @@ std::tuple< Tensor, Tensor, Tensor > fanout_pack_multi(at::TensorList x_parts, a
                                                        at::TensorList flat_dst_parts)
 {
    return pack_multi(x_parts.vec(), src_idx_parts.vec(), flat_dst_parts.vec(), "fanout_pack_multi", "source tensor",
-                     "src_idx", "flat_dst");
+                     "x_parts", "src_idx", "flat_dst");
 }
 
 std::tuple< Tensor, Tensor, Tensor > fanin_pack_multi(at::TensorList rel_parts, at::TensorList flat_src_parts,
                                                       at::TensorList dst_idx_parts)
 {
    return pack_multi(rel_parts.vec(), flat_src_parts.vec(), dst_idx_parts.vec(), "fanin_pack_multi",
-                     "relation tensor", "flat_src", "dst_idx");
+                     "relation tensor", "rel_parts", "flat_src", "dst_idx");
 }
 
+// Checks of one edge part of the *_pack_from_edges ops; returns its value part.
+int64_t check_edge_part(const Tensor& src, const Tensor& dst, const Tensor& ref, size_t i, int64_t part,
+                        size_t num_values, const char* op, const char* vname, const char* part_ids)
+{
+   check_int64_index(src, "edge_src_parts[i]");
+   check_int64_index(dst, "edge_dst_parts[i]");
+   TORCH_CHECK(src.device() == ref.device() && dst.device() == ref.device(), op,
+               " expects all edge index tensors on the same device as ", vname, ".");
+   TORCH_CHECK(src.size(0) == dst.size(0), op, " expects edge src/dst lengths to match for part ", i, ".");
+   TORCH_CHECK(part >= 0 && part < (int64_t)num_values, op, " ", part_ids, "[", i, "] out of range: ", part, ".");
+   return part;
+}
+
+// fanout_pack_from_edges (mp_ops.cpp:2511-2614): edge part k gathers rows
+// src_k of value part p_k (offset by the rows before it) into slots
+// slot_offset_k + dst_k * arity_k + pos_k.
 std::tuple< Tensor, Tensor, Tensor > fanout_pack_from_edges(at::TensorList x_parts, at::TensorList edge_src_parts,
                                                             at::TensorList edge_dst_parts, at::IntArrayRef src_part_ids,
                                                             at::IntArrayRef arity_parts, at::IntArrayRef pos_parts,
@@ -680,30 +800,30 @@ std::tuple< Tensor, Tensor, Tensor > fanout_pack_from_edges(at::TensorList x_par
    const char* op = "fanout_pack_from_edges";
    TORCH_CHECK(!x_parts.empty(), op, " requires at least one source tensor.");
    const size_t n = edge_src_parts.size();
-   TORCH_CHECK(
-      edge_dst_parts.size() == n && src_part_ids.size() == n && arity_parts.size() == n && pos_parts.size() == n
-         && slot_offset_parts.size() == n,
-      op, " expects matching sequence lengths."
-   );
+   TORCH_CHECK(edge_dst_parts.size() == n, op, " expects edge_src_parts and edge_dst_parts with equal lengths.");
+   TORCH_CHECK(src_part_ids.size() == n && arity_parts.size() == n && pos_parts.size() == n &&
+                  slot_offset_parts.size() == n,
+               op, " expects metadata arrays to match number of edge parts.");
+   const std::vector< Tensor > xs = x_parts.vec();
+   check_value_parts(xs, op, "x_parts");
    std::vector< int64_t > offsets;
    int64_t offset = 0;
-   for(const auto& x : x_parts) {
-      check_rank(x, 2, "source tensor");
+   for(const auto& x : xs) {
       offsets.push_back(offset);
       offset += x.size(0);
    }
+   const Tensor x_cat = cat_or_single(xs);
+   if(n == 0) return {x_cat, empty_index_like(xs[0]), empty_index_like(xs[0])};
    std::vector< Tensor > srcs, dsts;
    std::vector< int64_t > src_mul, src_add, dst_mul, dst_add;
    for(size_t i = 0; i < n; ++i) {
-      check_int64_index(edge_src_parts[i], "edge_src");
-      check_int64_index(edge_dst_parts[i], "edge_dst");
-      TORCH_CHECK(edge_src_parts[i].numel() == edge_dst_parts[i].numel(), op, " expects edge src/dst lengths to match.");
-      const int64_t part = src_part_ids[i];
-      TORCH_CHECK(part >= 0 && part < (int64_t)x_parts.size(), op, " src_part_ids out of range: ", part, ".");
+      const int64_t part = check_edge_part(edge_src_parts[i], edge_dst_parts[i], xs[0], i, src_part_ids[i],
+                                           xs.size(), op, "x_parts", "src_part_ids");
       const int64_t arity = arity_parts[i];
-      TORCH_CHECK(arity > 0, op, " expects arity > 0.");
       const int64_t pos = pos_parts[i];
-      TORCH_CHECK(pos >= 0 && pos < arity, op, " expects pos in [0, arity), got pos=", pos, " arity=", arity, ".");
+      TORCH_CHECK(arity > 0, op, " requires arity > 0 for edge part ", i, ".");
+      TORCH_CHECK(pos >= 0 && pos < arity, op, " pos out of range for edge part ", i, ": pos=", pos, " arity=", arity,
+                  ".");
       srcs.push_back(edge_src_parts[i]);
       src_mul.push_back(1);
       src_add.push_back(offsets[part]);
@@ -711,11 +831,12 @@ std::tuple< Tensor, Tensor, Tensor > fanout_pack_from_edges(at::TensorList x_par
       dst_mul.push_back(arity);
       dst_add.push_back(slot_offset_parts[i] + pos);
    }
-   const Tensor x_cat = cat_or_single(x_parts.vec());
-   if(n == 0) return {x_cat, empty_index_like(x_parts[0]), empty_index_like(x_parts[0])};
-   return {x_cat, pack_index(srcs, src_mul, src_add, x_parts[0]), pack_index(dsts, dst_mul, dst_add, x_parts[0])};
+   return {x_cat, pack_index(srcs, src_mul, src_add, xs[0]), pack_index(dsts, dst_mul, dst_add, xs[0])};
 }
 
+// fanin_pack_from_edges (mp_ops.cpp:2616-2773): edge part k reads message
+// rows (src_k * arity_k + pos_k) (mode 0, relation slots) or src_k (mode 1,
+// labels) of value part p_k, offset by the rows before it, into dst_k.
 std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_parts, at::TensorList edge_src_parts,
                                                            at::TensorList edge_dst_parts, at::IntArrayRef rel_part_ids,
                                                            at::IntArrayRef arity_parts, at::IntArrayRef pos_parts,
@@ -723,33 +844,33 @@ std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_pa
 {
    const char* op = "fanin_pack_from_edges";
    TORCH_CHECK(!rel_parts.empty(), op, " requires at least one relation tensor.");
+   TORCH_CHECK(mode == 0 || mode == 1, op, " mode must be 0 (relation) or 1 (label), got ", mode, ".");
    const size_t n = edge_src_parts.size();
-   TORCH_CHECK(
-      edge_dst_parts.size() == n && rel_part_ids.size() == n && arity_parts.size() == n && pos_parts.size() == n,
-      op, " expects matching sequence lengths."
-   );
-   TORCH_CHECK(mode == 0 || mode == 1, op, " expects mode in {0,1}, got ", mode, ".");
+   TORCH_CHECK(edge_dst_parts.size() == n, op, " expects edge_src_parts and edge_dst_parts with equal lengths.");
+   TORCH_CHECK(rel_part_ids.size() == n && arity_parts.size() == n && pos_parts.size() == n, op,
+               " expects metadata arrays to match number of edge parts.");
+   const std::vector< Tensor > rels = rel_parts.vec();
+   check_value_parts(rels, op, "rel_parts");
    std::vector< int64_t > offsets;
    int64_t offset = 0;
-   for(const auto& r : rel_parts) {
-      check_rank(r, 2, "relation tensor");
+   for(const auto& r : rels) {
       offsets.push_back(offset);
       offset += r.size(0);
    }
+   const Tensor rel_cat = cat_or_single(rels);
+   if(n == 0) return {rel_cat, empty_index_like(rels[0]), empty_index_like(rels[0])};
    std::vector< Tensor > srcs, dsts;
    std::vector< int64_t > src_mul, src_add;
    for(size_t i = 0; i < n; ++i) {
-      check_int64_index(edge_src_parts[i], "edge_src");
-      check_int64_index(edge_dst_parts[i], "edge_dst");
-      TORCH_CHECK(edge_src_parts[i].numel() == edge_dst_parts[i].numel(), op, " expects edge src/dst lengths to match.");
-      const int64_t part = rel_part_ids[i];
-      TORCH_CHECK(part >= 0 && part < (int64_t)rel_parts.size(), op, " rel_part_ids out of range: ", part, ".");
+      const int64_t part = check_edge_part(edge_src_parts[i], edge_dst_parts[i], rels[0], i, rel_part_ids[i],
+                                           rels.size(), op, "rel_parts", "rel_part_ids");
       int64_t mul = 1, add = offsets[part];
-      if(mode != 1) {
+      if(mode == 0) {
          const int64_t arity = arity_parts[i];
-         TORCH_CHECK(arity > 0, op, " expects arity > 0.");
          const int64_t pos = pos_parts[i];
-         TORCH_CHECK(pos >= 0 && pos < arity, op, " expects pos in [0, arity), got pos=", pos, " arity=", arity, ".");
+         TORCH_CHECK(arity > 0, op, " requires arity > 0 in relation mode for edge part ", i, ".");
+         TORCH_CHECK(pos >= 0 && pos < arity, op, " pos out of range for edge part ", i, ": pos=", pos,
+                     " arity=", arity, ".");
          mul = arity;
          add += pos;
       }
@@ -758,10 +879,8 @@ std::tuple< Tensor, Tensor, Tensor > fanin_pack_from_edges(at::TensorList rel_pa
       src_add.push_back(add);
       dsts.push_back(edge_dst_parts[i]);
    }
-   const Tensor rel_cat = cat_or_single(rel_parts.vec());
-   if(n == 0) return {rel_cat, empty_index_like(rel_parts[0]), empty_index_like(rel_parts[0])};
    const std::vector< int64_t > ones(n, 1), zeros(n, 0);
-   return {rel_cat, pack_index(srcs, src_mul, src_add, rel_parts[0]), pack_index(dsts, ones, zeros, rel_parts[0])};
+   return {rel_cat, pack_index(srcs, src_mul, src_add, rels[0]), pack_index(dsts, ones, zeros, rels[0])};
 }
 
 // build_torch / build_cuda_tag describe the torch this layer was compiled
@@ -1175,10 +1294,31 @@ TORCH_LIBRARY_IMPL(relm_mp, CompositeImplicitAutograd, m)
    m.impl("build_info", relm_b200::build_info);
 }
 
-// Plan-cache control, outside the reference namespace.
+// Ops of this package outside the reference namespace: plan-cache control and
+// the smoothed logsumexp of relmo's models.
 TORCH_LIBRARY(relm_mp_b200, m)
 {
    m.def("clear_plan_cache() -> ()", relm_b200::clear_plan_cache);
    m.def("plan_cache_stats() -> int[]", relm_b200::plan_cache_stats);
    m.def("set_plan_cache_capacity(int capacity) -> ()", relm_b200::set_plan_cache_capacity);
+   m.def(
+      "fanin_reduce_smoothed_logsumexp(Tensor rel_flat, Tensor flat_src, Tensor dst_idx, int dim_size, float beta, "
+      "float eps) -> Tensor"
+   );
+   m.def(
+      "fanin_reduce_smoothed_logsumexp_backward(Tensor grad_out, Tensor rel_flat, Tensor flat_src, Tensor dst_idx, "
+      "Tensor out, int rel_rows, float beta) -> Tensor"
+   );
+}
+
+TORCH_LIBRARY_IMPL(relm_mp_b200, CUDA, m)
+{
+   m.impl("fanin_reduce_smoothed_logsumexp", relm_b200::smoothed_logsumexp_cuda);
+   m.impl("fanin_reduce_smoothed_logsumexp_backward", relm_b200::smoothed_logsumexp_backward_cuda);
+}
+
+TORCH_LIBRARY_IMPL(relm_mp_b200, Meta, m)
+{
+   m.impl("fanin_reduce_smoothed_logsumexp", relm_b200::smoothed_logsumexp_meta);
+   m.impl("fanin_reduce_smoothed_logsumexp_backward", relm_b200::smoothed_logsumexp_backward_meta);
 }

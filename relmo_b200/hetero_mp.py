@@ -6,13 +6,16 @@ Two lanes, as in relmo's ``models/hetero_mp``:
 * ``CentralFusedLayer`` - ``CentralFusedLayerMP.forward`` (fused.py:121-406):
   one fan-out of object embeddings into ``max_arity`` slots per atom, one call
   of the shared central module on ``[condition | slot mask | arguments]``, one
-  fan-in of the slot messages back to the objects. With the kernels and
-  ``fuse_inputs=True`` the fan-out stores the arguments straight into the
-  central module's input buffer (the input assembly of fused.py:311-374
-  without a concatenation, ``CentralFusedLayer._fused_inputs``); off by
-  default, since the fan-out then needs a plan of its own (its slot index is
-  remapped), which costs more than the concatenation it saves (cfg3 train
-  step 15.9 ms fused, 15.1 ms with the concatenation).
+  fan-in of the slot messages back to the objects. The input assembly of
+  fused.py:311-374 (arguments and context copied into one buffer) is not
+  done at all when the central module is a residual MLP (what relmo's
+  ``ArityMLPFactory`` builds): its first Linear is applied by column blocks,
+  ``W [ctx | args] + b = (W_c ctx + b) + W_a args``, with the context term
+  computed once per forward (the context does not change across layers) and
+  the fan-out's own output as the argument block, so the fan-out shares the
+  fan-in's plan and no input buffer is written or read
+  (``CentralFusedLayer.fuse_inputs``, on by default; other central modules
+  take the concatenation).
 * ``BatchedRelationLayer`` - ``BatchedFanOutMP`` + ``BatchedFanInMP``
   (batched.py:41-1199) on the flattened slot handoff: one fan-out into the
   slots of all predicates (``arity`` slots per atom), one per-predicate update
@@ -40,14 +43,15 @@ The gradient is softmax(beta x) over the row in both.
 
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 
 import torch
+import torch.nn.functional as F
 from torch import nn
 
+from .nn import MLP, ResidualModule, SimpleMLP
 from .ops import mp
-from .ops.mp_constants import MODE_LOGSUMEXP, MODE_SUM
+from .ops.mp_constants import MODE_SUM
 from .workloads import RelationalBatch
 
 LSE_BETA = 12.0
@@ -86,10 +90,10 @@ def smoothed_logsumexp_reference(x: torch.Tensor, index: torch.Tensor, dim_size:
 
 
 def fanin(msgs: torch.Tensor, flat_src: torch.Tensor, dst: torch.Tensor, dim_size: int, aggr: str,
-          use_kernels: bool, empty_rows: torch.Tensor | None = None) -> torch.Tensor:
+          use_kernels: bool) -> torch.Tensor:
     """Aggregate message rows ``msgs[flat_src[e]]`` into ``dst[e]``: "sum" or the
-    smoothed "logsumexp". ``empty_rows`` (bool [dim_size]) marks rows without
-    messages (needed by the kernel path of logsumexp)."""
+    smoothed "logsumexp" (one kernel pass each way on the kernel path, rows
+    without messages included)."""
 
     if aggr == "sum":
         if use_kernels:
@@ -99,17 +103,8 @@ def fanin(msgs: torch.Tensor, flat_src: torch.Tensor, dst: torch.Tensor, dim_siz
     if aggr == "logsumexp":
         if not use_kernels:
             return smoothed_logsumexp_reference(msgs.index_select(0, flat_src), dst, int(dim_size))
-        out = mp.fanin_reduce(msgs * LSE_BETA, flat_src, dst, int(dim_size), MODE_LOGSUMEXP) * (1.0 / LSE_BETA)
-        if empty_rows is not None:
-            out = torch.where(empty_rows.unsqueeze(1), out.new_tensor(math.log(LSE_EPS) / LSE_BETA), out)
-        return out
+        return mp.fanin_reduce_smoothed_logsumexp(msgs, flat_src, dst, int(dim_size), LSE_BETA, LSE_EPS)
     raise ValueError(f"aggregation must be 'sum' or 'logsumexp', got {aggr!r}")
-
-
-def _empty_rows(dst: torch.Tensor, dim_size: int) -> torch.Tensor:
-    counts = torch.zeros(int(dim_size), dtype=torch.int32, device=dst.device)
-    counts.index_add_(0, dst, torch.ones_like(dst, dtype=torch.int32))  # no host sync, unlike bincount
-    return counts == 0
 
 
 # ---- routing ------------------------------------------------------------------------------
@@ -126,9 +121,7 @@ class FusedRouting:
     slot: torch.Tensor          # flat slot (atom_row * max_arity + pos) of each edge
     cond_index: torch.Tensor    # condition-embedding row of each atom row
     slot_mask: torch.Tensor     # [R, max_arity] 1 for pos < arity
-    empty_objects: torch.Tensor  # objects without any edge
     pred_meta: list = field(default_factory=list)  # (pred, start, n, arity)
-    padded_slots: dict = field(default_factory=dict)  # slot -> row of the padded input buffer, per layout
 
 
 def build_fused_routing(batch: RelationalBatch, relation_arities: dict, condition_index: dict, max_arity: int,
@@ -144,8 +137,7 @@ def build_fused_routing(batch: RelationalBatch, relation_arities: dict, conditio
     meta = [(p, offsets[p], int(batch.relations[p].size(0)), int(batch.relations[p].size(1))) for p in order]
     if not order:
         return FusedRouting(order, offsets, 0, empty_idx, empty_idx, empty_idx,
-                            torch.zeros((0, max_arity), device=device, dtype=dtype),
-                            _empty_rows(empty_idx, batch.num_objects), meta)
+                            torch.zeros((0, max_arity), device=device, dtype=dtype), meta)
     # (atom, pos) edges of every predicate through the fan-out pack op (one
     # device pass for all parts): object = args[atom, pos], slot =
     # (offset_p + atom) * max_arity + pos.
@@ -168,8 +160,7 @@ def build_fused_routing(batch: RelationalBatch, relation_arities: dict, conditio
     cond_table = torch.tensor([int(condition_index[p]) for p in order], device=device, dtype=torch.int64)
     mask_table = (torch.arange(max_arity).view(1, -1) < torch.tensor([k for *_, k in meta]).view(-1, 1))
     mask_table = mask_table.to(device=device, dtype=dtype)
-    return FusedRouting(order, offsets, total, obj, slot, cond_table[pred_of_row], mask_table[pred_of_row],
-                        _empty_rows(obj, batch.num_objects), meta)
+    return FusedRouting(order, offsets, total, obj, slot, cond_table[pred_of_row], mask_table[pred_of_row], meta)
 
 
 def _pack_from_edges(x_parts, edge_src, edge_dst, part_ids, arity, pos, slot_offsets):
@@ -193,7 +184,6 @@ class BatchedRouting:
     total_slots: int
     obj: torch.Tensor           # object of each slot
     slot: torch.Tensor          # arange(total_slots)
-    empty_objects: torch.Tensor
 
 
 def build_batched_routing(batch: RelationalBatch, relation_arities: dict) -> BatchedRouting:
@@ -211,7 +201,7 @@ def build_batched_routing(batch: RelationalBatch, relation_arities: dict) -> Bat
         start += n * k
     obj = torch.cat(objs) if objs else torch.empty(0, dtype=torch.int64, device=device)
     slot = torch.arange(start, dtype=torch.int64, device=device)
-    return BatchedRouting(meta, start, obj, slot, _empty_rows(obj, batch.num_objects))
+    return BatchedRouting(meta, start, obj, slot)
 
 
 # ---- layers ---------------------------------------------------------------------------------
@@ -223,7 +213,7 @@ class CentralFusedLayer(nn.Module):
 
     def __init__(self, *, central_module: nn.Module, condition_embedding: nn.Embedding, max_arity: int,
                  embedding_size: int, condition_position: str = "pre", include_slot_mask: bool = True,
-                 aggr: str = "logsumexp", use_kernels: bool | None = None, fuse_inputs: bool = False):
+                 aggr: str = "logsumexp", use_kernels: bool | None = None, fuse_inputs: bool = True):
         super().__init__()
         if condition_position not in ("pre", "post"):
             raise ValueError(f"condition_position must be 'pre' or 'post', got {condition_position!r}.")
@@ -237,68 +227,87 @@ class CentralFusedLayer(nn.Module):
         self.aggr = aggr
         self.use_kernels = use_kernels
 
-    def context(self, routing: FusedRouting) -> torch.Tensor:
-        """[R, cond_dim (+ max_arity)] condition (and slot-mask) columns, built
-        once per forward (the reference caches it for the whole forward)."""
+    def context(self, routing: FusedRouting):
+        """The [R, cond_dim (+ max_arity)] condition (and slot-mask) columns of
+        the central module's input, built once per forward (the reference
+        caches it for the whole forward); with the split first layer also its
+        term ``W_c ctx + b``, the same in every layer."""
 
         cond = self.condition_embedding.weight.index_select(0, routing.cond_index)
-        if not self.include_slot_mask:
+        if self.include_slot_mask:
+            mask = routing.slot_mask.to(cond.dtype)
+            cond = torch.cat([cond, mask], dim=1) if self.condition_position == "pre" else torch.cat([mask, cond], dim=1)
+        split = self._split_layers() if self.fuse_inputs else None
+        if split is None:
             return cond
-        mask = routing.slot_mask.to(cond.dtype)
-        return torch.cat([cond, mask], dim=1) if self.condition_position == "pre" else torch.cat([mask, cond], dim=1)
+        lin0, _ = split
+        A, d, C = self.max_arity, self.embedding_size, int(cond.size(1))
+        w_ctx = lin0.weight[:, :C] if self.condition_position == "pre" else lin0.weight[:, A * d :]
+        return SplitContext(cond, F.linear(cond.to(w_ctx.dtype), w_ctx, lin0.bias))
 
-    def forward(self, x: torch.Tensor, routing: FusedRouting, context: torch.Tensor):
+    def _split_layers(self):
+        """(first Linear, later layers) when the central module is
+        ``ResidualModule(MLP | SimpleMLP)`` over ``[context | arguments]``
+        ("pre"; ``[arguments | context]`` "post") whose residual is the argument
+        block; else None."""
+
+        res = self.central_module
+        A, d = self.max_arity, self.embedding_size
+        if not isinstance(res, ResidualModule) or res.truncated_dim != A * d:
+            return None
+        if bool(res.truncate_right) != (self.condition_position == "post"):
+            return None
+        inner = res.module
+        layers = list(inner.net) if isinstance(inner, MLP) else list(inner.mlp) if isinstance(inner, SimpleMLP) else None
+        if not layers or not isinstance(layers[0], nn.Linear) or layers[0].in_features <= A * d:
+            return None
+        return layers[0], layers[1:]
+
+    def forward(self, x: torch.Tensor, routing: FusedRouting, context):
         kern = _kernels(x, self.use_kernels)
         n_obj, d = x.size(0), self.embedding_size
         R = routing.total_atoms
         if R == 0:
             return {}, x.new_zeros((n_obj, d))
-        if kern and self.fuse_inputs:
-            all_inputs = self._fused_inputs(x, routing, context)
+        args_flat = fanout(x, routing.obj, routing.slot, R * self.max_arity, kern)
+        args_feat = args_flat.reshape(R, self.max_arity * d)
+        if isinstance(context, SplitContext):
+            all_outputs = self._split_forward(args_feat, context)
         else:
-            args_flat = fanout(x, routing.obj, routing.slot, R * self.max_arity, kern)
-            args_feat = args_flat.reshape(R, self.max_arity * d)
-            if self.condition_position == "pre":
-                all_inputs = torch.cat([context.to(args_feat.dtype), args_feat], dim=1)
-            else:
-                all_inputs = torch.cat([args_feat, context.to(args_feat.dtype)], dim=1)
-        all_outputs = self.central_module(all_inputs)
+            ctx = context.to(args_feat.dtype)
+            all_inputs = torch.cat([ctx, args_feat], dim=1) if self.condition_position == "pre" else torch.cat(
+                [args_feat, ctx], dim=1)
+            all_outputs = self.central_module(all_inputs)
         atom_msgs = {p: all_outputs[s : s + n, : k * d] for p, s, n, k in routing.pred_meta}
         out_flat = all_outputs.reshape(R * self.max_arity, d)
-        msgs = fanin(out_flat, routing.slot, routing.obj, n_obj, self.aggr, kern, routing.empty_objects)
+        msgs = fanin(out_flat, routing.slot, routing.obj, n_obj, self.aggr, kern)
         return atom_msgs, msgs
 
+    def _split_forward(self, args_feat: torch.Tensor, context: "SplitContext") -> torch.Tensor:
+        """The residual MLP on [context | arguments] without the concatenation:
+        args + rest(W_a args + (W_c ctx + b))."""
 
-    def _fused_inputs(self, x: torch.Tensor, routing: FusedRouting, context: torch.Tensor) -> torch.Tensor:
-        """The central module's input [R, C + A*D] ("pre"; [R, A*D + C] "post")
-        assembled in place by the fan-out (the fused input assembly of
-        fused.py:311-374): the buffer is [R, Cp + A*D] with Cp = C rounded up to
-        whole rows of D, seen by the fan-out as R * (Cp/D + A) rows of D, so
-        each slot's row is stored straight into its atom row (rows of the
-        context part stay zero) and the context is one strided copy into its
-        columns. The module reads a strided view (no concatenation), and the
-        fan-out backward reads the buffer's gradient as it comes (no copy of
-        its argument columns)."""
-
+        lin0, rest = self._split_layers()
         A, d = self.max_arity, self.embedding_size
-        R = routing.total_atoms
-        C = int(context.size(1))
-        cr = -(-C // d)  # context rows of D columns
-        per_atom = cr + A
-        pre = self.condition_position == "pre"
-        key = (cr, A, pre)
-        slot_p = routing.padded_slots.get(key)
-        if slot_p is None:
-            atom, pos = routing.slot // A, routing.slot % A
-            slot_p = atom * per_atom + (pos + cr if pre else pos)
-            routing.padded_slots[key] = slot_p
-        buf = mp.fanout_scatter(x, routing.obj, slot_p, R * per_atom).view(R, per_atom * d)
-        if pre:
-            lo = cr * d - C
-            buf[:, lo : cr * d] = context.to(buf.dtype)
-            return buf[:, lo:]
-        buf[:, A * d : A * d + C] = context.to(buf.dtype)
-        return buf[:, : A * d + C]
+        C = lin0.in_features - A * d
+        w_args = lin0.weight[:, C:] if self.condition_position == "pre" else lin0.weight[:, : A * d]
+        term = context.term
+        if torch.is_autocast_enabled(args_feat.device.type):
+            h = F.linear(args_feat, w_args) + term
+        else:
+            h = torch.addmm(term.to(args_feat.dtype), args_feat, w_args.t())
+        for layer in rest:
+            h = layer(h)
+        return args_feat + h
+
+
+@dataclass
+class SplitContext:
+    """Context of a forward whose central module takes its first layer by
+    column blocks: the context columns and their layer term ``W_c ctx + b``."""
+
+    columns: torch.Tensor
+    term: torch.Tensor
 
 
 class BatchedRelationLayer(nn.Module):
@@ -332,5 +341,5 @@ class BatchedRelationLayer(nn.Module):
             outs.append(y.reshape(n * k, d))
         dtype = torch.promote_types(outs[0].dtype, outs[-1].dtype)
         msgs = torch.cat([o.to(dtype) for o in outs], dim=0) if len(outs) > 1 else outs[0]
-        out = fanin(msgs, routing.slot, routing.obj, x.size(0), self.aggr, kern, routing.empty_objects)
+        out = fanin(msgs, routing.slot, routing.obj, x.size(0), self.aggr, kern)
         return atom_msgs, out

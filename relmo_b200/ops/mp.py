@@ -24,7 +24,12 @@ model family and are not part of this package.
 
 from __future__ import annotations
 
-from .mp_autograd import _FaninReduceLogSumExpFunction, _FaninReduceSumFunction, _FanoutScatterFunction
+from .mp_autograd import (
+    _FaninReduceLogSumExpFunction,
+    _FaninReduceSmoothedLogSumExpFunction,
+    _FaninReduceSumFunction,
+    _FanoutScatterFunction,
+)
 from .mp_constants import MODE_LOGSUMEXP, MODE_MEAN, MODE_SUM
 from .mp_dispatch import CUSTOM, call, route
 from .mp_lgan import (
@@ -73,6 +78,35 @@ def fanin_reduce(rel_flat, flat_src, dst_idx, dim_size: int, mode: int):
             return _FaninReduceSumFunction.apply(rel_flat, flat_src, dst_idx, int(dim_size))
         return _FaninReduceLogSumExpFunction.apply(rel_flat, flat_src, dst_idx, int(dim_size))
     return fanin_reduce_python(rel_flat, flat_src, dst_idx, int(dim_size), mode_int)
+
+
+def smoothed_logsumexp_python(rel_flat, flat_src, dst_idx, dim_size: int, beta: float, eps: float):
+    """relmo's LogSumExpAggregation.forward (models/aggr.py:103-123) on the
+    gathered messages: the formula the CPU path runs without the library."""
+
+    x = rel_flat.index_select(0, flat_src)
+    m = torch.zeros((int(dim_size), x.size(-1)), device=x.device, dtype=x.dtype)
+    m = m.index_reduce(0, dst_idx, x, "amax", include_self=False).detach()
+    s = torch.full_like(m, eps).index_add(0, dst_idx, (beta * (x - m.index_select(0, dst_idx))).exp())
+    return (1.0 / beta) * s.log() + m
+
+
+def fanin_reduce_smoothed_logsumexp(rel_flat, flat_src, dst_idx, dim_size: int, beta: float = 12.0,
+                                    eps: float = 1e-16):
+    """The smoothed logsumexp relmo's models aggregate with (LogSumExpAggregation,
+    models/aggr.py:96-123; beta = its maximum_smoothness): per column
+    ``m + (1/beta) log(eps + sum exp(beta (x - m)))`` over the row's messages
+    ``rel_flat[flat_src[e]]``, m the row max (no gradient through it); rows
+    without messages get ``(1/beta) log(eps)``. One planned kernel pass forward
+    and one backward (gradient ``exp(beta (x - out))``), instead of relmo's
+    four ATen passes. Not part of relmo's op facade."""
+
+    require_torch("fanin_reduce_smoothed_logsumexp")
+    if route("fanin_reduce_smoothed_logsumexp", rel_flat) == CUSTOM:
+        return _FaninReduceSmoothedLogSumExpFunction.apply(
+            rel_flat, flat_src, dst_idx, int(dim_size), float(beta), float(eps)
+        )
+    return smoothed_logsumexp_python(rel_flat, flat_src, dst_idx, int(dim_size), float(beta), float(eps))
 
 
 def fanout_pack_multi(x_parts, src_idx_parts, flat_dst_parts):
@@ -174,6 +208,7 @@ def set_plan_cache_capacity(capacity: int) -> None:
 __all__ = [
     "fanout_scatter",
     "fanin_reduce",
+    "fanin_reduce_smoothed_logsumexp",
     "fanout_pack_multi",
     "fanin_pack_multi",
     "fanout_pack_from_edges",

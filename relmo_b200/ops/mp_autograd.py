@@ -66,3 +66,26 @@ if torch is not None:
                 grad_out.contiguous(), rel_flat, flat_src, dst_idx, out, int(ctx.rel_rows)
             )
             return grad_rel, None, None, None
+
+    class _FaninReduceSmoothedLogSumExpFunction(torch.autograd.Function):
+        """The smoothed logsumexp of relmo's models (LogSumExpAggregation,
+        relmo/models/aggr.py:96-123) as one op pair; not a reference op. Saves
+        (rel_flat, flat_src, dst_idx, out) like the plain logsumexp."""
+
+        @staticmethod
+        def forward(ctx, rel_flat, flat_src, dst_idx, dim_size: int, beta: float, eps: float):
+            ctx.rel_rows = int(rel_flat.size(0))
+            ctx.beta = float(beta)
+            out = torch.ops.relm_mp_b200.fanin_reduce_smoothed_logsumexp(
+                rel_flat, flat_src, dst_idx, int(dim_size), float(beta), float(eps)
+            )
+            ctx.save_for_backward(rel_flat, flat_src, dst_idx, out)
+            return out
+
+        @staticmethod
+        def backward(ctx, grad_out):
+            rel_flat, flat_src, dst_idx, out = ctx.saved_tensors
+            grad_rel = torch.ops.relm_mp_b200.fanin_reduce_smoothed_logsumexp_backward(
+                grad_out.contiguous(), rel_flat, flat_src, dst_idx, out, int(ctx.rel_rows), ctx.beta
+            )
+            return grad_rel, None, None, None, None, None

@@ -26,7 +26,7 @@ def is_cuda(tensor: object) -> bool:
 
 
 def _has_op(op_name: str) -> bool:
-    return hasattr(library().ops(), op_name)
+    return library().has_op(op_name)
 
 
 def route(op_name: str, tensor: object) -> str:

@@ -46,6 +46,7 @@ else:
     TORCH_IMPORT_ERROR = None
 
 NAMESPACE = "relm_mp"
+OWN_NAMESPACE = "relm_mp_b200"  # ops of this package outside the reference schemas
 LIBRARY_GLOBS = ("relm_mp_ops*.so", "librelm_mp_ops*.so")
 
 
@@ -238,6 +239,14 @@ class Library:
     def ops(self):
         self.load()
         return getattr(self._t().ops, NAMESPACE)
+
+    def has_op(self, op_name: str) -> bool:
+        """Whether the loaded library registers ``op_name`` (in the reference
+        namespace or in this package's own, ``OWN_NAMESPACE``)."""
+
+        self.load()
+        ops = self._t().ops
+        return hasattr(getattr(ops, NAMESPACE), op_name) or hasattr(getattr(ops, OWN_NAMESPACE, None), op_name)
 
 
 _LIBRARY = Library()

@@ -56,6 +56,35 @@ def load_lgan_cases() -> list[LganCase]:
     return cases
 
 
+@dataclass
+class PackCase:
+    name: str
+    op: str
+    args: list  # lists of numpy arrays, lists of ints, or ints
+    outs: list[np.ndarray]
+    raises: str | None
+    message: str | None
+
+
+def load_pack_cases() -> list[PackCase]:
+    z = np.load(GOLDEN / "ref_pack.npz")
+    meta = json.loads(bytes(z["__meta__"]).decode())
+    cases = []
+    for name in sorted(meta):
+        entry = meta[name]
+        args = []
+        for a in entry["args"]:
+            if "tensors" in a:
+                args.append([z[k] for k in a["tensors"]])
+            elif "ints" in a:
+                args.append(list(a["ints"]))
+            else:
+                args.append(a["int"])
+        outs = [z[f"{name}__out{k}"] for k in range(3)] if entry["raises"] is None else []
+        cases.append(PackCase(name, entry["op"], args, outs, entry["raises"], entry.get("message")))
+    return cases
+
+
 def load_cfg1() -> tuple[dict, dict[str, np.ndarray]]:
     z = np.load(GOLDEN / "ref_cfg1.npz")
     meta = json.loads(bytes(z["__meta__"]).decode())

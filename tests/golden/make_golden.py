@@ -6,6 +6,7 @@ torch namespace, the same one ``relmo_b200`` registers):
     python oracle/build_ref.py          # builds oracle/_ref/relm_mp_ref.so
     python tests/golden/make_golden.py  # writes tests/golden/*.npz
     python tests/golden/make_golden.py --only-lgan   # ref_lgan.npz alone
+    python tests/golden/make_golden.py --only-pack   # ref_lgan.npz and ref_pack.npz
 
 Inputs come from the reference's own test fixtures
 (``tests/python/test_mp_ops.py:171-347`` of maichmueller/relmo: the literal index
@@ -22,6 +23,12 @@ Files:
   (seeded values where the test draws unseeded ``randn``), edge cases and a
   seeded random case; inputs and outputs stored in full. Tuple outputs are
   stored as ``<case>__out0``, ``__out1``, ...
+* ``ref_pack.npz`` - the four pack ops (``fanout_pack_multi``, ``fanin_pack_multi``,
+  ``fanout_pack_from_edges``, ``fanin_pack_from_edges``; mp_ops.cpp:412-570,
+  2511-2773): one part, several parts, more than 64 parts, empty parts, strided
+  index views, no edge parts, both ``fanin_pack_from_edges`` modes, and the
+  reference's argument errors. Tensor-list arguments are stored as
+  ``<case>__arg<i>_<k>``; outputs as ``<case>__out0..2``.
 * ``ref_cfg1.npz`` - cfg1 (N=2000, D=32, E=20000, seed 0). Inputs are regenerated
   from the seed and pinned by SHA-256; outputs stored in full when they are
   [N, D], by SHA-256 when bit-exact [E, D], and by a row sample plus float64
@@ -277,6 +284,92 @@ def run_lgan(ops) -> dict[str, np.ndarray]:
     return arrays
 
 
+def pack_cases():
+    """(name, op, args) for the pack ops; list arguments are Python lists."""
+
+    g = torch.Generator().manual_seed(77)
+
+    def randn(*shape):
+        return torch.randn(*shape, generator=g)
+
+    def ridx(n, hi):
+        return torch.randint(0, max(hi, 1), (n,), generator=g)
+
+    cases = []
+    # fanout_pack_multi / fanin_pack_multi: (value parts, gather-index parts, other-index parts)
+    for name, parts in (("one", [(5, 7)]), ("three", [(4, 3), (0, 0), (6, 9)]), ("many", [(3, 2)] * 70)):
+        xs = [randn(r, 4) for r, _ in parts]
+        src = [ridx(e, r) for r, e in parts]
+        dst = [ridx(e, 50) for _, e in parts]
+        cases.append((f"fanout_multi_{name}", "fanout_pack_multi", [xs, src, dst]))
+        cases.append((f"fanin_multi_{name}", "fanin_pack_multi", [xs, src, dst]))
+    base = ridx(40, 6)
+    cases.append(("fanout_multi_strided", "fanout_pack_multi",
+                  [[randn(6, 2), randn(3, 2)], [base[::2], base[1:8:3] % 3], [ridx(20, 9), ridx(3, 9)]]))
+    cases.append(("fanout_multi_len_mismatch", "fanout_pack_multi", [[randn(3, 2)], [ridx(4, 3)], [ridx(2, 3)]]))
+    cases.append(("fanin_multi_emb_mismatch", "fanin_pack_multi",
+                  [[randn(3, 2), randn(3, 5)], [ridx(2, 3), ridx(2, 3)], [ridx(2, 3), ridx(2, 3)]]))
+
+    # fanout_pack_from_edges(x_parts, edge_src, edge_dst, src_part_ids, arity, pos, slot_offsets)
+    def from_edges(n_parts, n_x=3, n_edges=5):
+        xs = [randn(4 + i, 3) for i in range(n_x)]
+        src, dst, part, ar, pos, off = [], [], [], [], [], []
+        for i in range(n_parts):
+            k = i % n_x
+            a = 1 + i % 3
+            e = 0 if i % 11 == 5 else n_edges
+            src.append(ridx(e, 4 + k))
+            dst.append(ridx(e, 8))
+            part.append(k)
+            ar.append(a)
+            pos.append(i % a)
+            off.append(100 * i)
+        return xs, src, dst, part, ar, pos, off
+
+    for name, n in (("one", 1), ("six", 6), ("many", 67), ("none", 0)):
+        xs, src, dst, part, ar, pos, off = from_edges(n)
+        cases.append((f"fanout_edges_{name}", "fanout_pack_from_edges", [xs, src, dst, part, ar, pos, off]))
+        for mode in (0, 1):
+            cases.append((f"fanin_edges_{name}_m{mode}", "fanin_pack_from_edges", [xs, src, dst, part, ar, pos, mode]))
+    xs, src, dst, part, ar, pos, off = from_edges(3)
+    cases.append(("fanout_edges_bad_part", "fanout_pack_from_edges", [xs, src, dst, [0, 5, 1], ar, pos, off]))
+    cases.append(("fanout_edges_bad_pos", "fanout_pack_from_edges", [xs, src, dst, part, [1, 2, 3], [0, 2, 1], off]))
+    cases.append(("fanout_edges_zero_arity", "fanout_pack_from_edges", [xs, src, dst, part, [1, 0, 3], [0, 0, 1], off]))
+    cases.append(("fanin_edges_bad_mode", "fanin_pack_from_edges", [xs, src, dst, part, ar, pos, 2]))
+    cases.append(("fanin_edges_bad_pos", "fanin_pack_from_edges", [xs, src, dst, part, [1, 2, 3], [0, 2, 1], 0]))
+    return cases
+
+
+def run_pack(ops) -> dict[str, np.ndarray]:
+    arrays: dict[str, np.ndarray] = {}
+    meta: dict[str, dict] = {}
+    for name, op, args in pack_cases():
+        entry = {"op": op, "args": []}
+        for i, a in enumerate(args):
+            if isinstance(a, list) and a and isinstance(a[0], torch.Tensor):
+                keys = []
+                for k, t in enumerate(a):
+                    key = f"{name}__arg{i}_{k}"
+                    arrays[key] = t.contiguous().numpy()
+                    keys.append(key)
+                entry["args"].append({"tensors": keys})
+            elif isinstance(a, list):
+                entry["args"].append({"ints": [int(v) for v in a]})
+            else:
+                entry["args"].append({"int": int(a)})
+        try:
+            outs = getattr(ops, op)(*args)
+            for k, o in enumerate(outs):
+                arrays[f"{name}__out{k}"] = o.numpy()
+            entry["raises"] = None
+        except Exception as exc:  # the reference's argument checks
+            entry["raises"] = type(exc).__name__
+            entry["message"] = str(exc).splitlines()[0]
+        meta[name] = entry
+    arrays["__meta__"] = np.frombuffer(json.dumps(meta, sort_keys=True).encode(), dtype=np.uint8)
+    return arrays
+
+
 def run_cfg1(ops) -> dict[str, np.ndarray]:
     wl = workloads.cfg1(seed=0)
     arrays: dict[str, np.ndarray] = {}
@@ -315,6 +408,12 @@ def main() -> int:
     np.savez_compressed(HERE / "ref_lgan.npz", **lgan)
     print("wrote", HERE / "ref_lgan.npz")
     if "--only-lgan" in sys.argv:
+        return 0
+    pack = run_pack(ops)
+    pack["__build_info__"] = np.frombuffer(info.encode(), dtype=np.uint8)
+    np.savez_compressed(HERE / "ref_pack.npz", **pack)
+    print("wrote", HERE / "ref_pack.npz")
+    if "--only-pack" in sys.argv:
         return 0
     small = run_small(ops)
     small["__build_info__"] = np.frombuffer(info.encode(), dtype=np.uint8)

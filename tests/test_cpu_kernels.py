@@ -19,10 +19,11 @@ import torch
 
 from relmo_b200 import workloads
 from relmo_b200.ops import mp
-from tests._golden import load_cases, load_cfg1, load_lgan_cases, sha256
+from tests._golden import load_cases, load_cfg1, load_lgan_cases, load_pack_cases, sha256
 
 CASES = load_cases()
 LGAN_CASES = load_lgan_cases()
+PACK_CASES = load_pack_cases()
 
 
 @pytest.fixture(autouse=True, scope="module")
@@ -59,6 +60,32 @@ def test_cpu_lgan_op_equals_reference_library(case) -> None:
     got = op(*_cpu(case.args))
     got = list(got) if isinstance(got, (tuple, list)) else [got]
     assert len(got) == len(case.outs)
+    for g, ref in zip(got, case.outs):
+        assert _equal(g, ref), case.name
+
+
+def _pack_args(args, device="cpu"):
+    out = []
+    for a in args:
+        if isinstance(a, list) and a and isinstance(a[0], np.ndarray):
+            out.append([torch.from_numpy(np.ascontiguousarray(t)).to(device) for t in a])
+        else:
+            out.append(a)
+    return out
+
+
+@pytest.mark.parametrize("case", PACK_CASES, ids=[c.name for c in PACK_CASES])
+def test_cpu_pack_op_equals_reference_library(case) -> None:
+    """The pack ops (index arithmetic + concatenation, mp_ops.cpp:412-570,
+    2511-2773) on CPU tensors, against the reference library's outputs."""
+
+    op = getattr(torch.ops.relm_mp, case.op)
+    if case.raises:
+        with pytest.raises(Exception, match=re.escape(case.message)):
+            op(*_pack_args(case.args))
+        return
+    got = op(*_pack_args(case.args))
+    assert len(got) == 3
     for g, ref in zip(got, case.outs):
         assert _equal(g, ref), case.name
 

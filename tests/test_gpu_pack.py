@@ -1,17 +1,26 @@
 """Pack ops on the GPU (their index arithmetic and concatenation as one device
 pass per 64 parts): torch.ops.relm_mp.*pack* and the C ABI
-relm_mp_pack_index against the reference's ATen formulas (relmo
+relm_mp_pack_index against the reference library's own outputs
+(tests/golden/ref_pack.npz, made from mp_ops.cpp:412-570, 2511-2773 by
+tests/golden/make_golden.py) and against its ATen formulas (relmo
 src/relmo/ops/mp_pack.py:66-292, restated in relmo_b200/ops/mp_pack.py) —
 bit-exact, with empty parts, strided parts and more than one launch's worth
-(64) of parts."""
+(64) of parts; argument errors with the reference's messages."""
 
 from __future__ import annotations
 
 import pytest
 import torch
 
+import re
+
+import numpy as np
+
 from relmo_b200 import capi
 from relmo_b200.ops import mp, mp_pack
+from tests._golden import load_pack_cases
+
+PACK_CASES = load_pack_cases()
 
 pytestmark = pytest.mark.gpu
 
@@ -75,3 +84,22 @@ def test_pack_from_edges_ops_match_formulas(mode):
     expect = mp_pack.fanin_pack_from_edges_python(vals, es, ed, part_ids, arity, pos, mode)
     for a, b in zip(got, expect):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("case", PACK_CASES, ids=[c.name for c in PACK_CASES])
+def test_pack_ops_equal_reference_library_on_cuda(case):
+    args = []
+    for a in case.args:
+        if isinstance(a, list) and a and isinstance(a[0], np.ndarray):
+            args.append([torch.from_numpy(np.ascontiguousarray(t)).cuda() for t in a])
+        else:
+            args.append(a)
+    op = getattr(torch.ops.relm_mp, case.op)
+    if case.raises:
+        with pytest.raises(Exception, match=re.escape(case.message)):
+            op(*args)
+        return
+    got = op(*args)
+    for g, ref in zip(got, case.outs):
+        assert g.is_cuda and g.dtype == torch.from_numpy(ref).dtype
+        assert np.array_equal(g.cpu().numpy(), ref), case.name

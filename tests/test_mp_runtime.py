@@ -181,6 +181,9 @@ class FakeLibrary:
         self.load()
         return self.ns
 
+    def has_op(self, op_name: str) -> bool:
+        return hasattr(self.ops(), op_name)
+
 
 CUDA_T = SimpleNamespace(is_cuda=True)
 CPU_T = SimpleNamespace(is_cuda=False)
