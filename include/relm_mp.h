@@ -234,6 +234,23 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
                                       void* plan_mem, size_t plan_bytes, void* scratch,
                                       size_t scratch_bytes, void* stream, relm_mp_plan* plan);
 
+/* relm_mp_plan_build_ex that also computes the coverage of the gather index
+ * over [0, gather_rows) in its validation pass: bit g of `cover` (device
+ * uint32 [relm_mp_cover_words(gather_rows)], the layout of
+ * relm_mp_plan_gather_cover) is set when some edge gathers row g, and
+ * *gather_repeats = 1 when some row is gathered more than once,
+ * *gather_covered (may be NULL) = the number of distinct gathered rows. No host sync
+ * beyond the build's own (the repeat flag comes back with its validation
+ * stats). Scratch: relm_mp_plan_cover_scratch_bytes. No counterpart in the
+ * reference (its ops keep no plans). */
+RELM_MP_API size_t relm_mp_plan_cover_scratch_bytes(int64_t num_edges, int64_t num_rows, int64_t gather_rows);
+RELM_MP_API int relm_mp_plan_build_cover(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                                         int64_t num_rows, int64_t out_bound, int64_t gather_rows,
+                                         const char* out_index_name, const char* gather_index_name,
+                                         int gather_checked_first, void* plan_mem, size_t plan_bytes, void* scratch,
+                                         size_t scratch_bytes, uint32_t* cover, int* gather_repeats,
+                                         int64_t* gather_covered, void* stream, relm_mp_plan* plan);
+
 /* Copies device_flags[0..1] into plan->flags (RELM_MP_PLAN_FLAGS_KNOWN,
  * RELM_MP_PLAN_REPEATS, RELM_MP_PLAN_LONG_ROWS). Synchronizes `stream`. */
 RELM_MP_API int relm_mp_plan_read_flags(relm_mp_plan* plan, void* stream);
@@ -266,13 +283,24 @@ static inline size_t relm_mp_cover_words(int64_t rows) { return rows > 0 ? (size
  * more than once. Synchronizes `stream` once. */
 RELM_MP_API int relm_mp_plan_gather_cover(const relm_mp_plan* plan, uint32_t* cover, int* has_dups,
                                           void* stream);
+/* relm_mp_plan_gather_cover with caller scratch
+ * (relm_mp_plan_gather_cover_scratch_bytes: one byte per gathered row): the
+ * gathered rows are marked with plain byte stores and packed into the bitmap,
+ * and repeats are found by counting the distinct rows, instead of one L2
+ * atomic per edge. Same results; synchronizes `stream` once. *covered_rows (may
+ * be NULL): the number of distinct gathered rows. */
+RELM_MP_API size_t relm_mp_plan_gather_cover_scratch_bytes(const relm_mp_plan* plan);
+RELM_MP_API int relm_mp_plan_gather_cover_ex(const relm_mp_plan* plan, uint32_t* cover, int* has_dups,
+                                             int64_t* covered_rows, void* scratch, size_t scratch_bytes,
+                                             void* stream);
 /* Number of the plan's output rows that hold at least one edge (counted by
  * the plan build on the device). Synchronizes `stream` once. No counterpart in
  * the reference (its ops keep no plans). */
 RELM_MP_API int relm_mp_plan_nonempty_rows(const relm_mp_plan* plan, int64_t* rows, void* stream);
 /* Scatter in plan-row order, for a gather index that covers each row at most
  * once: out[gidx[j]] = table[r] for every edge j of plan row r, and 0 in the
- * out rows `cover` marks as uncovered. fanout forward through the source plan
+ * out rows `cover` marks as uncovered (cover NULL: every out row is gathered by
+ * some edge, nothing is zeroed). fanout forward through the source plan
  * (plan rows = x rows, gather index = flat_dst): every x row is read once. */
 RELM_MP_API int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table,
                                           int64_t emb, const uint32_t* cover, void* out, void* stream);
@@ -280,7 +308,8 @@ RELM_MP_API int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtyp
  * rows = destination rows, gather index = flat_src), for a flat_src that uses
  * each message row at most once (cover from relm_mp_plan_gather_cover, no
  * repeats): grad_rel[m] = grad_out[d] * exp(rel[m] - lse_out[d]) for every edge
- * (d, m), 0 for message rows no edge uses. Reads each destination row's
+ * (d, m), 0 for message rows no edge uses (cover NULL: every message row is
+ * used, nothing is zeroed). Reads each destination row's
  * grad_out / lse_out once instead of once per message; rows of 16..256 bytes
  * (a power of two times 16) with 16-byte aligned tables, else UNSUPPORTED. */
 RELM_MP_API int relm_mp_plan_scatter_logsumexp_backward(const relm_mp_plan* plan, relm_mp_dtype dtype,

@@ -111,6 +111,16 @@ SIGNATURES: dict[str, tuple] = {
     "relm_mp_plan_read_flags": (_INT, [_PLANP, _P]),
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),
     "relm_mp_plan_gather_cover": (_INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), _P]),
+    "relm_mp_plan_gather_cover_scratch_bytes": (_SZ, [_PLANP]),
+    "relm_mp_plan_gather_cover_ex": (
+        _INT, [_PLANP, _P, ctypes.POINTER(ctypes.c_int), ctypes.POINTER(_I64), _P, _SZ, _P]
+    ),
+    "relm_mp_plan_cover_scratch_bytes": (_SZ, [_I64, _I64, _I64]),
+    "relm_mp_plan_build_cover": (
+        _INT,
+        [_P, _P, _I64, _I64, _I64, _I64, _STR, _STR, _INT, _P, _SZ, _P, _SZ, _P, ctypes.POINTER(ctypes.c_int),
+         ctypes.POINTER(_I64), _P, _PLANP],
+    ),
     "relm_mp_plan_nonempty_rows": (_INT, [_PLANP, ctypes.POINTER(_I64), _P]),
     "relm_mp_pack_index": (_INT, [_P, _INT, _P, _P]),
     "relm_mp_plan_scatter_logsumexp_backward": (_INT, [_PLANP, _INT, _P, _P, _P, _I64, _P, _P, _P]),
@@ -336,23 +346,38 @@ def fanin_reduce_noalloc(rel, flat_src, dst, dim_size: int, mode: int, out=None)
 class PlanHandle:
     """A plan built through the C ABI, owning its device memory (torch)."""
 
-    def __init__(self, out_index, gather_index, num_rows: int, gather_rows: int):
-        """gather_index None: the identity (edge e gathers row e)."""
+    def __init__(self, out_index, gather_index, num_rows: int, gather_rows: int, with_cover: bool = False):
+        """gather_index None: the identity (edge e gathers row e). with_cover:
+        build through relm_mp_plan_build_cover (self.cover, self.repeats)."""
 
         torch = _torch()
         out_index = out_index.contiguous()
         gather_index = gather_index.contiguous() if gather_index is not None else None
         e = out_index.numel()
         self.memory = _workspace(lib().relm_mp_plan_bytes(e, int(num_rows)), out_index.device)
-        scratch = _workspace(lib().relm_mp_plan_scratch_bytes(e, int(num_rows)), out_index.device)
         self.plan = Plan()
         self.device = out_index.device
+        if with_cover:
+            scratch = _workspace(lib().relm_mp_plan_cover_scratch_bytes(e, int(num_rows), int(gather_rows)),
+                                 out_index.device)
+            self.cover = torch.empty(max(1, (int(gather_rows) + 31) // 32), dtype=torch.int32,
+                                     device=out_index.device)
+            rep = ctypes.c_int(-1)
+            covered = ctypes.c_int64(-1)
+            check(lib().relm_mp_plan_build_cover(
+                _ptr(out_index), _ptr(gather_index), e, int(num_rows), int(num_rows), int(gather_rows), None, None,
+                0, self.memory.data_ptr(), self.memory.numel(), scratch.data_ptr(), scratch.numel(), _ptr(self.cover),
+                ctypes.byref(rep), ctypes.byref(covered), _stream(out_index.device), ctypes.byref(self.plan),
+            ))
+            self.repeats = bool(rep.value)
+            self.covered = int(covered.value)
+            return
+        scratch = _workspace(lib().relm_mp_plan_scratch_bytes(e, int(num_rows)), out_index.device)
         check(lib().relm_mp_plan_build(
             _ptr(out_index), _ptr(gather_index), e, int(num_rows), int(gather_rows), None, None,
             self.memory.data_ptr(), self.memory.numel(), scratch.data_ptr(), scratch.numel(),
             _stream(out_index.device), ctypes.byref(self.plan),
         ))
-        del torch
 
     def read_flags(self) -> int:
         """Copies the plan's device flags into plan.flags (later planned calls
@@ -497,6 +522,22 @@ class PlanHandle:
         dups = ctypes.c_int(0)
         check(lib().relm_mp_plan_gather_cover(ctypes.byref(self.plan), _ptr(cover), ctypes.byref(dups),
                                               _stream(self.device)))
+        return cover, bool(dups.value)
+
+    def gather_cover_ex(self):
+        """relm_mp_plan_gather_cover_ex (byte marks, caller scratch): (bitmap, has_dups)."""
+
+        torch = _torch()
+        words = max(1, (int(self.plan.gather_rows) + 31) // 32)
+        cover = torch.empty(words, dtype=torch.int32, device=self.device)
+        scratch = _workspace(lib().relm_mp_plan_gather_cover_scratch_bytes(ctypes.byref(self.plan)), self.device)
+        dups = ctypes.c_int(0)
+        covered = ctypes.c_int64(-1)
+        check(lib().relm_mp_plan_gather_cover_ex(
+            ctypes.byref(self.plan), _ptr(cover), ctypes.byref(dups), ctypes.byref(covered), scratch.data_ptr(),
+            scratch.numel(), _stream(self.device),
+        ))
+        self.covered = int(covered.value)
         return cover, bool(dups.value)
 
     def nonempty_rows(self) -> int:

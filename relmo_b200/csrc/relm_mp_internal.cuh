@@ -59,7 +59,8 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
                        int64_t num_rows, int64_t out_bound, int64_t gather_rows,
                        const char* out_name, const char* gather_name, bool gather_checked_first,
                        void* plan_mem, size_t plan_bytes, void* scratch, size_t scratch_bytes,
-                       cudaStream_t stream, relm_mp_plan* plan);
+                       cudaStream_t stream, relm_mp_plan* plan, uint32_t* cover = nullptr,
+                       int* gather_repeats = nullptr, int64_t* gather_covered = nullptr);
 
 int64_t plan_num_tiles(int64_t num_edges, int64_t num_rows);
 

@@ -734,7 +734,7 @@ int scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* tabl
 int relm_mp_plan_scatter_rows(const relm_mp_plan* plan, relm_mp_dtype dtype, const void* table, int64_t emb,
                               const uint32_t* cover, void* out, void* stream)
 {
-   if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
    return scatter_rows(plan, dtype, table, emb, nullptr, cover, out, static_cast< cudaStream_t >(stream));
 }
 
@@ -758,7 +758,7 @@ int relm_mp_plan_scatter_logsumexp_backward_ex(const relm_mp_plan* plan, relm_mp
                                                const void* lse_out, const void* rel, int64_t emb,
                                                const uint32_t* cover, void* grad_rel, void* stream)
 {
-   if(!plan || !cover) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan and cover must not be NULL.");
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
    if(!valid_dtype(dtype)) return fail(RELM_MP_ERR_UNSUPPORTED, "unsupported dtype.");
    if(emb < 0) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "emb must be >= 0.");
    cudaStream_t st = static_cast< cudaStream_t >(stream);

@@ -10,7 +10,13 @@
 //                     index and whether it is the identity, int32 copies of
 //                     both. An identity output index (edge e writes row e, the
 //                     message-row index of a fan-in) skips steps 2 and 3:
-//                     k_identity_rows writes row_ptr directly.
+//                     k_identity_rows writes row_ptr directly. On request it
+//                     also marks the gathered rows (a byte per row, plain
+//                     stores), which k_pack_marks turns into the coverage
+//                     bitmap and the count of distinct gathered rows: the
+//                     gather index repeats a row exactly when that count is
+//                     below the edge count. The count travels with the
+//                     build's one stats copy, so coverage costs no host sync.
 //   2. radix sort   - stable sort of (output row, gathered row) pairs by output
 //                     row, only over the bits num_rows needs (skipped when the
 //                     output index is already non-decreasing).
@@ -36,6 +42,7 @@ namespace {
 struct PlanStats {
    unsigned long long out_bad;     // first edge with an out-of-range output index
    unsigned long long gather_bad;  // first edge with an out-of-range gather index
+   unsigned long long covered;     // distinct gathered rows (when marks were requested)
    unsigned int descents;          // warps that saw out_index[e] > out_index[e+1]
    unsigned int not_identity;      // some out_index[e] != e
 };
@@ -44,6 +51,7 @@ __global__ void k_init_stats(PlanStats* st)
 {
    st->out_bad = ULLONG_MAX;
    st->gather_bad = ULLONG_MAX;
+   st->covered = 0;
    st->descents = 0;
    st->not_identity = 0;
 }
@@ -53,14 +61,18 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
                                                        int64_t key_bound, int64_t gat_bound,
                                                        uint32_t* __restrict__ key32,
                                                        int32_t* __restrict__ gat32,
-                                                       PlanStats* __restrict__ st, bool paired)
+                                                       PlanStats* __restrict__ st, bool paired,
+                                                       uint8_t* __restrict__ marks)
 {
    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
    bool descent = false;
    bool moved = false;
    auto check = [&](int64_t e, int64_t k, int64_t g) __attribute__((always_inline)) {
       if(k < 0 || k >= key_bound) atomicMin(&st->out_bad, (unsigned long long)e);
-      if(g < 0 || g >= gat_bound) atomicMin(&st->gather_bad, (unsigned long long)e);
+      if(g < 0 || g >= gat_bound)
+         atomicMin(&st->gather_bad, (unsigned long long)e);
+      else if(marks)
+         marks[g] = 1;  // in bounds: marks holds gat_bound bytes
       moved |= k != e;
    };
    if(paired) {
@@ -100,6 +112,50 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       atomicExch(&st->descents, 1u);
    if(__syncthreads_or(moved) && threadIdx.x == 0 && *((volatile unsigned*)&st->not_identity) == 0u)
       atomicExch(&st->not_identity, 1u);
+}
+
+// Coverage bitmap from the row marks: word w of `cover` gets bit b set when
+// marks[32 w + b] != 0; st->covered += the number of set bits. A thread per
+// word, 16-byte loads (marks is 256-byte aligned), the tail word byte by byte.
+__global__ void __launch_bounds__(kThreads) k_pack_marks(const uint8_t* __restrict__ marks, int64_t rows,
+                                                         uint32_t* __restrict__ cover, PlanStats* __restrict__ st)
+{
+   const int64_t words = (rows + 31) / 32;
+   unsigned long long count = 0;
+   for(int64_t w = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; w < words; w += (int64_t)gridDim.x * blockDim.x) {
+      uint32_t bits = 0;
+      if((w + 1) * 32 <= rows) {
+         const uint4 a = __ldg(reinterpret_cast< const uint4* >(marks) + 2 * w);
+         const uint4 b = __ldg(reinterpret_cast< const uint4* >(marks) + 2 * w + 1);
+         const uint32_t q[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+         for(int i = 0; i < 8; ++i)
+#pragma unroll
+            for(int k = 0; k < 4; ++k) bits |= ((q[i] >> (8 * k)) & 0xffu) ? (1u << (4 * i + k)) : 0u;
+      } else {
+         for(int64_t r = w * 32; r < rows; ++r) bits |= marks[r] ? (1u << (r - w * 32)) : 0u;
+      }
+      cover[w] = bits;
+      count += (unsigned long long)__popc(bits);
+   }
+#pragma unroll
+   for(int off = 16; off > 0; off >>= 1) count += __shfl_down_sync(0xffffffffu, count, off);
+   __shared__ unsigned long long s_count[kThreads / 32];
+   if((threadIdx.x & 31) == 0) s_count[threadIdx.x >> 5] = count;
+   __syncthreads();
+   if(threadIdx.x == 0) {
+      unsigned long long total = 0;
+      for(int i = 0; i < kThreads / 32; ++i) total += s_count[i];
+      if(total) atomicAdd(&st->covered, total);
+   }
+}
+
+// marks[gidx[j]] = 1 for every edge j of a built plan (validated indices).
+__global__ void __launch_bounds__(kThreads) k_mark_gathered(const int32_t* __restrict__ gidx, int64_t n,
+                                                            uint8_t* __restrict__ marks)
+{
+   for(int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
+      marks[__ldg(gidx + j)] = 1;
 }
 
 // Identity output index (out_index[e] == e): row r holds edge r alone for
@@ -260,6 +316,7 @@ PlanLayout plan_layout(void* mem, int64_t num_edges, int64_t num_rows)
 
 struct ScratchLayout {
    PlanStats* stats;
+   uint8_t* marks;  // gathered-row marks (cover_rows bytes), when coverage is requested
    uint32_t* key_in;
    uint32_t* key_alt;
    int32_t* val_alt;
@@ -271,11 +328,12 @@ struct ScratchLayout {
    size_t bytes;
 };
 
-ScratchLayout scratch_layout(void* mem, int64_t num_edges, int64_t num_rows)
+ScratchLayout scratch_layout(void* mem, int64_t num_edges, int64_t num_rows, int64_t cover_rows = 0)
 {
    Carver c(mem);
    ScratchLayout l;
    l.stats = c.take< PlanStats >(1);
+   l.marks = cover_rows > 0 ? c.take< uint8_t >((size_t)cover_rows) : nullptr;
    l.key_in = c.take< uint32_t >((size_t)num_edges);
    l.key_alt = c.take< uint32_t >((size_t)num_edges);
    l.val_alt = c.take< int32_t >((size_t)num_edges);
@@ -315,7 +373,8 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
                        int64_t num_rows, int64_t out_bound, int64_t gather_rows,
                        const char* out_name, const char* gather_name, bool gather_checked_first,
                        void* plan_mem, size_t plan_bytes, void* scratch, size_t scratch_bytes,
-                       cudaStream_t stream, relm_mp_plan* plan)
+                       cudaStream_t stream, relm_mp_plan* plan, uint32_t* cover, int* gather_repeats,
+                       int64_t* gather_covered)
 {
    if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
    if(num_edges < 0 || num_rows < 0 || gather_rows < 0)
@@ -325,13 +384,16 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
          RELM_MP_ERR_UNSUPPORTED, "relm_mp supports num_edges + num_rows < 2^31 and < 2^31 gathered rows."
       );
    if(num_edges > 0 && !out_index) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_index must not be NULL.");
+   if(cover && !gather_repeats) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "gather_repeats must not be NULL.");
    const PlanLayout pl = plan_layout(plan_mem, num_edges, num_rows);
-   const ScratchLayout sl = scratch_layout(scratch, num_edges, num_rows);
+   const ScratchLayout sl = scratch_layout(scratch, num_edges, num_rows, cover ? gather_rows : 0);
    if(!plan_mem || plan_bytes < pl.bytes)
       return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "plan memory is smaller than relm_mp_plan_bytes().");
    if(!scratch || scratch_bytes < sl.bytes)
       return fail(
-         RELM_MP_ERR_WORKSPACE_TOO_SMALL, "plan scratch is smaller than relm_mp_plan_scratch_bytes()."
+         RELM_MP_ERR_WORKSPACE_TOO_SMALL,
+         cover ? "plan scratch is smaller than relm_mp_plan_cover_scratch_bytes()."
+               : "plan scratch is smaller than relm_mp_plan_scratch_bytes()."
       );
    const char* oname = out_name ? out_name : "out_index";
    const char* gname = gather_name ? gather_name : "gather_index";
@@ -350,17 +412,37 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    plan->device_flags = pl.flags;
 
    int rc;
+   // The sort's values ping-pong between val_alt and gidx, one pass per 8 key
+   // bits (CUB onesweep); with an odd pass count the sorted values land in the
+   // plan's gidx when validation writes them to val_alt first.
+   const int sort_passes = (end_bit_for(num_rows) + 7) / 8;
+   int32_t* gather32 = (sort_passes & 1) ? sl.val_alt : pl.gidx;
    k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
    if((rc = check_launch("k_init_stats"))) return rc;
+   if(cover &&
+      (rc = check_cuda(cudaMemsetAsync(sl.marks, 0, (size_t)gather_rows, stream), "marks memset")))
+      return rc;
    if(num_edges > 0) {
       const bool paired = (reinterpret_cast< uintptr_t >(out_index) & 15u) == 0 &&
                           (reinterpret_cast< uintptr_t >(gather_index) & 15u) == 0 &&
                           (reinterpret_cast< uintptr_t >(sl.key_in) & 7u) == 0 &&
-                          (reinterpret_cast< uintptr_t >(pl.gidx) & 7u) == 0;
+                          (reinterpret_cast< uintptr_t >(gather32) & 7u) == 0;
       k_validate<<< grid_for(paired ? num_edges / 2 + 1 : num_edges), kThreads, 0, stream >>>(
-         out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, pl.gidx, sl.stats, paired
+         out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, gather32, sl.stats, paired,
+         cover ? sl.marks : nullptr
       );
       if((rc = check_launch("k_validate"))) return rc;
+   }
+   if(cover) {
+      const int64_t words = (int64_t)relm_mp_cover_words(gather_rows);
+      if(gather_rows > 0) {
+         unsigned grid = grid_for(words);
+         if(grid > 148u * 8u) grid = 148u * 8u;
+         k_pack_marks<<< grid, kThreads, 0, stream >>>(sl.marks, gather_rows, cover, sl.stats);
+         if((rc = check_launch("k_pack_marks"))) return rc;
+      } else if((rc = check_cuda(cudaMemsetAsync(cover, 0, sizeof(uint32_t), stream), "cover memset"))) {
+         return rc;
+      }
    }
    PlanStats host{};
    if((rc = check_cuda(
@@ -398,8 +480,17 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
       );
       return fail(RELM_MP_ERR_INDEX_OUT_OF_RANGE, msg);
    }
+   if(cover) *gather_repeats = host.covered != (unsigned long long)num_edges;
+   if(cover && gather_covered) *gather_covered = (int64_t)host.covered;
+   auto gidx_home = [&]() -> int {  // the unsorted gather values, into the plan's gidx
+      if(gather32 == pl.gidx || num_edges == 0) return RELM_MP_OK;
+      return check_cuda(cudaMemcpyAsync(pl.gidx, gather32, (size_t)num_edges * sizeof(int32_t),
+                                        cudaMemcpyDeviceToDevice, stream),
+                        "gidx copy");
+   };
 
    if(host.not_identity == 0) {  // edge e is row e: no sort, no segment scan
+      if((rc = gidx_home())) return rc;
       plan->flags |= RELM_MP_PLAN_SORTED_INPUT;
       if((rc = check_cuda(cudaMemsetAsync(pl.flags, 0, 4 * sizeof(int32_t), stream), "flags memset"))) return rc;
       unsigned grid = grid_for(num_rows + 1);
@@ -415,9 +506,10 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    const uint32_t* sorted_keys = sl.key_in;
    if(host.descents == 0) {
       plan->flags |= RELM_MP_PLAN_SORTED_INPUT;
+      if((rc = gidx_home())) return rc;
    } else {
       cub::DoubleBuffer< uint32_t > keys(sl.key_in, sl.key_alt);
-      cub::DoubleBuffer< int32_t > vals(pl.gidx, sl.val_alt);
+      cub::DoubleBuffer< int32_t > vals(gather32, gather32 == pl.gidx ? sl.val_alt : pl.gidx);
       size_t temp = sl.sort_bytes;
       if((rc = check_cuda(
              cub::DeviceRadixSort::SortPairs(
@@ -496,6 +588,78 @@ int relm_mp_plan_build(const int64_t* out_index, const int64_t* gather_index, in
       out_index, gather_index, num_edges, num_rows, num_rows, gather_rows, out_index_name,
       gather_index_name, false, plan_mem, plan_bytes, scratch, scratch_bytes,
       static_cast< cudaStream_t >(stream), plan
+   );
+}
+
+size_t relm_mp_plan_gather_cover_scratch_bytes(const relm_mp_plan* plan)
+{
+   if(!plan) return 0;
+   relm_mp::Carver c(nullptr);
+   c.take< relm_mp::PlanStats >(1);
+   c.take< uint8_t >((size_t)plan->gather_rows);
+   return c.used;
+}
+
+int relm_mp_plan_gather_cover_ex(const relm_mp_plan* plan, uint32_t* cover, int* has_dups, int64_t* covered_rows,
+                                 void* scratch, size_t scratch_bytes, void* stream)
+{
+   using namespace relm_mp;
+   if(!plan || !cover || !has_dups) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan, cover and has_dups must not be NULL.");
+   if(!scratch || scratch_bytes < relm_mp_plan_gather_cover_scratch_bytes(plan))
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "scratch is smaller than relm_mp_plan_gather_cover_scratch_bytes().");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   Carver c(scratch);
+   PlanStats* stats = c.take< PlanStats >(1);
+   uint8_t* marks = c.take< uint8_t >((size_t)plan->gather_rows);
+   int rc;
+   k_init_stats<<< 1, 1, 0, st >>>(stats);
+   if((rc = check_launch("k_init_stats"))) return rc;
+   if(plan->gather_rows == 0) {
+      *has_dups = 0;
+      if(covered_rows) *covered_rows = 0;
+      return check_cuda(cudaMemsetAsync(cover, 0, sizeof(uint32_t), st), "cover memset");
+   }
+   if((rc = check_cuda(cudaMemsetAsync(marks, 0, (size_t)plan->gather_rows, st), "marks memset"))) return rc;
+   if(plan->num_edges > 0) {
+      unsigned grid = grid_for(plan->num_edges);
+      if(grid > 148u * 16u) grid = 148u * 16u;
+      k_mark_gathered<<< grid, kThreads, 0, st >>>(plan->gidx, plan->num_edges, marks);
+      if((rc = check_launch("k_mark_gathered"))) return rc;
+   }
+   unsigned grid = grid_for((int64_t)relm_mp_cover_words(plan->gather_rows));
+   if(grid > 148u * 8u) grid = 148u * 8u;
+   k_pack_marks<<< grid, kThreads, 0, st >>>(marks, plan->gather_rows, cover, stats);
+   if((rc = check_launch("k_pack_marks"))) return rc;
+   unsigned long long covered = 0;
+   if((rc = check_cuda(cudaMemcpyAsync(&covered, &stats->covered, sizeof covered, cudaMemcpyDeviceToHost, st),
+                       "cover count copy")))
+      return rc;
+   if((rc = check_cuda(cudaStreamSynchronize(st), "cover sync"))) return rc;
+   *has_dups = covered != (unsigned long long)plan->num_edges;
+   if(covered_rows) *covered_rows = (int64_t)covered;
+   return RELM_MP_OK;
+}
+
+size_t relm_mp_plan_cover_scratch_bytes(int64_t num_edges, int64_t num_rows, int64_t gather_rows)
+{
+   if(num_edges < 0 || num_rows < 0 || gather_rows < 0) return 0;
+   return relm_mp::scratch_layout(nullptr, num_edges, num_rows, gather_rows).bytes;
+}
+
+int relm_mp_plan_build_cover(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                             int64_t num_rows, int64_t out_bound, int64_t gather_rows, const char* out_index_name,
+                             const char* gather_index_name, int gather_checked_first, void* plan_mem,
+                             size_t plan_bytes, void* scratch, size_t scratch_bytes, uint32_t* cover,
+                             int* gather_repeats, int64_t* gather_covered, void* stream, relm_mp_plan* plan)
+{
+   if(out_bound < 0 || out_bound > num_rows)
+      return relm_mp::fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_bound must be in [0, num_rows].");
+   if(!cover || !gather_repeats)
+      return relm_mp::fail(RELM_MP_ERR_INVALID_ARGUMENT, "cover and gather_repeats must not be NULL.");
+   return relm_mp::plan_build_bounded(
+      out_index, gather_index, num_edges, num_rows, out_bound, gather_rows, out_index_name, gather_index_name,
+      gather_checked_first != 0, plan_mem, plan_bytes, scratch, scratch_bytes, static_cast< cudaStream_t >(stream),
+      plan, cover, gather_repeats, gather_covered
    );
 }
 

@@ -140,7 +140,7 @@ int launch_scatter_lse_bwd(const SegParams& p, const uint32_t* cover, int64_t ou
    const unsigned grid = (unsigned)((p.num_tiles * 32 + kThreads - 1) / kThreads);
    k_scatter_lse_bwd_packed< T ><<< grid, kThreads, 0, stream >>>(p);
    int rc = check_launch("k_scatter_lse_bwd_packed");
-   if(rc) return rc;
+   if(rc || !cover) return rc;  // no bitmap: every message row is used by an edge
    int64_t blocks = (out_rows + kThreads - 1) / kThreads;
    const int64_t cap = (int64_t)148 * 8;
    if(blocks > cap) blocks = cap;

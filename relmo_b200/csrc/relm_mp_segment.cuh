@@ -180,23 +180,34 @@ __device__ __forceinline__ void lse_merge(A& m, A& s, A m2, A s2, A k)
    m = mn;
 }
 
-// Folds n <= N values into (m, s): one max pass, one rescale of s and one
-// exponential per value, all as selects (no divergence between lanes).
+// Folds n <= N values into (m, s): one max, one rescale of s and one
+// exponential per value, all as selects (no divergence between lanes). The
+// max and the sum of the exponentials are balanced trees: their dependency
+// chains are log2(N) deep instead of N, which the latency-bound stream kernel
+// notices more than the instruction count.
 template < typename A, int N >
 __device__ __forceinline__ void lse_fold(A& m, A& s, const A (&v)[N], int n, A k)
 {
-   A mr = m;
+   A t[N];
 #pragma unroll
-   for(int i = 0; i < N; ++i)
-      if(i < n) mr = nanmax(mr, v[i]);
+   for(int i = 0; i < N; ++i) t[i] = (i < n) ? v[i] : -(A)INFINITY;
+#pragma unroll
+   for(int w = 1; w < N; w <<= 1)
+#pragma unroll
+      for(int i = 0; i + w < N; i += 2 * w) t[i] = nanmax(t[i], t[i + w]);
+   const A mr = nanmax(m, t[0]);
    // (x - mr) is exact for the maximum itself, so a row's largest value
    // contributes exactly 1 and a single-value row returns that value.
-   A t = s * exp_k(m - mr, k);
+   A e[N];
 #pragma unroll
-   for(int i = 0; i < N; ++i)
-      if(i < n) t += exp_k(v[i] - mr, k);
+   for(int i = 0; i < N; ++i) e[i] = (i < n) ? exp_k(v[i] - mr, k) : A(0);
+#pragma unroll
+   for(int w = 1; w < N; w <<= 1)
+#pragma unroll
+      for(int i = 0; i + w < N; i += 2 * w) e[i] += e[i + w];
+   const A t_sum = s * exp_k(m - mr, k) + e[0];
    const bool only_ninf = mr == -(A)INFINITY;  // every value so far is -inf
-   s = only_ninf ? ((n > 0) ? -fabs(s) : s) : t;
+   s = only_ninf ? ((n > 0) ? -fabs(s) : s) : t_sum;
    m = mr;
 }
 
@@ -1315,10 +1326,18 @@ __device__ __forceinline__ void store_chunk(T* p, const typename AccOf< T >::typ
    }
 }
 
+// Tuning constants of the stream kernel (measured on B200; the values below
+// are the defaults, builds may override them to measure alternatives).
+#ifndef RELM_MP_STREAM_STAGE_BYTES
+#define RELM_MP_STREAM_STAGE_BYTES 4096
+#endif
+#ifndef RELM_MP_STREAM_MIN_BLOCKS
+#define RELM_MP_STREAM_MIN_BLOCKS 7
+#endif
 constexpr int kStreamWarps = 4;
 constexpr int kStreamThreads = kStreamWarps * 32;
 constexpr int kStreamStages = 2;
-constexpr int kStreamStageBytes = 4096;  // per warp, stage and gathered table
+constexpr int kStreamStageBytes = RELM_MP_STREAM_STAGE_BYTES;  // per warp, stage and gathered table
 constexpr int kStreamMeta = 96;         // staged gidx / row-end entries per warp
 
 // Per-warp shared memory: the stages, staged gidx and row ends, and for the
@@ -1346,7 +1365,7 @@ __device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes)
 // that began in an earlier tile go out as head partials, the row still open at
 // the end as the tail partial (combined by k_fixup in tile order).
 template < typename T, int PB, int MODE >
-__global__ void __launch_bounds__(kStreamThreads, 7) k_seg_stream(SegParams p)
+__global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_seg_stream(SegParams p)
 {
    using A = typename AccOf< T >::type;
    constexpr int VN = PB / (int)sizeof(T);

@@ -147,10 +147,12 @@ struct PlanEntry {
    relm_mp_plan plan;
    Tensor cover;         // gather-index coverage bitmap (int32 words), computed on first use
    int cover_dups = -1;  // -1 unknown, 0 each gather row at most once, 1 repeats
+   bool cover_full = false;  // every gather row is used by some edge (nothing to zero)
    int64_t nonempty_rows = -1;  // output rows holding edges, read on first use
    Tensor gather_counts;        // int32 edges per gathered row, computed on first use
    Tensor host_flags;           // pinned copy of the plan's device flags, filled after the build
-   std::shared_ptr< at::cuda::CUDAEvent > flags_copied;
+   std::shared_ptr< at::cuda::CUDAEvent > flags_copied;  // until the flag bits were learned
+   std::shared_ptr< at::cuda::CUDAEvent > flags_event;   // the copy's event (kept for the row count)
 };
 using PlanPtr = std::shared_ptr< PlanEntry >;
 
@@ -166,9 +168,12 @@ class PlanCache {
       return cache;
    }
 
-   // Returns the plan for (out_index, gather_index); builds it on a miss.
+   // Returns the plan for (out_index, gather_index); builds it on a miss. With
+   // want_cover, a build also computes the gather index's coverage in its
+   // validation pass (no separate pass, no extra host sync).
    PlanPtr lookup(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
-                  int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first)
+                  int64_t gather_rows, const char* out_name, const char* gather_name, bool gather_first,
+                  bool want_cover = false)
    {
       const IndexKey ok = IndexKey::of(out_index);
       const IndexKey gk = IndexKey::of(gather_index);
@@ -190,17 +195,32 @@ class PlanCache {
       }
       const int64_t num_edges = out_index.numel();
       Tensor memory = byte_buffer(relm_mp_plan_bytes(num_edges, num_rows), out_index);
-      Tensor scratch = byte_buffer(relm_mp_plan_scratch_bytes(num_edges, num_rows), out_index);
       relm_mp_plan plan;
-      const int rc = relm_mp_plan_build_ex(
-         out_index.data_ptr< int64_t >(), gather_index.data_ptr< int64_t >(), num_edges, num_rows, out_bound,
-         gather_rows, out_name, gather_name, gather_first ? 1 : 0, memory.data_ptr(), (size_t)memory.numel(),
-         scratch.data_ptr(), (size_t)scratch.numel(), stream_of(out_index), &plan
-      );
-      check_status(rc, "plan build");
+      Tensor cover;
+      int repeats = -1;
+      int64_t covered = -1;
+      if(want_cover) {
+         Tensor scratch = byte_buffer(relm_mp_plan_cover_scratch_bytes(num_edges, num_rows, gather_rows), out_index);
+         cover = at::empty({(int64_t)relm_mp_cover_words(gather_rows)}, out_index.options().dtype(at::kInt));
+         const int rc = relm_mp_plan_build_cover(
+            out_index.data_ptr< int64_t >(), gather_index.data_ptr< int64_t >(), num_edges, num_rows, out_bound,
+            gather_rows, out_name, gather_name, gather_first ? 1 : 0, memory.data_ptr(), (size_t)memory.numel(),
+            scratch.data_ptr(), (size_t)scratch.numel(), reinterpret_cast< uint32_t* >(cover.data_ptr< int32_t >()),
+            &repeats, &covered, stream_of(out_index), &plan
+         );
+         check_status(rc, "plan build");
+      } else {
+         Tensor scratch = byte_buffer(relm_mp_plan_scratch_bytes(num_edges, num_rows), out_index);
+         const int rc = relm_mp_plan_build_ex(
+            out_index.data_ptr< int64_t >(), gather_index.data_ptr< int64_t >(), num_edges, num_rows, out_bound,
+            gather_rows, out_name, gather_name, gather_first ? 1 : 0, memory.data_ptr(), (size_t)memory.numel(),
+            scratch.data_ptr(), (size_t)scratch.numel(), stream_of(out_index), &plan
+         );
+         check_status(rc, "plan build");
+      }
       auto entry = std::make_shared< PlanEntry >(
-         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, Tensor(), -1, -1,
-                   Tensor(), Tensor(), nullptr}
+         PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, cover, repeats,
+                   covered == gather_rows, -1, Tensor(), Tensor(), nullptr}
       );
       // The row facts of the plan, to the host without a sync: once the copy
       // has landed, later calls launch only the kernels the plan needs.
@@ -211,6 +231,7 @@ class PlanCache {
       TORCH_CHECK(err == cudaSuccess, "plan flags copy: ", cudaGetErrorString(err));
       entry->flags_copied = std::make_shared< at::cuda::CUDAEvent >();
       entry->flags_copied->record(cs);
+      entry->flags_event = entry->flags_copied;
       std::lock_guard< std::mutex > lock(mu_);
       ++builds_;
       entries_.push_front(entry);
@@ -232,30 +253,42 @@ class PlanCache {
       return nullptr;
    }
 
-   // Output rows of the entry's plan that hold edges (read once per plan).
+   // Output rows of the entry's plan that hold edges (read once per plan):
+   // from the pinned copy of the plan's device flags made after the build,
+   // waiting for that copy only (work queued after the build keeps running).
    int64_t nonempty_rows(const PlanPtr& e, const Tensor& like)
    {
       std::lock_guard< std::mutex > lock(cover_mu_);
       if(e->nonempty_rows < 0) {
-         int64_t rows = 0;
-         check_status(relm_mp_plan_nonempty_rows(&e->plan, &rows, stream_of(like)), "plan row count");
-         e->nonempty_rows = rows;
+         if(e->host_flags.defined() && e->flags_event) {
+            e->flags_event->synchronize();
+            e->nonempty_rows = e->host_flags.data_ptr< int32_t >()[2];
+         } else {
+            int64_t rows = 0;
+            check_status(relm_mp_plan_nonempty_rows(&e->plan, &rows, stream_of(like)), "plan row count");
+            e->nonempty_rows = rows;
+         }
       }
       return e->nonempty_rows;
    }
 
-   // Coverage of the entry's gather index (computed once per plan).
+   // Coverage of the entry's gather index (computed once per plan; a plan
+   // built with want_cover has it already).
    void ensure_cover(const PlanPtr& e, const Tensor& like)
    {
       std::lock_guard< std::mutex > lock(cover_mu_);
       if(e->cover_dups >= 0) return;
       Tensor cover = at::empty({(int64_t)relm_mp_cover_words(e->gather_rows)}, like.options().dtype(at::kInt));
+      Tensor scratch = byte_buffer(relm_mp_plan_gather_cover_scratch_bytes(&e->plan), like);
       int dups = 0;
-      check_status(relm_mp_plan_gather_cover(&e->plan, reinterpret_cast< uint32_t* >(cover.data_ptr< int32_t >()),
-                                             &dups, stream_of(like)),
+      int64_t covered = -1;
+      check_status(relm_mp_plan_gather_cover_ex(&e->plan, reinterpret_cast< uint32_t* >(cover.data_ptr< int32_t >()),
+                                                &dups, &covered, scratch.data_ptr(), (size_t)scratch.numel(),
+                                                stream_of(like)),
                    "gather cover");
       e->cover = cover;
       e->cover_dups = dups;
+      e->cover_full = covered == e->gather_rows;
    }
 
    // Edges per gathered row of the entry's plan (computed once per plan).
@@ -323,8 +356,11 @@ class PlanCache {
    int64_t builds_ = 0;
 };
 
+// The coverage bitmap of the entry's gather index for the scatter kernels, or
+// null when every gather row is covered (they then zero nothing).
 const uint32_t* cover_bits(const PlanPtr& e)
 {
+   if(e->cover_full) return nullptr;
    return reinterpret_cast< const uint32_t* >(e->cover.data_ptr< int32_t >());
 }
 
@@ -364,7 +400,7 @@ Tensor fanout_scatter_cuda(const Tensor& x_cat, const Tensor& src_global_idx, co
    // Source plan (shared with fanout_scatter_backward): each x row is read once
    // and stored into its slots, when every slot is written at most once.
    const PlanPtr sp = PlanCache::get().lookup(
-      src, dst, x.size(0), x.size(0), out_rows, "src_global_idx", "flat_dst", false
+      src, dst, x.size(0), x.size(0), out_rows, "src_global_idx", "flat_dst", false, /*want_cover=*/true
    );
    PlanCache::get().ensure_cover(sp, x);
    if(sp->cover_dups == 0) {

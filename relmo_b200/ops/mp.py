@@ -103,6 +103,15 @@ def fanin_reduce_smoothed_logsumexp(rel_flat, flat_src, dst_idx, dim_size: int, 
 
     require_torch("fanin_reduce_smoothed_logsumexp")
     if route("fanin_reduce_smoothed_logsumexp", rel_flat) == CUSTOM:
+        if rel_flat.dtype in (torch.bfloat16, torch.float16):
+            # The backward weight exp(beta (x - out)) would carry the rounding
+            # of a 2-byte `out` times beta (12: ~25% at bf16's 2^-9); run the op
+            # in fp32 so the gradient sees the fp32 output, and round the
+            # result for the caller.
+            out = _FaninReduceSmoothedLogSumExpFunction.apply(
+                rel_flat.float(), flat_src, dst_idx, int(dim_size), float(beta), float(eps)
+            )
+            return out.to(rel_flat.dtype)
         return _FaninReduceSmoothedLogSumExpFunction.apply(
             rel_flat, flat_src, dst_idx, int(dim_size), float(beta), float(eps)
         )

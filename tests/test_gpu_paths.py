@@ -353,3 +353,39 @@ def test_coverage_pass_keeps_plan_row_flags():
     cover, dups = plan.gather_cover()
     after = capi._device_int32(plan.plan.device_flags, 3, torch.device("cuda")).cpu().tolist()
     assert not dups and before == after and before[0] == 1 and before[1] == 1
+
+
+@pytest.mark.parametrize("gather_rows,edges,repeat", [(1000, 1000, False), (1000, 999, True), (70001, 50000, False),
+                                                      (70001, 50000, True), (33, 0, False), (5, 40, True)])
+def test_gather_coverage_paths_agree(gather_rows, edges, repeat):
+    """The coverage of a plan's gather index three ways: L2 atomics
+    (relm_mp_plan_gather_cover), byte marks packed into the bitmap
+    (relm_mp_plan_gather_cover_ex), and marks written by the build's
+    validation pass (relm_mp_plan_build_cover). Same bitmap, same repeat flag,
+    and both equal to the index's own content; the plans themselves equal the
+    plain build's."""
+
+    from relmo_b200 import capi
+
+    g = torch.Generator(device="cuda").manual_seed(gather_rows + edges)
+    rows = 300
+    out_index = torch.randint(0, rows, (edges,), device="cuda", generator=g)
+    if repeat:
+        gather = torch.randint(0, gather_rows, (edges,), device="cuda", generator=g)
+        if edges > 1:
+            gather[-1] = gather[0]
+    else:
+        gather = torch.randperm(gather_rows, device="cuda", generator=g)[:edges]
+    plain = capi.PlanHandle(out_index, gather, rows, gather_rows)
+    cover_a, dups_a = plain.gather_cover()
+    cover_b, dups_b = plain.gather_cover_ex()
+    built = capi.PlanHandle(out_index, gather, rows, gather_rows, with_cover=True)
+    assert torch.equal(cover_a, cover_b) and torch.equal(cover_a, built.cover)
+    assert dups_a == dups_b == built.repeats == (edges > 0 and gather.unique().numel() < edges)
+    expect = torch.zeros(max(1, (gather_rows + 31) // 32 * 32), dtype=torch.bool, device="cuda")
+    expect[gather] = True
+    bits = torch.tensor([1 << k for k in range(32)], dtype=torch.int64, device="cuda")
+    words = (expect.view(-1, 32).long() * bits).sum(dim=1)
+    assert torch.equal(cover_a.long() & 0xFFFFFFFF, words)
+    assert plain.covered == built.covered == int(gather.unique().numel())
+    assert torch.equal(plain.row_ptr(), built.row_ptr()) and torch.equal(plain.gidx(), built.gidx())
