@@ -34,6 +34,7 @@ TORCH_LIB = PKG / "relm_mp_ops.so"
 
 CUDA_SOURCES = [
     "relm_mp_plan.cu",
+    "relm_mp_sort.cu",
     "relm_mp_ops.cu",
     "relm_mp_seg_f32.cu",
     "relm_mp_seg_f64.cu",

@@ -71,4 +71,16 @@ int fill_value(relm_mp_dtype dtype, void* out, int64_t count, double value, cuda
 
 size_t dtype_size(relm_mp_dtype dtype);
 
+// Stable LSD radix sort of (key, value) pairs by key bits [0, end_bit)
+// (relm_mp_sort.cu). The pairs start in (keys, vals) and end in them, or in
+// (keys_alt, vals_alt) when *in_alt is set (odd pass counts).
+int radix_sort_passes(int end_bit);
+size_t radix_sort_temp_bytes(int64_t n, int end_bit);
+int radix_sort_pairs(uint32_t* keys, uint32_t* keys_alt, int32_t* vals, int32_t* vals_alt, int64_t n, int end_bit,
+                     void* temp, size_t temp_bytes, cudaStream_t stream, bool* in_alt);
+// out = inclusive max-scan of in[0, n) (in == out allowed).
+size_t scan_i32_temp_bytes(int64_t n);
+int scan_max_inclusive(const int32_t* in, int32_t* out, int64_t n, void* temp, size_t temp_bytes,
+                       cudaStream_t stream);
+
 }  // namespace relm_mp

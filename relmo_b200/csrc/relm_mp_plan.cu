@@ -26,9 +26,6 @@
 //   4. k_partition  - merge-path split of the (num_rows + num_edges) items into
 //                     equal tiles, so one hub row spreads over many warps and
 //                     runs of empty rows cost what their output bytes cost.
-#include <cub/device/device_radix_sort.cuh>
-#include <cub/device/device_scan.cuh>
-
 #include <climits>
 #include <cstdio>
 #include <string>
@@ -261,9 +258,6 @@ __global__ void __launch_bounds__(kThreads) k_partition(const int32_t* __restric
    tile_edge[t] = (int32_t)(d - lo);
 }
 
-struct MaxOp {
-   __device__ __forceinline__ int32_t operator()(int32_t a, int32_t b) const { return a > b ? a : b; }
-};
 
 int end_bit_for(int64_t num_rows)
 {
@@ -272,23 +266,6 @@ int end_bit_for(int64_t num_rows)
    return bits;
 }
 
-size_t sort_temp_bytes(int64_t num_edges)
-{
-   size_t bytes = 0;
-   cub::DoubleBuffer< uint32_t > keys(nullptr, nullptr);
-   cub::DoubleBuffer< int32_t > vals(nullptr, nullptr);
-   cub::DeviceRadixSort::SortPairs(nullptr, bytes, keys, vals, (int)num_edges, 0, 32);
-   return bytes;
-}
-
-size_t scan_temp_bytes(int64_t num_rows)
-{
-   size_t bytes = 0;
-   cub::DeviceScan::InclusiveScan(
-      nullptr, bytes, (const int32_t*)nullptr, (int32_t*)nullptr, MaxOp(), (int)(num_rows + 1)
-   );
-   return bytes;
-}
 
 struct PlanLayout {
    int32_t* flags;
@@ -338,9 +315,9 @@ ScratchLayout scratch_layout(void* mem, int64_t num_edges, int64_t num_rows, int
    l.key_alt = c.take< uint32_t >((size_t)num_edges);
    l.val_alt = c.take< int32_t >((size_t)num_edges);
    l.mark = c.take< int32_t >((size_t)num_rows + 1);
-   l.sort_bytes = sort_temp_bytes(num_edges);
+   l.sort_bytes = radix_sort_temp_bytes(num_edges, end_bit_for(num_rows));
    l.sort_temp = c.take< char >(l.sort_bytes);
-   l.scan_bytes = scan_temp_bytes(num_rows);
+   l.scan_bytes = scan_i32_temp_bytes(num_rows + 1);
    l.scan_temp = c.take< char >(l.scan_bytes);
    l.bytes = c.used;
    return l;
@@ -412,10 +389,10 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    plan->device_flags = pl.flags;
 
    int rc;
-   // The sort's values ping-pong between val_alt and gidx, one pass per 8 key
-   // bits (CUB onesweep); with an odd pass count the sorted values land in the
-   // plan's gidx when validation writes them to val_alt first.
-   const int sort_passes = (end_bit_for(num_rows) + 7) / 8;
+   // The sort's values ping-pong between val_alt and gidx, one pass per up to
+   // 11 key bits; with an odd pass count the sorted values land in the plan's
+   // gidx when validation writes them to val_alt first.
+   const int sort_passes = radix_sort_passes(end_bit_for(num_rows));
    int32_t* gather32 = (sort_passes & 1) ? sl.val_alt : pl.gidx;
    k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
    if((rc = check_launch("k_init_stats"))) return rc;
@@ -508,22 +485,17 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
       plan->flags |= RELM_MP_PLAN_SORTED_INPUT;
       if((rc = gidx_home())) return rc;
    } else {
-      cub::DoubleBuffer< uint32_t > keys(sl.key_in, sl.key_alt);
-      cub::DoubleBuffer< int32_t > vals(gather32, gather32 == pl.gidx ? sl.val_alt : pl.gidx);
-      size_t temp = sl.sort_bytes;
-      if((rc = check_cuda(
-             cub::DeviceRadixSort::SortPairs(
-                sl.sort_temp, temp, keys, vals, (int)num_edges, 0, end_bit_for(num_rows), stream
-             ),
-             "radix sort"
-          )))
+      int32_t* val_other = gather32 == pl.gidx ? sl.val_alt : pl.gidx;
+      bool in_alt = false;
+      if((rc = radix_sort_pairs(sl.key_in, sl.key_alt, gather32, val_other, num_edges, end_bit_for(num_rows),
+                                sl.sort_temp, sl.sort_bytes, stream, &in_alt)))
          return rc;
-      sorted_keys = keys.Current();
-      if(vals.Current() != pl.gidx) {
+      sorted_keys = in_alt ? sl.key_alt : sl.key_in;
+      const int32_t* sorted_vals = in_alt ? val_other : gather32;
+      if(sorted_vals != pl.gidx) {
          if((rc = check_cuda(
                 cudaMemcpyAsync(
-                   pl.gidx, vals.Current(), (size_t)num_edges * sizeof(int32_t),
-                   cudaMemcpyDeviceToDevice, stream
+                   pl.gidx, sorted_vals, (size_t)num_edges * sizeof(int32_t), cudaMemcpyDeviceToDevice, stream
                 ),
                 "gidx copy"
              )))
@@ -542,14 +514,7 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
       k_mark_ends<<< grid, kThreads, 0, stream >>>(sorted_keys, num_edges, sl.mark, pl.flags);
       if((rc = check_launch("k_mark_ends"))) return rc;
    }
-   size_t scan_temp = sl.scan_bytes;
-   if((rc = check_cuda(
-          cub::DeviceScan::InclusiveScan(
-             sl.scan_temp, scan_temp, sl.mark, pl.row_ptr, MaxOp(), (int)(num_rows + 1), stream
-          ),
-          "row_ptr scan"
-       )))
-      return rc;
+   if((rc = scan_max_inclusive(sl.mark, pl.row_ptr, num_rows + 1, sl.scan_temp, sl.scan_bytes, stream))) return rc;
    k_partition<<< grid_for(tiles + 1), kThreads, 0, stream >>>(
       pl.row_ptr, num_rows, num_edges, tiles, plan->tile_items, pl.tile_row, pl.tile_edge
    );

@@ -201,7 +201,7 @@ int launch_seg_reduce(const SegParams& pm, int vb_map, int ch_map, const SegPara
    return launch_fixups< T, kLseBwd >(p, stream);
 }
 
-template < typename T, int PB, int MODE >
+template < typename T, int PB, int MODE, bool FULL >
 int launch_stream_shape(const SegParams& p, cudaStream_t stream)
 {
    constexpr int NT = (MODE == kLseBwd) ? 2 : 1;
@@ -210,24 +210,39 @@ int launch_stream_shape(const SegParams& p, cudaStream_t stream)
    if(!configured) {
       const size_t most = (size_t)kStreamWarps * stream_warp_bytes(NT, MODE == kSumEpi);
       const int rc = check_cuda(
-         cudaFuncSetAttribute(k_seg_stream< T, PB, MODE >, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most),
+         cudaFuncSetAttribute(k_seg_stream< T, PB, MODE, FULL >, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)most),
          "k_seg_stream smem attribute"
       );
       if(rc) return rc;
       configured = true;
    }
    const unsigned grid = (unsigned)((p.num_tiles + kStreamWarps - 1) / kStreamWarps);
-   k_seg_stream< T, PB, MODE ><<< grid, kStreamThreads, smem, stream >>>(p);
+   k_seg_stream< T, PB, MODE, FULL ><<< grid, kStreamThreads, smem, stream >>>(p);
    return check_launch("k_seg_stream");
 }
 
+template < typename T, int PB, bool FULL >
+int launch_stream_full(const SegParams& p, int mode, cudaStream_t stream)
+{
+   if(mode == kSum) return launch_stream_shape< T, PB, kSum, FULL >(p, stream);
+   if(mode == kSumEpi) return launch_stream_shape< T, PB, kSumEpi, FULL >(p, stream);
+   if(mode == kLse) return launch_stream_shape< T, PB, kLse, FULL >(p, stream);
+   return launch_stream_shape< T, PB, kLseBwd, FULL >(p, stream);
+}
+
+// Rows of 32 * PB bytes (PB <= 16) take the FULL form of the kernel, whose
+// layout constants match what the host chose for them (choose_stream_shape).
 template < typename T, int PB >
 int launch_stream_mode(const SegParams& p, int mode, cudaStream_t stream)
 {
-   if(mode == kSum) return launch_stream_shape< T, PB, kSum >(p, stream);
-   if(mode == kSumEpi) return launch_stream_shape< T, PB, kSumEpi >(p, stream);
-   if(mode == kLse) return launch_stream_shape< T, PB, kLse >(p, stream);
-   return launch_stream_shape< T, PB, kLseBwd >(p, stream);
+   if constexpr(PB <= 16) {
+      constexpr int cbw = 32 * PB;
+      constexpr int rows = kStreamStageBytes / cbw < 32 ? kStreamStageBytes / cbw : 32;
+      if(p.lanes == 32 && p.col_blocks == 1 && p.block_cols * (int64_t)sizeof(T) == cbw && p.ch == rows &&
+         p.emb * (int64_t)sizeof(T) == cbw)
+         return launch_stream_full< T, PB, true >(p, mode, stream);
+   }
+   return launch_stream_full< T, PB, false >(p, mode, stream);
 }
 
 template < typename T >

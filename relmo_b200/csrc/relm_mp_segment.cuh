@@ -19,6 +19,8 @@
 
 #include <math.h>
 
+#include <type_traits>
+
 #include "relm_mp_internal.cuh"
 
 namespace relm_mp {
@@ -216,6 +218,70 @@ __device__ __forceinline__ void lse_push(A& m, A& s, A v, A k)
 {
    const A one[1] = {v};
    lse_fold< A, 1 >(m, s, one, 1, k);
+}
+
+// Two float columns per instruction: sm_100's packed f32x2 add / multiply /
+// fma round each half like the scalar instruction, so the pair forms below
+// give the scalar folds' results bit for bit in half the issue slots (the
+// stream kernel is issue-bound when a lane holds two columns of a row).
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) { return __fmul2_rn(a, b); }
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+// a - b as fma(b, -1, a): the exact difference, rounded once, like a subtraction.
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) { return __ffma2_rn(b, make_float2(-1.f, -1.f), a); }
+
+// lse_fold< float, N > on two columns at once (m, s, v[i] hold one value of
+// each column): the maxima and exponentials per column, the differences,
+// scalings, the sum tree and the rescale as packed pairs. The running state
+// starts at (-FLT_MAX, 0) rather than (-inf, 0): a floor below every finite
+// value, so -inf values add exp(-inf) = 0 and the state stays (-FLT_MAX, 0)
+// while nothing else was seen, without the selects lse_fold spends on that
+// case per fold (a value of -FLT_MAX itself adds exp(0) = 1). lse_floor_fix
+// turns a state still at the floor back into lse_fold's encoding of it once
+// the number of values folded is known.
+constexpr float kLseFloor = -3.40282346638528859812e+38f;
+template < int N >
+__device__ __forceinline__ void lse_fold2(float2& m, float2& s, const float2 (&v)[N], int n, float k)
+{
+   const float ninf = -INFINITY;
+   float2 t[N];
+#pragma unroll
+   for(int i = 0; i < N; ++i) t[i] = (i < n) ? v[i] : make_float2(ninf, ninf);
+#pragma unroll
+   for(int w = 1; w < N; w <<= 1)
+#pragma unroll
+      for(int i = 0; i + w < N; i += 2 * w) t[i] = make_float2(nanmax(t[i].x, t[i + w].x), nanmax(t[i].y, t[i + w].y));
+   const float2 mr = make_float2(nanmax(m.x, t[0].x), nanmax(m.y, t[0].y));
+   const float2 k2 = make_float2(k, k);
+   float2 e[N];
+#pragma unroll
+   for(int i = 0; i < N; ++i) {
+      if(i < n) {
+         const float2 d = mul2(sub2(v[i], mr), k2);
+         e[i] = make_float2(exp2_fast(d.x), exp2_fast(d.y));
+      } else {
+         e[i] = make_float2(0.f, 0.f);
+      }
+   }
+#pragma unroll
+   for(int w = 1; w < N; w <<= 1)
+#pragma unroll
+      for(int i = 0; i + w < N; i += 2 * w) e[i] = add2(e[i], e[i + w]);
+   // (floor - mr) * k is -inf or a large negative number once mr is finite,
+   // and exp2 of it 0; s is 0 there anyway
+   const float2 d = mul2(sub2(m, mr), k2);
+   s = fma2(s, make_float2(exp2_fast(d.x), exp2_fast(d.y)), e[0]);
+   m = mr;
+}
+
+// A state of lse_fold2 after `count` values, in lse_fold's encoding: still at
+// the floor means no value (+0) or only -inf values (-0) with m = -inf.
+__device__ __forceinline__ void lse_floor_fix(float& m, float& s, int count)
+{
+   if(m == kLseFloor && s == 0.f) {
+      m = -INFINITY;
+      s = count > 0 ? -0.f : 0.f;
+   }
 }
 
 struct SegParams {
@@ -1334,9 +1400,12 @@ __device__ __forceinline__ void store_chunk(T* p, const typename AccOf< T >::typ
 #ifndef RELM_MP_STREAM_MIN_BLOCKS
 #define RELM_MP_STREAM_MIN_BLOCKS 7
 #endif
+#ifndef RELM_MP_STREAM_STAGES
+#define RELM_MP_STREAM_STAGES 2
+#endif
 constexpr int kStreamWarps = 4;
 constexpr int kStreamThreads = kStreamWarps * 32;
-constexpr int kStreamStages = 2;
+constexpr int kStreamStages = RELM_MP_STREAM_STAGES;
 constexpr int kStreamStageBytes = RELM_MP_STREAM_STAGE_BYTES;  // per warp, stage and gathered table
 constexpr int kStreamMeta = 96;         // staged gidx / row-end entries per warp
 
@@ -1364,12 +1433,22 @@ __device__ __forceinline__ void prefetch_l2(const void* p, unsigned bytes)
 // fold walks the edges in order, finishing rows as it crosses their ends; rows
 // that began in an earlier tile go out as head partials, the row still open at
 // the end as the tail partial (combined by k_fixup in tile order).
-template < typename T, int PB, int MODE >
+//
+// FULL: rows of exactly 32 * PB bytes (one column block, all 32 lanes): the
+// block width, rows per stage and the copy layout are compile-time constants,
+// so a full batch issues its copies unrolled and every shared load of the
+// fold takes an immediate offset.
+template < typename T, int PB, int MODE, bool FULL >
 __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_seg_stream(SegParams p)
 {
    using A = typename AccOf< T >::type;
    constexpr int VN = PB / (int)sizeof(T);
    constexpr int NT = (MODE == kLseBwd) ? 2 : 1;
+   // float accumulators, an even number of columns per lane: the folds work on column pairs
+   constexpr bool kPairs = sizeof(A) == 4 && VN % 2 == 0;
+   // logsumexp on column pairs: running states start at the floor (lse_fold2)
+   constexpr bool kFloor = kPairs && MODE == kLse;
+   static_assert(!FULL || PB <= 16, "FULL rows take at most 32 16-byte chunks");
    extern __shared__ __align__(16) unsigned char smem[];
    const int wib = threadIdx.x >> 5;
    const int lane = threadIdx.x & 31;
@@ -1385,10 +1464,15 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
    int32_t* sg = reinterpret_cast< int32_t* >(wbase + NT * kStreamStages * kStreamStageBytes);
    int32_t* sr = sg + kStreamMeta;
    A* sdv = reinterpret_cast< A* >(sr + kStreamMeta);  // kSumEpi: divisor of row rbase + i
-   const int CBW = (int)p.block_cols * (int)sizeof(T);  // bytes of a column block
-   const int B = p.ch;                                   // rows per stage
-   const bool lane_ok = lane < p.lanes;
-   const int64_t row_bytes = p.emb * (int64_t)sizeof(T);
+   constexpr int kFullCBW = 32 * PB;
+   constexpr int kFullB = (kStreamStageBytes / kFullCBW) < 32 ? (kStreamStageBytes / kFullCBW) : 32;
+   const int CBW = FULL ? kFullCBW : (int)p.block_cols * (int)sizeof(T);  // bytes of a column block
+   const int B = FULL ? kFullB : p.ch;                                     // rows per stage
+   const bool lane_ok = FULL || lane < p.lanes;
+   const int64_t row_bytes = FULL ? (int64_t)kFullCBW : p.emb * (int64_t)sizeof(T);
+   const int ncb = FULL ? 1 : p.col_blocks;
+   constexpr int kFullChunks = kFullCBW / 16;  // copies of 16 bytes per row
+   constexpr int kFullCopies = kFullB / (kFullChunks <= 32 ? 32 / kFullChunks : 1);  // per lane and full batch
    const int r_begin = p.tile_row[tile];
    const int j_begin = p.tile_edge[tile];
    const int r_end = p.tile_row[tile + 1];
@@ -1409,18 +1493,47 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
    int head_row = -1;
    int tail_row = -1;
 
-   for(int cb = 0; cb < p.col_blocks; ++cb) {
+   for(int cb = 0; cb < ncb; ++cb) {
       const int64_t cbyte = (int64_t)cb * CBW;
       const int64_t col = (cbyte + (int64_t)lane * PB) / (int64_t)sizeof(T);
       int gbase = j_begin, gcount = 0;
       int rbase = r_begin, rcount = 0;
+      // The window after the staged one (gidx entries, row ends) is loaded into
+      // registers when a window is staged: the next refill stores values that
+      // arrived long before instead of waiting on global loads.
+      constexpr int MQ = kStreamMeta / 32;
+      int32_t g_next[MQ], r_next[MQ];
+      int g_next_at = -1, r_next_at = -1;
+      auto prefetch_g = [&](int j) __attribute__((always_inline)) {
+         g_next_at = j;
+#pragma unroll
+         for(int q = 0; q < MQ; ++q) {
+            const int i = j + lane + 32 * q;
+            g_next[q] = i < j_end ? p.gidx[i] : 0;
+         }
+      };
+      auto prefetch_r = [&](int R0) __attribute__((always_inline)) {
+         r_next_at = R0;
+#pragma unroll
+         for(int q = 0; q < MQ; ++q) {
+            const int R1 = R0 + lane + 32 * q;
+            r_next[q] = R1 < r_end ? p.row_ptr[R1 + 1] : 0;
+         }
+      };
       auto row_end = [&](int R) __attribute__((always_inline)) -> int {
          if(R - rbase >= rcount) {
             __syncwarp();
             rbase = R;
             rcount = (r_end - R) < kStreamMeta ? (r_end - R) : kStreamMeta;
+            if(R == r_next_at) {
+#pragma unroll
+               for(int q = 0; q < MQ; ++q)
+                  if(lane + 32 * q < rcount) sr[lane + 32 * q] = r_next[q];
+            } else {
+               for(int i = lane; i < rcount; i += 32) sr[i] = p.row_ptr[R + 1 + i];
+            }
+            if(R + rcount < r_end) prefetch_r(R + rcount);
             for(int i = lane; i < rcount; i += 32) {
-               sr[i] = p.row_ptr[R + 1 + i];
                if(PF && p.epi_div) {
                   const A dv = (A)p.epi_div[R + i];
                   sdv[i] = dv > A(1) ? dv : A(1);
@@ -1450,12 +1563,27 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
                __syncwarp();
                gbase = j0;
                gcount = (j_end - j0) < kStreamMeta ? (j_end - j0) : kStreamMeta;
-               for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j0 + i];
+               if(j0 == g_next_at) {
+#pragma unroll
+                  for(int q = 0; q < MQ; ++q)
+                     if(lane + 32 * q < gcount) sg[lane + 32 * q] = g_next[q];
+               } else {
+                  for(int i = lane; i < gcount; i += 32) sg[i] = p.gidx[j0 + i];
+               }
+               if(j0 + gcount < j_end) prefetch_g(j0 + gcount);
                __syncwarp();
             }
             unsigned char* st = wbase + (k % kStreamStages) * kStreamStageBytes;
             const int32_t* sgb = sg + (j0 - gbase);
-            if(chunks <= 32) {
+            if(FULL && nb == B) {
+               const unsigned sa = s_lane + (unsigned)((k % kStreamStages) * kStreamStageBytes);
+#pragma unroll
+               for(int i = 0; i < kFullCopies; ++i) {
+                  const uint64_t off = (uint64_t)(unsigned)sgb[b_first + i * rpi] * rbytes;
+                  cp_async16_s(sa + 512u * i, g_lane + off);
+                  if(NT == 2) cp_async16_s(sa + 512u * i + (unsigned)(kStreamStages * kStreamStageBytes), g2_lane + off);
+               }
+            } else if(chunks <= 32) {
                unsigned sa = s_lane + (unsigned)((k % kStreamStages) * kStreamStageBytes);
                for(int b = b_first; b < nb; b += rpi, sa += 512u) {
                   const uint64_t off = (uint64_t)(unsigned)sgb[b] * rbytes;
@@ -1499,6 +1627,7 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
             }
          }
       };
+      if(kFloor) e_rstart = j_begin;  // the open row's first edge in this tile
       if(PF) {
          if(cb == 0 && lane == 0 && p.epi_base) {  // this tile's base rows, to L2
             const int r_last = r_end < (int)p.num_rows ? r_end : (int)p.num_rows - 1;
@@ -1512,7 +1641,7 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
    do {                                                         \
       _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_)          \
       {                                                         \
-         acc[k_] = (MODE == kLse) ? ninf : A(0);                \
+         acc[k_] = (MODE == kLse) ? (kFloor ? (A)kLseFloor : ninf) : A(0); \
          aux[k_] = A(0);                                        \
       }                                                         \
    } while(0)
@@ -1521,10 +1650,13 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
    do {                                                                                         \
       const bool head_ = ((R_) == r_begin) && began_before;                                     \
       int cnt_ = 0;                                                                             \
-      if(PF) { /* RE_: row_end(R_), which also holds R_'s divisor in the staged window */       \
+      if(PF || kFloor) { /* RE_: row_end(R_), which also holds R_'s divisor (PF) */           \
          const int re_ = (RE_);                                                                 \
          cnt_ = re_ - e_rstart;                                                                 \
          e_rstart = re_;                                                                        \
+      }                                                                                         \
+      if constexpr(kFloor) {                                                                    \
+         _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_) lse_floor_fix(acc[k_], aux[k_], cnt_); \
       }                                                                                         \
       if(lane_ok) {                                                                             \
          if(head_) {                                                                            \
@@ -1589,6 +1721,49 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
 #pragma unroll
                      for(int x = 0; x < VN; ++x) acc[x] += v[x] * exp_k(ownv[x] - w[x], LF.k);
                   }
+               } else if constexpr(kPairs) {
+                  // folds of 8, then 4, then the last 1..3 edges of the run (one rescale each)
+                  auto fold = [&](auto width, int q0, int nval) __attribute__((always_inline)) {
+                     constexpr int N = decltype(width)::value;
+                     A v[N][VN];
+#pragma unroll
+                     for(int i = 0; i < N; ++i) {
+                        if(i < nval) {
+                           load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q0 + i) * CBW), v[i]);
+                        } else {
+#pragma unroll
+                           for(int x = 0; x < VN; ++x) v[i][x] = (sum_mode(MODE)) ? A(0) : ninf;
+                        }
+                     }
+#pragma unroll
+                     for(int x = 0; x < VN; x += 2) {
+                        float2 vx[N];
+#pragma unroll
+                        for(int i = 0; i < N; ++i) vx[i] = make_float2(v[i][x], v[i][x + 1]);
+                        float2 a = make_float2(acc[x], acc[x + 1]);
+                        if(sum_mode(MODE)) {
+#pragma unroll
+                           for(int w = 1; w < N; w <<= 1)
+#pragma unroll
+                              for(int i = 0; i + w < N; i += 2 * w) vx[i] = add2(vx[i], vx[i + w]);
+                           a = add2(a, vx[0]);
+                        } else {
+                           float2 sx = make_float2(aux[x], aux[x + 1]);
+                           lse_fold2< N >(a, sx, vx, nval, LF.k);
+                           aux[x] = sx.x;
+                           aux[x + 1] = sx.y;
+                        }
+                        acc[x] = a.x;
+                        acc[x + 1] = a.y;
+                     }
+                  };
+                  int q = 0;
+                  for(; q + 8 <= run; q += 8) fold(std::integral_constant< int, 8 >{}, q, 8);
+                  if(q + 4 <= run) {
+                     fold(std::integral_constant< int, 4 >{}, q, 4);
+                     q += 4;
+                  }
+                  if(q < run) fold(std::integral_constant< int, 3 >{}, q, run - q);
                } else {
                   int q = 0;
                   for(; q + 4 <= run; q += 4) {
@@ -1644,6 +1819,10 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
 #undef RELM_MP_STREAM_FLUSH
 #undef RELM_MP_STREAM_RESET
       if(pending) {
+         if constexpr(kFloor) {
+#pragma unroll
+            for(int k = 0; k < VN; ++k) lse_floor_fix(acc[k], aux[k], j_end - e_rstart);
+         }
          if(lane_ok) {
             const int64_t off = tile * p.emb + col;
 #pragma unroll

@@ -1,0 +1,494 @@
+// Plan-build sort and scans, written for the plan's shapes:
+//
+//   radix_sort_pairs - stable LSD radix sort of (uint32 key, int32 value)
+//                      pairs over the key bits a plan needs (the output row,
+//                      < num_rows), in as few passes of at most 10 bits as the
+//                      width allows: 2 passes for up to 2^20 rows, 3 for up to
+//                      2^30 (10-bit digits keep two CTAs per SM and runs of
+//                      about 8 items per digit and sub-tile; 11-bit digits
+//                      measured slower on 2^22 rows). Each pass is
+//                        k_sort_hist    digit counts of every CTA's item range,
+//                                       laid out digit-major [digit][cta];
+//                        exclusive scan of those counts -> every (digit, CTA)
+//                                       pair's first output position;
+//                        k_sort_scatter each CTA walks its range in sub-tiles
+//                                       of 8192 items: a warp ranks its 512
+//                                       items in order (ballots group equal
+//                                       digits, per-warp counters), the
+//                                       sub-tile is reordered by digit in
+//                                       shared memory and written out in
+//                                       digit runs with coalesced stores.
+//                      Items keep their input order within a digit (ranks
+//                      follow item order within warps, warps, sub-tiles and
+//                      CTAs), so the sort is stable and the plan's edge order
+//                      within a row is the input order, run to run.
+//   scan_i32         - exclusive sum or inclusive max scan of int32 arrays
+//                      (reduce per block, scan of the block totals, apply).
+//
+// No atomics on global memory, no inter-CTA waiting.
+#include <climits>
+
+#include "relm_mp_internal.cuh"
+
+namespace relm_mp {
+
+namespace {
+
+constexpr int kSortThreads = 512;
+constexpr int kSortWarps = kSortThreads / 32;
+constexpr int kSortPerThread = 16;
+constexpr int kSortSub = kSortThreads * kSortPerThread;  // items per sub-tile
+#ifndef RELM_MP_SORT_MAX_BITS
+#define RELM_MP_SORT_MAX_BITS 10
+#endif
+constexpr int kSortMaxBits = RELM_MP_SORT_MAX_BITS;  // digit bits per pass
+constexpr int kScanThreads = 512;
+constexpr int kScanPerThread = 8;
+constexpr int kScanChunk = kScanThreads * kScanPerThread;
+
+struct SumOp {
+   static constexpr int32_t identity = 0;
+   __device__ __forceinline__ int32_t operator()(int32_t a, int32_t b) const { return a + b; }
+};
+struct MaxOp32 {
+   static constexpr int32_t identity = INT_MIN;
+   __device__ __forceinline__ int32_t operator()(int32_t a, int32_t b) const { return a > b ? a : b; }
+};
+
+// Exclusive scan of one value per thread over the block; *total gets the
+// reduction of all of them. `wtot` holds one entry per warp (shared memory).
+template < class Op >
+__device__ __forceinline__ int32_t block_exclusive(int32_t v, int32_t* wtot, int32_t* total)
+{
+   const Op op;
+   const int lane = threadIdx.x & 31;
+   const int w = threadIdx.x >> 5;
+   const int nw = blockDim.x >> 5;
+   int32_t x = v;
+#pragma unroll
+   for(int o = 1; o < 32; o <<= 1) {
+      const int32_t y = __shfl_up_sync(0xffffffffu, x, o);
+      if(lane >= o) x = op(x, y);
+   }
+   int32_t excl = __shfl_up_sync(0xffffffffu, x, 1);
+   if(lane == 0) excl = Op::identity;
+   if(lane == 31) wtot[w] = x;
+   __syncthreads();
+   if(w == 0) {
+      int32_t t = lane < nw ? wtot[lane] : Op::identity;
+#pragma unroll
+      for(int o = 1; o < 32; o <<= 1) {
+         const int32_t y = __shfl_up_sync(0xffffffffu, t, o);
+         if(lane >= o) t = op(t, y);
+      }
+      if(lane < nw) wtot[lane] = t;
+   }
+   __syncthreads();
+   const int32_t before = w > 0 ? wtot[w - 1] : Op::identity;
+   *total = wtot[nw - 1];
+   __syncthreads();  // wtot may be reused right away
+   return op(before, excl);
+}
+
+// ---- scan -----------------------------------------------------------------------------
+
+template < class Op >
+__global__ void __launch_bounds__(kScanThreads) k_scan_reduce(const int32_t* __restrict__ in, int64_t n,
+                                                              int32_t* __restrict__ part)
+{
+   __shared__ int32_t wtot[kScanThreads / 32];
+   const Op op;
+   const int64_t base = (int64_t)blockIdx.x * kScanChunk + (int64_t)threadIdx.x * kScanPerThread;
+   int32_t acc = Op::identity;
+#pragma unroll
+   for(int i = 0; i < kScanPerThread; ++i)
+      if(base + i < n) acc = op(acc, in[base + i]);
+   int32_t total;
+   block_exclusive< Op >(acc, wtot, &total);
+   if(threadIdx.x == 0) part[blockIdx.x] = total;
+}
+
+// Exclusive scan of part[0, nb) in place, one block.
+template < class Op >
+__global__ void __launch_bounds__(kScanThreads) k_scan_top(int32_t* __restrict__ part, int64_t nb)
+{
+   __shared__ int32_t wtot[kScanThreads / 32];
+   const Op op;
+   int32_t carry = Op::identity;
+   for(int64_t b0 = 0; b0 < nb; b0 += kScanThreads) {
+      const int64_t i = b0 + threadIdx.x;
+      const int32_t v = i < nb ? part[i] : Op::identity;
+      int32_t total;
+      const int32_t ex = block_exclusive< Op >(v, wtot, &total);
+      if(i < nb) part[i] = op(carry, ex);
+      carry = op(carry, total);
+   }
+}
+
+template < class Op, bool INCLUSIVE >
+__global__ void __launch_bounds__(kScanThreads) k_scan_apply(const int32_t* __restrict__ in, int64_t n,
+                                                             const int32_t* __restrict__ part,
+                                                             int32_t* __restrict__ out)
+{
+   __shared__ int32_t wtot[kScanThreads / 32];
+   const Op op;
+   const int64_t base = (int64_t)blockIdx.x * kScanChunk + (int64_t)threadIdx.x * kScanPerThread;
+   int32_t v[kScanPerThread];
+   int32_t acc = Op::identity;
+#pragma unroll
+   for(int i = 0; i < kScanPerThread; ++i) {
+      v[i] = base + i < n ? in[base + i] : Op::identity;
+      acc = op(acc, v[i]);
+   }
+   int32_t total;
+   int32_t run = op(part[blockIdx.x], block_exclusive< Op >(acc, wtot, &total));
+#pragma unroll
+   for(int i = 0; i < kScanPerThread; ++i) {
+      if(base + i < n) {
+         if(INCLUSIVE) {
+            run = op(run, v[i]);
+            out[base + i] = run;
+         } else {
+            out[base + i] = run;
+            run = op(run, v[i]);
+         }
+      }
+   }
+}
+
+int64_t scan_blocks(int64_t n) { return (n + kScanChunk - 1) / kScanChunk; }
+
+// ---- radix sort -----------------------------------------------------------------------
+
+struct SortShape {
+   int passes;
+   int bits[32];
+   int shift[32];
+   int subs;      // sub-tiles per CTA
+   int64_t ctas;  // CTAs of a pass (the same item ranges in the histogram and the scatter)
+};
+
+SortShape sort_shape(int64_t n, int end_bit)
+{
+   SortShape s{};
+   if(end_bit < 1) end_bit = 1;
+   s.passes = (end_bit + kSortMaxBits - 1) / kSortMaxBits;
+   int done = 0;
+   for(int i = 0; i < s.passes; ++i) {
+      const int left = end_bit - done;
+      const int b = (left + (s.passes - i) - 1) / (s.passes - i);
+      s.bits[i] = b;
+      s.shift[i] = done;
+      done += b;
+   }
+   // about two CTAs per SM, at most 16 sub-tiles each
+   const int64_t sub_tiles = (n + kSortSub - 1) / kSortSub;
+   int64_t subs = (sub_tiles + 2 * 148 - 1) / (2 * 148);
+   if(subs < 1) subs = 1;
+   if(subs > 16) subs = 16;
+   s.subs = (int)subs;
+   s.ctas = (sub_tiles + subs - 1) / subs;
+   if(s.ctas < 1) s.ctas = 1;
+   return s;
+}
+
+// Lanes of the warp holding the same digit d (< 2^DB) as this lane, or d == 2^DB
+// (an invalid lane, matched with the other invalid lanes only): one ballot per
+// digit bit instead of match.any, which is slow with many distinct values.
+template < int DB >
+__device__ __forceinline__ unsigned same_digit_lanes(unsigned d)
+{
+   unsigned peers = 0xffffffffu;
+#pragma unroll
+   for(int b = 0; b <= DB; ++b) {
+      const unsigned bal = __ballot_sync(0xffffffffu, (d >> b) & 1u);
+      peers &= ((d >> b) & 1u) ? bal : ~bal;
+   }
+   return peers;
+}
+
+__device__ __forceinline__ unsigned lanemask_lt()
+{
+   unsigned m;
+   asm("mov.u32 %0, %%lanemask_lt;" : "=r"(m));
+   return m;
+}
+
+// Digit counts of CTA c's items [c * subs * kSortSub, ...): ghist[d * ctas + c].
+// Each sub-tile's keys are loaded up front (16 independent loads per thread)
+// and counted with shared-memory atomics into 4 sub-histograms (warp mod 4),
+// which spreads the collisions of a hot digit over more addresses.
+template < int DB >
+__global__ void __launch_bounds__(kSortThreads) k_sort_hist(const uint32_t* __restrict__ keys, int64_t n, int shift,
+                                                            int32_t* __restrict__ ghist, int64_t ctas, int subs)
+{
+   constexpr int D = 1 << DB;
+   __shared__ int32_t h[4][D];
+   for(int d = threadIdx.x; d < 4 * D; d += kSortThreads) (&h[0][0])[d] = 0;
+   __syncthreads();
+   const int lane = threadIdx.x & 31;
+   const int w = threadIdx.x >> 5;
+   int32_t* hw = h[w & 3];
+   const int64_t c = blockIdx.x;
+   for(int sub = 0; sub < subs; ++sub) {
+      const int64_t base = (c * subs + sub) * (int64_t)kSortSub;
+      if(base >= n) break;
+      const int subn = (n - base) < kSortSub ? (int)(n - base) : kSortSub;
+      uint32_t k[kSortPerThread];
+#pragma unroll
+      for(int r = 0; r < kSortPerThread; ++r) {
+         const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
+         k[r] = idx < subn ? __ldg(keys + base + idx) : 0u;
+      }
+#pragma unroll
+      for(int r = 0; r < kSortPerThread; ++r) {
+         const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
+         if(idx < subn) atomicAdd(&hw[(k[r] >> shift) & (D - 1)], 1);
+      }
+   }
+   __syncthreads();
+   for(int d = threadIdx.x; d < D; d += kSortThreads)
+      ghist[(int64_t)d * ctas + c] = h[0][d] + h[1][d] + h[2][d] + h[3][d];
+}
+
+template < int DB >
+constexpr size_t scatter_smem()
+{
+   constexpr int D = 1 << DB;
+   // staged keys + values, per-warp u16 counters, run / sub-tile start / total per digit, warp totals
+   return (size_t)kSortSub * 8 + (size_t)kSortWarps * D * 2 + (size_t)3 * D * 4 + 32 * 4;
+}
+
+// Two CTAs per SM where the shared memory allows it (digits of up to 10 bits):
+// the values are read again at the reordering step instead of being held in
+// registers through the ranking.
+template < int DB >
+__global__ void __launch_bounds__(kSortThreads, DB <= 10 ? 2 : 1) k_sort_scatter(const uint32_t* __restrict__ kin,
+                                                               const int32_t* __restrict__ vin,
+                                                               uint32_t* __restrict__ kout,
+                                                               int32_t* __restrict__ vout, int64_t n, int shift,
+                                                               const int32_t* __restrict__ goff, int64_t ctas,
+                                                               int subs)
+{
+   constexpr int D = 1 << DB;
+   constexpr int DPT = (D + kSortThreads - 1) / kSortThreads;  // digits per thread in the digit loops
+   extern __shared__ __align__(16) unsigned char sm[];
+   uint32_t* skey = reinterpret_cast< uint32_t* >(sm);
+   int32_t* sval = reinterpret_cast< int32_t* >(skey + kSortSub);
+   // [warp][digit] counts, then prefixes (16-byte aligned: zeroed with 16-byte stores)
+   uint16_t* wh = reinterpret_cast< uint16_t* >(sval + kSortSub);
+   int32_t* run = reinterpret_cast< int32_t* >(wh + kSortWarps * D);  // global position of the CTA's next item of digit d
+   int32_t* sstart = run + D;  // first local position of digit d in the reordered sub-tile
+   int32_t* tot = sstart + D;  // items of digit d in the sub-tile
+   int32_t* wtot = tot + D;
+   const int tid = threadIdx.x;
+   const int lane = tid & 31;
+   const int w = tid >> 5;
+   const int64_t c = blockIdx.x;
+   for(int d = tid; d < D; d += kSortThreads) run[d] = goff[(int64_t)d * ctas + c];
+   uint16_t* myh = wh + w * D;
+   const unsigned lt = lanemask_lt();
+   for(int sub = 0; sub < subs; ++sub) {
+      const int64_t base = (c * subs + sub) * (int64_t)kSortSub;
+      if(base >= n) break;
+      const int subn = (n - base) < kSortSub ? (int)(n - base) : kSortSub;
+      for(int i = tid; i < kSortWarps * D / 8; i += kSortThreads)
+         reinterpret_cast< uint4* >(wh)[i] = make_uint4(0u, 0u, 0u, 0u);
+      uint32_t k[kSortPerThread];
+#pragma unroll
+      for(int r = 0; r < kSortPerThread; ++r) {
+         const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
+         k[r] = idx < subn ? __ldg(kin + base + idx) : 0u;
+      }
+      __syncthreads();  // counters zeroed
+      // rank each item among the earlier items of its warp with the same digit
+      uint16_t rank[kSortPerThread];
+#pragma unroll
+      for(int r = 0; r < kSortPerThread; ++r) {
+         const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
+         const bool valid = idx < subn;
+         const unsigned d = valid ? (k[r] >> shift) & (D - 1) : (unsigned)D;
+         const unsigned peers = same_digit_lanes< DB >(d);
+         const int leader = __ffs(peers) - 1;
+         int b = 0;
+         if(valid && lane == leader) {
+            b = myh[d];
+            myh[d] = (uint16_t)(b + __popc(peers));
+         }
+         b = __shfl_sync(0xffffffffu, b, leader);
+         rank[r] = (uint16_t)(b + __popc(peers & lt));
+         __syncwarp();
+      }
+      __syncthreads();
+      // per digit: prefix over the warps (in warp order) and the sub-tile total
+#pragma unroll
+      for(int j = 0; j < DPT; ++j) {
+         const int d = tid + j * kSortThreads;
+         if(d < D) {
+            int acc = 0;
+#pragma unroll
+            for(int ww = 0; ww < kSortWarps; ++ww) {
+               const int cnt = wh[ww * D + d];
+               wh[ww * D + d] = (uint16_t)acc;
+               acc += cnt;
+            }
+            tot[d] = acc;
+         }
+      }
+      __syncthreads();
+      // local digit starts: exclusive scan of the totals, DPT consecutive digits per thread
+      {
+         int32_t t[DPT];
+         int32_t sum = 0;
+#pragma unroll
+         for(int j = 0; j < DPT; ++j) {
+            const int d = tid * DPT + j;
+            t[j] = d < D ? tot[d] : 0;
+            sum += t[j];
+         }
+         int32_t total;
+         int32_t ex = block_exclusive< SumOp >(sum, wtot, &total);
+#pragma unroll
+         for(int j = 0; j < DPT; ++j) {
+            const int d = tid * DPT + j;
+            if(d < D) sstart[d] = ex;
+            ex += t[j];
+         }
+      }
+      __syncthreads();
+#pragma unroll
+      for(int r = 0; r < kSortPerThread; ++r) {
+         const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
+         if(idx < subn) {
+            const unsigned d = (k[r] >> shift) & (D - 1);
+            const int lp = sstart[d] + myh[d] + rank[r];
+            skey[lp] = k[r];
+            sval[lp] = __ldg(vin + base + idx);
+         }
+      }
+      __syncthreads();
+      for(int i = tid; i < subn; i += kSortThreads) {
+         const uint32_t key = skey[i];
+         const unsigned d = (key >> shift) & (D - 1);
+         const int64_t pos = (int64_t)run[d] + (i - sstart[d]);
+         kout[pos] = key;
+         vout[pos] = sval[i];
+      }
+      __syncthreads();
+      for(int d = tid; d < D; d += kSortThreads) run[d] += tot[d];
+      __syncthreads();
+   }
+}
+
+template < class Op, bool INCLUSIVE >
+int scan_launch(const int32_t* in, int32_t* out, int64_t n, int32_t* part, cudaStream_t stream)
+{
+   if(n <= 0) return RELM_MP_OK;
+   const int64_t nb = scan_blocks(n);
+   k_scan_reduce< Op ><<< (unsigned)nb, kScanThreads, 0, stream >>>(in, n, part);
+   int rc;
+   if((rc = check_launch("k_scan_reduce"))) return rc;
+   k_scan_top< Op ><<< 1, kScanThreads, 0, stream >>>(part, nb);
+   if((rc = check_launch("k_scan_top"))) return rc;
+   k_scan_apply< Op, INCLUSIVE ><<< (unsigned)nb, kScanThreads, 0, stream >>>(in, n, part, out);
+   return check_launch("k_scan_apply");
+}
+
+template < int DB >
+int sort_pass(const uint32_t* kin, const int32_t* vin, uint32_t* kout, int32_t* vout, int64_t n, int shift,
+              const SortShape& s, int32_t* ghist, int32_t* part, cudaStream_t stream)
+{
+   constexpr int D = 1 << DB;
+   static bool configured = false;  // one attribute call per instantiation (per process)
+   if(!configured) {
+      const int rc = check_cuda(
+         cudaFuncSetAttribute(k_sort_scatter< DB >, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              (int)scatter_smem< DB >()),
+         "k_sort_scatter smem attribute"
+      );
+      if(rc) return rc;
+      configured = true;
+   }
+   int rc;
+   k_sort_hist< DB ><<< (unsigned)s.ctas, kSortThreads, 0, stream >>>(kin, n, shift, ghist, s.ctas, s.subs);
+   if((rc = check_launch("k_sort_hist"))) return rc;
+   if((rc = scan_launch< SumOp, false >(ghist, ghist, (int64_t)D * s.ctas, part, stream))) return rc;
+   k_sort_scatter< DB ><<< (unsigned)s.ctas, kSortThreads, scatter_smem< DB >(), stream >>>(
+      kin, vin, kout, vout, n, shift, ghist, s.ctas, s.subs
+   );
+   return check_launch("k_sort_scatter");
+}
+
+int sort_pass_bits(int bits, const uint32_t* kin, const int32_t* vin, uint32_t* kout, int32_t* vout, int64_t n,
+                   int shift, const SortShape& s, int32_t* ghist, int32_t* part, cudaStream_t stream)
+{
+   switch(bits) {
+      case 1: return sort_pass< 1 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 2: return sort_pass< 2 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 3: return sort_pass< 3 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 4: return sort_pass< 4 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 5: return sort_pass< 5 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 6: return sort_pass< 6 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 7: return sort_pass< 7 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 8: return sort_pass< 8 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 9: return sort_pass< 9 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 10: return sort_pass< 10 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      case 11: return sort_pass< 11 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
+      default: return fail(RELM_MP_ERR_UNSUPPORTED, "radix sort digit width out of range.");
+   }
+}
+
+}  // namespace
+
+int radix_sort_passes(int end_bit)
+{
+   const int b = end_bit < 1 ? 1 : end_bit;
+   return (b + kSortMaxBits - 1) / kSortMaxBits;
+}
+
+size_t radix_sort_temp_bytes(int64_t n, int end_bit)
+{
+   const SortShape s = sort_shape(n, end_bit);
+   int maxbits = 0;
+   for(int i = 0; i < s.passes; ++i) maxbits = s.bits[i] > maxbits ? s.bits[i] : maxbits;
+   const int64_t counters = ((int64_t)1 << maxbits) * s.ctas;
+   return align_up((size_t)counters * 4) + align_up((size_t)scan_blocks(counters) * 4);
+}
+
+int radix_sort_pairs(uint32_t* keys, uint32_t* keys_alt, int32_t* vals, int32_t* vals_alt, int64_t n, int end_bit,
+                     void* temp, size_t temp_bytes, cudaStream_t stream, bool* in_alt)
+{
+   *in_alt = false;
+   if(n <= 1) return RELM_MP_OK;
+   if(temp_bytes < radix_sort_temp_bytes(n, end_bit))
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "radix sort scratch too small");
+   const SortShape s = sort_shape(n, end_bit);
+   int maxbits = 0;
+   for(int i = 0; i < s.passes; ++i) maxbits = s.bits[i] > maxbits ? s.bits[i] : maxbits;
+   const int64_t counters = ((int64_t)1 << maxbits) * s.ctas;
+   Carver cv(temp);
+   int32_t* ghist = cv.take< int32_t >((size_t)counters);
+   int32_t* part = cv.take< int32_t >((size_t)scan_blocks(counters));
+   uint32_t* kb[2] = {keys, keys_alt};
+   int32_t* vb[2] = {vals, vals_alt};
+   int cur = 0;
+   for(int i = 0; i < s.passes; ++i) {
+      const int rc = sort_pass_bits(s.bits[i], kb[cur], vb[cur], kb[cur ^ 1], vb[cur ^ 1], n, s.shift[i], s, ghist,
+                                    part, stream);
+      if(rc) return rc;
+      cur ^= 1;
+   }
+   *in_alt = cur == 1;
+   return RELM_MP_OK;
+}
+
+size_t scan_i32_temp_bytes(int64_t n) { return align_up((size_t)scan_blocks(n) * 4 + 4); }
+
+int scan_max_inclusive(const int32_t* in, int32_t* out, int64_t n, void* temp, size_t temp_bytes,
+                       cudaStream_t stream)
+{
+   if(temp_bytes < scan_i32_temp_bytes(n)) return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "scan scratch too small");
+   return scan_launch< MaxOp32, true >(in, out, n, static_cast< int32_t* >(temp), stream);
+}
+
+}  // namespace relm_mp

@@ -1,0 +1,97 @@
+"""Plan layout on the GPU against numpy: the plan's gathered-row order is the
+stable sort of the edges by output row (edge order kept within a row), and
+row_ptr[r] is the number of edges with output row < r.
+
+The cases reach every sort shape of the plan build: one radix pass (up to 11
+key bits), two passes of 10 and 11 bits (cfg2's 2^20 rows, cfg5's 2^22), three
+passes (2^23 and more rows), sub-tile and CTA boundaries of the sort (8192
+items per sub-tile), one hot row holding most edges (Zipf), all edges in one
+row, reversed and already sorted output indices, and the identity.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from relmo_b200 import capi
+from relmo_b200.ops import mp
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True, scope="module")
+def _load_library():
+    assert mp.available(), "relm_mp library not loadable"
+
+
+def _expect(out_index: np.ndarray, gather: np.ndarray, rows: int):
+    order = np.argsort(out_index, kind="stable")
+    gidx = gather[order]
+    row_ptr = np.searchsorted(out_index[order], np.arange(rows + 1), side="left")
+    return gidx, row_ptr
+
+
+def _check(out_index: torch.Tensor, gather: torch.Tensor | None, rows: int, gather_rows: int):
+    plan = capi.PlanHandle(out_index.cuda(), None if gather is None else gather.cuda(), rows, gather_rows)
+    torch.cuda.synchronize()
+    o = out_index.numpy()
+    g = np.arange(o.size) if gather is None else gather.numpy()
+    want_gidx, want_ptr = _expect(o, g, rows)
+    assert np.array_equal(plan.row_ptr().numpy(), want_ptr)
+    assert np.array_equal(plan.gidx().numpy(), want_gidx)
+
+
+def _zipf(rows: int, edges: int, gen: torch.Generator, alpha: float = 1.3) -> torch.Tensor:
+    ranks = torch.arange(1, rows + 1, dtype=torch.float64)
+    w = ranks.pow(-alpha)
+    pick = torch.multinomial(w, edges, replacement=True, generator=gen)
+    perm = torch.randperm(rows, generator=gen)
+    return perm[pick]
+
+
+CASES = [
+    # (rows, edges, kind)
+    (1, 1000, "uniform"),
+    (2, 8191, "uniform"),
+    (3, 8193, "uniform"),
+    (100, 100_000, "uniform"),
+    (2047, 70_000, "uniform"),
+    (2048, 16_384, "uniform"),
+    (2049, 300_000, "zipf"),
+    (1 << 20, 1 << 21, "zipf"),
+    (1 << 20, 3_000_001, "uniform"),
+    ((1 << 22) + 5, 1 << 21, "uniform"),
+    ((1 << 23) + 1, 1 << 20, "uniform"),
+    (1 << 20, 1 << 20, "reversed"),
+    (5000, 1 << 20, "one_row"),
+    (1 << 16, 1 << 20, "sorted_runs"),
+]
+
+
+@pytest.mark.parametrize("rows,edges,kind", CASES)
+def test_plan_matches_stable_sort(rows: int, edges: int, kind: str) -> None:
+    gen = torch.Generator().manual_seed(rows * 31 + edges)
+    if kind == "uniform":
+        out = torch.randint(0, rows, (edges,), generator=gen)
+    elif kind == "zipf":
+        out = _zipf(rows, edges, gen)
+    elif kind == "reversed":
+        out = torch.arange(edges - 1, -1, -1) % rows
+    elif kind == "one_row":
+        out = torch.full((edges,), rows // 2, dtype=torch.int64)
+        out[:: 997] = torch.randint(0, rows, (out[:: 997].numel(),), generator=gen)
+    else:  # runs of equal rows in order, then a few out of order
+        out = torch.sort(torch.randint(0, rows, (edges,), generator=gen)).values
+        out[-10:] = torch.randint(0, rows, (10,), generator=gen)
+    gather_rows = edges + 7
+    gather = torch.randint(0, gather_rows, (edges,), generator=gen)
+    _check(out, gather, rows, gather_rows)
+
+
+def test_identity_gather_and_already_sorted() -> None:
+    gen = torch.Generator().manual_seed(5)
+    out = torch.sort(torch.randint(0, 1 << 18, (1 << 20,), generator=gen)).values
+    _check(out, None, 1 << 18, 1 << 20)
+    _check(torch.arange(1 << 20), None, 1 << 20, 1 << 20)
