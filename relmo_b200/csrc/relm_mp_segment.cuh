@@ -1448,6 +1448,10 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
    constexpr bool kPairs = sizeof(A) == 4 && VN % 2 == 0;
    // logsumexp on column pairs: running states start at the floor (lse_fold2)
    constexpr bool kFloor = kPairs && MODE == kLse;
+   // the flush counts each row's edges in the tile (rows without any are written
+   // straight from the empty-row value: most rows of a Zipf fan-in are empty);
+   // kSumEpi rows take their base row instead
+   constexpr bool kCount = MODE != kSumEpi;
    static_assert(!FULL || PB <= 16, "FULL rows take at most 32 16-byte chunks");
    extern __shared__ __align__(16) unsigned char smem[];
    const int wib = threadIdx.x >> 5;
@@ -1627,7 +1631,11 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
             }
          }
       };
-      if(kFloor) e_rstart = j_begin;  // the open row's first edge in this tile
+      if(kCount) e_rstart = j_begin;  // the open row's first edge in this tile
+      // value of a row without edges (the reduction of nothing)
+      A empty_[VN];
+#pragma unroll
+      for(int k_ = 0; k_ < VN; ++k_) empty_[k_] = (MODE == kLse) ? LF.empty : A(0);
       if(PF) {
          if(cb == 0 && lane == 0 && p.epi_base) {  // this tile's base rows, to L2
             const int r_last = r_end < (int)p.num_rows ? r_end : (int)p.num_rows - 1;
@@ -1650,10 +1658,14 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
    do {                                                                                         \
       const bool head_ = ((R_) == r_begin) && began_before;                                     \
       int cnt_ = 0;                                                                             \
-      if(PF || kFloor) { /* RE_: row_end(R_), which also holds R_'s divisor (PF) */           \
+      if(PF || kCount) { /* RE_: row_end(R_), which also holds R_'s divisor (PF) */           \
          const int re_ = (RE_);                                                                 \
          cnt_ = re_ - e_rstart;                                                                 \
          e_rstart = re_;                                                                        \
+      }                                                                                         \
+      if(kCount && cnt_ == 0 && !head_) { /* no edge: the empty-row value, state untouched */  \
+         if(lane_ok) store_chunk< T, PB >(out + (int64_t)(R_)*p.emb + col, empty_);             \
+         break;                                                                                 \
       }                                                                                         \
       if constexpr(kFloor) {                                                                    \
          _Pragma("unroll") for(int k_ = 0; k_ < VN; ++k_) lse_floor_fix(acc[k_], aux[k_], cnt_); \
