@@ -234,6 +234,29 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
                                       void* plan_mem, size_t plan_bytes, void* scratch,
                                       size_t scratch_bytes, void* stream, relm_mp_plan* plan);
 
+/* relm_mp_plan_build_ex in two halves, so that the builds of several plans
+ * (the three or four index pairs of one LGAN op) share one host wait:
+ * relm_mp_plan_build_start validates the indices and queues the copy of the
+ * validation's result into `host_stats` (pinned host memory of
+ * relm_mp_plan_stats_bytes() bytes); once the caller has waited for `stream`
+ * (once for every build it started), relm_mp_plan_build_finish, with the same
+ * arguments, memory and scratch, raises the index error if there was one and
+ * lays the plan out without another wait. plan_mem, scratch and host_stats
+ * must stay untouched between the two calls. No counterpart in the
+ * reference (its ops keep no plans). */
+RELM_MP_API size_t relm_mp_plan_stats_bytes(void);
+RELM_MP_API int relm_mp_plan_build_start(const int64_t* out_index, const int64_t* gather_index,
+                                         int64_t num_edges, int64_t num_rows, int64_t out_bound,
+                                         int64_t gather_rows, void* plan_mem, size_t plan_bytes,
+                                         void* scratch, size_t scratch_bytes, void* host_stats, void* stream);
+RELM_MP_API int relm_mp_plan_build_finish(const int64_t* out_index, const int64_t* gather_index,
+                                          int64_t num_edges, int64_t num_rows, int64_t out_bound,
+                                          int64_t gather_rows, const char* out_index_name,
+                                          const char* gather_index_name, int gather_checked_first,
+                                          void* plan_mem, size_t plan_bytes, void* scratch,
+                                          size_t scratch_bytes, const void* host_stats, void* stream,
+                                          relm_mp_plan* plan);
+
 /* relm_mp_plan_build_ex that also computes the coverage of the gather index
  * over [0, gather_rows) in its validation pass: bit g of `cover` (device
  * uint32 [relm_mp_cover_words(gather_rows)], the layout of

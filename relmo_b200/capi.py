@@ -107,6 +107,12 @@ SIGNATURES: dict[str, tuple] = {
         _INT,
         [_P, _P, _I64, _I64, _I64, _I64, _STR, _STR, _INT, _P, _SZ, _P, _SZ, _P, _PLANP],
     ),
+    "relm_mp_plan_stats_bytes": (_SZ, []),
+    "relm_mp_plan_build_start": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _SZ, _P, _P]),
+    "relm_mp_plan_build_finish": (
+        _INT,
+        [_P, _P, _I64, _I64, _I64, _I64, _STR, _STR, _INT, _P, _SZ, _P, _SZ, _P, _P, _PLANP],
+    ),
     "relm_mp_plan_reduce_scratch_bytes": (_SZ, [_PLANP, _I64, _INT, _INT]),
     "relm_mp_plan_read_flags": (_INT, [_PLANP, _P]),
     "relm_mp_plan_gather_last": (_INT, [_PLANP, _INT, _P, _I64, _P, _P]),

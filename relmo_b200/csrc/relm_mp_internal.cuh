@@ -55,12 +55,18 @@ struct Carver {
 
 // Builds a plan with a separate validation bound for the output index
 // (`out_bound` <= num_rows; rows >= out_bound may exist but receive no edges).
+// kBuildStart validates and queues the copy of the statistics into host_stats
+// (pinned host memory), kBuildFinish (same arguments, after the caller waited
+// for the stream) checks them and lays the plan out; kBuildAll does both with
+// its own wait.
+enum BuildPhase : int { kBuildAll = 0, kBuildStart = 1, kBuildFinish = 2 };
 int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
                        int64_t num_rows, int64_t out_bound, int64_t gather_rows,
                        const char* out_name, const char* gather_name, bool gather_checked_first,
                        void* plan_mem, size_t plan_bytes, void* scratch, size_t scratch_bytes,
                        cudaStream_t stream, relm_mp_plan* plan, uint32_t* cover = nullptr,
-                       int* gather_repeats = nullptr, int64_t* gather_covered = nullptr);
+                       int* gather_repeats = nullptr, int64_t* gather_covered = nullptr,
+                       BuildPhase phase = kBuildAll, void* host_stats = nullptr);
 
 int64_t plan_num_tiles(int64_t num_edges, int64_t num_rows);
 

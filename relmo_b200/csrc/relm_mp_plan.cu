@@ -351,9 +351,10 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
                        const char* out_name, const char* gather_name, bool gather_checked_first,
                        void* plan_mem, size_t plan_bytes, void* scratch, size_t scratch_bytes,
                        cudaStream_t stream, relm_mp_plan* plan, uint32_t* cover, int* gather_repeats,
-                       int64_t* gather_covered)
+                       int64_t* gather_covered, BuildPhase phase, void* host_stats)
 {
    if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   if(phase != kBuildAll && !host_stats) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "host_stats must not be NULL.");
    if(num_edges < 0 || num_rows < 0 || gather_rows < 0)
       return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan sizes must be >= 0.");
    if(num_edges + num_rows >= (int64_t)INT32_MAX || gather_rows >= (int64_t)INT32_MAX)
@@ -394,40 +395,48 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    // gidx when validation writes them to val_alt first.
    const int sort_passes = radix_sort_passes(end_bit_for(num_rows));
    int32_t* gather32 = (sort_passes & 1) ? sl.val_alt : pl.gidx;
-   k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
-   if((rc = check_launch("k_init_stats"))) return rc;
-   if(cover &&
-      (rc = check_cuda(cudaMemsetAsync(sl.marks, 0, (size_t)gather_rows, stream), "marks memset")))
-      return rc;
-   if(num_edges > 0) {
-      const bool paired = (reinterpret_cast< uintptr_t >(out_index) & 15u) == 0 &&
-                          (reinterpret_cast< uintptr_t >(gather_index) & 15u) == 0 &&
-                          (reinterpret_cast< uintptr_t >(sl.key_in) & 7u) == 0 &&
-                          (reinterpret_cast< uintptr_t >(gather32) & 7u) == 0;
-      k_validate<<< grid_for(paired ? num_edges / 2 + 1 : num_edges), kThreads, 0, stream >>>(
-         out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, gather32, sl.stats, paired,
-         cover ? sl.marks : nullptr
-      );
-      if((rc = check_launch("k_validate"))) return rc;
-   }
-   if(cover) {
-      const int64_t words = (int64_t)relm_mp_cover_words(gather_rows);
-      if(gather_rows > 0) {
-         unsigned grid = grid_for(words);
-         if(grid > 148u * 8u) grid = 148u * 8u;
-         k_pack_marks<<< grid, kThreads, 0, stream >>>(sl.marks, gather_rows, cover, sl.stats);
-         if((rc = check_launch("k_pack_marks"))) return rc;
-      } else if((rc = check_cuda(cudaMemsetAsync(cover, 0, sizeof(uint32_t), stream), "cover memset"))) {
+   // The validation's statistics reach the host through `host`: the build's
+   // own (synchronous) copy, or the caller's pinned buffer when the build is
+   // split (start: validate and queue the copy; finish: after the caller's
+   // wait, check them and lay the plan out).
+   PlanStats local{};
+   PlanStats& host = phase == kBuildAll ? local : *static_cast< PlanStats* >(host_stats);
+   if(phase != kBuildFinish) {
+      k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
+      if((rc = check_launch("k_init_stats"))) return rc;
+      if(cover &&
+         (rc = check_cuda(cudaMemsetAsync(sl.marks, 0, (size_t)gather_rows, stream), "marks memset")))
          return rc;
+      if(num_edges > 0) {
+         const bool paired = (reinterpret_cast< uintptr_t >(out_index) & 15u) == 0 &&
+                             (reinterpret_cast< uintptr_t >(gather_index) & 15u) == 0 &&
+                             (reinterpret_cast< uintptr_t >(sl.key_in) & 7u) == 0 &&
+                             (reinterpret_cast< uintptr_t >(gather32) & 7u) == 0;
+         k_validate<<< grid_for(paired ? num_edges / 2 + 1 : num_edges), kThreads, 0, stream >>>(
+            out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, gather32, sl.stats, paired,
+            cover ? sl.marks : nullptr
+         );
+         if((rc = check_launch("k_validate"))) return rc;
       }
-   }
-   PlanStats host{};
-   if((rc = check_cuda(
-          cudaMemcpyAsync(&host, sl.stats, sizeof(PlanStats), cudaMemcpyDeviceToHost, stream),
-          "plan stats copy"
-       )))
-      return rc;
-   if((rc = check_cuda(cudaStreamSynchronize(stream), "plan stats sync"))) return rc;
+      if(cover) {
+         const int64_t words = (int64_t)relm_mp_cover_words(gather_rows);
+         if(gather_rows > 0) {
+            unsigned grid = grid_for(words);
+            if(grid > 148u * 8u) grid = 148u * 8u;
+            k_pack_marks<<< grid, kThreads, 0, stream >>>(sl.marks, gather_rows, cover, sl.stats);
+            if((rc = check_launch("k_pack_marks"))) return rc;
+         } else if((rc = check_cuda(cudaMemsetAsync(cover, 0, sizeof(uint32_t), stream), "cover memset"))) {
+            return rc;
+         }
+      }
+      if((rc = check_cuda(
+             cudaMemcpyAsync(&host, sl.stats, sizeof(PlanStats), cudaMemcpyDeviceToHost, stream),
+             "plan stats copy"
+          )))
+         return rc;
+      if(phase == kBuildStart) return RELM_MP_OK;
+      if((rc = check_cuda(cudaStreamSynchronize(stream), "plan stats sync"))) return rc;
+   }  // validation
 
    if(host.out_bad != ULLONG_MAX || host.gather_bad != ULLONG_MAX) {
       bool use_gather;
@@ -625,6 +634,37 @@ int relm_mp_plan_build_cover(const int64_t* out_index, const int64_t* gather_ind
       out_index, gather_index, num_edges, num_rows, out_bound, gather_rows, out_index_name, gather_index_name,
       gather_checked_first != 0, plan_mem, plan_bytes, scratch, scratch_bytes, static_cast< cudaStream_t >(stream),
       plan, cover, gather_repeats, gather_covered
+   );
+}
+
+size_t relm_mp_plan_stats_bytes(void) { return sizeof(relm_mp::PlanStats); }
+
+int relm_mp_plan_build_start(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                             int64_t num_rows, int64_t out_bound, int64_t gather_rows, void* plan_mem,
+                             size_t plan_bytes, void* scratch, size_t scratch_bytes, void* host_stats, void* stream)
+{
+   if(out_bound < 0 || out_bound > num_rows)
+      return relm_mp::fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_bound must be in [0, num_rows].");
+   relm_mp_plan plan;
+   return relm_mp::plan_build_bounded(
+      out_index, gather_index, num_edges, num_rows, out_bound, gather_rows, nullptr, nullptr, false, plan_mem,
+      plan_bytes, scratch, scratch_bytes, static_cast< cudaStream_t >(stream), &plan, nullptr, nullptr, nullptr,
+      relm_mp::kBuildStart, host_stats
+   );
+}
+
+int relm_mp_plan_build_finish(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                              int64_t num_rows, int64_t out_bound, int64_t gather_rows, const char* out_index_name,
+                              const char* gather_index_name, int gather_checked_first, void* plan_mem,
+                              size_t plan_bytes, void* scratch, size_t scratch_bytes, const void* host_stats,
+                              void* stream, relm_mp_plan* plan)
+{
+   if(out_bound < 0 || out_bound > num_rows)
+      return relm_mp::fail(RELM_MP_ERR_INVALID_ARGUMENT, "out_bound must be in [0, num_rows].");
+   return relm_mp::plan_build_bounded(
+      out_index, gather_index, num_edges, num_rows, out_bound, gather_rows, out_index_name, gather_index_name,
+      gather_checked_first != 0, plan_mem, plan_bytes, scratch, scratch_bytes, static_cast< cudaStream_t >(stream),
+      plan, nullptr, nullptr, nullptr, relm_mp::kBuildFinish, const_cast< void* >(host_stats)
    );
 }
 

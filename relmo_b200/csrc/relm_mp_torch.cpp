@@ -222,21 +222,76 @@ class PlanCache {
          PlanEntry{ok, gk, num_rows, out_bound, gather_rows, (int)gather_first, memory, plan, cover, repeats,
                    covered == gather_rows, -1, Tensor(), Tensor(), nullptr}
       );
-      // The row facts of the plan, to the host without a sync: once the copy
-      // has landed, later calls launch only the kernels the plan needs.
-      entry->host_flags = at::empty({4}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
-      const c10::cuda::CUDAStream cs = at::cuda::getCurrentCUDAStream(out_index.device().index());
-      const cudaError_t err = cudaMemcpyAsync(entry->host_flags.data_ptr(), plan.device_flags, 4 * sizeof(int32_t),
-                                              cudaMemcpyDeviceToHost, cs.stream());
-      TORCH_CHECK(err == cudaSuccess, "plan flags copy: ", cudaGetErrorString(err));
-      entry->flags_copied = std::make_shared< at::cuda::CUDAEvent >();
-      entry->flags_copied->record(cs);
-      entry->flags_event = entry->flags_copied;
-      std::lock_guard< std::mutex > lock(mu_);
-      ++builds_;
-      entries_.push_front(entry);
-      while(entries_.size() > capacity_) entries_.pop_back();
-      return entry;
+      return insert(entry, out_index);
+   }
+
+   // One request of prebuild: the arguments of lookup (no coverage).
+   struct Request {
+      const Tensor* out_index;
+      const Tensor* gather_index;
+      int64_t num_rows;
+      int64_t out_bound;
+      int64_t gather_rows;
+      const char* out_name;
+      const char* gather_name;
+      bool gather_first;
+   };
+
+   // Builds the plans of the requests that are not cached yet with one host
+   // wait for all of them (relm_mp_plan_build_start / _finish): the index
+   // validations run back to back, their results come to the host with one
+   // sync, then the layouts are queued. Index errors are raised in request
+   // order, so the first failing request gives the error a build of each in
+   // turn would have given.
+   void prebuild(const std::vector< Request >& reqs)
+   {
+      struct Pending {
+         const Request* r;
+         Tensor memory, scratch, stats;
+      };
+      std::vector< Pending > todo;
+      for(const Request& r : reqs) {
+         if(r.out_index->numel() == 0) continue;
+         if(peek(*r.out_index, *r.gather_index, r.num_rows, r.out_bound, r.gather_rows)) continue;
+         bool dup = false;  // the same pair twice in one call
+         for(const Pending& q : todo)
+            if(q.r->out_index->is_same(*r.out_index) && q.r->gather_index->is_same(*r.gather_index) &&
+               q.r->num_rows == r.num_rows && q.r->out_bound == r.out_bound && q.r->gather_rows == r.gather_rows)
+               dup = true;
+         if(dup) continue;
+         const int64_t e = r.out_index->numel();
+         Pending q{&r, byte_buffer(relm_mp_plan_bytes(e, r.num_rows), *r.out_index),
+                   byte_buffer(relm_mp_plan_scratch_bytes(e, r.num_rows), *r.out_index),
+                   at::empty({(int64_t)relm_mp_plan_stats_bytes()}, at::TensorOptions().dtype(at::kByte).pinned_memory(true))};
+         check_status(relm_mp_plan_build_start(
+                         r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
+                         e, r.num_rows, r.out_bound, r.gather_rows, q.memory.data_ptr(), (size_t)q.memory.numel(),
+                         q.scratch.data_ptr(), (size_t)q.scratch.numel(), q.stats.data_ptr(), stream_of(*r.out_index)),
+                      "plan build");
+         todo.push_back(std::move(q));
+      }
+      if(todo.empty()) return;
+      {
+         const cudaError_t err = cudaStreamSynchronize(static_cast< cudaStream_t >(stream_of(*todo.front().r->out_index)));
+         TORCH_CHECK(err == cudaSuccess, "plan build sync: ", cudaGetErrorString(err));
+      }
+      for(Pending& q : todo) {
+         const Request& r = *q.r;
+         const int64_t e = r.out_index->numel();
+         relm_mp_plan plan;
+         check_status(relm_mp_plan_build_finish(
+                         r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
+                         e, r.num_rows, r.out_bound, r.gather_rows, r.out_name, r.gather_name, r.gather_first ? 1 : 0,
+                         q.memory.data_ptr(), (size_t)q.memory.numel(), q.scratch.data_ptr(), (size_t)q.scratch.numel(),
+                         q.stats.data_ptr(), stream_of(*r.out_index), &plan),
+                      "plan build");
+         auto entry = std::make_shared< PlanEntry >(
+            PlanEntry{IndexKey::of(*r.out_index), IndexKey::of(*r.gather_index), r.num_rows,
+                      r.out_bound, r.gather_rows, (int)r.gather_first, q.memory, plan, Tensor(), -1, false, -1,
+                      Tensor(), Tensor(), nullptr}
+         );
+         insert(entry, *r.out_index);
+      }
    }
 
    // The cached plan for the pair, or null (never builds).
@@ -330,6 +385,26 @@ class PlanCache {
 
  private:
    // Sets the plan's host flag bits once the copy of its device flags landed.
+   // Adds a built plan: queues the copy of its device flags to pinned host
+   // memory (no sync; once it has landed, later calls launch only the kernels
+   // the plan needs) and puts the entry at the front of the cache.
+   PlanPtr insert(const PlanPtr& entry, const Tensor& like)
+   {
+      entry->host_flags = at::empty({4}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
+      const c10::cuda::CUDAStream cs = at::cuda::getCurrentCUDAStream(like.device().index());
+      const cudaError_t err = cudaMemcpyAsync(entry->host_flags.data_ptr(), entry->plan.device_flags,
+                                              4 * sizeof(int32_t), cudaMemcpyDeviceToHost, cs.stream());
+      TORCH_CHECK(err == cudaSuccess, "plan flags copy: ", cudaGetErrorString(err));
+      entry->flags_copied = std::make_shared< at::cuda::CUDAEvent >();
+      entry->flags_copied->record(cs);
+      entry->flags_event = entry->flags_copied;
+      std::lock_guard< std::mutex > lock(mu_);
+      ++builds_;
+      entries_.push_front(entry);
+      while(entries_.size() > capacity_) entries_.pop_back();
+      return entry;
+   }
+
    static void learn_flags(PlanEntry& e)
    {
       if((e.plan.flags & RELM_MP_PLAN_FLAGS_KNOWN) || !e.flags_copied || !e.flags_copied->query()) return;
@@ -1040,11 +1115,43 @@ void lgan_reverse_agg(relm_mp_dtype dt, const Tensor& grad, const Tensor& src, c
    planned_sum_ex(e, dt, table, base, nullptr, false, out, op);
 }
 
+// The plans of a graph step's forward aggregations (after `first`, the slot
+// pooling's, when given), built with one host wait; the conditions are
+// lgan_forward_agg's, so exactly the plans it would build are built, in its order.
+void lgan_prebuild_forward(const LganIndices& ix, int64_t R, int64_t N, int64_t emb,
+                           const PlanCache::Request* first = nullptr)
+{
+   std::vector< PlanCache::Request > reqs;
+   if(first) reqs.push_back(*first);
+   if(emb > 0) {
+      if(ix.rr_src.numel() > 0 && R > 0) reqs.push_back({&ix.rr_dst, &ix.rr_src, R, R, R, "rr_dst", "rr_src", false});
+      if(ix.tn_rel.numel() > 0 && N > 0) reqs.push_back({&ix.tn_ent, &ix.tn_rel, N, N, R, "tn_ent", "tn_rel", false});
+      if(ix.nn_rel.numel() > 0 && N > 0) reqs.push_back({&ix.nn_ent, &ix.nn_rel, N, N, R, "nn_ent", "nn_rel", false});
+   }
+   PlanCache::get().prebuild(reqs);
+}
+
+// The same for the backward's reverse aggregations (lgan_reverse_agg's
+// conditions and order), then `last`, the slot gradient's pooling plan.
+void lgan_prebuild_backward(const LganIndices& ix, int64_t R, int64_t n_tn, int64_t n_nn, int64_t emb,
+                            const PlanCache::Request* last = nullptr)
+{
+   std::vector< PlanCache::Request > reqs;
+   if(emb > 0 && R > 0) {
+      if(ix.tn_rel.numel() > 0) reqs.push_back({&ix.tn_rel, &ix.tn_ent, R, R, n_tn, "tn_rel", "tn_ent", false});
+      if(ix.nn_rel.numel() > 0) reqs.push_back({&ix.nn_rel, &ix.nn_ent, R, R, n_nn, "nn_rel", "nn_ent", false});
+      if(ix.rr_src.numel() > 0) reqs.push_back({&ix.rr_src, &ix.rr_dst, R, R, R, "rr_src", "rr_dst", false});
+   }
+   if(last) reqs.push_back(*last);
+   PlanCache::get().prebuild(reqs);
+}
+
 // x1 = x + agg_rr(x); tn = agg_tn(x1); nn = agg_nn(x1)
 std::tuple< Tensor, Tensor, Tensor > lgan_graph_forward(relm_mp_dtype dt, const Tensor& x, const LganIndices& ix,
                                                         int64_t entity_dim_size, bool mean, const char* op)
 {
    const int64_t R = x.size(0), emb = x.size(1);
+   lgan_prebuild_forward(ix, R, entity_dim_size, emb);
    Tensor x1 = at::empty({R, emb}, x.options());
    Tensor tn = at::empty({entity_dim_size, emb}, x.options());
    Tensor nn = at::empty({entity_dim_size, emb}, x.options());
@@ -1059,6 +1166,7 @@ Tensor lgan_graph_backward(relm_mp_dtype dt, const Tensor& gx, const Tensor& gtn
                            const LganIndices& ix, int64_t relation_count, bool mean, const char* op)
 {
    const int64_t emb = gx.size(1);
+   lgan_prebuild_backward(ix, relation_count, gtn.size(0), gnn.size(0), emb);
    Tensor g1 = at::empty({relation_count, emb}, gx.options());
    lgan_reverse_agg(dt, gtn, ix.tn_rel, ix.tn_ent, relation_count, "tn_rel", "tn_ent", &gx, mean, g1, op);
    lgan_reverse_agg(dt, gnn, ix.nn_rel, ix.nn_ent, relation_count, "nn_rel", "nn_ent", &g1, mean, g1, op);
@@ -1155,6 +1263,12 @@ std::tuple< Tensor, Tensor, Tensor > lgan_pool_reduce_cuda(const Tensor& slot_me
    const int64_t R = arities.size(0), emb = slots.size(1);
    // x[r] = (sum of the slot rows of r) / max(arity[r], 1)  (mp_ops.cpp:3424-3432)
    Tensor x0 = at::empty({R, emb}, slots.options());
+   {
+      const Tensor ident = identity_index(s2r.numel(), slots);
+      const PlanCache::Request pool{&s2r, &ident, R, R, s2r.numel(), "slot_to_relation_instance", "slot", false};
+      const bool pooled = !(slots.size(0) == 0 || R == 0 || emb == 0);
+      lgan_prebuild_forward(ix, R, entity_dim_size, emb, pooled ? &pool : nullptr);
+   }
    if(slots.size(0) == 0 || R == 0 || emb == 0) {
       x0.zero_();
    } else {
@@ -1187,9 +1301,17 @@ Tensor lgan_pool_reduce_backward_cuda(const Tensor& grad_relation_pair_x, const 
    c10::cuda::CUDAGuard guard(grad_relation_pair_x.device());
    const relm_mp_dtype dt = to_dtype(grad_relation_pair_x, op);
    const Tensor gx = contig(grad_relation_pair_x);
+   const Tensor s2r = index64(slot_to_relation_instance);
+   {
+      const Tensor ident = identity_index(s2r.numel(), gx);
+      const PlanCache::Request pool{&s2r, &ident, relation_count, relation_count, s2r.numel(),
+                                    "slot_to_relation_instance", "slot", false};
+      const bool pooled = s2r.numel() > 0 && gx.size(1) > 0;
+      lgan_prebuild_backward(ix, relation_count, grad_tn_msgs.size(0), grad_nn_msgs.size(0), gx.size(1),
+                             pooled ? &pool : nullptr);
+   }
    const Tensor g0 = lgan_graph_backward(dt, gx, contig(grad_tn_msgs), contig(grad_nn_msgs), ix, relation_count,
                                          mode == kModeMean, op);
-   const Tensor s2r = index64(slot_to_relation_instance);
    const Tensor arities = contig(relation_instance_arities);
    const int64_t S = s2r.size(0), emb = gx.size(1);
    Tensor grad_slots = at::empty({S, emb}, gx.options());

@@ -95,3 +95,57 @@ def test_identity_gather_and_already_sorted() -> None:
     out = torch.sort(torch.randint(0, 1 << 18, (1 << 20,), generator=gen)).values
     _check(out, None, 1 << 18, 1 << 20)
     _check(torch.arange(1 << 20), None, 1 << 20, 1 << 20)
+
+
+def test_split_build_shares_one_wait_and_reports_the_first_error() -> None:
+    """relm_mp_plan_build_start / _finish through the C ABI: three builds
+    started back to back, one stream wait, then finished in order, give the
+    plans of three separate builds; a bad index in the second pair raises that
+    pair's message at its finish."""
+
+    import ctypes
+
+    lib = capi.lib()
+    gen = torch.Generator().manual_seed(11)
+    dev = torch.device("cuda")
+    stream = capi._stream(dev)
+    pairs = [
+        (torch.randint(0, 5000, (70_000,), generator=gen), torch.randint(0, 9000, (70_000,), generator=gen), 5000, 9000),
+        (torch.randint(0, 1 << 20, (1 << 20,), generator=gen), torch.randint(0, 300, (1 << 20,), generator=gen), 1 << 20, 300),
+        (torch.randint(0, 77, (1000,), generator=gen), torch.randint(0, 10, (1000,), generator=gen), 77, 10),
+    ]
+
+    def run(pairs):
+        held = []
+        for out_i, gat_i, rows, grows in pairs:
+            o, g = out_i.to(dev), gat_i.to(dev)
+            e = o.numel()
+            mem = capi._workspace(lib.relm_mp_plan_bytes(e, rows), dev)
+            scr = capi._workspace(lib.relm_mp_plan_scratch_bytes(e, rows), dev)
+            stats = torch.empty(lib.relm_mp_plan_stats_bytes(), dtype=torch.uint8).pin_memory()
+            capi.check(lib.relm_mp_plan_build_start(o.data_ptr(), g.data_ptr(), e, rows, rows, grows, mem.data_ptr(),
+                                                    mem.numel(), scr.data_ptr(), scr.numel(), stats.data_ptr(), stream))
+            held.append((o, g, e, rows, grows, mem, scr, stats))
+        torch.cuda.synchronize()
+        plans = []
+        for o, g, e, rows, grows, mem, scr, stats in held:
+            plan = capi.Plan()
+            capi.check(lib.relm_mp_plan_build_finish(o.data_ptr(), g.data_ptr(), e, rows, rows, grows, b"out_i", b"gat_i",
+                                                     0, mem.data_ptr(), mem.numel(), scr.data_ptr(), scr.numel(),
+                                                     stats.data_ptr(), stream, ctypes.byref(plan)))
+            plans.append((plan, mem))
+        return plans
+
+    for (out_i, gat_i, rows, grows), (plan, _mem) in zip(pairs, run(pairs)):
+        want_gidx, want_ptr = _expect(out_i.numpy(), gat_i.numpy(), rows)
+        got_ptr = capi._device_int32(plan.row_ptr, rows + 1, dev).cpu().numpy()
+        got_gidx = capi._device_int32(plan.gidx, out_i.numel(), dev).cpu().numpy()
+        assert np.array_equal(got_ptr, want_ptr)
+        assert np.array_equal(got_gidx, want_gidx)
+
+    bad = list(pairs)
+    broken = pairs[1][1].clone()
+    broken[12345] = 300  # gathered row out of [0, 300)
+    bad[1] = (pairs[1][0], broken, pairs[1][2], pairs[1][3])
+    with pytest.raises(capi.RelmMpError, match=r"gat_i index out of bounds: 300 not in \[0, 300\)"):
+        run(bad)
