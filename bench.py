@@ -317,7 +317,7 @@ def cfg5_partitioned(ops, mp, device, rank: int, world: int, barrier, max_over_r
     mine = ev0.elapsed_time(ev1) / steps
     elapsed_ms = max_over_ranks(mine)
     job_bytes = sum_over_ranks(step_bytes)
-    per_rank = [[float(mine), float(wl.num_edges), float(wl.dim_size)]]
+    per_rank = [[float(mine), float(wl.dst.numel()), float(wl.dim_size)]]  # fan-in edges of this rank
     if world > 1:
         import torch.distributed as dist
 
