@@ -53,6 +53,8 @@ __global__ void k_init_stats(PlanStats* st)
    st->not_identity = 0;
 }
 
+constexpr int kValidatePairs = 4;  // edge pairs per thread in the paired validation
+
 __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict__ key,
                                                        const int64_t* __restrict__ gat, int64_t n,
                                                        int64_t key_bound, int64_t gat_bound,
@@ -73,21 +75,33 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       moved |= k != e;
    };
    if(paired) {
-      // Two edges per thread with 16-byte loads (16-byte aligned indices): twice
-      // the bytes in flight of the one-edge form. Odd n: the last thread takes
-      // the final edge alone.
+      // Pairs of edges with 16-byte loads (16-byte aligned indices), kValidatePairs
+      // pairs per thread a grid apart, all loads issued before the checks. Odd n:
+      // thread 0 also takes the final edge alone.
       const int64_t pairs = n / 2;
-      if(t < pairs) {
-         const longlong2 kk = __ldg(reinterpret_cast< const longlong2* >(key) + t);
-         const longlong2 gg =
-            gat ? __ldg(reinterpret_cast< const longlong2* >(gat) + t) : make_longlong2(2 * t, 2 * t + 1);
-         const int64_t e = 2 * t;
-         check(e, kk.x, gg.x);
-         check(e + 1, kk.y, gg.y);
-         reinterpret_cast< uint2* >(key32)[t] = make_uint2((uint32_t)kk.x, (uint32_t)kk.y);
-         reinterpret_cast< int2* >(gat32)[t] = make_int2((int32_t)gg.x, (int32_t)gg.y);
-         descent = kk.y < kk.x || (e + 2 < n && __ldg(key + e + 2) < kk.y);
-      } else if(t == pairs && (n & 1)) {
+      const int64_t T = (int64_t)gridDim.x * blockDim.x;
+      longlong2 kk[kValidatePairs], gg[kValidatePairs];
+#pragma unroll
+      for(int q = 0; q < kValidatePairs; ++q) {
+         const int64_t i = t + q * T;
+         if(i < pairs) {
+            kk[q] = __ldg(reinterpret_cast< const longlong2* >(key) + i);
+            gg[q] = gat ? __ldg(reinterpret_cast< const longlong2* >(gat) + i) : make_longlong2(2 * i, 2 * i + 1);
+         }
+      }
+#pragma unroll
+      for(int q = 0; q < kValidatePairs; ++q) {
+         const int64_t i = t + q * T;
+         if(i < pairs) {
+            const int64_t e = 2 * i;
+            check(e, kk[q].x, gg[q].x);
+            check(e + 1, kk[q].y, gg[q].y);
+            reinterpret_cast< uint2* >(key32)[i] = make_uint2((uint32_t)kk[q].x, (uint32_t)kk[q].y);
+            reinterpret_cast< int2* >(gat32)[i] = make_int2((int32_t)gg[q].x, (int32_t)gg[q].y);
+            descent |= kk[q].y < kk[q].x || (e + 2 < n && __ldg(key + e + 2) < kk[q].y);
+         }
+      }
+      if(t == 0 && (n & 1)) {
          const int64_t e = n - 1;
          const int64_t k = key[e];
          const int64_t g = gat ? gat[e] : e;
@@ -412,7 +426,8 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
                              (reinterpret_cast< uintptr_t >(gather_index) & 15u) == 0 &&
                              (reinterpret_cast< uintptr_t >(sl.key_in) & 7u) == 0 &&
                              (reinterpret_cast< uintptr_t >(gather32) & 7u) == 0;
-         k_validate<<< grid_for(paired ? num_edges / 2 + 1 : num_edges), kThreads, 0, stream >>>(
+         k_validate<<< grid_for(paired ? (num_edges / 2 + kValidatePairs - 1) / kValidatePairs + 1 : num_edges),
+                    kThreads, 0, stream >>>(
             out_index, gather_index, num_edges, out_bound, gather_rows, sl.key_in, gather32, sl.stats, paired,
             cover ? sl.marks : nullptr
          );

@@ -19,6 +19,7 @@
 
 #include <math.h>
 
+#include <cstring>
 #include <type_traits>
 
 #include "relm_mp_internal.cuh"
@@ -270,6 +271,80 @@ __device__ __forceinline__ void lse_fold2(float2& m, float2& s, const float2 (&v
    // (floor - mr) * k is -inf or a large negative number once mr is finite,
    // and exp2 of it 0; s is 0 there anyway
    const float2 d = mul2(sub2(m, mr), k2);
+   s = fma2(s, make_float2(exp2_fast(d.x), exp2_fast(d.y)), e[0]);
+   m = mr;
+}
+
+// Two 2-byte values packed in a 32-bit word (element 0 in the low half):
+// their NaN-propagating maximum as a packed pair, the pair as floats, and the
+// pair of -inf.
+template < typename T >
+__device__ __forceinline__ uint32_t max2_nan(uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ uint32_t max2_nan< __nv_bfloat16 >(uint32_t a, uint32_t b)
+{
+   uint32_t r;
+   asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+   return r;
+}
+template <>
+__device__ __forceinline__ uint32_t max2_nan< __half >(uint32_t a, uint32_t b)
+{
+   uint32_t r;
+   asm("max.NaN.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+   return r;
+}
+template < typename T >
+__device__ __forceinline__ float2 unpack2(uint32_t w);
+template <>
+__device__ __forceinline__ float2 unpack2< __nv_bfloat16 >(uint32_t w)
+{
+   return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <>
+__device__ __forceinline__ float2 unpack2< __half >(uint32_t w)
+{
+   __half2 h;
+   memcpy(&h, &w, 4);
+   return __half22float2(h);
+}
+template < typename T >
+constexpr uint32_t kNegInf2 = sizeof(T) == 2 && std::is_same< T, __half >::value ? 0xfc00fc00u : 0xff80ff80u;
+
+// lse_fold2 for 2-byte inputs held as packed pairs (w[i] = one word per edge):
+// the maximum of the N new values per column is taken on the packed pairs
+// (exact: a maximum of 2-byte values is one of them), and each exponent
+// 2^((v - mr) k) is one fma, 2^(v k - mr k), with -mr k clamped to FLT_MAX so
+// that a column still at the floor gives 2^-inf = 0 instead of inf - inf.
+// The fma form rounds once instead of twice: its error, an ulp of mr k in the
+// exponent, is far below the 2-byte output's rounding.
+template < typename T, int N >
+__device__ __forceinline__ void lse_fold2_packed(float2& m, float2& s, const uint32_t (&w)[N], int n, float k)
+{
+   uint32_t t = w[0];
+#pragma unroll
+   for(int i = 1; i < N; ++i)
+      if(i < n) t = max2_nan< T >(t, w[i]);
+   const float2 tf = unpack2< T >(t);
+   const float2 mr = make_float2(nanmax(m.x, tf.x), nanmax(m.y, tf.y));
+   const float2 k2 = make_float2(k, k);
+   float2 nmk = mul2(mr, make_float2(-k, -k));
+   nmk = make_float2(fminf(nmk.x, 3.402823466e38f), fminf(nmk.y, 3.402823466e38f));
+   float2 e[N];
+#pragma unroll
+   for(int i = 0; i < N; ++i) {
+      if(i < n) {
+         const float2 d = fma2(unpack2< T >(w[i]), k2, nmk);
+         e[i] = make_float2(exp2_fast(d.x), exp2_fast(d.y));
+      } else {
+         e[i] = make_float2(0.f, 0.f);
+      }
+   }
+#pragma unroll
+   for(int g = 1; g < N; g <<= 1)
+#pragma unroll
+      for(int i = 0; i + g < N; i += 2 * g) e[i] = add2(e[i], e[i + g]);
+   const float2 d = fma2(m, k2, nmk);
    s = fma2(s, make_float2(exp2_fast(d.x), exp2_fast(d.y)), e[0]);
    m = mr;
 }
@@ -1737,6 +1812,34 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
                   // folds of 8, then 4, then the last 1..3 edges of the run (one rescale each)
                   auto fold = [&](auto width, int q0, int nval) __attribute__((always_inline)) {
                      constexpr int N = decltype(width)::value;
+                     if constexpr(sizeof(T) == 2 && MODE == kLse && PB == 4) {
+                        // one packed pair per edge straight from shared memory (wider
+                        // lane chunks keep the float path: their eight-edge folds
+                        // would not fit the registers)
+                        constexpr int NW = PB / 4;
+                        uint32_t w[N][NW];
+#pragma unroll
+                        for(int i = 0; i < N; ++i) {
+#pragma unroll
+                           for(int j = 0; j < NW; ++j)
+                              w[i][j] = i < nval ? reinterpret_cast< const uint32_t* >(src + (q0 + i) * CBW)[j]
+                                                 : kNegInf2< T >;
+                        }
+#pragma unroll
+                        for(int j = 0; j < NW; ++j) {
+                           uint32_t wj[N];
+#pragma unroll
+                           for(int i = 0; i < N; ++i) wj[i] = w[i][j];
+                           float2 a = make_float2(acc[2 * j], acc[2 * j + 1]);
+                           float2 sx = make_float2(aux[2 * j], aux[2 * j + 1]);
+                           lse_fold2_packed< T, N >(a, sx, wj, nval, LF.k);
+                           acc[2 * j] = a.x;
+                           acc[2 * j + 1] = a.y;
+                           aux[2 * j] = sx.x;
+                           aux[2 * j + 1] = sx.y;
+                        }
+                        return;
+                     }
                      A v[N][VN];
 #pragma unroll
                      for(int i = 0; i < N; ++i) {
@@ -1769,12 +1872,12 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
                         acc[x + 1] = a.y;
                      }
                   };
+                  // lanes of two columns fold 8 edges at a time; wider lane chunks 4
+                  // (their eight-edge folds would not fit the registers)
                   int q = 0;
-                  for(; q + 8 <= run; q += 8) fold(std::integral_constant< int, 8 >{}, q, 8);
-                  if(q + 4 <= run) {
-                     fold(std::integral_constant< int, 4 >{}, q, 4);
-                     q += 4;
-                  }
+                  if constexpr(VN <= 2)
+                     for(; q + 8 <= run; q += 8) fold(std::integral_constant< int, 8 >{}, q, 8);
+                  for(; q + 4 <= run; q += 4) fold(std::integral_constant< int, 4 >{}, q, 4);
                   if(q < run) fold(std::integral_constant< int, 3 >{}, q, run - q);
                } else {
                   int q = 0;

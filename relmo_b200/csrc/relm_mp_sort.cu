@@ -23,7 +23,8 @@
 //                      CTAs), so the sort is stable and the plan's edge order
 //                      within a row is the input order, run to run.
 //   scan_i32         - exclusive sum or inclusive max scan of int32 arrays
-//                      (reduce per block, scan of the block totals, apply).
+//                      (block totals, then each block adds up the totals
+//                      before it and scans its own chunk).
 //
 // No atomics on global memory, no inter-CTA waiting.
 #include <climits>
@@ -108,23 +109,6 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_reduce(const int32_t* __r
    if(threadIdx.x == 0) part[blockIdx.x] = total;
 }
 
-// Exclusive scan of part[0, nb) in place, one block.
-template < class Op >
-__global__ void __launch_bounds__(kScanThreads) k_scan_top(int32_t* __restrict__ part, int64_t nb)
-{
-   __shared__ int32_t wtot[kScanThreads / 32];
-   const Op op;
-   int32_t carry = Op::identity;
-   for(int64_t b0 = 0; b0 < nb; b0 += kScanThreads) {
-      const int64_t i = b0 + threadIdx.x;
-      const int32_t v = i < nb ? part[i] : Op::identity;
-      int32_t total;
-      const int32_t ex = block_exclusive< Op >(v, wtot, &total);
-      if(i < nb) part[i] = op(carry, ex);
-      carry = op(carry, total);
-   }
-}
-
 template < class Op, bool INCLUSIVE >
 __global__ void __launch_bounds__(kScanThreads) k_scan_apply(const int32_t* __restrict__ in, int64_t n,
                                                              const int32_t* __restrict__ part,
@@ -140,8 +124,13 @@ __global__ void __launch_bounds__(kScanThreads) k_scan_apply(const int32_t* __re
       v[i] = base + i < n ? in[base + i] : Op::identity;
       acc = op(acc, v[i]);
    }
+   // the reduction of the blocks before this one (their totals in `part`)
+   int32_t carry = Op::identity;
+   for(int64_t b = threadIdx.x; b < (int64_t)blockIdx.x; b += kScanThreads) carry = op(carry, part[b]);
+   int32_t before;
+   block_exclusive< Op >(carry, wtot, &before);
    int32_t total;
-   int32_t run = op(part[blockIdx.x], block_exclusive< Op >(acc, wtot, &total));
+   int32_t run = op(before, block_exclusive< Op >(acc, wtot, &total));
 #pragma unroll
    for(int i = 0; i < kScanPerThread; ++i) {
       if(base + i < n) {
@@ -388,8 +377,6 @@ int scan_launch(const int32_t* in, int32_t* out, int64_t n, int32_t* part, cudaS
    k_scan_reduce< Op ><<< (unsigned)nb, kScanThreads, 0, stream >>>(in, n, part);
    int rc;
    if((rc = check_launch("k_scan_reduce"))) return rc;
-   k_scan_top< Op ><<< 1, kScanThreads, 0, stream >>>(part, nb);
-   if((rc = check_launch("k_scan_top"))) return rc;
    k_scan_apply< Op, INCLUSIVE ><<< (unsigned)nb, kScanThreads, 0, stream >>>(in, n, part, out);
    return check_launch("k_scan_apply");
 }
