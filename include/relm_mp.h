@@ -82,9 +82,8 @@ RELM_MP_API const char* relm_mp_status_string(int status);
 RELM_MP_API const char* relm_mp_build_info(void);
 /* Message of the last failing call on the calling thread ("" if none). */
 RELM_MP_API const char* relm_mp_last_error(void);
-/* Number of kernels this library has launched in the process (its own
- * kernels; the radix-sort and scan kernels of the plan build come from CUB and
- * are not counted). */
+/* Number of kernels this library has launched in the process (every kernel
+ * is its own, the plan build's radix sort and scans included). */
 RELM_MP_API unsigned long long relm_mp_kernel_launches(void);
 
 /* ---------------------------------------------------------------------------
@@ -194,6 +193,9 @@ RELM_MP_API int relm_mp_fanin_reduce_noalloc(relm_mp_dtype dtype, const void* re
 #define RELM_MP_PLAN_FLAGS_KNOWN 2u
 #define RELM_MP_PLAN_REPEATS 4u   /* device_flags[0]: some row holds more than one edge */
 #define RELM_MP_PLAN_LONG_ROWS 8u /* device_flags[1]: some row holds more than 32 edges */
+/* Set by a build whose gather index is the identity (gather_index[e] == e for
+ * every edge; e.g. the message-row index of a fan-in). */
+#define RELM_MP_PLAN_GATHER_IDENTITY 16u
 
 typedef struct relm_mp_plan {
    int64_t num_edges;
@@ -233,6 +235,18 @@ RELM_MP_API int relm_mp_plan_build_ex(const int64_t* out_index, const int64_t* g
                                       const char* gather_index_name, int gather_checked_first,
                                       void* plan_mem, size_t plan_bytes, void* scratch,
                                       size_t scratch_bytes, void* stream, relm_mp_plan* plan);
+
+/* The plan of the identity output index over [0, num_edges) (row r <
+ * num_edges holds edge r, rows up to num_rows hold none) and `gather_index`,
+ * built without validation and without a host wait: gather_index must
+ * already be known to lie in [0, gather_rows), e.g. because the build of
+ * another plan over the same index validated it. A fan-in's backward over
+ * flat_src = arange uses it with the forward plan's destination index (the
+ * forward plan's flags carry RELM_MP_PLAN_GATHER_IDENTITY). The result has
+ * RELM_MP_PLAN_FLAGS_KNOWN set. No counterpart in the reference. */
+RELM_MP_API int relm_mp_plan_build_identity(const int64_t* gather_index, int64_t num_edges, int64_t num_rows,
+                                            int64_t gather_rows, void* plan_mem, size_t plan_bytes, void* stream,
+                                            relm_mp_plan* plan);
 
 /* relm_mp_plan_build_ex in two halves, so that the builds of several plans
  * (the three or four index pairs of one LGAN op) share one host wait:

@@ -108,6 +108,7 @@ SIGNATURES: dict[str, tuple] = {
         [_P, _P, _I64, _I64, _I64, _I64, _STR, _STR, _INT, _P, _SZ, _P, _SZ, _P, _PLANP],
     ),
     "relm_mp_plan_stats_bytes": (_SZ, []),
+    "relm_mp_plan_build_identity": (_INT, [_P, _I64, _I64, _I64, _P, _SZ, _P, _PLANP]),
     "relm_mp_plan_build_start": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _SZ, _P, _P]),
     "relm_mp_plan_build_finish": (
         _INT,

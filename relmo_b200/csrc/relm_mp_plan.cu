@@ -42,6 +42,7 @@ struct PlanStats {
    unsigned long long covered;     // distinct gathered rows (when marks were requested)
    unsigned int descents;          // warps that saw out_index[e] > out_index[e+1]
    unsigned int not_identity;      // some out_index[e] != e
+   unsigned int gather_moved;      // some gather_index[e] != e
 };
 
 __global__ void k_init_stats(PlanStats* st)
@@ -51,6 +52,7 @@ __global__ void k_init_stats(PlanStats* st)
    st->covered = 0;
    st->descents = 0;
    st->not_identity = 0;
+   st->gather_moved = 0;
 }
 
 constexpr int kValidatePairs = 4;  // edge pairs per thread in the paired validation
@@ -66,7 +68,9 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
    bool descent = false;
    bool moved = false;
+   bool gmoved = false;
    auto check = [&](int64_t e, int64_t k, int64_t g) __attribute__((always_inline)) {
+      gmoved |= g != e;
       if(k < 0 || k >= key_bound) atomicMin(&st->out_bad, (unsigned long long)e);
       if(g < 0 || g >= gat_bound)
          atomicMin(&st->gather_bad, (unsigned long long)e);
@@ -123,6 +127,16 @@ __global__ void __launch_bounds__(kThreads) k_validate(const int64_t* __restrict
       atomicExch(&st->descents, 1u);
    if(__syncthreads_or(moved) && threadIdx.x == 0 && *((volatile unsigned*)&st->not_identity) == 0u)
       atomicExch(&st->not_identity, 1u);
+   if(__syncthreads_or(gmoved) && threadIdx.x == 0 && *((volatile unsigned*)&st->gather_moved) == 0u)
+      atomicExch(&st->gather_moved, 1u);
+}
+
+// gidx[e] = gather[e] as int32 (a gather index validated elsewhere).
+__global__ void __launch_bounds__(kThreads) k_gather32(const int64_t* __restrict__ gather, int64_t n,
+                                                       int32_t* __restrict__ gidx)
+{
+   for(int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x)
+      gidx[e] = (int32_t)__ldg(gather + e);
 }
 
 // Coverage bitmap from the row marks: word w of `cover` gets bit b set when
@@ -483,6 +497,7 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    }
    if(cover) *gather_repeats = host.covered != (unsigned long long)num_edges;
    if(cover && gather_covered) *gather_covered = (int64_t)host.covered;
+   if(num_edges > 0 && host.gather_moved == 0) plan->flags |= RELM_MP_PLAN_GATHER_IDENTITY;
    auto gidx_home = [&]() -> int {  // the unsorted gather values, into the plan's gidx
       if(gather32 == pl.gidx || num_edges == 0) return RELM_MP_OK;
       return check_cuda(cudaMemcpyAsync(pl.gidx, gather32, (size_t)num_edges * sizeof(int32_t),
@@ -653,6 +668,55 @@ int relm_mp_plan_build_cover(const int64_t* out_index, const int64_t* gather_ind
 }
 
 size_t relm_mp_plan_stats_bytes(void) { return sizeof(relm_mp::PlanStats); }
+
+int relm_mp_plan_build_identity(const int64_t* gather_index, int64_t num_edges, int64_t num_rows,
+                                int64_t gather_rows, void* plan_mem, size_t plan_bytes, void* stream,
+                                relm_mp_plan* plan)
+{
+   using namespace relm_mp;
+   if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
+   if(num_edges < 0 || num_rows < num_edges || gather_rows < 0)
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "relm_mp_plan_build_identity needs 0 <= num_edges <= num_rows.");
+   if(num_edges + num_rows >= (int64_t)INT32_MAX || gather_rows >= (int64_t)INT32_MAX)
+      return fail(
+         RELM_MP_ERR_UNSUPPORTED, "relm_mp supports num_edges + num_rows < 2^31 and < 2^31 gathered rows."
+      );
+   if(num_edges > 0 && !gather_index) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "gather_index must not be NULL.");
+   const PlanLayout pl = plan_layout(plan_mem, num_edges, num_rows);
+   if(!plan_mem || plan_bytes < pl.bytes)
+      return fail(RELM_MP_ERR_WORKSPACE_TOO_SMALL, "plan memory is smaller than relm_mp_plan_bytes().");
+   cudaStream_t st = static_cast< cudaStream_t >(stream);
+   const int64_t tiles = plan_num_tiles(num_edges, num_rows);
+   *plan = relm_mp_plan{};
+   plan->num_edges = num_edges;
+   plan->num_rows = num_rows;
+   plan->gather_rows = gather_rows;
+   plan->num_tiles = tiles;
+   plan->tile_items = plan_tile_items(num_edges, num_rows);
+   plan->row_ptr = pl.row_ptr;
+   plan->gidx = pl.gidx;
+   plan->tile_row = pl.tile_row;
+   plan->tile_edge = pl.tile_edge;
+   plan->device_flags = pl.flags;
+   // every row holds at most one edge: the row facts are known without a device pass
+   plan->flags = RELM_MP_PLAN_SORTED_INPUT | RELM_MP_PLAN_FLAGS_KNOWN;
+   int rc;
+   if((rc = check_cuda(cudaMemsetAsync(pl.flags, 0, 4 * sizeof(int32_t), st), "flags memset"))) return rc;
+   if(num_edges > 0) {
+      unsigned grid = grid_for(num_edges);
+      if(grid > 148u * 16u) grid = 148u * 16u;
+      k_gather32<<< grid, kThreads, 0, st >>>(gather_index, num_edges, pl.gidx);
+      if((rc = check_launch("k_gather32"))) return rc;
+   }
+   unsigned grid = grid_for(num_rows + 1);
+   if(grid > 148u * 8u) grid = 148u * 8u;
+   k_identity_rows<<< grid, kThreads, 0, st >>>(pl.row_ptr, num_rows, num_edges, pl.flags);
+   if((rc = check_launch("k_identity_rows"))) return rc;
+   k_partition<<< grid_for(tiles + 1), kThreads, 0, st >>>(
+      pl.row_ptr, num_rows, num_edges, tiles, plan->tile_items, pl.tile_row, pl.tile_edge
+   );
+   return check_launch("k_partition");
+}
 
 int relm_mp_plan_build_start(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
                              int64_t num_rows, int64_t out_bound, int64_t gather_rows, void* plan_mem,

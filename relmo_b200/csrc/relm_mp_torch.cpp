@@ -294,6 +294,37 @@ class PlanCache {
       }
    }
 
+   // The plan of (flat_src, dst) of a fan-in backward, from the forward's
+   // cached plan of (dst, flat_src) when that build found flat_src to be the
+   // identity (RELM_MP_PLAN_GATHER_IDENTITY): message row e then holds edge e
+   // alone, so the plan is dst as int32 beside row_ptr[r] = min(r, E), built
+   // without validation (the forward validated both indices against the same
+   // bounds) and without a host wait. Null when that does not apply (the
+   // caller then builds the plan the usual way).
+   PlanPtr identity_from_forward(const Tensor& src, const Tensor& dst, int64_t num_rows, int64_t out_bound,
+                                 int64_t gather_rows, int64_t fwd_gather_rows)
+   {
+      if(PlanPtr e = peek(src, dst, num_rows, out_bound, gather_rows)) {
+         std::lock_guard< std::mutex > lock(mu_);
+         ++hits_;
+         return e;
+      }
+      const PlanPtr fp = peek(dst, src, gather_rows, gather_rows, fwd_gather_rows);
+      if(!fp || !(fp->plan.flags & RELM_MP_PLAN_GATHER_IDENTITY)) return nullptr;
+      const int64_t E = src.numel();
+      if(E > out_bound) return nullptr;  // message rows [0, E) must lie in the backward's bound
+      Tensor memory = byte_buffer(relm_mp_plan_bytes(E, num_rows), src);
+      relm_mp_plan plan;
+      check_status(relm_mp_plan_build_identity(dst.data_ptr< int64_t >(), E, num_rows, gather_rows, memory.data_ptr(),
+                                               (size_t)memory.numel(), stream_of(src), &plan),
+                   "plan build");
+      auto entry = std::make_shared< PlanEntry >(
+         PlanEntry{IndexKey::of(src), IndexKey::of(dst), num_rows, out_bound, gather_rows, 0, memory, plan, Tensor(), -1,
+                   false, E, Tensor(), Tensor(), nullptr}
+      );
+      return insert(entry, src);
+   }
+
    // The cached plan for the pair, or null (never builds).
    PlanPtr peek(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
                 int64_t gather_rows)
@@ -615,7 +646,13 @@ Tensor fanin_reduce_sum_backward_cuda(const Tensor& grad_out, const Tensor& flat
       }
    }
    Tensor keep;
-   const relm_mp_plan plan = get_plan(src, dst, rel_rows, rel_rows, g.size(0), "flat_src", "dst_idx", false, &keep);
+   relm_mp_plan plan;
+   if(const PlanPtr ip = PlanCache::get().identity_from_forward(src, dst, rel_rows, rel_rows, g.size(0), rel_rows)) {
+      keep = ip->memory;
+      plan = ip->plan;
+   } else {
+      plan = get_plan(src, dst, rel_rows, rel_rows, g.size(0), "flat_src", "dst_idx", false, &keep);
+   }
    return planned_sum(plan, dt, g, emb, grad_rel, RELM_MP_MODE_SUM, "fanin_reduce_sum_backward");
 }
 
@@ -686,7 +723,13 @@ Tensor lse_backward_cuda_impl(const Tensor& grad_out, const Tensor& rel_flat, co
    }
    Tensor keep;
    const int64_t bound = std::min(rel_rows, rel.size(0));
-   const relm_mp_plan plan = get_plan(src, dst, rel_rows, bound, g.size(0), "flat_src", "dst_idx", false, &keep);
+   relm_mp_plan plan;
+   if(const PlanPtr ip = PlanCache::get().identity_from_forward(src, dst, rel_rows, bound, g.size(0), rel.size(0))) {
+      keep = ip->memory;
+      plan = ip->plan;
+   } else {
+      plan = get_plan(src, dst, rel_rows, bound, g.size(0), "flat_src", "dst_idx", false, &keep);
+   }
    Tensor scratch = byte_buffer(relm_mp_plan_reduce_scratch_bytes(&plan, emb, dt, RELM_MP_MODE_LOGSUMEXP_BACKWARD), g);
    check_status(
       relm_mp_plan_logsumexp_backward_ex(&plan, dt, form, g.data_ptr(), o.data_ptr(), rel.data_ptr(), emb,

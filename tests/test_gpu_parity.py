@@ -327,3 +327,41 @@ def test_errors_match_reference_semantics() -> None:
             mp.fanin_reduce(x, torch.tensor([0], device=DEV), torch.tensor([0], device=DEV), 2, 0)
     finally:
         del os.environ["RELM_MP_ENABLE"]
+
+
+@pytest.mark.parametrize("flat_src_kind", ["arange", "permutation"])
+@pytest.mark.parametrize("extra_rows", [0, 5])
+def test_backward_plan_from_the_forward(flat_src_kind: str, extra_rows: int) -> None:
+    """A fan-in backward after its forward: with flat_src = arange the
+    backward's plan comes from the forward's validated destination index
+    without a validation pass of its own (no extra validated build); with a
+    permuted flat_src it is built the usual way. Both backwards, both cases,
+    against the oracle; rel_rows above the edge count leaves the extra message
+    rows zero."""
+
+    mp.clear_plan_cache()
+    g = torch.Generator(device=DEV).manual_seed(3)
+    rows, edges, emb = 700, 20_000, 32
+    dst = torch.randint(0, rows, (edges,), device=DEV, generator=g)
+    if flat_src_kind == "arange":
+        fsrc = torch.arange(edges, device=DEV)
+    else:
+        fsrc = torch.randperm(edges, device=DEV, generator=g)
+    rel_rows = edges + extra_rows
+    msgs = torch.randn(rel_rows, emb, device=DEV, generator=g)
+    grad = torch.randn(rows, emb, device=DEV, generator=g)
+    ops = torch.ops.relm_mp
+    lse = ops.fanin_reduce(msgs, fsrc, dst, rows, 1)
+    s0 = mp.plan_cache_stats()
+    gs = ops.fanin_reduce_sum_backward(grad, fsrc, dst, rel_rows)
+    gl = ops.fanin_reduce_logsumexp_backward(grad, msgs, fsrc, dst, lse, rel_rows)
+    s1 = mp.plan_cache_stats()
+    assert s1["builds"] == s0["builds"] + 1  # one plan of (flat_src, dst), shared by both backwards
+    m, f, d, gr = msgs.cpu().numpy(), fsrc.cpu().numpy(), dst.cpu().numpy(), grad.cpu().numpy()
+    ref_s = oracle.fanin_reduce_sum_backward(gr, f, d, rel_rows)
+    assert np.array_equal(gs.cpu().numpy(), ref_s)  # every message row is one copied grad row
+    ref_lse = oracle.fanin_reduce(m, f, d, rows, 1)
+    ref_l = oracle.fanin_reduce_logsumexp_backward(gr, m, f, d, ref_lse, rel_rows)
+    assert np.allclose(gl.cpu().numpy(), ref_l, rtol=1e-5, atol=1e-6)
+    if extra_rows:
+        assert not gs[edges:].any() and not gl[edges:].any()
