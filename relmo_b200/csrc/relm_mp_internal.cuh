@@ -16,7 +16,10 @@ namespace relm_mp {
 // The tile size is chosen from the problem size alone, aiming at about
 // kTargetTiles tiles (4 resident waves of 32 warps on each of the B200's 148
 // SMs), within [kMinTileItems, kMaxTileItems].
-constexpr int64_t kTargetTiles = 148 * 128;
+#ifndef RELM_MP_TARGET_TILES
+#define RELM_MP_TARGET_TILES (148 * 128)
+#endif
+constexpr int64_t kTargetTiles = RELM_MP_TARGET_TILES;
 constexpr int kMinTileItems = 128;
 constexpr int kMaxTileItems = 4096;
 int plan_tile_items(int64_t num_edges, int64_t num_rows);
