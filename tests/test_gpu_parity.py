@@ -365,3 +365,51 @@ def test_backward_plan_from_the_forward(flat_src_kind: str, extra_rows: int) -> 
     assert np.allclose(gl.cpu().numpy(), ref_l, rtol=1e-5, atol=1e-6)
     if extra_rows:
         assert not gs[edges:].any() and not gl[edges:].any()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("emb", [64, 32])
+def test_half_storage_logsumexp_special_values(dtype, emb: int) -> None:
+    """2-byte logsumexp on rows long enough for the merge-path kernels (more
+    than 32 edges, one row over many tiles): a row of only -inf gives NaN, an
+    empty row -inf, a +inf or NaN value NaN, -inf values among finite ones
+    contribute nothing, a single value comes back as itself; the rest within
+    1e-2 of the float32 oracle on the same (2-byte) values."""
+
+    g = torch.Generator().manual_seed(17)
+    rows, special = 300, 6
+    counts = torch.randint(33, 120, (rows,), generator=g)
+    counts[0] = 40  # only -inf
+    counts[1] = 40  # one +inf among finite
+    counts[2] = 40  # one NaN among finite
+    counts[3] = 40  # half -inf, half finite
+    counts[4] = 0  # empty
+    counts[5] = 1  # a single value
+    counts[7] = 6000  # spans many tiles, with -inf values inside
+    dst = torch.repeat_interleave(torch.arange(rows), counts)
+    edges = int(dst.numel())
+    perm = torch.randperm(edges, generator=g)
+    dst = dst[perm]
+    vals = torch.randn(edges, emb, generator=g) * 3
+    pos = torch.empty(edges, dtype=torch.int64)
+    pos[perm] = torch.arange(edges)  # edge of each (row-ordered) slot
+    start = torch.cumsum(counts, 0) - counts
+    vals[pos[start[0]:start[0] + 40]] = -float("inf")
+    vals[pos[start[1] + 7], 3] = float("inf")
+    vals[pos[start[2] + 11], 5] = float("nan")
+    vals[pos[start[3]:start[3] + 20]] = -float("inf")
+    vals[pos[start[7]:start[7] + 6000:3], :emb // 2] = -float("inf")
+    flat_src = torch.arange(edges)
+    lowp = vals.to(dtype)
+    up = lowp.float().numpy()
+    got = torch.ops.relm_mp.fanin_reduce(lowp.to(DEV), flat_src.to(DEV), dst.to(DEV), rows, 1)
+    got = got.float().cpu().numpy()
+    ref = oracle.fanin_reduce(up, flat_src, dst, rows, 1)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert np.array_equal(np.isinf(got), np.isinf(ref)) and np.array_equal(got[np.isinf(got)], ref[np.isinf(ref)])
+    assert np.isnan(got[0]).all() and np.isneginf(got[4]).all()
+    assert np.isnan(got[1, 3]) and np.isnan(got[2, 5])
+    single = lowp[pos[start[5]]].float().numpy()
+    assert np.array_equal(got[5], single)
+    fin = np.isfinite(ref)
+    assert np.allclose(got[fin], ref[fin], rtol=1e-2, atol=1e-2)
