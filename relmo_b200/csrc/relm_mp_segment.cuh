@@ -1838,38 +1838,38 @@ __global__ void __launch_bounds__(kStreamThreads, RELM_MP_STREAM_MIN_BLOCKS) k_s
                            aux[2 * j] = sx.x;
                            aux[2 * j + 1] = sx.y;
                         }
-                        return;
-                     }
-                     A v[N][VN];
+                     } else {
+                        A v[N][VN];
 #pragma unroll
-                     for(int i = 0; i < N; ++i) {
-                        if(i < nval) {
-                           load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q0 + i) * CBW), v[i]);
-                        } else {
+                        for(int i = 0; i < N; ++i) {
+                           if(i < nval) {
+                              load_chunk< T, PB >(reinterpret_cast< const T* >(src + (q0 + i) * CBW), v[i]);
+                           } else {
 #pragma unroll
-                           for(int x = 0; x < VN; ++x) v[i][x] = (sum_mode(MODE)) ? A(0) : ninf;
+                              for(int x = 0; x < VN; ++x) v[i][x] = (sum_mode(MODE)) ? A(0) : ninf;
+                           }
                         }
-                     }
 #pragma unroll
-                     for(int x = 0; x < VN; x += 2) {
-                        float2 vx[N];
+                        for(int x = 0; x < VN; x += 2) {
+                           float2 vx[N];
 #pragma unroll
-                        for(int i = 0; i < N; ++i) vx[i] = make_float2(v[i][x], v[i][x + 1]);
-                        float2 a = make_float2(acc[x], acc[x + 1]);
-                        if(sum_mode(MODE)) {
+                           for(int i = 0; i < N; ++i) vx[i] = make_float2(v[i][x], v[i][x + 1]);
+                           float2 a = make_float2(acc[x], acc[x + 1]);
+                           if(sum_mode(MODE)) {
 #pragma unroll
-                           for(int w = 1; w < N; w <<= 1)
+                              for(int w = 1; w < N; w <<= 1)
 #pragma unroll
-                              for(int i = 0; i + w < N; i += 2 * w) vx[i] = add2(vx[i], vx[i + w]);
-                           a = add2(a, vx[0]);
-                        } else {
-                           float2 sx = make_float2(aux[x], aux[x + 1]);
-                           lse_fold2< N >(a, sx, vx, nval, LF.k);
-                           aux[x] = sx.x;
-                           aux[x + 1] = sx.y;
+                                 for(int i = 0; i + w < N; i += 2 * w) vx[i] = add2(vx[i], vx[i + w]);
+                              a = add2(a, vx[0]);
+                           } else {
+                              float2 sx = make_float2(aux[x], aux[x + 1]);
+                              lse_fold2< N >(a, sx, vx, nval, LF.k);
+                              aux[x] = sx.x;
+                              aux[x + 1] = sx.y;
+                           }
+                           acc[x] = a.x;
+                           acc[x + 1] = a.y;
                         }
-                        acc[x] = a.x;
-                        acc[x + 1] = a.y;
                      }
                   };
                   // lanes of two columns fold 8 edges at a time; wider lane chunks 4
