@@ -13,8 +13,9 @@
 //                                       pair's first output position;
 //                        k_sort_scatter each CTA walks its range in sub-tiles
 //                                       of 8192 items: a warp ranks its 512
-//                                       items in order (ballots group equal
-//                                       digits, per-warp counters), the
+//                                       items in order (lane masks of equal
+//                                       digits OR-ed together in shared
+//                                       memory, per-warp counters), the
 //                                       sub-tile is reordered by digit in
 //                                       shared memory and written out in
 //                                       digit runs with coalesced stores.
@@ -35,14 +36,15 @@ namespace relm_mp {
 
 namespace {
 
-constexpr int kSortThreads = 512;
+#ifndef RELM_MP_SORT_THREADS
+#define RELM_MP_SORT_THREADS 512
+#endif
+constexpr int kSortThreads = RELM_MP_SORT_THREADS;
+constexpr int kSortCtasPerSm = kSortThreads <= 512 ? 2 : 1;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kSortPerThread = 16;
 constexpr int kSortSub = kSortThreads * kSortPerThread;  // items per sub-tile
-#ifndef RELM_MP_SORT_MAX_BITS
-#define RELM_MP_SORT_MAX_BITS 10
-#endif
-constexpr int kSortMaxBits = RELM_MP_SORT_MAX_BITS;  // digit bits per pass
+constexpr int kSortMaxBits = 10;  // digit bits per pass
 constexpr int kScanThreads = 512;
 constexpr int kScanPerThread = 8;
 constexpr int kScanChunk = kScanThreads * kScanPerThread;
@@ -172,28 +174,13 @@ SortShape sort_shape(int64_t n, int end_bit)
    }
    // about two CTAs per SM, at most 16 sub-tiles each
    const int64_t sub_tiles = (n + kSortSub - 1) / kSortSub;
-   int64_t subs = (sub_tiles + 2 * 148 - 1) / (2 * 148);
+   int64_t subs = (sub_tiles + kSortCtasPerSm * 148 - 1) / (kSortCtasPerSm * 148);
    if(subs < 1) subs = 1;
    if(subs > 16) subs = 16;
    s.subs = (int)subs;
    s.ctas = (sub_tiles + subs - 1) / subs;
    if(s.ctas < 1) s.ctas = 1;
    return s;
-}
-
-// Lanes of the warp holding the same digit d (< 2^DB) as this lane, or d == 2^DB
-// (an invalid lane, matched with the other invalid lanes only): one ballot per
-// digit bit instead of match.any, which is slow with many distinct values.
-template < int DB >
-__device__ __forceinline__ unsigned same_digit_lanes(unsigned d)
-{
-   unsigned peers = 0xffffffffu;
-#pragma unroll
-   for(int b = 0; b <= DB; ++b) {
-      const unsigned bal = __ballot_sync(0xffffffffu, (d >> b) & 1u);
-      peers &= ((d >> b) & 1u) ? bal : ~bal;
-   }
-   return peers;
 }
 
 __device__ __forceinline__ unsigned lanemask_lt()
@@ -244,38 +231,54 @@ template < int DB >
 constexpr size_t scatter_smem()
 {
    constexpr int D = 1 << DB;
-   // staged keys + values, per-warp u16 counters, run / sub-tile start / total per digit, warp totals
-   return (size_t)kSortSub * 8 + (size_t)kSortWarps * D * 2 + (size_t)3 * D * 4 + 32 * 4;
+   // staged keys + values (the ranking's per-warp digit words before that),
+   // per-warp u16 counters, next global position and output offset per digit,
+   // warp totals
+   return (size_t)kSortSub * 8 + (size_t)kSortWarps * D * 2 + (size_t)2 * D * 4 + 32 * 4;
 }
 
-// Two CTAs per SM where the shared memory allows it (digits of up to 10 bits):
-// the values are read again at the reordering step instead of being held in
-// registers through the ranking.
+// One sub-tile of kSortSub items at a time:
+//   rank     each warp ranks its 512 items (16 rounds of 32) among the earlier
+//            items of the warp with the same digit: a lane ORs its bit into
+//            the warp's word of its digit, reads the word back (the lanes of
+//            equal digit), and the group's first lane adds the group to the
+//            warp's u16 counter of the digit and clears the word;
+//   prefix   per digit (DPT consecutive digits per thread): the sub-tile
+//            total over the warps, the local start (block scan of the
+//            totals), and each warp's first local position of the digit
+//            written over its counter;
+//   reorder  items to their local positions in shared memory (values read
+//            from global memory here, not held through the ranking);
+//   write    in local order to global position off[d] + local position:
+//            coalesced runs of each digit.
+// Two CTAs per SM (108 KB of shared memory, 64 registers each).
 template < int DB >
-__global__ void __launch_bounds__(kSortThreads, DB <= 10 ? 2 : 1) k_sort_scatter(const uint32_t* __restrict__ kin,
-                                                               const int32_t* __restrict__ vin,
-                                                               uint32_t* __restrict__ kout,
-                                                               int32_t* __restrict__ vout, int64_t n, int shift,
-                                                               const int32_t* __restrict__ goff, int64_t ctas,
-                                                               int subs)
+__global__ void __launch_bounds__(kSortThreads, kSortCtasPerSm) k_sort_scatter(const uint32_t* __restrict__ kin,
+                                                                  const int32_t* __restrict__ vin,
+                                                                  uint32_t* __restrict__ kout,
+                                                                  int32_t* __restrict__ vout, int64_t n, int shift,
+                                                                  const int32_t* __restrict__ goff, int64_t ctas,
+                                                                  int subs)
 {
    constexpr int D = 1 << DB;
-   constexpr int DPT = (D + kSortThreads - 1) / kSortThreads;  // digits per thread in the digit loops
+   constexpr int DPT = (D + kSortThreads - 1) / kSortThreads;  // digits per thread in the prefix step
+   static_assert((size_t)kSortWarps * D * 4 <= (size_t)kSortSub * 8, "digit words must fit in the staging area");
    extern __shared__ __align__(16) unsigned char sm[];
    uint32_t* skey = reinterpret_cast< uint32_t* >(sm);
    int32_t* sval = reinterpret_cast< int32_t* >(skey + kSortSub);
-   // [warp][digit] counts, then prefixes (16-byte aligned: zeroed with 16-byte stores)
+   uint32_t* words = reinterpret_cast< uint32_t* >(sm);  // [warp][digit] lane masks while ranking
+   // [warp][digit] counts, then first local positions (16-byte aligned: zeroed with 16-byte stores)
    uint16_t* wh = reinterpret_cast< uint16_t* >(sval + kSortSub);
    int32_t* run = reinterpret_cast< int32_t* >(wh + kSortWarps * D);  // global position of the CTA's next item of digit d
-   int32_t* sstart = run + D;  // first local position of digit d in the reordered sub-tile
-   int32_t* tot = sstart + D;  // items of digit d in the sub-tile
-   int32_t* wtot = tot + D;
+   int32_t* off = run + D;  // this sub-tile: global position of digit d's items minus their local position
+   int32_t* wtot = off + D;
    const int tid = threadIdx.x;
    const int lane = tid & 31;
    const int w = tid >> 5;
    const int64_t c = blockIdx.x;
    for(int d = tid; d < D; d += kSortThreads) run[d] = goff[(int64_t)d * ctas + c];
    uint16_t* myh = wh + w * D;
+   uint32_t* myw = words + w * D;
    const unsigned lt = lanemask_lt();
    for(int sub = 0; sub < subs; ++sub) {
       const int64_t base = (c * subs + sub) * (int64_t)kSortSub;
@@ -283,64 +286,68 @@ __global__ void __launch_bounds__(kSortThreads, DB <= 10 ? 2 : 1) k_sort_scatter
       const int subn = (n - base) < kSortSub ? (int)(n - base) : kSortSub;
       for(int i = tid; i < kSortWarps * D / 8; i += kSortThreads)
          reinterpret_cast< uint4* >(wh)[i] = make_uint4(0u, 0u, 0u, 0u);
+      for(int i = tid; i < kSortWarps * D / 4; i += kSortThreads)
+         reinterpret_cast< uint4* >(words)[i] = make_uint4(0u, 0u, 0u, 0u);
       uint32_t k[kSortPerThread];
 #pragma unroll
       for(int r = 0; r < kSortPerThread; ++r) {
          const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
          k[r] = idx < subn ? __ldg(kin + base + idx) : 0u;
       }
-      __syncthreads();  // counters zeroed
-      // rank each item among the earlier items of its warp with the same digit
+      __syncthreads();  // counters and digit words zeroed
       uint16_t rank[kSortPerThread];
 #pragma unroll
       for(int r = 0; r < kSortPerThread; ++r) {
          const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
          const bool valid = idx < subn;
-         const unsigned d = valid ? (k[r] >> shift) & (D - 1) : (unsigned)D;
-         const unsigned peers = same_digit_lanes< DB >(d);
-         const int leader = __ffs(peers) - 1;
+         const unsigned d = (k[r] >> shift) & (D - 1);
+         if(valid) atomicOr(&myw[d], 1u << lane);
+         __syncwarp();
+         const unsigned peers = valid ? myw[d] : 0u;
+         __syncwarp();
+         const int leader = valid ? __ffs(peers) - 1 : lane;
          int b = 0;
          if(valid && lane == leader) {
             b = myh[d];
             myh[d] = (uint16_t)(b + __popc(peers));
+            myw[d] = 0u;
          }
          b = __shfl_sync(0xffffffffu, b, leader);
          rank[r] = (uint16_t)(b + __popc(peers & lt));
          __syncwarp();
       }
       __syncthreads();
-      // per digit: prefix over the warps (in warp order) and the sub-tile total
-#pragma unroll
-      for(int j = 0; j < DPT; ++j) {
-         const int d = tid + j * kSortThreads;
-         if(d < D) {
-            int acc = 0;
-#pragma unroll
-            for(int ww = 0; ww < kSortWarps; ++ww) {
-               const int cnt = wh[ww * D + d];
-               wh[ww * D + d] = (uint16_t)acc;
-               acc += cnt;
-            }
-            tot[d] = acc;
-         }
-      }
-      __syncthreads();
-      // local digit starts: exclusive scan of the totals, DPT consecutive digits per thread
       {
          int32_t t[DPT];
          int32_t sum = 0;
 #pragma unroll
          for(int j = 0; j < DPT; ++j) {
             const int d = tid * DPT + j;
-            t[j] = d < D ? tot[d] : 0;
-            sum += t[j];
+            int acc = 0;
+            if(d < D) {
+#pragma unroll
+               for(int ww = 0; ww < kSortWarps; ++ww) acc += wh[ww * D + d];
+            }
+            t[j] = acc;
+            sum += acc;
          }
          int32_t total;
          int32_t ex = block_exclusive< SumOp >(sum, wtot, &total);
 #pragma unroll
          for(int j = 0; j < DPT; ++j) {
             const int d = tid * DPT + j;
-            if(d < D) sstart[d] = ex;
+            if(d < D) {
+               int acc = ex;
+#pragma unroll
+               for(int ww = 0; ww < kSortWarps; ++ww) {
+                  const int cnt = wh[ww * D + d];
+                  wh[ww * D + d] = (uint16_t)acc;
+                  acc += cnt;
+               }
+               const int32_t r0 = run[d];
+               off[d] = r0 - ex;
+               run[d] = r0 + t[j];
+            }
             ex += t[j];
          }
       }
@@ -350,7 +357,7 @@ __global__ void __launch_bounds__(kSortThreads, DB <= 10 ? 2 : 1) k_sort_scatter
          const int idx = w * (kSortSub / kSortWarps) + r * 32 + lane;
          if(idx < subn) {
             const unsigned d = (k[r] >> shift) & (D - 1);
-            const int lp = sstart[d] + myh[d] + rank[r];
+            const int lp = myh[d] + rank[r];
             skey[lp] = k[r];
             sval[lp] = __ldg(vin + base + idx);
          }
@@ -359,13 +366,11 @@ __global__ void __launch_bounds__(kSortThreads, DB <= 10 ? 2 : 1) k_sort_scatter
       for(int i = tid; i < subn; i += kSortThreads) {
          const uint32_t key = skey[i];
          const unsigned d = (key >> shift) & (D - 1);
-         const int64_t pos = (int64_t)run[d] + (i - sstart[d]);
+         const int64_t pos = (int64_t)off[d] + i;
          kout[pos] = key;
          vout[pos] = sval[i];
       }
-      __syncthreads();
-      for(int d = tid; d < D; d += kSortThreads) run[d] += tot[d];
-      __syncthreads();
+      __syncthreads();  // staging, counters and offsets are rewritten by the next sub-tile
    }
 }
 
@@ -420,7 +425,6 @@ int sort_pass_bits(int bits, const uint32_t* kin, const int32_t* vin, uint32_t* 
       case 8: return sort_pass< 8 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
       case 9: return sort_pass< 9 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
       case 10: return sort_pass< 10 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
-      case 11: return sort_pass< 11 >(kin, vin, kout, vout, n, shift, s, ghist, part, stream);
       default: return fail(RELM_MP_ERR_UNSUPPORTED, "radix sort digit width out of range.");
    }
 }
