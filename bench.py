@@ -194,12 +194,15 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def make_workload(name: str, seed: int, device, dtype: torch.dtype, nodes=None, edges=None) -> workloads.FanWorkload:
+def make_workload(name: str, seed: int, device, dtype: torch.dtype, nodes=None, edges=None,
+                  emb=None) -> workloads.FanWorkload:
     size = {}
     if nodes is not None:
         size["n"] = int(nodes)
     if edges is not None:
         size["edges"] = int(edges)
+    if emb is not None:
+        size["emb"] = int(emb)
     if name == "cfg2-unsorted":
         return workloads.cfg2(seed=seed, device=device, sorted_dst=False, dtype=dtype, **size)
     if name == "cfg2-sorted":
@@ -522,6 +525,8 @@ def main() -> int:
     parser.add_argument("--reps", type=int, default=5, help="timed repetitions per op in the per-op timing")
     parser.add_argument("--nodes", type=int, default=None, help="override the workload's node count (profiling)")
     parser.add_argument("--edges", type=int, default=None, help="override the workload's edge count (profiling)")
+    parser.add_argument("--emb", type=int, default=None,
+                        help="override the workload's embedding width (profiling: plan builds at full index size)")
     parser.add_argument("--models", default="cfg3,cfg4",
                         help="RGNN train-step workloads added to the cfg2 line ('' for none)")
     parser.add_argument("--model-steps", type=int, default=2, help="timed train steps per model workload")
@@ -570,7 +575,7 @@ def main() -> int:
     partitioned = args.workload == "cfg5" and world > 1
     # weak scaling: an independent batch per rank; cfg5: one global workload split by destination range
     wl = make_workload(args.workload, seed=0 if partitioned else rank, device=device, dtype=dtype,
-                       nodes=args.nodes, edges=args.edges)
+                       nodes=args.nodes, edges=args.edges, emb=args.emb)
     global_nodes, global_edges = int(wl.dim_size), wl.num_edges
     if partitioned:
         wl = shard_workload(wl, rank, world)

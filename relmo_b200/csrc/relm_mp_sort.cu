@@ -190,6 +190,19 @@ __device__ __forceinline__ unsigned lanemask_lt()
    return m;
 }
 
+// Bulk prefetch of items [from, from + count) of a 32-bit array into L2 (the
+// copy engine fetches it while the CTA works on the sub-tile before), for a
+// 16-byte aligned start; the last count % 4 items are left out.
+template < class T >
+__device__ __forceinline__ void prefetch_items_l2(const T* a, int64_t from, int64_t count)
+{
+   static_assert(sizeof(T) == 4, "32-bit items");
+   const T* p = a + from;
+   const uint32_t bytes = (uint32_t)(count * 4) & ~15u;
+   if(bytes == 0 || (reinterpret_cast< uintptr_t >(p) & 15u)) return;
+   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 // Digit counts of CTA c's items [c * subs * kSortSub, ...): ghist[d * ctas + c].
 // Each sub-tile's keys are loaded up front (16 independent loads per thread)
 // and counted with shared-memory atomics into 4 sub-histograms (warp mod 4),
@@ -210,6 +223,8 @@ __global__ void __launch_bounds__(kSortThreads) k_sort_hist(const uint32_t* __re
       const int64_t base = (c * subs + sub) * (int64_t)kSortSub;
       if(base >= n) break;
       const int subn = (n - base) < kSortSub ? (int)(n - base) : kSortSub;
+      if(threadIdx.x == 0 && sub + 1 < subs && base + kSortSub < n)
+         prefetch_items_l2(keys, base + kSortSub, n - base - kSortSub < kSortSub ? n - base - kSortSub : kSortSub);
       uint32_t k[kSortPerThread];
 #pragma unroll
       for(int r = 0; r < kSortPerThread; ++r) {
@@ -284,6 +299,13 @@ __global__ void __launch_bounds__(kSortThreads, kSortCtasPerSm) k_sort_scatter(c
       const int64_t base = (c * subs + sub) * (int64_t)kSortSub;
       if(base >= n) break;
       const int subn = (n - base) < kSortSub ? (int)(n - base) : kSortSub;
+      if(tid == 0) {
+         // this sub-tile's values (read at the reorder step) and the next
+         // sub-tile's keys
+         prefetch_items_l2(vin, base, subn);
+         if(sub + 1 < subs && base + kSortSub < n)
+            prefetch_items_l2(kin, base + kSortSub, n - base - kSortSub < kSortSub ? n - base - kSortSub : kSortSub);
+      }
       for(int i = tid; i < kSortWarps * D / 8; i += kSortThreads)
          reinterpret_cast< uint4* >(wh)[i] = make_uint4(0u, 0u, 0u, 0u);
       for(int i = tid; i < kSortWarps * D / 4; i += kSortThreads)

@@ -275,23 +275,50 @@ class PlanCache {
          const cudaError_t err = cudaStreamSynchronize(static_cast< cudaStream_t >(stream_of(*todo.front().r->out_index)));
          TORCH_CHECK(err == cudaSuccess, "plan build sync: ", cudaGetErrorString(err));
       }
-      for(Pending& q : todo) {
-         const Request& r = *q.r;
-         const int64_t e = r.out_index->numel();
-         relm_mp_plan plan;
-         check_status(relm_mp_plan_build_finish(
-                         r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
-                         e, r.num_rows, r.out_bound, r.gather_rows, r.out_name, r.gather_name, r.gather_first ? 1 : 0,
-                         q.memory.data_ptr(), (size_t)q.memory.numel(), q.scratch.data_ptr(), (size_t)q.scratch.numel(),
-                         q.stats.data_ptr(), stream_of(*r.out_index), &plan),
-                      "plan build");
-         auto entry = std::make_shared< PlanEntry >(
-            PlanEntry{IndexKey::of(*r.out_index), IndexKey::of(*r.gather_index), r.num_rows,
-                      r.out_bound, r.gather_rows, (int)r.gather_first, q.memory, plan, Tensor(), -1, false, -1,
-                      Tensor(), Tensor(), nullptr}
-         );
-         insert(entry, *r.out_index);
+      // The layouts (sort, segment ends, partition) of the plans run side by
+      // side on pool streams: a plan of a few million edges fills part of the
+      // GPU, one short pass after another. Everything they read was complete
+      // at the host wait above. The current stream waits for all of them
+      // before anything else is queued on it (the scratch buffers are freed in
+      // its order when this returns), also when a build raises.
+      const int dev = todo.front().r->out_index->device().index();
+      const c10::cuda::CUDAStream main = at::cuda::getCurrentCUDAStream(dev);
+      const bool fork = todo.size() > 1;
+      std::vector< c10::cuda::CUDAStream > forked;
+      auto join = [&]() {
+         for(const c10::cuda::CUDAStream& s : forked) {
+            at::cuda::CUDAEvent done;
+            done.record(s);
+            done.block(main);
+         }
+         forked.clear();
+      };
+      std::vector< PlanPtr > built;
+      try {
+         for(Pending& q : todo) {
+            const Request& r = *q.r;
+            const int64_t e = r.out_index->numel();
+            const c10::cuda::CUDAStream s = fork ? at::cuda::getStreamFromPool(false, dev) : main;
+            if(fork) forked.push_back(s);
+            relm_mp_plan plan;
+            check_status(relm_mp_plan_build_finish(
+                            r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
+                            e, r.num_rows, r.out_bound, r.gather_rows, r.out_name, r.gather_name,
+                            r.gather_first ? 1 : 0, q.memory.data_ptr(), (size_t)q.memory.numel(),
+                            q.scratch.data_ptr(), (size_t)q.scratch.numel(), q.stats.data_ptr(), s.stream(), &plan),
+                         "plan build");
+            built.push_back(std::make_shared< PlanEntry >(
+               PlanEntry{IndexKey::of(*r.out_index), IndexKey::of(*r.gather_index), r.num_rows,
+                         r.out_bound, r.gather_rows, (int)r.gather_first, q.memory, plan, Tensor(), -1, false, -1,
+                         Tensor(), Tensor(), nullptr}
+            ));
+         }
+      } catch(...) {
+         join();
+         throw;
       }
+      join();
+      for(size_t i = 0; i < built.size(); ++i) insert(built[i], *todo[i].r->out_index);
    }
 
    // The plan of (flat_src, dst) of a fan-in backward, from the forward's
