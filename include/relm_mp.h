@@ -248,6 +248,18 @@ RELM_MP_API int relm_mp_plan_build_identity(const int64_t* gather_index, int64_t
                                             int64_t gather_rows, void* plan_mem, size_t plan_bytes, void* stream,
                                             relm_mp_plan* plan);
 
+/* The plan of an (output index, gather index) pair the caller has validated
+ * already, against num_rows and gather_rows (e.g. the transposed pair of a
+ * plan built before: its gather index is this output index and the other way
+ * round, with the same bounds): both are narrowed to int32 and the output
+ * index is sorted, with no bounds checks and no host wait. Indices out of
+ * range are undefined behaviour here. No counterpart in the reference (its
+ * ops keep no plans). */
+RELM_MP_API int relm_mp_plan_build_trusted(const int64_t* out_index, const int64_t* gather_index,
+                                           int64_t num_edges, int64_t num_rows, int64_t gather_rows,
+                                           void* plan_mem, size_t plan_bytes, void* scratch,
+                                           size_t scratch_bytes, void* stream, relm_mp_plan* plan);
+
 /* relm_mp_plan_build_ex in two halves, so that the builds of several plans
  * (the three or four index pairs of one LGAN op) share one host wait:
  * relm_mp_plan_build_start validates the indices and queues the copy of the

@@ -109,6 +109,7 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "relm_mp_plan_stats_bytes": (_SZ, []),
     "relm_mp_plan_build_identity": (_INT, [_P, _I64, _I64, _I64, _P, _SZ, _P, _PLANP]),
+    "relm_mp_plan_build_trusted": (_INT, [_P, _P, _I64, _I64, _I64, _P, _SZ, _P, _SZ, _P, _PLANP]),
     "relm_mp_plan_build_start": (_INT, [_P, _P, _I64, _I64, _I64, _I64, _P, _SZ, _P, _SZ, _P, _P]),
     "relm_mp_plan_build_finish": (
         _INT,

@@ -61,8 +61,10 @@ struct Carver {
 // kBuildStart validates and queues the copy of the statistics into host_stats
 // (pinned host memory), kBuildFinish (same arguments, after the caller waited
 // for the stream) checks them and lays the plan out; kBuildAll does both with
-// its own wait.
-enum BuildPhase : int { kBuildAll = 0, kBuildStart = 1, kBuildFinish = 2 };
+// its own wait. kBuildTrusted lays out indices the caller has validated
+// against the same bounds already: no checks, no statistics copy, no host wait,
+// and the output index is sorted without looking at its order first.
+enum BuildPhase : int { kBuildAll = 0, kBuildStart = 1, kBuildFinish = 2, kBuildTrusted = 3 };
 int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
                        int64_t num_rows, int64_t out_bound, int64_t gather_rows,
                        const char* out_name, const char* gather_name, bool gather_checked_first,

@@ -382,7 +382,8 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
                        int64_t* gather_covered, BuildPhase phase, void* host_stats)
 {
    if(!plan) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan must not be NULL.");
-   if(phase != kBuildAll && !host_stats) return fail(RELM_MP_ERR_INVALID_ARGUMENT, "host_stats must not be NULL.");
+   if((phase == kBuildStart || phase == kBuildFinish) && !host_stats)
+      return fail(RELM_MP_ERR_INVALID_ARGUMENT, "host_stats must not be NULL.");
    if(num_edges < 0 || num_rows < 0 || gather_rows < 0)
       return fail(RELM_MP_ERR_INVALID_ARGUMENT, "plan sizes must be >= 0.");
    if(num_edges + num_rows >= (int64_t)INT32_MAX || gather_rows >= (int64_t)INT32_MAX)
@@ -428,8 +429,29 @@ int plan_build_bounded(const int64_t* out_index, const int64_t* gather_index, in
    // split (start: validate and queue the copy; finish: after the caller's
    // wait, check them and lay the plan out).
    PlanStats local{};
-   PlanStats& host = phase == kBuildAll ? local : *static_cast< PlanStats* >(host_stats);
-   if(phase != kBuildFinish) {
+   PlanStats& host = (phase == kBuildAll || phase == kBuildTrusted) ? local : *static_cast< PlanStats* >(host_stats);
+   if(phase == kBuildTrusted) {
+      // validated elsewhere against these bounds: the validation kernel only
+      // narrows both indices (no bound can fail), its flags stay on the device
+      if(num_edges > 0) {
+         const bool paired = (reinterpret_cast< uintptr_t >(out_index) & 15u) == 0 &&
+                             (reinterpret_cast< uintptr_t >(gather_index) & 15u) == 0 &&
+                             (reinterpret_cast< uintptr_t >(sl.key_in) & 7u) == 0 &&
+                             (reinterpret_cast< uintptr_t >(gather32) & 7u) == 0;
+         k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
+         if((rc = check_launch("k_init_stats"))) return rc;
+         k_validate<<< grid_for(paired ? (num_edges / 2 + kValidatePairs - 1) / kValidatePairs + 1 : num_edges),
+                    kThreads, 0, stream >>>(
+            out_index, gather_index, num_edges, INT64_MAX, INT64_MAX, sl.key_in, gather32, sl.stats, paired, nullptr
+         );
+         if((rc = check_launch("k_validate"))) return rc;
+      }
+      local.out_bad = ULLONG_MAX;
+      local.gather_bad = ULLONG_MAX;
+      local.descents = 1;
+      local.not_identity = 1;
+      local.gather_moved = 1;
+   } else if(phase != kBuildFinish) {
       k_init_stats<<< 1, 1, 0, stream >>>(sl.stats);
       if((rc = check_launch("k_init_stats"))) return rc;
       if(cover &&
@@ -729,6 +751,19 @@ int relm_mp_plan_build_start(const int64_t* out_index, const int64_t* gather_ind
       out_index, gather_index, num_edges, num_rows, out_bound, gather_rows, nullptr, nullptr, false, plan_mem,
       plan_bytes, scratch, scratch_bytes, static_cast< cudaStream_t >(stream), &plan, nullptr, nullptr, nullptr,
       relm_mp::kBuildStart, host_stats
+   );
+}
+
+int relm_mp_plan_build_trusted(const int64_t* out_index, const int64_t* gather_index, int64_t num_edges,
+                               int64_t num_rows, int64_t gather_rows, void* plan_mem, size_t plan_bytes,
+                               void* scratch, size_t scratch_bytes, void* stream, relm_mp_plan* plan)
+{
+   if(num_edges > 0 && !gather_index)
+      return relm_mp::fail(RELM_MP_ERR_INVALID_ARGUMENT, "gather_index must not be NULL.");
+   return relm_mp::plan_build_bounded(
+      out_index, gather_index, num_edges, num_rows, num_rows, gather_rows, nullptr, nullptr, false, plan_mem,
+      plan_bytes, scratch, scratch_bytes, static_cast< cudaStream_t >(stream), plan, nullptr, nullptr, nullptr,
+      relm_mp::kBuildTrusted, nullptr
    );
 }
 

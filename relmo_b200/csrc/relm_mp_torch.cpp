@@ -193,6 +193,9 @@ class PlanCache {
             }
          }
       }
+      if(!want_cover)
+         if(const PlanPtr t = transposed(out_index, gather_index, out_bound, gather_rows))
+            return build_trusted(out_index, gather_index, num_rows, out_bound, gather_rows, t);
       const int64_t num_edges = out_index.numel();
       Tensor memory = byte_buffer(relm_mp_plan_bytes(num_edges, num_rows), out_index);
       relm_mp_plan plan;
@@ -248,8 +251,10 @@ class PlanCache {
       struct Pending {
          const Request* r;
          Tensor memory, scratch, stats;
+         PlanPtr transposed;  // set: a trusted build (its pair was validated by this plan's build)
       };
       std::vector< Pending > todo;
+      size_t checked = 0;
       for(const Request& r : reqs) {
          if(r.out_index->numel() == 0) continue;
          if(peek(*r.out_index, *r.gather_index, r.num_rows, r.out_bound, r.gather_rows)) continue;
@@ -261,26 +266,28 @@ class PlanCache {
          if(dup) continue;
          const int64_t e = r.out_index->numel();
          Pending q{&r, byte_buffer(relm_mp_plan_bytes(e, r.num_rows), *r.out_index),
-                   byte_buffer(relm_mp_plan_scratch_bytes(e, r.num_rows), *r.out_index),
-                   at::empty({(int64_t)relm_mp_plan_stats_bytes()}, at::TensorOptions().dtype(at::kByte).pinned_memory(true))};
-         check_status(relm_mp_plan_build_start(
-                         r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
-                         e, r.num_rows, r.out_bound, r.gather_rows, q.memory.data_ptr(), (size_t)q.memory.numel(),
-                         q.scratch.data_ptr(), (size_t)q.scratch.numel(), q.stats.data_ptr(), stream_of(*r.out_index)),
-                      "plan build");
+                   byte_buffer(relm_mp_plan_scratch_bytes(e, r.num_rows), *r.out_index), Tensor(),
+                   transposed(*r.out_index, *r.gather_index, r.out_bound, r.gather_rows)};
+         if(!q.transposed) {
+            q.stats = at::empty({(int64_t)relm_mp_plan_stats_bytes()}, at::TensorOptions().dtype(at::kByte).pinned_memory(true));
+            check_status(relm_mp_plan_build_start(
+                            r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
+                            e, r.num_rows, r.out_bound, r.gather_rows, q.memory.data_ptr(), (size_t)q.memory.numel(),
+                            q.scratch.data_ptr(), (size_t)q.scratch.numel(), q.stats.data_ptr(), stream_of(*r.out_index)),
+                         "plan build");
+            ++checked;
+         }
          todo.push_back(std::move(q));
       }
       if(todo.empty()) return;
-      {
-         const cudaError_t err = cudaStreamSynchronize(static_cast< cudaStream_t >(stream_of(*todo.front().r->out_index)));
-         TORCH_CHECK(err == cudaSuccess, "plan build sync: ", cudaGetErrorString(err));
-      }
       // The layouts (sort, segment ends, partition) of the plans run side by
       // side on pool streams: a plan of a few million edges fills part of the
-      // GPU, one short pass after another. Everything they read was complete
-      // at the host wait above. The current stream waits for all of them
-      // before anything else is queued on it (the scratch buffers are freed in
-      // its order when this returns), also when a build raises.
+      // GPU, one short pass after another. Trusted builds start at once (after
+      // the work queued so far on the current stream); the checked ones after
+      // the host wait for their validations. The current stream waits for all
+      // of them before anything else is queued on it (the memory and scratch
+      // buffers, held until then, are freed in its order), also when a build
+      // raises.
       const int dev = todo.front().r->out_index->device().index();
       const c10::cuda::CUDAStream main = at::cuda::getCurrentCUDAStream(dev);
       const bool fork = todo.size() > 1;
@@ -293,13 +300,32 @@ class PlanCache {
          }
          forked.clear();
       };
-      std::vector< PlanPtr > built;
+      std::vector< PlanPtr > built(todo.size());
       try {
-         for(Pending& q : todo) {
+         at::cuda::CUDAEvent ready;
+         if(fork && checked < todo.size()) ready.record(main);
+         for(size_t i = 0; i < todo.size(); ++i) {
+            Pending& q = todo[i];
+            if(!q.transposed) continue;
+            const c10::cuda::CUDAStream s = fork ? at::cuda::getStreamFromPool(false, dev) : main;
+            if(fork) {
+               ready.block(s);
+               forked.push_back(s);
+            }
+            built[i] = trusted_entry(*q.r->out_index, *q.r->gather_index, q.r->num_rows, q.r->out_bound,
+                                     q.r->gather_rows, q.transposed, q.memory, q.scratch, s.stream());
+         }
+         if(checked > 0) {
+            const cudaError_t err = cudaStreamSynchronize(main.stream());
+            TORCH_CHECK(err == cudaSuccess, "plan build sync: ", cudaGetErrorString(err));
+         }
+         for(size_t i = 0; i < todo.size(); ++i) {
+            Pending& q = todo[i];
+            if(q.transposed) continue;
             const Request& r = *q.r;
             const int64_t e = r.out_index->numel();
             const c10::cuda::CUDAStream s = fork ? at::cuda::getStreamFromPool(false, dev) : main;
-            if(fork) forked.push_back(s);
+            if(fork) forked.push_back(s);  // ordered after everything queued before the host wait
             relm_mp_plan plan;
             check_status(relm_mp_plan_build_finish(
                             r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
@@ -307,11 +333,11 @@ class PlanCache {
                             r.gather_first ? 1 : 0, q.memory.data_ptr(), (size_t)q.memory.numel(),
                             q.scratch.data_ptr(), (size_t)q.scratch.numel(), q.stats.data_ptr(), s.stream(), &plan),
                          "plan build");
-            built.push_back(std::make_shared< PlanEntry >(
+            built[i] = std::make_shared< PlanEntry >(
                PlanEntry{IndexKey::of(*r.out_index), IndexKey::of(*r.gather_index), r.num_rows,
                          r.out_bound, r.gather_rows, (int)r.gather_first, q.memory, plan, Tensor(), -1, false, -1,
                          Tensor(), Tensor(), nullptr}
-            ));
+            );
          }
       } catch(...) {
          join();
@@ -319,6 +345,65 @@ class PlanCache {
       }
       join();
       for(size_t i = 0; i < built.size(); ++i) insert(built[i], *todo[i].r->out_index);
+   }
+
+   // A cached plan of the transposed pair (its output index is this gather
+   // index and the other way round) whose bounds are within this pair's: its
+   // build validated both indices, so this pair's build need not. Null if
+   // there is none. (The LGAN backwards run over the transposes of their
+   // forwards' index pairs.)
+   PlanPtr transposed(const Tensor& out_index, const Tensor& gather_index, int64_t out_bound, int64_t gather_rows)
+   {
+      const IndexKey ok = IndexKey::of(out_index);
+      const IndexKey gk = IndexKey::of(gather_index);
+      std::lock_guard< std::mutex > lock(mu_);
+      for(const PlanPtr& e : entries_)
+         if(e->out_key.same(gk) && e->gather_key.same(ok) && e->gather_rows <= out_bound &&
+            e->out_bound <= gather_rows && e->memory.device() == out_index.device())
+            return e;
+      return nullptr;
+   }
+
+   // The plan entry of a pair that `t`'s build validated, laid out on `stream`
+   // into `memory` (relm_mp_plan_bytes) with `scratch`
+   // (relm_mp_plan_scratch_bytes, in use until the stream passes this build),
+   // without validation and without a host wait: relm_mp_plan_build_identity
+   // when t's gather index (this output index) was the identity, else
+   // relm_mp_plan_build_trusted (the same sort and layout as a checked build,
+   // so the same plan). Not inserted into the cache.
+   static PlanPtr trusted_entry(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows,
+                                int64_t out_bound, int64_t gather_rows, const PlanPtr& t, const Tensor& memory,
+                                const Tensor& scratch, cudaStream_t stream)
+   {
+      const int64_t e = out_index.numel();
+      relm_mp_plan plan;
+      const bool identity = (t->plan.flags & RELM_MP_PLAN_GATHER_IDENTITY) && e <= num_rows;
+      if(identity) {
+         check_status(relm_mp_plan_build_identity(gather_index.data_ptr< int64_t >(), e, num_rows, gather_rows,
+                                                  memory.data_ptr(), (size_t)memory.numel(), stream, &plan),
+                      "plan build");
+      } else {
+         check_status(relm_mp_plan_build_trusted(out_index.data_ptr< int64_t >(), gather_index.data_ptr< int64_t >(), e,
+                                                 num_rows, gather_rows, memory.data_ptr(), (size_t)memory.numel(),
+                                                 scratch.data_ptr(), (size_t)scratch.numel(), stream, &plan),
+                      "plan build");
+      }
+      return std::make_shared< PlanEntry >(
+         PlanEntry{IndexKey::of(out_index), IndexKey::of(gather_index), num_rows, out_bound, gather_rows, 0, memory,
+                   plan, Tensor(), -1, false, identity ? e : -1, Tensor(), Tensor(), nullptr}
+      );
+   }
+
+   // trusted_entry on the current stream, cached.
+   PlanPtr build_trusted(const Tensor& out_index, const Tensor& gather_index, int64_t num_rows, int64_t out_bound,
+                         int64_t gather_rows, const PlanPtr& t)
+   {
+      const int64_t e = out_index.numel();
+      const Tensor memory = byte_buffer(relm_mp_plan_bytes(e, num_rows), out_index);
+      const Tensor scratch = byte_buffer(relm_mp_plan_scratch_bytes(e, num_rows), out_index);
+      return insert(trusted_entry(out_index, gather_index, num_rows, out_bound, gather_rows, t, memory, scratch,
+                                  stream_of(out_index)),
+                    out_index);
    }
 
    // The plan of (flat_src, dst) of a fan-in backward, from the forward's

@@ -149,3 +149,61 @@ def test_split_build_shares_one_wait_and_reports_the_first_error() -> None:
     bad[1] = (pairs[1][0], broken, pairs[1][2], pairs[1][3])
     with pytest.raises(capi.RelmMpError, match=r"gat_i index out of bounds: 300 not in \[0, 300\)"):
         run(bad)
+
+
+@pytest.mark.parametrize("rows, gather_rows, edges", [(5000, 9000, 70_000), (1 << 20, 300, 1 << 20), (77, 10, 1000),
+                                                      (1 << 17, 1 << 20, 1 << 22)])
+def test_trusted_build_equals_the_checked_build(rows: int, gather_rows: int, edges: int) -> None:
+    """relm_mp_plan_build_trusted (no validation, no host wait) lays out the
+    same plan as the checked build: the stable sort by output row."""
+
+    import ctypes
+
+    lib = capi.lib()
+    gen = torch.Generator().manual_seed(rows + edges)
+    dev = torch.device("cuda")
+    out_i = torch.randint(0, rows, (edges,), generator=gen)
+    gat_i = torch.randint(0, gather_rows, (edges,), generator=gen)
+    o, g = out_i.to(dev), gat_i.to(dev)
+    mem = capi._workspace(lib.relm_mp_plan_bytes(edges, rows), dev)
+    scr = capi._workspace(lib.relm_mp_plan_scratch_bytes(edges, rows), dev)
+    plan = capi.Plan()
+    capi.check(lib.relm_mp_plan_build_trusted(o.data_ptr(), g.data_ptr(), edges, rows, gather_rows, mem.data_ptr(),
+                                              mem.numel(), scr.data_ptr(), scr.numel(), capi._stream(dev),
+                                              ctypes.byref(plan)))
+    torch.cuda.synchronize()
+    want_gidx, want_ptr = _expect(out_i.numpy(), gat_i.numpy(), rows)
+    assert np.array_equal(capi._device_int32(plan.row_ptr, rows + 1, dev).cpu().numpy(), want_ptr)
+    assert np.array_equal(capi._device_int32(plan.gidx, edges, dev).cpu().numpy(), want_gidx)
+    checked = capi.PlanHandle(o, g, rows, gather_rows)
+    torch.cuda.synchronize()
+    assert np.array_equal(checked.gidx().numpy(), want_gidx)
+
+
+def test_transposed_pair_reuses_the_forward_validation() -> None:
+    """A fan-in sum over (dst, flat_src) with a permuted flat_src, then its
+    backward over the transposed pair (flat_src, dst): the backward's plan is
+    built without a validation of its own (one build more, no index error
+    possible) and gives the oracle's gradient; with a new (unvalidated) dst
+    tensor the backward validates and raises on a bad index as before."""
+
+    gen = torch.Generator().manual_seed(3)
+    dev = torch.device("cuda")
+    n, e, d = 5000, 60_000, 32
+    rel = torch.randn(e, d, generator=gen).to(dev)
+    flat_src = torch.randperm(e, generator=gen).to(dev)
+    dst = torch.randint(0, n, (e,), generator=gen).to(dev)
+    g = torch.randn(n, d, generator=gen).to(dev)
+    ops = torch.ops.relm_mp
+    mp.clear_plan_cache()
+    ops.fanin_reduce(rel, flat_src, dst, n, 0)
+    before = mp.plan_cache_stats()["builds"]
+    grad = ops.fanin_reduce_sum_backward(g, flat_src, dst, e)
+    assert mp.plan_cache_stats()["builds"] == before + 1
+    want = torch.zeros(e, d, dtype=torch.float64)
+    want[flat_src.cpu()] = g.double().cpu()[dst.cpu()]
+    torch.testing.assert_close(grad.double().cpu(), want, rtol=0, atol=0)
+    bad = dst.clone()
+    bad[777] = n
+    with pytest.raises(RuntimeError, match=r"index out of bounds"):
+        ops.fanin_reduce_sum_backward(g, flat_src, bad, e)
