@@ -25,6 +25,7 @@
 #include <ATen/ATen.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <ATen/cuda/CUDAEvent.h>
+#include <c10/cuda/CUDACachingAllocator.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <c10/util/intrusive_ptr.h>
 #include <torch/library.h>
@@ -153,6 +154,7 @@ struct PlanEntry {
    Tensor host_flags;           // pinned copy of the plan's device flags, filled after the build
    std::shared_ptr< at::cuda::CUDAEvent > flags_copied;  // until the flag bits were learned
    std::shared_ptr< at::cuda::CUDAEvent > flags_event;   // the copy's event (kept for the row count)
+   std::shared_ptr< at::cuda::CUDAEvent > ready;  // laid out on a side stream: its end (null: on the user's stream)
 };
 using PlanPtr = std::shared_ptr< PlanEntry >;
 
@@ -189,6 +191,7 @@ class PlanCache {
                entries_.splice(entries_.begin(), entries_, it);
                ++hits_;
                learn_flags(*entries_.front());
+               wait_ready(entries_.front());
                return entries_.front();
             }
          }
@@ -301,6 +304,7 @@ class PlanCache {
          forked.clear();
       };
       std::vector< PlanPtr > built(todo.size());
+      std::vector< c10::cuda::CUDAStream > on(todo.size(), main);
       try {
          at::cuda::CUDAEvent ready;
          if(fork && checked < todo.size()) ready.record(main);
@@ -312,6 +316,7 @@ class PlanCache {
                ready.block(s);
                forked.push_back(s);
             }
+            on[i] = s;
             built[i] = trusted_entry(*q.r->out_index, *q.r->gather_index, q.r->num_rows, q.r->out_bound,
                                      q.r->gather_rows, q.transposed, q.memory, q.scratch, s.stream());
          }
@@ -326,6 +331,7 @@ class PlanCache {
             const int64_t e = r.out_index->numel();
             const c10::cuda::CUDAStream s = fork ? at::cuda::getStreamFromPool(false, dev) : main;
             if(fork) forked.push_back(s);  // ordered after everything queued before the host wait
+            on[i] = s;
             relm_mp_plan plan;
             check_status(relm_mp_plan_build_finish(
                             r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
@@ -340,11 +346,27 @@ class PlanCache {
             );
          }
       } catch(...) {
-         join();
+         join();  // the memory the builds use is freed in the current stream's order
          throw;
       }
-      join();
-      for(size_t i = 0; i < built.size(); ++i) insert(built[i], *todo[i].r->out_index);
+      // No join: each plan carries the end of its layout as an event, which the
+      // first use of the plan (a cache hit) puts in front of its kernels, so an
+      // op waits for its own plan only and the other layouts run on beside it.
+      // The buffers a side stream still uses (the plan memory, its scratch and
+      // the two index tensors) are held back from reuse until that stream is
+      // past this point.
+      for(size_t i = 0; i < built.size(); ++i) {
+         const c10::cuda::CUDAStream& s = on[i];
+         if(fork) {
+            Pending& q = todo[i];
+            for(const Tensor* t : std::initializer_list< const Tensor* >{&q.memory, &q.scratch, q.r->out_index,
+                                                                          q.r->gather_index})
+               c10::cuda::CUDACachingAllocator::recordStream(t->storage().data_ptr(), s);
+            built[i]->ready = std::make_shared< at::cuda::CUDAEvent >();
+            built[i]->ready->record(s);
+         }
+         insert(built[i], *todo[i].r->out_index, s);
+      }
    }
 
    // A cached plan of the transposed pair (its output index is this gather
@@ -446,9 +468,18 @@ class PlanCache {
       std::lock_guard< std::mutex > lock(mu_);
       for(const auto& e : entries_)
          if(e->out_key.same(ok) && e->gather_key.same(gk) && e->num_rows == num_rows && e->out_bound == out_bound
-            && e->gather_rows == gather_rows && e->memory.device() == out_index.device())
+            && e->gather_rows == gather_rows && e->memory.device() == out_index.device()) {
+            wait_ready(e);
             return e;
+         }
       return nullptr;
+   }
+
+   // Work queued next on the current stream waits for the entry's layout
+   // when that ran on a side stream (a no-op once it is done).
+   static void wait_ready(const PlanPtr& e)
+   {
+      if(e->ready) e->ready->block(at::cuda::getCurrentCUDAStream(e->memory.device().index()));
    }
 
    // Output rows of the entry's plan that hold edges (read once per plan):
@@ -531,10 +562,12 @@ class PlanCache {
    // Adds a built plan: queues the copy of its device flags to pinned host
    // memory (no sync; once it has landed, later calls launch only the kernels
    // the plan needs) and puts the entry at the front of the cache.
-   PlanPtr insert(const PlanPtr& entry, const Tensor& like)
+   // Caches the entry; its flags are copied to the host on the stream that
+   // built it (the current stream unless given).
+   PlanPtr insert(const PlanPtr& entry, const Tensor& like, const c10::optional< c10::cuda::CUDAStream >& built_on = {})
    {
       entry->host_flags = at::empty({4}, at::TensorOptions().dtype(at::kInt).pinned_memory(true));
-      const c10::cuda::CUDAStream cs = at::cuda::getCurrentCUDAStream(like.device().index());
+      const c10::cuda::CUDAStream cs = built_on ? *built_on : at::cuda::getCurrentCUDAStream(like.device().index());
       const cudaError_t err = cudaMemcpyAsync(entry->host_flags.data_ptr(), entry->plan.device_flags,
                                               4 * sizeof(int32_t), cudaMemcpyDeviceToHost, cs.stream());
       TORCH_CHECK(err == cudaSuccess, "plan flags copy: ", cudaGetErrorString(err));

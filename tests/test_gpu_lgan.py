@@ -292,3 +292,27 @@ def test_plans_are_reused_across_layers() -> None:
                                       wl.relation_count, 2)
     assert mp.plan_cache_stats()["builds"] == builds
     assert builds - before == 7  # pool, rr, tn, nn forward; tn, nn, rr reverse
+
+
+@pytest.mark.parametrize("mode", [0, 2])
+def test_side_stream_plan_builds_are_awaited(mode) -> None:
+    """The torch ops lay out an op's plans side by side on pool streams and
+    each op waits for its own plan only: with the plan cache cleared before
+    every repetition (all plans built inside the call, the backward's over the
+    forward's transposed pairs), forward and backward equal the C ABI's
+    (sequential builds) bit for bit, at a size where the layouts take long
+    enough to overlap the first op."""
+
+    wl = workloads.lgan(seed=11, entities=1 << 15, relations=1 << 18, emb=32).to("cuda", torch.float32)
+    ops = torch.ops.relm_mp
+    want = capi.lgan_pool_reduce(wl.slots, wl.slot_to_rel, wl.arities, *wl.graph(), wl.entity_dim_size, mode)
+    want_g = capi.lgan_pool_reduce_backward(wl.grad_x, wl.grad_tn, wl.grad_nn, wl.slot_to_rel, wl.arities,
+                                            *wl.graph(), wl.relation_count, mode)
+    for _ in range(4):
+        mp.clear_plan_cache()
+        outs = ops.lgan_pool_reduce(wl.slots, wl.slot_to_rel, wl.arities, *wl.graph(), wl.entity_dim_size, mode)
+        grad = ops.lgan_pool_reduce_backward(wl.grad_x, wl.grad_tn, wl.grad_nn, wl.slot_to_rel, wl.arities,
+                                             *wl.graph(), wl.relation_count, mode)
+        for a, b in zip(outs, want):
+            assert torch.equal(a, b)
+        assert torch.equal(grad, want_g)
