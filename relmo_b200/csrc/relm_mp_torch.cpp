@@ -287,10 +287,10 @@ class PlanCache {
       // side on pool streams: a plan of a few million edges fills part of the
       // GPU, one short pass after another. Trusted builds start at once (after
       // the work queued so far on the current stream); the checked ones after
-      // the host wait for their validations. The current stream waits for all
-      // of them before anything else is queued on it (the memory and scratch
-      // buffers, held until then, are freed in its order), also when a build
-      // raises.
+      // the host wait for their validations. When a build raises, the current
+      // stream waits for all of them before anything else is queued on it
+      // (the memory and scratch buffers are freed in its order); otherwise
+      // each plan's first use waits for its own layout (below).
       const int dev = todo.front().r->out_index->device().index();
       const c10::cuda::CUDAStream main = at::cuda::getCurrentCUDAStream(dev);
       const bool fork = todo.size() > 1;
