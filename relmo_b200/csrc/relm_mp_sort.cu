@@ -36,6 +36,7 @@ namespace relm_mp {
 
 namespace {
 
+// Threads of a sort CTA (512 or 1024; a build-time setting of tuning builds).
 #ifndef RELM_MP_SORT_THREADS
 #define RELM_MP_SORT_THREADS 512
 #endif
@@ -266,7 +267,9 @@ constexpr size_t scatter_smem()
 //            from global memory here, not held through the ranking);
 //   write    in local order to global position off[d] + local position:
 //            coalesced runs of each digit.
-// Two CTAs per SM (108 KB of shared memory, 64 registers each).
+// Two CTAs of 512 threads per SM (104 KB of shared memory, 64 registers each;
+// RELM_MP_SORT_THREADS=1024 builds one CTA of 1024 threads per SM with
+// 16384-item sub-tiles, faster on uniform keys and slower on skewed ones).
 template < int DB >
 __global__ void __launch_bounds__(kSortThreads, kSortCtasPerSm) k_sort_scatter(const uint32_t* __restrict__ kin,
                                                                   const int32_t* __restrict__ vin,
