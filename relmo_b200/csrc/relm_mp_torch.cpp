@@ -476,10 +476,22 @@ class PlanCache {
    }
 
    // Work queued next on the current stream waits for the entry's layout
-   // when that ran on a side stream (a no-op once it is done).
+   // when that ran on a side stream and has not finished yet (the event is
+   // dropped once it has). Under stream capture nothing is queued: event
+   // queries are not allowed there, and a plan used in a capture was built
+   // by an earlier, uncaptured call.
    static void wait_ready(const PlanPtr& e)
    {
-      if(e->ready) e->ready->block(at::cuda::getCurrentCUDAStream(e->memory.device().index()));
+      if(!e->ready) return;
+      const c10::cuda::CUDAStream s = at::cuda::getCurrentCUDAStream(e->memory.device().index());
+      cudaStreamCaptureStatus capturing = cudaStreamCaptureStatusNone;
+      if(cudaStreamIsCapturing(s.stream(), &capturing) != cudaSuccess || capturing != cudaStreamCaptureStatusNone)
+         return;
+      if(e->ready->query()) {
+         e->ready.reset();
+         return;
+      }
+      e->ready->block(s);
    }
 
    // Output rows of the entry's plan that hold edges (read once per plan):
