@@ -316,3 +316,28 @@ def test_side_stream_plan_builds_are_awaited(mode) -> None:
         for a, b in zip(outs, want):
             assert torch.equal(a, b)
         assert torch.equal(grad, want_g)
+
+
+def test_side_stream_plan_builds_on_a_user_stream() -> None:
+    """The same with the ops issued on a stream of the caller's (the plan
+    layouts fork from and are awaited on that stream, not the default one),
+    and the default stream reading the results after waiting for it."""
+
+    wl = workloads.lgan(seed=12, entities=1 << 14, relations=1 << 17, emb=16).to("cuda", torch.float32)
+    ops = torch.ops.relm_mp
+    want = capi.lgan_pool_reduce(wl.slots, wl.slot_to_rel, wl.arities, *wl.graph(), wl.entity_dim_size, 2)
+    want_g = capi.lgan_pool_reduce_backward(wl.grad_x, wl.grad_tn, wl.grad_nn, wl.slot_to_rel, wl.arities,
+                                            *wl.graph(), wl.relation_count, 2)
+    torch.cuda.synchronize()
+    user = torch.cuda.Stream()
+    for _ in range(3):
+        mp.clear_plan_cache()
+        user.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(user):
+            outs = ops.lgan_pool_reduce(wl.slots, wl.slot_to_rel, wl.arities, *wl.graph(), wl.entity_dim_size, 2)
+            grad = ops.lgan_pool_reduce_backward(wl.grad_x, wl.grad_tn, wl.grad_nn, wl.slot_to_rel, wl.arities,
+                                                 *wl.graph(), wl.relation_count, 2)
+        torch.cuda.current_stream().wait_stream(user)
+        for a, b in zip(outs, want):
+            assert torch.equal(a, b)
+        assert torch.equal(grad, want_g)
