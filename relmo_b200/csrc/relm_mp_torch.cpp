@@ -257,7 +257,6 @@ class PlanCache {
          PlanPtr transposed;  // set: a trusted build (its pair was validated by this plan's build)
       };
       std::vector< Pending > todo;
-      size_t checked = 0;
       for(const Request& r : reqs) {
          if(r.out_index->numel() == 0) continue;
          if(peek(*r.out_index, *r.gather_index, r.num_rows, r.out_bound, r.gather_rows)) continue;
@@ -273,23 +272,17 @@ class PlanCache {
                    transposed(*r.out_index, *r.gather_index, r.out_bound, r.gather_rows)};
          if(!q.transposed) {
             q.stats = at::empty({(int64_t)relm_mp_plan_stats_bytes()}, at::TensorOptions().dtype(at::kByte).pinned_memory(true));
-            check_status(relm_mp_plan_build_start(
-                            r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
-                            e, r.num_rows, r.out_bound, r.gather_rows, q.memory.data_ptr(), (size_t)q.memory.numel(),
-                            q.scratch.data_ptr(), (size_t)q.scratch.numel(), q.stats.data_ptr(), stream_of(*r.out_index)),
-                         "plan build");
-            ++checked;
          }
          todo.push_back(std::move(q));
       }
       if(todo.empty()) return;
-      // The layouts (sort, segment ends, partition) of the plans run side by
-      // side on pool streams: a plan of a few million edges fills part of the
-      // GPU, one short pass after another. Trusted builds start at once (after
-      // the work queued so far on the current stream); the checked ones after
-      // the host wait for their validations. When a build raises, the current
-      // stream waits for all of them before anything else is queued on it
-      // (the memory and scratch buffers are freed in its order); otherwise
+      // The builds run side by side on pool streams, each after the work
+      // queued so far on the current stream: a plan of a few million edges
+      // fills part of the GPU, one short pass after another. Checked builds
+      // validate, the host waits for those streams, then they lay out on the
+      // same streams; trusted builds lay out at once. When a build raises, the
+      // current stream waits for all of them before anything else is queued on
+      // it (the memory and scratch buffers are freed in its order); otherwise
       // each plan's first use waits for its own layout (below).
       const int dev = todo.front().r->out_index->device().index();
       const c10::cuda::CUDAStream main = at::cuda::getCurrentCUDAStream(dev);
@@ -307,21 +300,31 @@ class PlanCache {
       std::vector< c10::cuda::CUDAStream > on(todo.size(), main);
       try {
          at::cuda::CUDAEvent ready;
-         if(fork && checked < todo.size()) ready.record(main);
+         if(fork) ready.record(main);
          for(size_t i = 0; i < todo.size(); ++i) {
             Pending& q = todo[i];
-            if(!q.transposed) continue;
+            const Request& r = *q.r;
             const c10::cuda::CUDAStream s = fork ? at::cuda::getStreamFromPool(false, dev) : main;
             if(fork) {
                ready.block(s);
                forked.push_back(s);
             }
             on[i] = s;
-            built[i] = trusted_entry(*q.r->out_index, *q.r->gather_index, q.r->num_rows, q.r->out_bound,
-                                     q.r->gather_rows, q.transposed, q.memory, q.scratch, s.stream());
+            if(q.transposed) {
+               built[i] = trusted_entry(*r.out_index, *r.gather_index, r.num_rows, r.out_bound, r.gather_rows,
+                                        q.transposed, q.memory, q.scratch, s.stream());
+            } else {
+               check_status(relm_mp_plan_build_start(
+                               r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
+                               r.out_index->numel(), r.num_rows, r.out_bound, r.gather_rows, q.memory.data_ptr(),
+                               (size_t)q.memory.numel(), q.scratch.data_ptr(), (size_t)q.scratch.numel(),
+                               q.stats.data_ptr(), s.stream()),
+                            "plan build");
+            }
          }
-         if(checked > 0) {
-            const cudaError_t err = cudaStreamSynchronize(main.stream());
+         for(size_t i = 0; i < todo.size(); ++i) {
+            if(todo[i].transposed) continue;
+            const cudaError_t err = cudaStreamSynchronize(on[i].stream());
             TORCH_CHECK(err == cudaSuccess, "plan build sync: ", cudaGetErrorString(err));
          }
          for(size_t i = 0; i < todo.size(); ++i) {
@@ -329,9 +332,7 @@ class PlanCache {
             if(q.transposed) continue;
             const Request& r = *q.r;
             const int64_t e = r.out_index->numel();
-            const c10::cuda::CUDAStream s = fork ? at::cuda::getStreamFromPool(false, dev) : main;
-            if(fork) forked.push_back(s);  // ordered after everything queued before the host wait
-            on[i] = s;
+            const c10::cuda::CUDAStream s = on[i];
             relm_mp_plan plan;
             check_status(relm_mp_plan_build_finish(
                             r.out_index->data_ptr< int64_t >(), r.gather_index->data_ptr< int64_t >(),
